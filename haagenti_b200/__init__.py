@@ -1,0 +1,362 @@
+"""haagenti_b200: B200-native HCT weight decode behind the reference's API.
+
+Python mirror of the reference's interfaces for this path, calling the
+CUDA library (libhct_b200.so) through its C ABI:
+
+* ``Lz4Decompressor`` -- haagenti_lz4::Lz4Decompressor's ``Decompressor``
+  surface (crates/haagenti-lz4/src/decompress.rs:28-73), decoded on the GPU,
+  plus a batched ``decompress_blocks`` for many independent blocks.
+* ``dequantize_int4`` -- haagenti::testing::dequantize_int4
+  (crates/haagenti/src/testing/quantization.rs:82-131).
+* ``idct_2d`` -- haagenti_core::dct::idct_2d (crates/haagenti-core/src/dct.rs:311-337).
+* ``HctReader`` / ``HctReaderV2`` -- crates/haagenti-hct/src/tensor.rs:408-516,
+  832-1021, with ``decompress_all`` on the GPU and ``decode`` for the full
+  LZ4 -> INT4 -> IDCT pipeline.
+
+Errors are raised as ``HaagentiError`` subclasses named after the
+haagenti_core::Error variants (crates/haagenti-core/src/error.rs:10-65).
+Device buffers are torch CUDA tensors (plumbing only).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _lib as L
+from ._lib import BF16, F16, F32, FLAG_SPECTRAL_Q4
+
+__all__ = [
+    "HaagentiError", "CorruptedData", "BufferTooSmall", "UnexpectedEof", "ChecksumMismatch",
+    "Unsupported", "DeviceError", "Context", "Lz4Decompressor", "dequantize_int4", "idct_2d",
+    "spectral_q4_decode", "HctReader", "HctReaderV2", "F32", "F16", "BF16", "FLAG_SPECTRAL_Q4",
+]
+
+
+class HaagentiError(Exception):
+    def __init__(self, code: int, message: str, block: int = -1, position: int = 0,
+                 required: int = 0, provided: int = 0):
+        super().__init__(message)
+        self.code, self.block, self.position = code, block, position
+        self.required, self.provided = required, provided
+
+
+class CorruptedData(HaagentiError):
+    pass
+
+
+class BufferTooSmall(HaagentiError):
+    pass
+
+
+class UnexpectedEof(HaagentiError):
+    @property
+    def bytes_read(self) -> int:
+        return self.position
+
+
+class ChecksumMismatch(CorruptedData):
+    pass
+
+
+class Unsupported(HaagentiError):
+    pass
+
+
+class DeviceError(HaagentiError):
+    pass
+
+
+_CLASS = {
+    L.UNEXPECTED_EOF: UnexpectedEof, L.BUFFER_TOO_SMALL: BufferTooSmall,
+    L.ZERO_OFFSET: CorruptedData, L.OFFSET_BEYOND: CorruptedData, L.CORRUPTED: CorruptedData,
+    L.CHECKSUM: ChecksumMismatch, L.UNSUPPORTED: Unsupported, L.SIZE_MISMATCH: CorruptedData,
+}
+
+
+def _raise(code: int, err: L.Error | None = None):
+    lib = L.load()
+    if err is not None and err.code:
+        msg = err.message.decode(errors="replace") or lib.hct_b200_status_string(code).decode()
+        cls = _CLASS.get(code, DeviceError)
+        raise cls(code, msg, err.block, err.position, err.required, err.provided)
+    raise _CLASS.get(code, DeviceError)(code, lib.hct_b200_status_string(code).decode())
+
+
+def _check(code: int, err: L.Error | None = None):
+    if code != L.OK:
+        _raise(code, err)
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _stream_ptr(stream=None) -> int:
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return int(s.cuda_stream)
+
+
+_DT = {F32: "float32", F16: "float16", BF16: "bfloat16"}
+
+
+def _torch_dtype(dt: int):
+    return getattr(_torch(), _DT[dt])
+
+
+def _as_host_u8(data) -> np.ndarray:
+    if isinstance(data, np.ndarray):
+        return np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+    return np.frombuffer(bytes(data), dtype=np.uint8)
+
+
+class Context:
+    """One per device: scratch memory, cached DCT bases (GpuContext's role)."""
+
+    _default: dict = {}
+
+    def __init__(self, device: int = 0):
+        lib = L.load()
+        h = C.c_void_p()
+        _check(lib.hct_b200_ctx_create(device, C.byref(h)))
+        self._h = h
+        self.device = device
+
+    @classmethod
+    def default(cls, device: int | None = None) -> "Context":
+        if device is None:
+            device = _torch().cuda.current_device()
+        if device not in cls._default:
+            cls._default[device] = Context(device)
+        return cls._default[device]
+
+    @property
+    def handle(self):
+        return self._h
+
+    def reserve(self, rows: int, cols: int):
+        _check(L.load().hct_b200_ctx_reserve(self._h, rows, cols))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            L.load().hct_b200_ctx_destroy(self._h)
+            self._h = None
+
+    def __del__(self):  # pragma: no cover - interpreter teardown order
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------------ LZ4
+
+class Lz4Decompressor:
+    """GPU implementation of the reference's ``Decompressor`` trait for LZ4."""
+
+    def __init__(self, ctx: Context | None = None):
+        self.ctx = ctx or Context.default()
+
+    @staticmethod
+    def algorithm() -> str:
+        return "lz4"
+
+    def _call(self, data, cap: int, output_size: int) -> bytes:
+        lib = L.load()
+        src = _as_host_u8(data)
+        out = np.zeros(max(cap, 1), dtype=np.uint8)
+        written = C.c_size_t(0)
+        err = L.Error()
+        if cap == output_size:
+            fn = lib.hct_b200_lz4_decompress_with_size
+            rc = fn(self.ctx.handle, src.ctypes.data if src.size else None, src.size, output_size,
+                    out.ctypes.data, C.byref(written), C.byref(err))
+        else:
+            raise ValueError("capacity must equal output size")
+        _check(rc, err)
+        return out[: written.value].tobytes()
+
+    def decompress_with_size(self, data, output_size: int) -> bytes:
+        """decompress.rs:63-68: block decode into output_size bytes, truncated to the result."""
+        return self._call(data, output_size, output_size)
+
+    def decompress_to(self, data, output) -> int:
+        """decompress.rs:59-61: decode into ``output`` (a writable buffer); returns bytes written."""
+        mv = memoryview(output).cast("B")
+        res = self._call(data, len(mv), len(mv))
+        mv[: len(res)] = res
+        return len(res)
+
+    def decompress(self, data) -> bytes:
+        """decompress.rs:33-57: unknown size; start at 4x input, double on BufferTooSmall."""
+        src = _as_host_u8(data)
+        size = src.size * 4
+        while True:
+            try:
+                return self.decompress_with_size(src, size)
+            except BufferTooSmall as e:
+                size = max(e.required, size * 2)
+                if size > 256 * 1024 * 1024:
+                    raise CorruptedData(L.CORRUPTED, "corrupted data: decompressed size exceeds limit")
+
+    def decompress_blocks(self, d_src, blocks: np.ndarray, d_dst, stream=None):
+        """Batched block decode on device buffers.
+
+        ``blocks`` is a structured array of (src_off, dst_off, src_len, dst_cap,
+        out_size) rows; returns the per-block status array (code, position,
+        provided, written), synchronising the stream.
+        """
+        torch = _torch()
+        blk = np.zeros(len(blocks), dtype=[("src_off", "<u8"), ("dst_off", "<u8"),
+                                           ("src_len", "<u4"), ("dst_cap", "<u4"),
+                                           ("out_size", "<u4"), ("reserved", "<u4")])
+        for f in ("src_off", "dst_off", "src_len", "dst_cap", "out_size"):
+            blk[f] = blocks[f]
+        dev = d_src.device
+        d_blk = torch.from_numpy(blk.view(np.uint8).copy()).to(dev)
+        d_st = torch.zeros(len(blocks) * 32, dtype=torch.uint8, device=dev)
+        _check(L.load().hct_b200_lz4_decompress_blocks(
+            d_src.data_ptr(), d_blk.data_ptr(), len(blocks), d_dst.data_ptr(), d_st.data_ptr(),
+            _stream_ptr(stream)))
+        st = d_st.cpu().numpy().view([("code", "<i4"), ("reserved", "<i4"), ("position", "<u8"),
+                                       ("provided", "<u8"), ("written", "<u8")])
+        return st
+
+
+# ------------------------------------------------------------------ INT4
+
+def dequantize_int4(data, num_elements: int, out_dtype: int = F32, device=None, stream=None):
+    """quantization.rs:82-131 on the GPU; returns a CUDA tensor of ``written`` elements.
+
+    ``data`` is a CUDA uint8 tensor or host bytes (copied to the device first).
+    """
+    torch = _torch()
+    if not (hasattr(data, "is_cuda") and data.is_cuda):
+        host = _as_host_u8(data)
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        data = torch.from_numpy(host.copy()).to(dev)
+    out = torch.empty(max(num_elements, 1), dtype=_torch_dtype(out_dtype), device=data.device)
+    written = C.c_size_t(0)
+    _check(L.load().hct_b200_dequantize_int4(data.data_ptr(), data.numel(), num_elements,
+                                             out.data_ptr(), out_dtype, C.byref(written),
+                                             _stream_ptr(stream)))
+    return out[: written.value]
+
+
+# ------------------------------------------------------------------ IDCT
+
+def idct_2d(coeffs, width: int | None = None, height: int | None = None, out_dtype: int = F32,
+            ctx: Context | None = None, stream=None):
+    """dct.rs:311 idct_2d of a (height, width) f32 CUDA tensor on tcgen05 tensor cores."""
+    torch = _torch()
+    x = coeffs.contiguous().to(torch.float32)
+    if height is None or width is None:
+        height, width = (1, x.numel()) if x.dim() == 1 else (x.shape[-2], x.shape[-1])
+    ctx = ctx or Context.default(x.device.index)
+    out = torch.empty((height, width), dtype=_torch_dtype(out_dtype), device=x.device)
+    _check(L.load().hct_b200_idct_2d(ctx.handle, x.data_ptr(), out.data_ptr(), out_dtype, width,
+                                     height, _stream_ptr(stream)))
+    return out
+
+
+def spectral_q4_decode(payload, rows: int, cols: int, out_dtype: int = F32,
+                       ctx: Context | None = None, stream=None):
+    """Decode a device-resident spectral payload (bitmap ++ INT4) to a rows x cols tensor."""
+    torch = _torch()
+    ctx = ctx or Context.default(payload.device.index)
+    out = torch.empty((rows, cols), dtype=_torch_dtype(out_dtype), device=payload.device)
+    _check(L.load().hct_b200_spectral_q4_decode(ctx.handle, payload.data_ptr(), payload.numel(),
+                                                rows, cols, out.data_ptr(), out_dtype,
+                                                _stream_ptr(stream)))
+    return out
+
+
+# ------------------------------------------------------------------ HCT reader
+
+class HctReader:
+    """tensor.rs:408-516 over an HCT file held in memory (bytes / numpy)."""
+
+    _validate = False
+
+    def __init__(self, file, ctx: Context | None = None):
+        self.ctx = ctx or Context.default()
+        self._file = _as_host_u8(file)
+        h = C.c_void_p()
+        err = L.Error()
+        rc = L.load().hct_b200_reader_open(self.ctx.handle, self._file.ctypes.data,
+                                           self._file.size, 1 if self._validate else 0,
+                                           C.byref(h), C.byref(err))
+        _check(rc, err)
+        self._h = h
+        hdr = L.Header()
+        _check(L.load().hct_b200_reader_header(self._h, C.byref(hdr)))
+        self._hdr = hdr
+
+    def header(self) -> dict:
+        h = self._hdr
+        return dict(version=h.version, algorithm=h.algorithm, dtype=h.dtype, flags=h.flags,
+                    original_size=h.original_size, compressed_size=h.compressed_size,
+                    block_size=h.block_size, num_blocks=h.num_blocks,
+                    shape=[int(h.shape[i]) for i in range(min(h.rank, 4))])
+
+    def num_blocks(self) -> int:
+        return int(L.load().hct_b200_reader_num_blocks(self._h))
+
+    @property
+    def shape(self):
+        return self.header()["shape"]
+
+    def upload(self, file, stream=None):
+        """Re-upload the compressed data of a same-layout file (stream-ordered)."""
+        f = _as_host_u8(file) if not isinstance(file, np.ndarray) else file
+        _check(L.load().hct_b200_reader_upload(self._h, f.ctypes.data, f.size, _stream_ptr(stream)))
+
+    def decompress_all(self, stream=None):
+        """tensor.rs:506-515 on the GPU: the concatenated payload as a CUDA uint8 tensor."""
+        torch = _torch()
+        n = self._hdr.original_size
+        out = torch.empty(max(n, 1), dtype=torch.uint8,
+                          device=torch.device("cuda", self.ctx.device))
+        written = C.c_size_t(0)
+        err = L.Error()
+        rc = L.load().hct_b200_reader_decompress_all(self._h, out.data_ptr(), out.numel(),
+                                                     C.byref(written), _stream_ptr(stream),
+                                                     C.byref(err))
+        _check(rc, err)
+        return out[: written.value]
+
+    def decode(self, out_dtype: int = BF16, out=None, stream=None):
+        """Full decode (LZ4 -> INT4 -> [scatter -> IDCT]) into a CUDA tensor of the tensor's shape."""
+        torch = _torch()
+        shape = self.shape
+        if out is None:
+            out = torch.empty(shape, dtype=_torch_dtype(out_dtype),
+                              device=torch.device("cuda", self.ctx.device))
+        err = L.Error()
+        rc = L.load().hct_b200_reader_decode(self._h, out.data_ptr(), out_dtype,
+                                             _stream_ptr(stream), C.byref(err))
+        _check(rc, err)
+        return out
+
+    def close(self):
+        if getattr(self, "_h", None):
+            L.load().hct_b200_reader_close(self._h)
+            self._h = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class HctReaderV2(HctReader):
+    """tensor.rs:832-1021: v1/v2 files, header checksum, per-block XXH3 validation."""
+
+    _validate = True
+
+    def decompress_all_validated(self, stream=None):
+        return self.decompress_all(stream)

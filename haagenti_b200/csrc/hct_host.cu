@@ -1,0 +1,777 @@
+// Host side of libhct_b200.so: the C ABI declared in include/hct_b200.h.
+//
+// This is the C++ counterpart of the reference's Rust host code for the
+// decode path: the Decompressor trait surface of Lz4Decompressor
+// (crates/haagenti-lz4/src/decompress.rs:28-73), dequantize_int4
+// (crates/haagenti/src/testing/quantization.rs:82-131), and the HCT readers
+// (crates/haagenti-hct/src/tensor.rs:408-516, 832-1021).  Container parsing
+// stays on the host; every byte of payload work runs in the CUDA kernels of
+// lz4_decode.cu, int4_dequant.cu and idct_gemm.cu.  There is no CPU decode
+// path: without a device the calls fail with HCT_B200_ERR_NO_DEVICE.
+#include <dlfcn.h>
+
+#include <cstdarg>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+
+using namespace hct;
+
+namespace {
+
+// ---- small utilities -------------------------------------------------------
+
+struct DevBuf {
+    void *p = nullptr;
+    size_t cap = 0;
+    DevBuf() = default;
+    DevBuf(const DevBuf &) = delete;
+    DevBuf &operator=(const DevBuf &) = delete;
+    ~DevBuf() { release(); }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+    }
+    // Grows (never shrinks); contents are not preserved.
+    cudaError_t reserve(size_t bytes) {
+        if (bytes <= cap && p) return cudaSuccess;
+        release();
+        size_t want = bytes < 256 ? 256 : bytes;
+        cudaError_t e = cudaMalloc(&p, want);
+        if (e != cudaSuccess) {
+            p = nullptr;
+            return e;
+        }
+        cap = want;
+        return cudaSuccess;
+    }
+    template <class T>
+    T *as() const {
+        return reinterpret_cast<T *>(p);
+    }
+};
+
+inline uint64_t round_up(uint64_t v, uint64_t m) { return (v + m - 1) / m * m; }
+
+void set_err(hct_b200_error *err, int code, int block, uint64_t pos, uint64_t req, uint64_t prov,
+             const char *fmt, ...) __attribute__((format(printf, 7, 8)));
+
+void set_err(hct_b200_error *err, int code, int block, uint64_t pos, uint64_t req, uint64_t prov,
+             const char *fmt, ...) {
+    if (!err) return;
+    err->code = code;
+    err->block = block;
+    err->position = pos;
+    err->required = req;
+    err->provided = prov;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(err->message, sizeof(err->message), fmt, ap);
+    va_end(ap);
+}
+
+void clear_err(hct_b200_error *err) {
+    if (!err) return;
+    memset(err, 0, sizeof(*err));
+    err->block = -1;
+}
+
+int cuda_code(cudaError_t e) {
+    if (e == cudaSuccess) return HCT_B200_OK;
+    if (e == cudaErrorMemoryAllocation) return HCT_B200_ERR_OUT_OF_MEMORY;
+    if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) return HCT_B200_ERR_NO_DEVICE;
+    return HCT_B200_ERR_CUDA;
+}
+
+#define CK(expr)                                                                       \
+    do {                                                                               \
+        cudaError_t _e = (expr);                                                       \
+        if (_e != cudaSuccess) {                                                       \
+            set_err(err, cuda_code(_e), -1, 0, 0, 0, "%s: %s", #expr, cudaGetErrorString(_e)); \
+            return cuda_code(_e);                                                      \
+        }                                                                              \
+    } while (0)
+
+// XXH3-64 comes from the system libxxhash (the reference uses xxhash-rust
+// 0.8.15, same algorithm); resolved at run time so the library loads
+// without it and only checksum validation needs it.
+using Xxh3Fn = unsigned long long (*)(const void *, size_t);
+Xxh3Fn xxh3_fn() {
+    static Xxh3Fn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        const char *names[] = {"libxxhash.so.0", "libxxhash.so"};
+        for (const char *n : names) {
+            void *h = dlopen(n, RTLD_NOW | RTLD_LOCAL);
+            if (h) {
+                fn = reinterpret_cast<Xxh3Fn>(dlsym(h, "XXH3_64bits"));
+                if (fn) break;
+            }
+        }
+    });
+    return fn;
+}
+
+inline uint16_t rd16(const uint8_t *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+inline uint32_t rd32(const uint8_t *p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+inline uint64_t rd64(const uint8_t *p) { return (uint64_t)rd32(p) | ((uint64_t)rd32(p + 4) << 32); }
+
+constexpr uint16_t FLAG_HEADER_CHECKSUM = 0x0001;  // tensor.rs:53
+constexpr uint16_t FLAG_BLOCK_CHECKSUMS = 0x0002;  // tensor.rs:56
+constexpr uint16_t FLAG_QUANTIZATION = 0x0004;     // tensor.rs:59
+
+struct Basis {
+    DevBuf buf;
+    uint64_t ld = 0;
+};
+
+}  // namespace
+
+// ---- context ---------------------------------------------------------------
+
+struct hct_b200_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;  // used by the host-buffer entry points
+    DevBuf payload, dense, tt, chunk, meta, flag;
+    DevBuf io_in, io_out, io_blk, io_status;
+    std::map<uint64_t, std::unique_ptr<Basis>> bases;
+    DevBuf cos_tbl;
+};
+
+struct hct_b200_reader {
+    hct_b200_ctx *ctx = nullptr;
+    hct_b200_header hdr{};
+    std::vector<uint32_t> offsets, sizes;
+    std::vector<uint64_t> checksums;
+    size_t data_offset = 0;  // within the file
+    size_t data_len = 0;
+    DevBuf d_data, d_blocks, d_status;
+    std::vector<uint32_t> expected;
+    uint64_t rows = 0, cols = 0;
+    bool spectral = false;
+};
+
+namespace {
+
+int ensure_device(hct_b200_ctx *ctx) {
+    cudaError_t e = cudaSetDevice(ctx->device);
+    return cuda_code(e);
+}
+
+// Cached fp16 DCT-III basis of length n (row stride round_up(n, 8)).
+int get_basis(hct_b200_ctx *ctx, uint64_t n, const Basis **out, cudaStream_t s,
+              hct_b200_error *err) {
+    auto it = ctx->bases.find(n);
+    if (it != ctx->bases.end()) {
+        *out = it->second.get();
+        return HCT_B200_OK;
+    }
+    auto b = std::make_unique<Basis>();
+    b->ld = round_up(n, 8);
+    CK(b->buf.reserve(n * b->ld * 2));
+    // cos(pi j / 2n), j < 4n, in f64 from libm on the host
+    std::vector<double> tbl(4 * n);
+    for (uint64_t j = 0; j < 4 * n; j++) tbl[j] = std::cos(M_PI * (double)j / (2.0 * (double)n));
+    CK(ctx->cos_tbl.reserve(tbl.size() * sizeof(double)));
+    CK(cudaMemcpyAsync(ctx->cos_tbl.p, tbl.data(), tbl.size() * sizeof(double),
+                       cudaMemcpyHostToDevice, s));
+    CK(launch_basis(ctx->cos_tbl.as<double>(), n, b->buf.as<half_bits>(), b->ld, s));
+    CK(cudaStreamSynchronize(s));  // tbl is released on return
+    *out = b.get();
+    ctx->bases[n] = std::move(b);
+    return HCT_B200_OK;
+}
+
+int reserve_spectral(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols, size_t payload_bytes,
+                     hct_b200_error *err) {
+    CK(ctx->payload.reserve(payload_bytes + 64));
+    CK(ctx->dense.reserve(rows * round_up(cols, 8) * 2 + 16));
+    CK(ctx->tt.reserve(cols * round_up(rows, 8) * 2 + 16));
+    CK(ctx->chunk.reserve((spectral_chunks(rows * cols) + 1) * sizeof(uint32_t)));
+    CK(ctx->meta.reserve(4 * sizeof(uint64_t)));
+    CK(ctx->flag.reserve(sizeof(int)));
+    return HCT_B200_OK;
+}
+
+// The two contractions on a dense fp16 coefficient matrix held in ctx->dense
+// (rows x round_up(cols, 8)).
+int run_idct(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols, void *d_out, int out_dtype,
+             cudaStream_t s, hct_b200_error *err) {
+    const uint64_t ldw = round_up(cols, 8), ldh = round_up(rows, 8);
+    int *flag = ctx->flag.as<int>();
+    const Basis *bw = nullptr, *bh = nullptr;
+    int rc = get_basis(ctx, cols, &bw, s, err);
+    if (rc) return rc;
+    if (rows == 1) {
+        // a single row: the column transform of length 1 is the identity
+        GemmArgs g{ctx->dense.as<half_bits>(), bw->buf.as<half_bits>(), rows, cols, cols, ldw,
+                   bw->ld, d_out, cols, 1, out_dtype, flag};
+        CK(launch_umma_gemm(g, s));
+        return HCT_B200_OK;
+    }
+    rc = get_basis(ctx, rows, &bh, s, err);
+    if (rc) return rc;
+    GemmArgs g1{ctx->dense.as<half_bits>(), bw->buf.as<half_bits>(), rows, cols, cols, ldw,
+                bw->ld, ctx->tt.p, ldh, 0, HCT_B200_F16, flag};
+    CK(launch_umma_gemm(g1, s));
+    GemmArgs g2{bh->buf.as<half_bits>(), ctx->tt.as<half_bits>(), rows, cols, rows, bh->ld, ldh,
+                d_out, cols, 1, out_dtype, flag};
+    CK(launch_umma_gemm(g2, s));
+    return HCT_B200_OK;
+}
+
+int read_flag(hct_b200_ctx *ctx, cudaStream_t s, hct_b200_error *err) {
+    int f = 0;
+    CK(cudaMemcpyAsync(&f, ctx->flag.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    if (f) {
+        set_err(err, f, -1, 0, 0, 0, "%s", hct_b200_status_string(f));
+        return f;
+    }
+    return HCT_B200_OK;
+}
+
+// First failing block in index order, as HctReader::decompress_all stops there.
+int check_block_status(const std::vector<hct_b200_status> &st, hct_b200_error *err) {
+    for (size_t i = 0; i < st.size(); i++) {
+        const hct_b200_status &s = st[i];
+        if (s.code == HCT_B200_OK) continue;
+        switch (s.code) {
+            case HCT_B200_ERR_UNEXPECTED_EOF:
+                set_err(err, s.code, (int)i, s.position, 0, 0, "unexpected EOF after %llu bytes",
+                        (unsigned long long)s.position);
+                break;
+            case HCT_B200_ERR_BUFFER_TOO_SMALL:
+                set_err(err, s.code, (int)i, s.position, s.position, s.provided,
+                        "buffer too small: need %llu bytes, got %llu",
+                        (unsigned long long)s.position, (unsigned long long)s.provided);
+                break;
+            case HCT_B200_ERR_ZERO_OFFSET:
+                set_err(err, s.code, (int)i, s.position, 0, 0,
+                        "corrupted data: invalid zero offset");
+                break;
+            case HCT_B200_ERR_OFFSET_BEYOND:
+                set_err(err, s.code, (int)i, s.position, 0, 0,
+                        "corrupted data: offset beyond output at offset %llu",
+                        (unsigned long long)s.position);
+                break;
+            default:
+                set_err(err, s.code, (int)i, s.position, 0, 0, "block status %d", s.code);
+        }
+        return s.code;
+    }
+    return HCT_B200_OK;
+}
+
+int lz4_host_call(hct_b200_ctx *ctx, const uint8_t *in, size_t in_len, size_t cap,
+                  size_t output_size, uint8_t *out, size_t *written, hct_b200_error *err) {
+    clear_err(err);
+    if (!ctx || (!in && in_len) || (!out && cap) || !written) {
+        set_err(err, HCT_B200_ERR_INVALID_ARGUMENT, -1, 0, 0, 0, "null argument");
+        return HCT_B200_ERR_INVALID_ARGUMENT;
+    }
+    if (in_len > 0xffffffffull || cap > 0xffffffffull) {
+        set_err(err, HCT_B200_ERR_INVALID_ARGUMENT, -1, 0, 0, 0, "block larger than 4 GiB");
+        return HCT_B200_ERR_INVALID_ARGUMENT;
+    }
+    int rc = ensure_device(ctx);
+    if (rc) { set_err(err, rc, -1, 0, 0, 0, "no CUDA device"); return rc; }
+    cudaStream_t s = ctx->stream;
+    CK(ctx->io_in.reserve(in_len + 16));
+    CK(ctx->io_out.reserve(cap + 16));
+    CK(ctx->io_blk.reserve(sizeof(hct_b200_lz4_block)));
+    CK(ctx->io_status.reserve(sizeof(hct_b200_status)));
+    hct_b200_lz4_block b{0, 0, (uint32_t)in_len, (uint32_t)cap,
+                         (uint32_t)std::min<size_t>(output_size, 0xffffffffull), 0};
+    if (in_len) CK(cudaMemcpyAsync(ctx->io_in.p, in, in_len, cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(ctx->io_blk.p, &b, sizeof(b), cudaMemcpyHostToDevice, s));
+    CK(launch_lz4_blocks(ctx->io_in.as<uint8_t>(), ctx->io_blk.as<hct_b200_lz4_block>(), 1,
+                         ctx->io_out.as<uint8_t>(), ctx->io_status.as<hct_b200_status>(), s));
+    std::vector<hct_b200_status> st(1);
+    CK(cudaMemcpyAsync(st.data(), ctx->io_status.p, sizeof(hct_b200_status),
+                       cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    rc = check_block_status(st, err);
+    if (rc) return rc;
+    if (st[0].written)
+        CK(cudaMemcpy(out, ctx->io_out.p, st[0].written, cudaMemcpyDeviceToHost));
+    *written = st[0].written;
+    return HCT_B200_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int hct_b200_abi_version(void) { return HCT_B200_ABI_VERSION; }
+
+const char *hct_b200_status_string(int code) {
+    switch (code) {
+        case HCT_B200_OK: return "ok";
+        case HCT_B200_ERR_UNEXPECTED_EOF: return "unexpected EOF";
+        case HCT_B200_ERR_BUFFER_TOO_SMALL: return "buffer too small";
+        case HCT_B200_ERR_ZERO_OFFSET: return "corrupted data: invalid zero offset";
+        case HCT_B200_ERR_OFFSET_BEYOND: return "corrupted data: offset beyond output";
+        case HCT_B200_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case HCT_B200_ERR_CORRUPTED: return "corrupted data";
+        case HCT_B200_ERR_CHECKSUM: return "checksum mismatch";
+        case HCT_B200_ERR_UNSUPPORTED: return "unsupported";
+        case HCT_B200_ERR_CUDA: return "CUDA error";
+        case HCT_B200_ERR_NO_DEVICE: return "no CUDA device";
+        case HCT_B200_ERR_TIMEOUT: return "device wait timed out";
+        case HCT_B200_ERR_OUT_OF_MEMORY: return "out of device memory";
+        case HCT_B200_ERR_SIZE_MISMATCH: return "payload size does not match the tensor";
+        default: return "unknown status";
+    }
+}
+
+int hct_b200_ctx_create(int device, hct_b200_ctx **out) {
+    if (!out) return HCT_B200_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return HCT_B200_ERR_NO_DEVICE;
+    if (device < 0 || device >= n) return HCT_B200_ERR_INVALID_ARGUMENT;
+    if (cudaSetDevice(device) != cudaSuccess) return HCT_B200_ERR_NO_DEVICE;
+    auto *c = new hct_b200_ctx();
+    c->device = device;
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        delete c;
+        return HCT_B200_ERR_CUDA;
+    }
+    if (c->flag.reserve(sizeof(int)) != cudaSuccess || c->meta.reserve(32) != cudaSuccess) {
+        cudaStreamDestroy(c->stream);
+        delete c;
+        return HCT_B200_ERR_OUT_OF_MEMORY;
+    }
+    cudaMemset(c->flag.p, 0, sizeof(int));
+    *out = c;
+    return HCT_B200_OK;
+}
+
+void hct_b200_ctx_destroy(hct_b200_ctx *ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    cudaDeviceSynchronize();
+    ctx->bases.clear();
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+}
+
+int hct_b200_ctx_reserve(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols) {
+    if (!ctx) return HCT_B200_ERR_INVALID_ARGUMENT;
+    int rc = ensure_device(ctx);
+    if (rc) return rc;
+    const uint64_t total = rows * cols;
+    hct_b200_error e;
+    return reserve_spectral(ctx, rows, cols, (total + 7) / 8 + total, &e);
+}
+
+int hct_b200_lz4_decompress_blocks(const uint8_t *d_src, const hct_b200_lz4_block *d_blocks,
+                                   uint32_t num_blocks, uint8_t *d_dst, hct_b200_status *d_status,
+                                   void *stream) {
+    if (num_blocks == 0) return HCT_B200_OK;
+    if (!d_src || !d_blocks || !d_dst || !d_status) return HCT_B200_ERR_INVALID_ARGUMENT;
+    return cuda_code(launch_lz4_blocks(d_src, d_blocks, num_blocks, d_dst, d_status,
+                                       (cudaStream_t)stream));
+}
+
+int hct_b200_lz4_decompress_with_size(hct_b200_ctx *ctx, const uint8_t *in, size_t in_len,
+                                      size_t output_size, uint8_t *out, size_t *written,
+                                      hct_b200_error *err) {
+    return lz4_host_call(ctx, in, in_len, output_size, output_size, out, written, err);
+}
+
+int hct_b200_lz4_decompress_to(hct_b200_ctx *ctx, const uint8_t *in, size_t in_len, uint8_t *out,
+                               size_t out_len, size_t *written, hct_b200_error *err) {
+    return lz4_host_call(ctx, in, in_len, out_len, out_len, out, written, err);
+}
+
+int hct_b200_dequantize_int4(const uint8_t *d_data, size_t data_len, size_t num_elements,
+                             void *d_out, int out_dtype, size_t *written, void *stream) {
+    if (!written) return HCT_B200_ERR_INVALID_ARGUMENT;
+    *written = 0;
+    if (out_dtype < HCT_B200_F32 || out_dtype > HCT_B200_BF16) return HCT_B200_ERR_INVALID_ARGUMENT;
+    if (num_elements == 0) return HCT_B200_OK;  // quantization.rs:83-85
+    const size_t nb = (num_elements + 31) / 32, sb = nb * 2;
+    if (data_len < sb) return HCT_B200_OK;       // quantization.rs:90-92
+    const size_t n = std::min<size_t>(num_elements, 2 * (data_len - sb));  // :113-115
+    if (n && (!d_data || !d_out)) return HCT_B200_ERR_INVALID_ARGUMENT;
+    cudaError_t e = launch_dequant_int4(d_data, data_len, n, num_elements, d_out, out_dtype,
+                                        (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_code(e);
+    *written = n;
+    return HCT_B200_OK;
+}
+
+int hct_b200_idct_2d(hct_b200_ctx *ctx, const float *d_in, void *d_out, int out_dtype,
+                     size_t width, size_t height, void *stream) {
+    if (!ctx || !d_in || !d_out) return HCT_B200_ERR_INVALID_ARGUMENT;
+    if (out_dtype < HCT_B200_F32 || out_dtype > HCT_B200_BF16) return HCT_B200_ERR_INVALID_ARGUMENT;
+    if (width == 0 || height == 0) return HCT_B200_OK;
+    int rc = ensure_device(ctx);
+    if (rc) return rc;
+    hct_b200_error e, *err = &e;
+    clear_err(err);
+    cudaStream_t s = (cudaStream_t)stream;
+    uint64_t rows = height, cols = width;
+    if (cols == 1 && rows > 1) std::swap(rows, cols);  // a column vector: one row transform
+    rc = reserve_spectral(ctx, rows, cols, 0, err);
+    if (rc) return rc;
+    CK(cudaMemsetAsync(ctx->flag.p, 0, sizeof(int), s));
+    CK(launch_f32_to_f16_padded(d_in, rows, cols, ctx->dense.as<half_bits>(), round_up(cols, 8), s));
+    rc = run_idct(ctx, rows, cols, d_out, out_dtype, s, err);
+    if (rc) return rc;
+    return read_flag(ctx, s, err);
+}
+
+int hct_b200_spectral_q4_decode(hct_b200_ctx *ctx, const uint8_t *d_payload, size_t payload_len,
+                                size_t rows_in, size_t cols_in, void *d_out, int out_dtype,
+                                void *stream) {
+    if (!ctx || !d_payload || !d_out) return HCT_B200_ERR_INVALID_ARGUMENT;
+    if (((uintptr_t)d_payload & 15u) != 0) return HCT_B200_ERR_INVALID_ARGUMENT;
+    if (out_dtype < HCT_B200_F32 || out_dtype > HCT_B200_BF16) return HCT_B200_ERR_INVALID_ARGUMENT;
+    if (rows_in == 0 || cols_in == 0) return HCT_B200_OK;
+    int rc = ensure_device(ctx);
+    if (rc) return rc;
+    hct_b200_error e, *err = &e;
+    clear_err(err);
+    cudaStream_t s = (cudaStream_t)stream;
+    uint64_t rows = rows_in, cols = cols_in;
+    if (cols == 1 && rows > 1) std::swap(rows, cols);
+    const uint64_t total = rows * cols;
+    if (payload_len < (total + 7) / 8) return HCT_B200_ERR_SIZE_MISMATCH;
+    rc = reserve_spectral(ctx, rows, cols, 0, err);
+    if (rc) return rc;
+    CK(cudaMemsetAsync(ctx->flag.p, 0, sizeof(int), s));
+    CK(launch_spectral_scatter(d_payload, payload_len, rows, cols, ctx->chunk.as<uint32_t>(),
+                               ctx->meta.as<uint64_t>(), ctx->dense.as<half_bits>(),
+                               round_up(cols, 8), ctx->flag.as<int>(), s));
+    rc = run_idct(ctx, rows, cols, d_out, out_dtype, s, err);
+    if (rc) return rc;
+    return read_flag(ctx, s, err);
+}
+
+// ---- reader ----------------------------------------------------------------
+
+int hct_b200_reader_open(hct_b200_ctx *ctx, const uint8_t *file, size_t file_len,
+                         int validate_checksums, hct_b200_reader **out, hct_b200_error *err) {
+    clear_err(err);
+    if (!ctx || !file || !out) {
+        set_err(err, HCT_B200_ERR_INVALID_ARGUMENT, -1, 0, 0, 0, "null argument");
+        return HCT_B200_ERR_INVALID_ARGUMENT;
+    }
+    *out = nullptr;
+    // header (HctHeader::from_bytes, tensor.rs:332-374)
+    if (file_len < 64) {
+        set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0,
+                "hct error: failed to read header: file shorter than 64 bytes");
+        return HCT_B200_ERR_CORRUPTED;
+    }
+    if (memcmp(file, "HCTN", 4) != 0) {
+        set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0, "corrupted data: invalid HCT magic");
+        return HCT_B200_ERR_CORRUPTED;
+    }
+    auto r = std::make_unique<hct_b200_reader>();
+    hct_b200_header &h = r->hdr;
+    h.version = rd32(file + 4);
+    if (h.version > 2) {
+        set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0,
+                "corrupted data: unsupported HCT version: %u (max: 2)", h.version);
+        return HCT_B200_ERR_CORRUPTED;
+    }
+    h.algorithm = file[8];
+    h.dtype = file[9];
+    if (h.algorithm > 1) {
+        set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0, "corrupted data: unknown algorithm: %u",
+                h.algorithm);
+        return HCT_B200_ERR_CORRUPTED;
+    }
+    if (h.dtype > 4) {
+        set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0, "corrupted data: unknown dtype: %u",
+                h.dtype);
+        return HCT_B200_ERR_CORRUPTED;
+    }
+    h.flags = rd16(file + 10);
+    h.original_size = rd64(file + 12);
+    h.compressed_size = rd64(file + 20);
+    h.block_size = rd32(file + 28);
+    h.num_blocks = rd32(file + 32);
+    h.rank = file[36];
+    for (uint32_t i = 0; i < std::min<uint32_t>(h.rank, 4); i++) h.shape[i] = rd64(file + 37 + 8 * i);
+    const bool v2 = h.version >= 2;
+    // v2 header checksum (HctReaderV2::new, tensor.rs:853-865)
+    if (v2 && (h.flags & FLAG_HEADER_CHECKSUM)) {
+        Xxh3Fn x = xxh3_fn();
+        if (!x) {
+            set_err(err, HCT_B200_ERR_UNSUPPORTED, -1, 0, 0, 0, "XXH3 (libxxhash) unavailable");
+            return HCT_B200_ERR_UNSUPPORTED;
+        }
+        const uint64_t stored = rd64(file + 56), computed = x(file, 56);
+        if (stored != computed) {
+            set_err(err, HCT_B200_ERR_CHECKSUM, -1, 0, 0, 0,
+                    "corrupted data: header checksum mismatch: expected %016llx, got %016llx",
+                    (unsigned long long)stored, (unsigned long long)computed);
+            return HCT_B200_ERR_CHECKSUM;
+        }
+    }
+    size_t pos = 64;
+    if (v2 && (h.flags & FLAG_QUANTIZATION)) {
+        if (file_len < pos + 8) {
+            set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0,
+                    "hct error: failed to read quantization");
+            return HCT_B200_ERR_CORRUPTED;
+        }
+        memcpy(h.quant_meta, file + pos, 8);
+        h.has_quant_meta = 1;
+        pos += 8;
+    }
+    const bool sums = v2 && (h.flags & FLAG_BLOCK_CHECKSUMS);
+    const size_t ent = sums ? 16 : 8;
+    const uint32_t nb = h.num_blocks;
+    if ((file_len - pos) / ent < nb) {
+        set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0, "hct error: failed to read block index");
+        return HCT_B200_ERR_CORRUPTED;
+    }
+    r->offsets.resize(nb);
+    r->sizes.resize(nb);
+    r->checksums.assign(nb, 0);
+    for (uint32_t i = 0; i < nb; i++) {
+        const uint8_t *e = file + pos + (size_t)i * ent;
+        r->offsets[i] = rd32(e);
+        r->sizes[i] = rd32(e + 4);
+        if (sums) r->checksums[i] = rd64(e + 8);
+    }
+    pos += (size_t)nb * ent;
+    r->data_offset = pos;
+    r->data_len = file_len - pos;
+    for (uint32_t i = 0; i < nb; i++) {
+        if ((uint64_t)r->offsets[i] + r->sizes[i] > r->data_len) {
+            set_err(err, HCT_B200_ERR_CORRUPTED, (int)i, 0, 0, 0,
+                    "hct error: failed to read block %u", i);
+            return HCT_B200_ERR_CORRUPTED;
+        }
+    }
+    // per-block expected sizes (tensor.rs:494-500)
+    r->expected.resize(nb);
+    if (nb) {
+        const uint64_t full = (uint64_t)(nb - 1) * h.block_size;
+        if (h.original_size < full || h.original_size - full > 0xffffffffull) {
+            set_err(err, HCT_B200_ERR_CORRUPTED, nb - 1, 0, 0, 0,
+                    "corrupted data: original size inconsistent with the block count");
+            return HCT_B200_ERR_CORRUPTED;
+        }
+        for (uint32_t i = 0; i + 1 < nb; i++) r->expected[i] = h.block_size;
+        r->expected[nb - 1] = (uint32_t)(h.original_size - full);
+    }
+    if (validate_checksums && sums) {
+        Xxh3Fn x = xxh3_fn();
+        if (!x) {
+            set_err(err, HCT_B200_ERR_UNSUPPORTED, -1, 0, 0, 0, "XXH3 (libxxhash) unavailable");
+            return HCT_B200_ERR_UNSUPPORTED;
+        }
+        for (uint32_t i = 0; i < nb; i++) {
+            if (r->checksums[i] == 0) continue;  // tensor.rs:957
+            const uint64_t c = x(file + pos + r->offsets[i], r->sizes[i]);
+            if (c != r->checksums[i]) {
+                set_err(err, HCT_B200_ERR_CHECKSUM, (int)i, 0, 0, 0,
+                        "corrupted data: block %u checksum mismatch: expected %016llx, got %016llx",
+                        i, (unsigned long long)r->checksums[i], (unsigned long long)c);
+                return HCT_B200_ERR_CHECKSUM;
+            }
+        }
+    }
+    // tensor geometry for the decode
+    uint64_t rows = 1, cols = 1;
+    if (h.rank == 1) {
+        cols = h.shape[0];
+    } else if (h.rank >= 2) {
+        for (uint32_t i = 0; i + 1 < std::min<uint32_t>(h.rank, 4); i++) rows *= h.shape[i];
+        cols = h.shape[std::min<uint32_t>(h.rank, 4) - 1];
+    } else {
+        cols = 0;
+    }
+    r->rows = rows;
+    r->cols = cols;
+    r->spectral = (h.flags & HCT_B200_FLAG_SPECTRAL_Q4) != 0;
+    r->ctx = ctx;
+
+    int rc = ensure_device(ctx);
+    if (rc) { set_err(err, rc, -1, 0, 0, 0, "no CUDA device"); return rc; }
+    cudaStream_t s = ctx->stream;
+    CK(r->d_data.reserve(r->data_len + 64));
+    CK(r->d_blocks.reserve((size_t)std::max<uint32_t>(nb, 1) * sizeof(hct_b200_lz4_block)));
+    CK(r->d_status.reserve((size_t)std::max<uint32_t>(nb, 1) * sizeof(hct_b200_status)));
+    std::vector<hct_b200_lz4_block> blocks(nb);
+    for (uint32_t i = 0; i < nb; i++) {
+        blocks[i].src_off = r->offsets[i];
+        blocks[i].dst_off = (uint64_t)i * h.block_size;
+        blocks[i].src_len = r->sizes[i];
+        blocks[i].dst_cap = r->expected[i];
+        blocks[i].out_size = r->expected[i];
+        blocks[i].reserved = 0;
+    }
+    if (r->data_len)
+        CK(cudaMemcpyAsync(r->d_data.p, file + pos, r->data_len, cudaMemcpyHostToDevice, s));
+    if (nb)
+        CK(cudaMemcpyAsync(r->d_blocks.p, blocks.data(), nb * sizeof(hct_b200_lz4_block),
+                           cudaMemcpyHostToDevice, s));
+    if (h.dtype == 4 && r->spectral) {
+        rc = reserve_spectral(ctx, rows, cols, h.original_size, err);
+        if (rc) return rc;
+    } else {
+        CK(ctx->payload.reserve(h.original_size + 64));
+        CK(ctx->flag.reserve(sizeof(int)));
+    }
+    CK(cudaStreamSynchronize(s));
+    *out = r.release();
+    return HCT_B200_OK;
+}
+
+int hct_b200_reader_upload(hct_b200_reader *r, const uint8_t *file, size_t file_len, void *stream) {
+    if (!r || !file) return HCT_B200_ERR_INVALID_ARGUMENT;
+    if (file_len != r->data_offset + r->data_len) return HCT_B200_ERR_SIZE_MISMATCH;
+    cudaError_t e = cudaMemcpyAsync(r->d_data.p, file + r->data_offset, r->data_len,
+                                    cudaMemcpyHostToDevice, (cudaStream_t)stream);
+    return cuda_code(e);
+}
+
+int hct_b200_reader_header(const hct_b200_reader *r, hct_b200_header *out) {
+    if (!r || !out) return HCT_B200_ERR_INVALID_ARGUMENT;
+    *out = r->hdr;
+    return HCT_B200_OK;
+}
+
+uint32_t hct_b200_reader_num_blocks(const hct_b200_reader *r) { return r ? r->hdr.num_blocks : 0; }
+
+namespace {
+
+// LZ4 stage into dst; returns the total written after the reference's
+// truncate-and-concatenate rule (compacting on the device if a block is short).
+int reader_lz4(hct_b200_reader *r, uint8_t *d_dst, size_t cap, size_t *written, cudaStream_t s,
+               hct_b200_error *err) {
+    const uint32_t nb = r->hdr.num_blocks;
+    if (cap < r->hdr.original_size) {
+        set_err(err, HCT_B200_ERR_BUFFER_TOO_SMALL, -1, r->hdr.original_size, r->hdr.original_size,
+                cap, "buffer too small: need %llu bytes, got %zu",
+                (unsigned long long)r->hdr.original_size, cap);
+        return HCT_B200_ERR_BUFFER_TOO_SMALL;
+    }
+    *written = 0;
+    if (nb == 0) return HCT_B200_OK;
+    CK(launch_lz4_blocks(r->d_data.as<uint8_t>(), r->d_blocks.as<hct_b200_lz4_block>(), nb, d_dst,
+                         r->d_status.as<hct_b200_status>(), s));
+    std::vector<hct_b200_status> st(nb);
+    CK(cudaMemcpyAsync(st.data(), r->d_status.p, nb * sizeof(hct_b200_status),
+                       cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    int rc = check_block_status(st, err);
+    if (rc) return rc;
+    uint64_t total = 0;
+    bool compact = false;
+    for (uint32_t i = 0; i < nb; i++) {
+        if (compact && st[i].written)
+            CK(cudaMemcpyAsync(d_dst + total, d_dst + (uint64_t)i * r->hdr.block_size,
+                               st[i].written, cudaMemcpyDeviceToDevice, s));
+        if (st[i].written != r->expected[i]) compact = true;
+        total += st[i].written;
+    }
+    if (compact) CK(cudaStreamSynchronize(s));
+    *written = total;
+    return HCT_B200_OK;
+}
+
+}  // namespace
+
+int hct_b200_reader_decompress_all(hct_b200_reader *r, uint8_t *d_out, size_t out_cap,
+                                   size_t *written, void *stream, hct_b200_error *err) {
+    clear_err(err);
+    if (!r || (!d_out && r->hdr.original_size) || !written) {
+        set_err(err, HCT_B200_ERR_INVALID_ARGUMENT, -1, 0, 0, 0, "null argument");
+        return HCT_B200_ERR_INVALID_ARGUMENT;
+    }
+    if (r->hdr.algorithm != 0) {
+        set_err(err, HCT_B200_ERR_UNSUPPORTED, -1, 0, 0, 0, "only LZ4 containers are decoded");
+        return HCT_B200_ERR_UNSUPPORTED;
+    }
+    int rc = ensure_device(r->ctx);
+    if (rc) return rc;
+    return reader_lz4(r, d_out, out_cap, written, (cudaStream_t)stream, err);
+}
+
+int hct_b200_reader_decode(hct_b200_reader *r, void *d_out, int out_dtype, void *stream,
+                           hct_b200_error *err) {
+    clear_err(err);
+    if (!r || !d_out) {
+        set_err(err, HCT_B200_ERR_INVALID_ARGUMENT, -1, 0, 0, 0, "null argument");
+        return HCT_B200_ERR_INVALID_ARGUMENT;
+    }
+    if (out_dtype < HCT_B200_F32 || out_dtype > HCT_B200_BF16) {
+        set_err(err, HCT_B200_ERR_INVALID_ARGUMENT, -1, 0, 0, 0, "bad output dtype");
+        return HCT_B200_ERR_INVALID_ARGUMENT;
+    }
+    if (r->hdr.algorithm != 0) {
+        set_err(err, HCT_B200_ERR_UNSUPPORTED, -1, 0, 0, 0, "only LZ4 containers are decoded");
+        return HCT_B200_ERR_UNSUPPORTED;
+    }
+    if (r->hdr.dtype != 4) {
+        set_err(err, HCT_B200_ERR_UNSUPPORTED, -1, 0, 0, 0, "only I4 tensors are decoded");
+        return HCT_B200_ERR_UNSUPPORTED;
+    }
+    hct_b200_ctx *ctx = r->ctx;
+    int rc = ensure_device(ctx);
+    if (rc) return rc;
+    cudaStream_t s = (cudaStream_t)stream;
+    size_t written = 0;
+    rc = reader_lz4(r, ctx->payload.as<uint8_t>(), ctx->payload.cap, &written, s, err);
+    if (rc) return rc;
+    const uint64_t total = r->rows * r->cols;
+    if (total == 0) return HCT_B200_OK;
+    if (!r->spectral) {
+        // plain INT4 weights (examples/safetensors_to_int4_hct.rs:241-284)
+        size_t n = 0;
+        rc = hct_b200_dequantize_int4(ctx->payload.as<uint8_t>(), written, total, d_out, out_dtype,
+                                      &n, s);
+        if (rc) return rc;
+        if (n != total) {
+            set_err(err, HCT_B200_ERR_SIZE_MISMATCH, -1, 0, total, n,
+                    "INT4 payload holds %zu of %llu elements", n, (unsigned long long)total);
+            return HCT_B200_ERR_SIZE_MISMATCH;
+        }
+        CK(cudaStreamSynchronize(s));
+        return HCT_B200_OK;
+    }
+    if (written != r->hdr.original_size) {
+        set_err(err, HCT_B200_ERR_SIZE_MISMATCH, -1, 0, r->hdr.original_size, written,
+                "spectral payload truncated");
+        return HCT_B200_ERR_SIZE_MISMATCH;
+    }
+    uint64_t rows = r->rows, cols = r->cols;
+    if (cols == 1 && rows > 1) std::swap(rows, cols);
+    CK(cudaMemsetAsync(ctx->flag.p, 0, sizeof(int), s));
+    CK(launch_spectral_scatter(ctx->payload.as<uint8_t>(), written, rows, cols,
+                               ctx->chunk.as<uint32_t>(), ctx->meta.as<uint64_t>(),
+                               ctx->dense.as<half_bits>(), round_up(cols, 8), ctx->flag.as<int>(),
+                               s));
+    rc = run_idct(ctx, rows, cols, d_out, out_dtype, s, err);
+    if (rc) return rc;
+    return read_flag(ctx, s, err);
+}
+
+void hct_b200_reader_close(hct_b200_reader *r) {
+    if (!r) return;
+    cudaSetDevice(r->ctx->device);
+    delete r;
+}
+
+}  // extern "C"

@@ -1,0 +1,204 @@
+/*
+ * hct_b200.h -- C ABI of the B200 HCT weight-decode library (libhct_b200.so).
+ *
+ * Drop-in boundary for haagenti's HCT decode path: LZ4 block decompression
+ * -> INT4 dequantisation with per-block FP16 scales -> inverse-DCT spectral
+ * reconstruction.  Each entry point names the reference interface it
+ * replaces (paths relative to the haagenti repository root).
+ *
+ * Conventions
+ *  - Plain pointers and sizes only.  `d_` pointers are CUDA device pointers,
+ *    other buffers are host memory.  `stream` is a cudaStream_t (NULL = the
+ *    legacy default stream).
+ *  - Every function returns an hct_b200 status code (0 = success).  Codes
+ *    1..4 map 1:1 onto haagenti_core::Error variants raised by
+ *    crates/haagenti-lz4/src/block.rs:261-366.
+ *  - Kernels never trap: a corrupt block yields a per-block status, a device
+ *    wait that does not complete within its bound yields HCT_B200_ERR_TIMEOUT.
+ *  - There is no CPU fallback: without a usable CUDA device every entry
+ *    point returns HCT_B200_ERR_NO_DEVICE.
+ */
+#ifndef HCT_B200_H
+#define HCT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HCT_B200_ABI_VERSION 1
+
+/* ---- status codes ------------------------------------------------------ */
+enum {
+    HCT_B200_OK = 0,
+    HCT_B200_ERR_UNEXPECTED_EOF = 1,     /* Error::UnexpectedEof{bytes_read}      (block.rs:279,294,315,331) */
+    HCT_B200_ERR_BUFFER_TOO_SMALL = 2,   /* Error::BufferTooSmall{required,provided} (block.rs:297,346)    */
+    HCT_B200_ERR_ZERO_OFFSET = 3,        /* Error::corrupted("invalid zero offset")   (block.rs:321)        */
+    HCT_B200_ERR_OFFSET_BEYOND = 4,      /* Error::corrupted_at("offset beyond output", pos) (block.rs:324) */
+    HCT_B200_ERR_INVALID_ARGUMENT = 16,
+    HCT_B200_ERR_CORRUPTED = 17,         /* container-level Error::CorruptedData (tensor.rs:334-374, 463-468) */
+    HCT_B200_ERR_CHECKSUM = 18,          /* XXH3 mismatch (tensor.rs:857-865, 966-973)                       */
+    HCT_B200_ERR_UNSUPPORTED = 19,       /* e.g. Zstd-compressed container                                  */
+    HCT_B200_ERR_CUDA = 20,
+    HCT_B200_ERR_NO_DEVICE = 21,
+    HCT_B200_ERR_TIMEOUT = 22,           /* a bounded device-side wait expired                              */
+    HCT_B200_ERR_OUT_OF_MEMORY = 23,
+    HCT_B200_ERR_SIZE_MISMATCH = 24      /* decoded payload shorter/longer than the tensor needs           */
+};
+
+/* Output element types; values equal haagenti_hct::DType tags (tensor.rs:98-105). */
+enum { HCT_B200_F32 = 0, HCT_B200_F16 = 1, HCT_B200_BF16 = 2 };
+
+/* One independent LZ4 block: decompress_block(src[src_off..+src_len],
+ * &mut dst[dst_off..+dst_cap], out_size).  dst_cap is `output.len()`,
+ * out_size is `output_size` (block.rs:261). */
+typedef struct {
+    uint64_t src_off;
+    uint64_t dst_off;
+    uint32_t src_len;
+    uint32_t dst_cap;
+    uint32_t out_size;
+    uint32_t reserved;
+} hct_b200_lz4_block;
+
+/* Per-block result.  position = bytes_read (EOF), required (BufferTooSmall)
+ * or output_pos (offset errors); provided = `provided` of BufferTooSmall;
+ * written = bytes produced (the Ok(usize) value on success). */
+typedef struct {
+    int32_t code;
+    int32_t reserved;
+    uint64_t position;
+    uint64_t provided;
+    uint64_t written;
+} hct_b200_status;
+
+/* Host-side error report for the higher-level calls. */
+typedef struct {
+    int32_t code;
+    int32_t block;        /* failing block index, -1 if not block-specific */
+    uint64_t position;
+    uint64_t required;
+    uint64_t provided;
+    char message[192];
+} hct_b200_error;
+
+/* HctHeader (tensor.rs:275-292) plus version and the v2 extras. */
+typedef struct {
+    uint32_t version;
+    uint8_t algorithm;
+    uint8_t dtype;
+    uint16_t flags;
+    uint64_t original_size;
+    uint64_t compressed_size;
+    uint32_t block_size;
+    uint32_t num_blocks;
+    uint32_t rank;
+    uint32_t reserved;
+    uint64_t shape[4];
+    uint8_t quant_meta[8]; /* QuantizationMetadata bytes when FLAG_QUANTIZATION */
+    uint32_t has_quant_meta;
+    uint32_t reserved2;
+} hct_b200_header;
+
+/* Flag of this library's composite spectral payload (bitmap ++ INT4 of the
+ * retained DCT coefficients).  Not a reference flag: the reference defines
+ * 0x0001..0x0010 (tensor.rs:53-69). */
+#define HCT_B200_FLAG_SPECTRAL_Q4 0x0100u
+
+typedef struct hct_b200_ctx hct_b200_ctx;
+typedef struct hct_b200_reader hct_b200_reader;
+
+/* ---- context ------------------------------------------------------------
+ * One context per device owns the scratch memory, the cached DCT bases and
+ * the TMA descriptors.  Replaces GpuContext (crates/haagenti-cuda/src/lib.rs:89-230).
+ * Calls on one context must be serialised by the caller (as GpuContext). */
+int hct_b200_ctx_create(int device, hct_b200_ctx **out);
+void hct_b200_ctx_destroy(hct_b200_ctx *ctx);
+/* Grow the context's scratch so that decoding a rows x cols spectral
+ * tensor needs no further allocation. */
+int hct_b200_ctx_reserve(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols);
+const char *hct_b200_status_string(int code);
+int hct_b200_abi_version(void);
+
+/* ---- LZ4 ----------------------------------------------------------------
+ * Batched form of block::decompress_block (crates/haagenti-lz4/src/block.rs:261),
+ * one warp per independent block.  Results are exact: byte-for-byte output and
+ * the same error variant/position as the reference for every block.
+ * Stream-ordered; d_status is written when the kernel completes. */
+int hct_b200_lz4_decompress_blocks(const uint8_t *d_src, const hct_b200_lz4_block *d_blocks,
+                                   uint32_t num_blocks, uint8_t *d_dst,
+                                   hct_b200_status *d_status, void *stream);
+
+/* Lz4Decompressor::decompress_with_size (crates/haagenti-lz4/src/decompress.rs:63-68)
+ * on host buffers: `out` must hold output_size bytes; *written = truncated length. */
+int hct_b200_lz4_decompress_with_size(hct_b200_ctx *ctx, const uint8_t *in, size_t in_len,
+                                      size_t output_size, uint8_t *out, size_t *written,
+                                      hct_b200_error *err);
+
+/* Lz4Decompressor::decompress_to (decompress.rs:59-61): output.len() == out_len. */
+int hct_b200_lz4_decompress_to(hct_b200_ctx *ctx, const uint8_t *in, size_t in_len, uint8_t *out,
+                               size_t out_len, size_t *written, hct_b200_error *err);
+
+/* ---- INT4 ---------------------------------------------------------------
+ * haagenti::testing::dequantize_int4 (crates/haagenti/src/testing/quantization.rs:82-131):
+ * out[i] = f32(nibble_i - 8) * f32(scale[i/32]); layout [ceil(n/32) f16 LE scales]
+ * [ceil(n/2) nibble bytes, low nibble first].  *written follows the reference's
+ * short-input rules (0 if the scales do not fit, fewer than n if the nibbles run
+ * out) and is known on return without a device sync.  F32 output is bit-exact;
+ * F16/BF16 outputs are the round-to-nearest-even of that f32 value. */
+int hct_b200_dequantize_int4(const uint8_t *d_data, size_t data_len, size_t num_elements,
+                             void *d_out, int out_dtype, size_t *written, void *stream);
+
+/* ---- IDCT ---------------------------------------------------------------
+ * haagenti_core::dct::idct_2d (crates/haagenti-core/src/dct.rs:311-337) and
+ * GpuDctContext::idct_2d (crates/haagenti-cuda/src/dct_gpu.rs:1404-1412):
+ * orthonormal 2-D DCT-III of a row-major height x width f32 matrix, as two
+ * dense contractions against the DCT basis on tcgen05 tensor cores (fp16
+ * operands, fp32 accumulation in TMEM). */
+int hct_b200_idct_2d(hct_b200_ctx *ctx, const float *d_in, void *d_out, int out_dtype,
+                     size_t width, size_t height, void *stream);
+
+/* Decode an already LZ4-decompressed spectral payload held on the device
+ * (bitmap ++ quantize_int4(values)), rows x cols, into d_out.  The INT4
+ * dequantisation and bitmap scatter run on the GPU and feed the two IDCT
+ * contractions (CompressiveSpectralDecoder::reconstruct, crates/haagenti/src/
+ * compressive.rs:732-752, with INT4 values in place of FP16). */
+int hct_b200_spectral_q4_decode(hct_b200_ctx *ctx, const uint8_t *d_payload, size_t payload_len,
+                                size_t rows, size_t cols, void *d_out, int out_dtype,
+                                void *stream);
+
+/* ---- HCT reader ---------------------------------------------------------
+ * HctReader::new / HctReaderV2::new (crates/haagenti-hct/src/tensor.rs:417-444,
+ * 841-922): parse the header, optional quantization metadata and block index of
+ * an HCT file held in host memory, validate the v2 header checksum, and upload
+ * the compressed data section to the device (one copy).  With
+ * validate_checksums != 0 the per-block XXH3-64 checksums are verified on the
+ * host first (HctReaderV2::read_block_validated, tensor.rs:941-975). */
+int hct_b200_reader_open(hct_b200_ctx *ctx, const uint8_t *file, size_t file_len,
+                         int validate_checksums, hct_b200_reader **out, hct_b200_error *err);
+/* Re-upload the compressed data of a file with the same layout into an open
+ * reader (stream-ordered H2D copy; pinned host memory makes it asynchronous). */
+int hct_b200_reader_upload(hct_b200_reader *r, const uint8_t *file, size_t file_len, void *stream);
+int hct_b200_reader_header(const hct_b200_reader *r, hct_b200_header *out);
+uint32_t hct_b200_reader_num_blocks(const hct_b200_reader *r);
+/* HctReader::decompress_all (tensor.rs:506-515) on the GPU: all blocks in one
+ * launch into d_out (capacity out_cap).  Reference semantics: each block's
+ * expected size is block_size except the last (tensor.rs:494-500); a short
+ * block is truncated and the rest concatenated.  *written = total bytes. */
+int hct_b200_reader_decompress_all(hct_b200_reader *r, uint8_t *d_out, size_t out_cap,
+                                   size_t *written, void *stream, hct_b200_error *err);
+/* Full decode of the tensor into d_out (rows*cols elements of out_dtype):
+ *   spectral (flag HCT_B200_FLAG_SPECTRAL_Q4): LZ4 -> INT4 -> scatter -> IDCT;
+ *   plain INT4 (dtype I4 without the flag, examples/safetensors_to_int4_hct.rs):
+ *     LZ4 -> dequantize_int4. */
+int hct_b200_reader_decode(hct_b200_reader *r, void *d_out, int out_dtype, void *stream,
+                           hct_b200_error *err);
+void hct_b200_reader_close(hct_b200_reader *r);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HCT_B200_H */
