@@ -54,6 +54,11 @@ class Header(C.Structure):
                 ("has_quant_meta", C.c_uint32), ("reserved2", C.c_uint32)]
 
 
+class KernelStats(C.Structure):
+    _fields_ = [("name", C.c_char * 32), ("launches", C.c_uint64), ("total_ms", C.c_double),
+                ("work", C.c_double)]
+
+
 # Every exported symbol with (restype, argtypes); tests check the list
 # against include/hct_b200.h.
 _vp, _sz, _u8p = C.c_void_p, C.c_size_t, C.c_void_p
@@ -63,6 +68,15 @@ SIGNATURES = {
     "hct_b200_ctx_create": (C.c_int, [C.c_int, C.POINTER(C.c_void_p)]),
     "hct_b200_ctx_destroy": (None, [_vp]),
     "hct_b200_ctx_reserve": (C.c_int, [_vp, C.c_uint64, C.c_uint64]),
+    "hct_b200_ctx_profile": (C.c_int, [_vp, C.c_int]),
+    "hct_b200_ctx_profile_read": (C.c_int, [_vp, C.POINTER(KernelStats), C.c_int,
+                                            C.POINTER(C.c_int)]),
+    "hct_b200_lz4_max_compressed_size": (C.c_size_t, [C.c_size_t]),
+    "hct_b200_lz4_compress_block": (C.c_int, [_u8p, _sz, _u8p, _sz, C.POINTER(C.c_size_t)]),
+    "hct_b200_lz4_compress_chunks": (C.c_int, [_u8p, _sz, _sz, _u8p, _sz,
+                                               C.POINTER(C.c_uint32)]),
+    "hct_b200_quantize_int4": (C.c_int, [_vp, _sz, _u8p]),
+    "hct_b200_spectral_select": (C.c_int, [_vp, _sz, _sz, _u8p, _vp, C.POINTER(C.c_size_t)]),
     "hct_b200_lz4_decompress_blocks": (C.c_int, [_vp, _vp, C.c_uint32, _vp, _vp, _vp]),
     "hct_b200_lz4_decompress_with_size": (C.c_int, [_vp, _u8p, _sz, _sz, _u8p,
                                                     C.POINTER(C.c_size_t), C.POINTER(Error)]),

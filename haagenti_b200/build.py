@@ -15,7 +15,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libhct_b200.so")
-SOURCES = ["lz4_decode.cu", "int4_dequant.cu", "idct_gemm.cu", "hct_host.cu"]
+SOURCES = ["lz4_decode.cu", "int4_dequant.cu", "idct_gemm.cu", "hct_host.cu", "hct_encode.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -33,8 +33,8 @@ def build(verbose: bool = False, force: bool = False) -> str:
     if (not force and os.path.exists(OUT)
             and all(os.path.getmtime(OUT) >= os.path.getmtime(d) for d in deps)):
         return OUT
-    cmd = [nvcc(), "-O3", "-std=c++17", *ARCH, "-lineinfo", "-Xcompiler", "-fPIC",
-           "-Xcompiler", "-Wall", "-shared", "-o", OUT, *srcs, "-ldl"]
+    cmd = [nvcc(), "-O3", "-std=c++17", *ARCH, "-lineinfo", "-Xcompiler", "-fPIC,-fopenmp",
+           "-Xcompiler", "-Wall", "-shared", "-o", OUT, *srcs, "-ldl", "-lgomp"]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     subprocess.run(cmd, check=True)

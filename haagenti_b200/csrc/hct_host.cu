@@ -140,6 +140,17 @@ struct Basis {
 
 // ---- context ---------------------------------------------------------------
 
+// Per-launch timing records (CUDA events on the launching stream), kept only
+// while profiling is enabled on the context.
+enum ProfKind { PK_LZ4 = 0, PK_SCATTER = 1, PK_GEMM = 2, PK_DEQUANT = 3, PK_COUNT = 4 };
+static const char *const kProfNames[PK_COUNT] = {"lz4_decode_blocks", "spectral_scatter",
+                                                 "umma_gemm", "dequant_int4"};
+struct ProfRec {
+    int kind;
+    cudaEvent_t a, b;
+    double work;  // algorithmic flops (umma_gemm) or bytes (the others)
+};
+
 struct hct_b200_ctx {
     int device = 0;
     cudaStream_t stream = nullptr;  // used by the host-buffer entry points
@@ -147,6 +158,34 @@ struct hct_b200_ctx {
     DevBuf io_in, io_out, io_blk, io_status;
     std::map<uint64_t, std::unique_ptr<Basis>> bases;
     DevBuf cos_tbl;
+    bool profiling = false;
+    std::vector<ProfRec> prof;
+    std::vector<cudaEvent_t> event_pool;
+    size_t pool_used = 0;
+
+    cudaEvent_t event() {
+        if (pool_used == event_pool.size()) {
+            cudaEvent_t e;
+            if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+            event_pool.push_back(e);
+        }
+        return event_pool[pool_used++];
+    }
+    // Brackets one launch: call begin() before and end() after it.
+    int prof_begin(cudaStream_t s) {
+        if (!profiling) return -1;
+        ProfRec r{0, event(), event(), 0.0};
+        if (!r.a || !r.b) return -1;
+        cudaEventRecord(r.a, s);
+        prof.push_back(r);
+        return (int)prof.size() - 1;
+    }
+    void prof_end(int slot, int kind, double work, cudaStream_t s) {
+        if (slot < 0) return;
+        prof[slot].kind = kind;
+        prof[slot].work = work;
+        cudaEventRecord(prof[slot].b, s);
+    }
 };
 
 struct hct_b200_reader {
@@ -217,17 +256,23 @@ int run_idct(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols, void *d_out, int o
         // a single row: the column transform of length 1 is the identity
         GemmArgs g{ctx->dense.as<half_bits>(), bw->buf.as<half_bits>(), rows, cols, cols, ldw,
                    bw->ld, d_out, cols, 1, out_dtype, flag};
+        int slot = ctx->prof_begin(s);
         CK(launch_umma_gemm(g, s));
+        ctx->prof_end(slot, PK_GEMM, 2.0 * rows * cols * cols, s);
         return HCT_B200_OK;
     }
     rc = get_basis(ctx, rows, &bh, s, err);
     if (rc) return rc;
     GemmArgs g1{ctx->dense.as<half_bits>(), bw->buf.as<half_bits>(), rows, cols, cols, ldw,
                 bw->ld, ctx->tt.p, ldh, 0, HCT_B200_F16, flag};
+    int slot = ctx->prof_begin(s);
     CK(launch_umma_gemm(g1, s));
+    ctx->prof_end(slot, PK_GEMM, 2.0 * rows * cols * cols, s);
     GemmArgs g2{bh->buf.as<half_bits>(), ctx->tt.as<half_bits>(), rows, cols, rows, bh->ld, ldh,
                 d_out, cols, 1, out_dtype, flag};
+    slot = ctx->prof_begin(s);
     CK(launch_umma_gemm(g2, s));
+    ctx->prof_end(slot, PK_GEMM, 2.0 * rows * cols * rows, s);
     return HCT_B200_OK;
 }
 
@@ -364,6 +409,7 @@ void hct_b200_ctx_destroy(hct_b200_ctx *ctx) {
     cudaSetDevice(ctx->device);
     cudaDeviceSynchronize();
     ctx->bases.clear();
+    for (cudaEvent_t e : ctx->event_pool) cudaEventDestroy(e);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
 }
@@ -375,6 +421,40 @@ int hct_b200_ctx_reserve(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols) {
     const uint64_t total = rows * cols;
     hct_b200_error e;
     return reserve_spectral(ctx, rows, cols, (total + 7) / 8 + total, &e);
+}
+
+int hct_b200_ctx_profile(hct_b200_ctx *ctx, int enable) {
+    if (!ctx) return HCT_B200_ERR_INVALID_ARGUMENT;
+    ctx->profiling = enable != 0;
+    ctx->prof.clear();
+    ctx->pool_used = 0;
+    return HCT_B200_OK;
+}
+
+int hct_b200_ctx_profile_read(hct_b200_ctx *ctx, hct_b200_kernel_stats *out, int max_entries,
+                              int *count) {
+    if (!ctx || !count || (!out && max_entries > 0)) return HCT_B200_ERR_INVALID_ARGUMENT;
+    int rc = ensure_device(ctx);
+    if (rc) return rc;
+    hct_b200_kernel_stats agg[PK_COUNT];
+    memset(agg, 0, sizeof(agg));
+    for (int k = 0; k < PK_COUNT; k++) snprintf(agg[k].name, sizeof(agg[k].name), "%s", kProfNames[k]);
+    for (const ProfRec &r : ctx->prof) {
+        if (cudaEventSynchronize(r.b) != cudaSuccess) return HCT_B200_ERR_CUDA;
+        float ms = 0.f;
+        if (cudaEventElapsedTime(&ms, r.a, r.b) != cudaSuccess) return HCT_B200_ERR_CUDA;
+        agg[r.kind].launches += 1;
+        agg[r.kind].total_ms += ms;
+        agg[r.kind].work += r.work;
+    }
+    int n = 0;
+    for (int k = 0; k < PK_COUNT; k++) {
+        if (!agg[k].launches) continue;
+        if (n < max_entries) out[n] = agg[k];
+        n++;
+    }
+    *count = n;
+    return HCT_B200_OK;
 }
 
 int hct_b200_lz4_decompress_blocks(const uint8_t *d_src, const hct_b200_lz4_block *d_blocks,
@@ -454,9 +534,11 @@ int hct_b200_spectral_q4_decode(hct_b200_ctx *ctx, const uint8_t *d_payload, siz
     rc = reserve_spectral(ctx, rows, cols, 0, err);
     if (rc) return rc;
     CK(cudaMemsetAsync(ctx->flag.p, 0, sizeof(int), s));
+    int slot = ctx->prof_begin(s);
     CK(launch_spectral_scatter(d_payload, payload_len, rows, cols, ctx->chunk.as<uint32_t>(),
                                ctx->meta.as<uint64_t>(), ctx->dense.as<half_bits>(),
                                round_up(cols, 8), ctx->flag.as<int>(), s));
+    ctx->prof_end(slot, PK_SCATTER, (double)payload_len + 2.0 * total, s);
     rc = run_idct(ctx, rows, cols, d_out, out_dtype, s, err);
     if (rc) return rc;
     return read_flag(ctx, s, err);
@@ -669,8 +751,10 @@ int reader_lz4(hct_b200_reader *r, uint8_t *d_dst, size_t cap, size_t *written, 
     }
     *written = 0;
     if (nb == 0) return HCT_B200_OK;
+    int slot = r->ctx->prof_begin(s);
     CK(launch_lz4_blocks(r->d_data.as<uint8_t>(), r->d_blocks.as<hct_b200_lz4_block>(), nb, d_dst,
                          r->d_status.as<hct_b200_status>(), s));
+    r->ctx->prof_end(slot, PK_LZ4, (double)r->hdr.compressed_size + (double)r->hdr.original_size, s);
     std::vector<hct_b200_status> st(nb);
     CK(cudaMemcpyAsync(st.data(), r->d_status.p, nb * sizeof(hct_b200_status),
                        cudaMemcpyDeviceToHost, s));
@@ -740,8 +824,11 @@ int hct_b200_reader_decode(hct_b200_reader *r, void *d_out, int out_dtype, void 
     if (!r->spectral) {
         // plain INT4 weights (examples/safetensors_to_int4_hct.rs:241-284)
         size_t n = 0;
+        int slot = ctx->prof_begin(s);
         rc = hct_b200_dequantize_int4(ctx->payload.as<uint8_t>(), written, total, d_out, out_dtype,
                                       &n, s);
+        ctx->prof_end(slot, PK_DEQUANT, (double)written + (out_dtype == HCT_B200_F32 ? 4.0 : 2.0) * n,
+                      s);
         if (rc) return rc;
         if (n != total) {
             set_err(err, HCT_B200_ERR_SIZE_MISMATCH, -1, 0, total, n,
@@ -759,10 +846,12 @@ int hct_b200_reader_decode(hct_b200_reader *r, void *d_out, int out_dtype, void 
     uint64_t rows = r->rows, cols = r->cols;
     if (cols == 1 && rows > 1) std::swap(rows, cols);
     CK(cudaMemsetAsync(ctx->flag.p, 0, sizeof(int), s));
+    int slot = ctx->prof_begin(s);
     CK(launch_spectral_scatter(ctx->payload.as<uint8_t>(), written, rows, cols,
                                ctx->chunk.as<uint32_t>(), ctx->meta.as<uint64_t>(),
                                ctx->dense.as<half_bits>(), round_up(cols, 8), ctx->flag.as<int>(),
                                s));
+    ctx->prof_end(slot, PK_SCATTER, (double)written + 2.0 * total, s);
     rc = run_idct(ctx, rows, cols, d_out, out_dtype, s, err);
     if (rc) return rc;
     return read_flag(ctx, s, err);

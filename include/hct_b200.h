@@ -122,6 +122,24 @@ int hct_b200_ctx_reserve(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols);
 const char *hct_b200_status_string(int code);
 int hct_b200_abi_version(void);
 
+/* Per-kernel timing of the context's own launches, for roofline reports.
+ * With profiling enabled every kernel launch made through the context is
+ * bracketed by CUDA events recorded on its launch stream; _read synchronises
+ * those events and returns one entry per kernel kind (lz4_decode_blocks,
+ * spectral_scatter, umma_gemm, dequant_int4).  `work` is the algorithmic
+ * work summed over launches: FLOPs (2*M*N*K) for umma_gemm, bytes read +
+ * written for the others.  No reference counterpart (the reference keeps
+ * ad-hoc DecompressStats, crates/haagenti-cuda/src/decompress.rs:55-94). */
+typedef struct {
+    char name[32];
+    uint64_t launches;
+    double total_ms;
+    double work;
+} hct_b200_kernel_stats;
+int hct_b200_ctx_profile(hct_b200_ctx *ctx, int enable); /* enable/disable; clears records */
+int hct_b200_ctx_profile_read(hct_b200_ctx *ctx, hct_b200_kernel_stats *out, int max_entries,
+                              int *count);
+
 /* ---- LZ4 ----------------------------------------------------------------
  * Batched form of block::decompress_block (crates/haagenti-lz4/src/block.rs:261),
  * one warp per independent block.  Results are exact: byte-for-byte output and
@@ -140,6 +158,25 @@ int hct_b200_lz4_decompress_with_size(hct_b200_ctx *ctx, const uint8_t *in, size
 /* Lz4Decompressor::decompress_to (decompress.rs:59-61): output.len() == out_len. */
 int hct_b200_lz4_decompress_to(hct_b200_ctx *ctx, const uint8_t *in, size_t in_len, uint8_t *out,
                                size_t out_len, size_t *written, hct_b200_error *err);
+
+/* Writer side (host CPU; produces the blocks the decoder consumes):
+ * block::compress_block (crates/haagenti-lz4/src/block.rs:73-147) and
+ * max_compressed_size (block.rs:370-373).  _chunks compresses block_size
+ * chunks as HctWriter::compress_data does (crates/haagenti-hct/src/tensor.rs:
+ * 556-562), chunk i written at out + i*out_stride, its length in lens[i]. */
+size_t hct_b200_lz4_max_compressed_size(size_t n);
+int hct_b200_lz4_compress_block(const uint8_t *in, size_t in_len, uint8_t *out, size_t out_cap,
+                                size_t *out_len);
+int hct_b200_lz4_compress_chunks(const uint8_t *in, size_t in_len, size_t block_size,
+                                 uint8_t *out, size_t out_stride, uint32_t *lens);
+/* quantize_int4 (crates/haagenti/src/testing/quantization.rs:30-70): `out`
+ * holds ceil(n/32)*2 + ceil(n/2) bytes (scales first, low nibble first). */
+int hct_b200_quantize_int4(const float *w, size_t n, uint8_t *out);
+/* Retention step of CompressiveSpectralEncoder::encode_2d (crates/haagenti/src/
+ * compressive.rs:140-172): the k largest |c| (ties to the lower index) as an
+ * LSB-first bitmap of ceil(n/8) bytes and their values in index order. */
+int hct_b200_spectral_select(const float *coeffs, size_t n, size_t k, uint8_t *bitmap,
+                             float *values, size_t *count);
 
 /* ---- INT4 ---------------------------------------------------------------
  * haagenti::testing::dequantize_int4 (crates/haagenti/src/testing/quantization.rs:82-131):

@@ -269,13 +269,19 @@ def decode_int4_hct_cpu(file: bytes, threads: int = 0) -> np.ndarray:
 # ------------------------------------------------------------ seeded generators
 
 def gen_weight(shape, seed: int, outlier_frac: float = 0.01, std: float = 0.02) -> np.ndarray:
-    """N(0, std) f32 from numpy PCG64 default_rng(seed); a seeded 1% of columns x10."""
-    rng = np.random.default_rng(seed)
-    w = rng.standard_normal(size=tuple(shape), dtype=np.float32)
-    w *= np.float32(std)
+    """N(0, std) f32: 2^22-element chunks, chunk i from PCG64(SeedSequence(seed).spawn(n)[i]);
+    the first 1% of a default_rng([seed, 1]) column permutation is scaled x10."""
+    shape = tuple(int(s) for s in shape)
+    n = int(np.prod(shape))
+    chunk = 1 << 22
+    nch = max(1, (n + chunk - 1) // chunk)
+    w = np.empty(n, np.float32)
+    for i, ss in enumerate(np.random.SeedSequence(seed).spawn(nch)):
+        a, b = i * chunk, min(n, (i + 1) * chunk)
+        np.random.Generator(np.random.PCG64(ss)).standard_normal(out=w[a:b], dtype=np.float32)
+        w[a:b] *= np.float32(std)
+    w = w.reshape(shape)
     if outlier_frac > 0 and len(shape) == 2:
-        cols = shape[1]
-        nout = max(1, int(cols * outlier_frac))
-        idx = rng.permutation(cols)[:nout]
-        w[:, idx] *= np.float32(10.0)
+        nout = max(1, int(shape[1] * outlier_frac))
+        w[:, np.random.default_rng([seed, 1]).permutation(shape[1])[:nout]] *= np.float32(10.0)
     return w

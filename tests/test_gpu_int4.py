@@ -1,0 +1,81 @@
+"""INT4 dequantisation on the GPU against the oracle: bit-exact f32, and
+f16/bf16 equal to round-to-nearest-even of the exact f32 value."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _bits(a):
+    return np.ascontiguousarray(a).view(np.uint32 if a.dtype == np.float32 else np.uint16)
+
+
+def test_config1_4096sq_bit_exact(hb, orc):
+    """4096x4096 N(0,0.02), seed 0, 1% outlier columns x10."""
+    from oracle import hct as OH
+
+    w = OH.gen_weight((4096, 4096), 0)
+    q = orc.quantize_int4_np(w.reshape(-1))
+    assert q.size == 9_437_184
+    ref = orc.dequantize_int4(q, w.size)
+    got = hb.dequantize_int4(q, w.size).cpu().numpy()
+    assert got.shape == ref.shape
+    assert np.array_equal(_bits(got), _bits(ref))
+
+
+@pytest.mark.parametrize("n", [1, 2, 7, 8, 9, 31, 32, 33, 63, 64, 65, 1000, 4097, 123457])
+def test_ragged_sizes(hb, orc, n):
+    rng = np.random.default_rng(n)
+    w = (rng.standard_normal(n) * 0.05).astype(np.float32)
+    q = orc.quantize_int4(w)
+    ref = orc.dequantize_int4(q, n)
+    got = hb.dequantize_int4(q, n).cpu().numpy()
+    assert np.array_equal(_bits(got), _bits(ref))
+
+
+def test_short_inputs_follow_reference_rules(hb, orc):
+    n = 1000
+    q = orc.quantize_int4((np.random.default_rng(1).standard_normal(n)).astype(np.float32))
+    sb = 2 * ((n + 31) // 32)
+    for cut in [0, 1, sb - 1, sb, sb + 1, sb + 7, len(q) - 1]:
+        ref = orc.dequantize_int4(q[:cut], n)
+        got = hb.dequantize_int4(q[:cut], n).cpu().numpy()
+        assert got.size == ref.size, cut
+        assert np.array_equal(_bits(got), _bits(ref)), cut
+    assert hb.dequantize_int4(b"", 0).numel() == 0
+
+
+def test_half_outputs(hb, orc):
+    import torch
+
+    n = 100_003
+    w = (np.random.default_rng(2).standard_normal(n) * 3).astype(np.float32)
+    q = orc.quantize_int4(w)
+    ref = orc.dequantize_int4(q, n)
+    f16 = hb.dequantize_int4(q, n, out_dtype=hb.F16).cpu()
+    assert np.array_equal(f16.numpy().view(np.uint16), ref.astype(np.float16).view(np.uint16))
+    bf = hb.dequantize_int4(q, n, out_dtype=hb.BF16).cpu()
+    assert torch.equal(bf, torch.from_numpy(ref).to(torch.bfloat16))
+
+
+def test_unaligned_device_buffers(hb, orc, dev):
+    """Input at odd byte offsets, output at an odd element offset: same values."""
+    import torch
+    import ctypes as C
+    from haagenti_b200 import _lib as L
+
+    n = 4099
+    w = (np.random.default_rng(3).standard_normal(n)).astype(np.float32)
+    q = np.frombuffer(orc.quantize_int4(w), np.uint8)
+    ref = orc.dequantize_int4(q, n)
+    for off in range(4):
+        buf = torch.zeros(q.size + 8, dtype=torch.uint8, device=dev)
+        buf[off:off + q.size] = torch.from_numpy(q.copy()).to(dev)
+        out = torch.zeros(n + 1, dtype=torch.float32, device=dev)
+        written = C.c_size_t(0)
+        rc = L.load().hct_b200_dequantize_int4(buf.data_ptr() + off, q.size, n,
+                                               out.data_ptr() + 4, L.F32, C.byref(written),
+                                               torch.cuda.current_stream().cuda_stream)
+        assert rc == 0 and written.value == n
+        got = out[1:].cpu().numpy()
+        assert np.array_equal(_bits(got), _bits(ref)), off
