@@ -237,6 +237,8 @@ def run_b200(args):
     import torch
     import torch.distributed as dist
 
+    TENS = [t for t in LAYER_70B if not args.tensors or t[0] in args.tensors.split(",")]
+
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -255,14 +257,14 @@ def run_b200(args):
 
     files = layer_files(local, world, barrier)
     ctx = H.Context(local)
-    readers = {n: H.HctReader(files[n], ctx) for n, _, _ in LAYER_70B}
-    outs = {n: torch.empty((m, c), dtype=torch.bfloat16, device=dev) for n, m, c in LAYER_70B}
+    readers = {n: H.HctReader(files[n], ctx) for n, _, _ in TENS}
+    outs = {n: torch.empty((m, c), dtype=torch.bfloat16, device=dev) for n, m, c in TENS}
     stream = torch.cuda.current_stream(dev)
-    out_bytes = sum(2 * m * c for _, m, c in LAYER_70B)
-    comp_bytes = sum(len(files[n]) for n, _, _ in LAYER_70B)
+    out_bytes = sum(2 * m * c for _, m, c in TENS)
+    comp_bytes = sum(len(files[n]) for n, _, _ in TENS)
 
     def step():
-        for n, _, _ in LAYER_70B:
+        for n, _, _ in TENS:
             readers[n].decode(H.BF16, out=outs[n], stream=stream)
 
     # correctness guard on the timed configuration: finite output, sane scale
@@ -305,7 +307,7 @@ def run_b200(args):
         pinned[n] = a.numpy()
 
     def e2e_step():
-        for n, _, _ in LAYER_70B:
+        for n, _, _ in TENS:
             readers[n].upload(pinned[n], stream=stream)
             readers[n].decode(H.BF16, out=outs[n], stream=stream)
 
@@ -323,20 +325,20 @@ def run_b200(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t.item()) / args.steps
-    h2d = sum(_data_len(files[n]) for n, _, _ in LAYER_70B)  # compressed data sections
+    h2d = sum(_data_len(files[n]) for n, _, _ in TENS)  # compressed data sections
     d2h = sum(32 * readers[n].num_blocks() + 4 for n in readers)
     e2e_value = world * out_bytes / (e2e_ms / 1e3) / 1e9
 
     # ---- secondary: LZ4 (config 2) and INT4 (config 1) ------------------
-    lz4 = bench_lz4(H, torch, dev, stream, args) if rank == 0 else None
-    int4 = bench_int4(H, torch, dev, stream, args) if rank == 0 else None
+    lz4 = bench_lz4(H, torch, dev, stream, args) if rank == 0 and not args.no_secondary else None
+    int4 = bench_int4(H, torch, dev, stream, args) if rank == 0 and not args.no_secondary else None
 
     # ---- roofline of the dominant kernel --------------------------------
     pk = peaks()
     g = ks.get("umma_gemm", {})
     launches_total = sum(v["launches"] for v in ks.values())
     gemm_tflops = g["work"] / (g["ms"] / 1e3) / 1e12 if g else None
-    step_flops = dense_idct_flops(LAYER_70B)
+    step_flops = dense_idct_flops(TENS)
     traffic = read_traffic()
     roofline = {"bound": "tensor", "kernel": "umma_gemm_kernel (tcgen05 IDCT contraction)",
                 "achieved": round(gemm_tflops, 2) if gemm_tflops else None,
@@ -365,8 +367,9 @@ def run_b200(args):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms_step, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "llama2-70b-layer-hct-q4 (BASELINE config 3)",
-                       "tensors": {n: [m, c] for n, m, c in LAYER_70B}, "retention": RETENTION,
+            "config": {"workload": "llama2-70b-layer-hct-q4 (BASELINE config 3)"
+                                   + (f" subset {args.tensors}" if args.tensors else ""),
+                       "tensors": {n: [m, c] for n, m, c in TENS}, "retention": RETENTION,
                        "seed": SEED, "block_size": 16384, "out_dtype": "bf16",
                        "decoded_bytes_per_gpu_step": out_bytes,
                        "compressed_bytes_per_gpu_step": comp_bytes,
@@ -497,6 +500,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the LZ4 / INT4 lines")
+    ap.add_argument("--tensors", default="", help="comma list of layer tensors (default: all)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

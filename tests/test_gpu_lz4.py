@@ -30,9 +30,17 @@ def test_reference_roundtrips_host_api(hb, orc, golden):
         assert dec.decompress_to(comp, buf) == len(data) and bytes(buf) == data
         # interop blocks from another LZ4 implementation
         assert dec.decompress_with_size(bytes.fromhex(golden["lz4_interop"][name]), len(data)) == data
-        # unknown size: 4x guess, doubling (decompress.rs:33-57)
-        if data:
-            assert dec.decompress(comp) == data
+        # unknown size: 4x guess, doubling only on BufferTooSmall (decompress.rs:33-57).
+        # A complete block decoded with a larger guess ends in UnexpectedEof in the
+        # reference; the GPU path must give the same outcome as the oracle.
+        guess = 4 * len(comp)
+        ref = orc.lz4_decompress_block(comp, guess)
+        if ref.code == 0:
+            assert dec.decompress(comp) == ref.data
+        elif ref.code != 2:
+            with pytest.raises(hb.HaagentiError) as ei:
+                dec.decompress(comp)
+            assert ei.value.code == ref.code and ei.value.position == ref.position
 
 
 def test_error_semantics_match_oracle(hb, orc, golden):
