@@ -86,6 +86,7 @@ SIGNATURES = {
                                            C.POINTER(C.c_size_t), _vp]),
     "hct_b200_idct_2d": (C.c_int, [_vp, _vp, _vp, C.c_int, _sz, _sz, _vp]),
     "hct_b200_spectral_q4_decode": (C.c_int, [_vp, _vp, _sz, _sz, _sz, _vp, C.c_int, _vp]),
+    "hct_b200_spectral_q4_decode_noalloc": (C.c_int, [_vp, _sz, _sz, _sz, _vp, C.c_int, _vp]),
     "hct_b200_reader_open": (C.c_int, [_vp, _u8p, _sz, C.c_int, C.POINTER(C.c_void_p),
                                        C.POINTER(Error)]),
     "hct_b200_reader_upload": (C.c_int, [_vp, _u8p, _sz, _vp]),

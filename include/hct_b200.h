@@ -206,6 +206,21 @@ int hct_b200_spectral_q4_decode(hct_b200_ctx *ctx, const uint8_t *d_payload, siz
                                 size_t rows, size_t cols, void *d_out, int out_dtype,
                                 void *stream);
 
+/* Allocation-free variant of hct_b200_spectral_q4_decode for callers that
+ * cannot allocate device memory while they decode (a serving runtime whose
+ * allocator owns all of HBM, or code that must not trigger the device-wide
+ * synchronisation of cudaMalloc/cudaFree).  It has no counterpart in the
+ * reference.  It takes no context and allocates nothing: its scratch is one
+ * fixed 32 MiB device array inside the library (held on every device that
+ * uses the library until the process exits), so rows and cols must each be
+ * <= 2048; larger tensors return HCT_B200_ERR_INVALID_ARGUMENT.  The first
+ * call on a device looks up that array's device address; make that first
+ * call before any stream capture.  All calls share the array: calls whose
+ * GPU work overlaps race and must be serialised by the caller.  Synchronises
+ * `stream` to report the device-side status. */
+int hct_b200_spectral_q4_decode_noalloc(const uint8_t *d_payload, size_t payload_len, size_t rows,
+                                        size_t cols, void *d_out, int out_dtype, void *stream);
+
 /* ---- HCT reader ---------------------------------------------------------
  * HctReader::new / HctReaderV2::new (crates/haagenti-hct/src/tensor.rs:417-444,
  * 841-922): parse the header, optional quantization metadata and block index of
