@@ -26,6 +26,8 @@ import numpy as np
 from . import _lib as L
 from ._lib import BF16, F16, F32, FLAG_SPECTRAL_Q4
 
+IDCT_AUTO, IDCT_DENSE = 0, 1
+
 __all__ = [
     "HaagentiError", "CorruptedData", "BufferTooSmall", "UnexpectedEof", "ChecksumMismatch",
     "Unsupported", "DeviceError", "Context", "Lz4Decompressor", "dequantize_int4", "idct_2d",
@@ -139,6 +141,10 @@ class Context:
 
     def reserve(self, rows: int, cols: int):
         _check(L.load().hct_b200_ctx_reserve(self._h, rows, cols))
+
+    def set_idct(self, mode: int):
+        """IDCT_AUTO (factored tcgen05 DFT stages when the lengths factor) or IDCT_DENSE."""
+        _check(L.load().hct_b200_ctx_set_idct(self._h, mode))
 
     def close(self):
         if getattr(self, "_h", None):

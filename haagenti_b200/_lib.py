@@ -68,6 +68,7 @@ SIGNATURES = {
     "hct_b200_ctx_create": (C.c_int, [C.c_int, C.POINTER(C.c_void_p)]),
     "hct_b200_ctx_destroy": (None, [_vp]),
     "hct_b200_ctx_reserve": (C.c_int, [_vp, C.c_uint64, C.c_uint64]),
+    "hct_b200_ctx_set_idct": (C.c_int, [_vp, C.c_int]),
     "hct_b200_ctx_profile": (C.c_int, [_vp, C.c_int]),
     "hct_b200_ctx_profile_read": (C.c_int, [_vp, C.POINTER(KernelStats), C.c_int,
                                             C.POINTER(C.c_int)]),

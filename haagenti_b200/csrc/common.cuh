@@ -46,6 +46,12 @@ cudaError_t launch_basis(const double *d_cos_table, uint64_t n, half_bits *d_bas
 // (multiples of 8 elements).  Epilogue:
 //   mode 0: C^T stored fp16 at out[n * ldo + m]          (transposed)
 //   mode 1: C stored out_dtype at out[m * ldo + n]         (row-major)
+//   mode 2: DFT stage 1 of the factored IDCT (fdct.cu): row R = (b, k2), the
+//           complex output m1 = column pair (2m1, 2m1+1), times twiddle[k2*m1],
+//           stored as fp16 pair at ((m1 * batch + b) * Q + k2)
+//   mode 3: DFT stage 2: row R = (m1, b), complex output m2, j = m1 + P*m2,
+//           scaled and scattered to out[(4j + 2 ri) * ldo + b] (j < H/2) or
+//           out[(4(H-1-j) + 3 - 2 ri) * ldo + b] in out_dtype
 struct GemmArgs {
     const half_bits *A;
     const half_bits *B;
@@ -56,7 +62,26 @@ struct GemmArgs {
     int mode;
     int out_dtype;
     int *d_flag;  // device error flag (HCT_B200_ERR_TIMEOUT on an expired wait)
+    // factored-DCT stage parameters (modes 2 and 3)
+    uint32_t P = 0, Q = 0, H = 0;
+    uint64_t batch = 0;
+    const float *twiddle = nullptr;  // e^{2 pi i j / H}, complex fp32 (mode 2)
+    float scale = 1.0f;              // mode 3
 };
 cudaError_t launch_umma_gemm(const GemmArgs &args, cudaStream_t s);
+
+// ---- factored DCT-III (fdct.cu) -----------------------------------------
+// L even, H = L/2 = P*Q with P, Q multiples of 4 and <= 128.
+bool fdct_factor(uint64_t L, uint32_t *P, uint32_t *Q);
+// rows of length L (fp16, stride ld_in) -> Z[b][k2][k1] complex fp16 pairs.
+// d_tables: the 3L/2 complex fp32 twiddles written by launch_pack_tables(L).
+cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t batch, uint32_t L,
+                                uint32_t P, uint32_t Q, const float *d_tables, half_bits *d_out,
+                                cudaStream_t s);
+cudaError_t launch_pack_tables(uint32_t L, float *d_tables, cudaStream_t s);
+// realified n-point inverse-DFT matrix, 2n x 2n fp16 (rows_pad x ld).
+cudaError_t launch_dft_matrix(uint32_t n, uint32_t rows_pad, uint32_t ld, half_bits *d_out,
+                              cudaStream_t s);
+cudaError_t launch_twiddle_table(uint32_t H, float *d_out, cudaStream_t s);
 
 }  // namespace hct

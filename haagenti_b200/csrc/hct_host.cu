@@ -142,9 +142,18 @@ struct Basis {
 
 // Per-launch timing records (CUDA events on the launching stream), kept only
 // while profiling is enabled on the context.
-enum ProfKind { PK_LZ4 = 0, PK_SCATTER = 1, PK_GEMM = 2, PK_DEQUANT = 3, PK_COUNT = 4 };
+enum ProfKind {
+    PK_LZ4 = 0,
+    PK_SCATTER = 1,
+    PK_GEMM = 2,
+    PK_DEQUANT = 3,
+    PK_PACK = 4,
+    PK_DFT = 5,
+    PK_COUNT = 6
+};
 static const char *const kProfNames[PK_COUNT] = {"lz4_decode_blocks", "spectral_scatter",
-                                                 "umma_gemm", "dequant_int4"};
+                                                 "umma_gemm",         "dequant_int4",
+                                                 "makhoul_pack",      "dft_stage"};
 struct ProfRec {
     int kind;
     cudaEvent_t a, b;
@@ -155,9 +164,14 @@ struct hct_b200_ctx {
     int device = 0;
     cudaStream_t stream = nullptr;  // used by the host-buffer entry points
     DevBuf payload, dense, tt, chunk, meta, flag;
+    DevBuf za, zb;  // factored-IDCT intermediates (rows*cols fp16 each)
     DevBuf io_in, io_out, io_blk, io_status;
     std::map<uint64_t, std::unique_ptr<Basis>> bases;
+    std::map<uint32_t, std::unique_ptr<DevBuf>> dft_mats;  // realified n-point DFT, fp16
+    std::map<uint32_t, std::unique_ptr<DevBuf>> twiddles;  // e^{2 pi i j / H}, complex f32
+    std::map<uint32_t, std::unique_ptr<DevBuf>> pack_tabs;  // Makhoul-pack twiddles per length
     DevBuf cos_tbl;
+    int idct_mode = HCT_B200_IDCT_AUTO;
     bool profiling = false;
     std::vector<ProfRec> prof;
     std::vector<cudaEvent_t> event_pool;
@@ -237,6 +251,8 @@ int reserve_spectral(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols, size_t pay
     CK(ctx->payload.reserve(payload_bytes + 64));
     CK(ctx->dense.reserve(rows * round_up(cols, 8) * 2 + 16));
     CK(ctx->tt.reserve(cols * round_up(rows, 8) * 2 + 16));
+    CK(ctx->za.reserve(rows * cols * 2 + 16));
+    CK(ctx->zb.reserve(rows * cols * 2 + 16));
     CK(ctx->chunk.reserve((spectral_chunks(rows * cols) + 1) * sizeof(uint32_t)));
     CK(ctx->meta.reserve(4 * sizeof(uint64_t)));
     CK(ctx->flag.reserve(sizeof(int)));
@@ -245,10 +261,98 @@ int reserve_spectral(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols, size_t pay
 
 // The two contractions on a dense fp16 coefficient matrix held in ctx->dense
 // (rows x round_up(cols, 8)).
+int get_dft_matrix(hct_b200_ctx *ctx, uint32_t n, const half_bits **out, cudaStream_t s,
+                   hct_b200_error *err) {
+    auto it = ctx->dft_mats.find(n);
+    if (it == ctx->dft_mats.end()) {
+        auto b = std::make_unique<DevBuf>();
+        CK(b->reserve((size_t)4 * n * n * 2));
+        CK(launch_dft_matrix(n, 2 * n, 2 * n, b->as<half_bits>(), s));
+        it = ctx->dft_mats.emplace(n, std::move(b)).first;
+    }
+    *out = it->second->as<half_bits>();
+    return HCT_B200_OK;
+}
+
+int get_twiddle(hct_b200_ctx *ctx, uint32_t H, const float **out, cudaStream_t s,
+                hct_b200_error *err) {
+    auto it = ctx->twiddles.find(H);
+    if (it == ctx->twiddles.end()) {
+        auto b = std::make_unique<DevBuf>();
+        CK(b->reserve((size_t)H * 8));
+        CK(launch_twiddle_table(H, b->as<float>(), s));
+        it = ctx->twiddles.emplace(H, std::move(b)).first;
+    }
+    *out = it->second->as<float>();
+    return HCT_B200_OK;
+}
+
+// One axis of the factored IDCT: rows of length L (fp16, stride ld_in) in
+// `in`, batch rows; the result is written transposed, out[n * ldo + b], in
+// out_dtype (pack -> DFT stage 1 -> DFT stage 2, see fdct.cu).
+int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, uint64_t batch, uint64_t L,
+              uint32_t P, uint32_t Q, void *out, uint64_t ldo, int out_dtype, cudaStream_t s,
+              hct_b200_error *err) {
+    const uint32_t H = (uint32_t)(L / 2);
+    const half_bits *wp = nullptr, *wq = nullptr;
+    const float *tw = nullptr;
+    int rc = get_dft_matrix(ctx, P, &wp, s, err);
+    if (!rc) rc = get_dft_matrix(ctx, Q, &wq, s, err);
+    if (!rc) rc = get_twiddle(ctx, H, &tw, s, err);
+    if (rc) return rc;
+    auto pt = ctx->pack_tabs.find((uint32_t)L);
+    if (pt == ctx->pack_tabs.end()) {
+        auto b = std::make_unique<DevBuf>();
+        CK(b->reserve((size_t)L * 12));
+        CK(launch_pack_tables((uint32_t)L, b->as<float>(), s));
+        pt = ctx->pack_tabs.emplace((uint32_t)L, std::move(b)).first;
+    }
+    int *flag = ctx->flag.as<int>();
+    const double elems = (double)batch * (double)L;
+    int slot = ctx->prof_begin(s);
+    CK(launch_makhoul_pack(in, ld_in, batch, (uint32_t)L, P, Q, pt->second->as<float>(),
+                           ctx->za.as<half_bits>(), s));
+    ctx->prof_end(slot, PK_PACK, 4.0 * elems, s);
+    GemmArgs g1{ctx->za.as<half_bits>(), wp, batch * Q, 2ull * P, 2ull * P, 2ull * P, 2ull * P,
+                ctx->zb.p, 0, 2, HCT_B200_F16, flag};
+    g1.P = P;
+    g1.Q = Q;
+    g1.H = H;
+    g1.batch = batch;
+    g1.twiddle = tw;
+    slot = ctx->prof_begin(s);
+    CK(launch_umma_gemm(g1, s));
+    ctx->prof_end(slot, PK_DFT, 4.0 * elems, s);
+    GemmArgs g2{ctx->zb.as<half_bits>(), wq, (uint64_t)P * batch, 2ull * Q, 2ull * Q, 2ull * Q,
+                2ull * Q, out, ldo, 3, out_dtype, flag};
+    g2.P = P;
+    g2.Q = Q;
+    g2.H = H;
+    g2.batch = batch;
+    g2.scale = (float)std::sqrt(2.0 / (double)L);
+    slot = ctx->prof_begin(s);
+    CK(launch_umma_gemm(g2, s));
+    ctx->prof_end(slot, PK_DFT, (2.0 + (out_dtype == HCT_B200_F32 ? 4.0 : 2.0)) * elems, s);
+    return HCT_B200_OK;
+}
+
 int run_idct(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols, void *d_out, int out_dtype,
              cudaStream_t s, hct_b200_error *err) {
     const uint64_t ldw = round_up(cols, 8), ldh = round_up(rows, 8);
     int *flag = ctx->flag.as<int>();
+    uint32_t pn = 0, qn = 0, pm = 0, qm = 0;
+    if (ctx->idct_mode == HCT_B200_IDCT_AUTO && fdct_factor(cols, &pn, &qn) &&
+        (rows == 1 || fdct_factor(rows, &pm, &qm))) {
+        // factored path: rows first (output T^T, cols x ldh), then the rows of T^T
+        if (rows == 1)
+            return fdct_axis(ctx, ctx->dense.as<half_bits>(), ldw, 1, cols, pn, qn, d_out, 1,
+                             out_dtype, s, err);
+        int rc = fdct_axis(ctx, ctx->dense.as<half_bits>(), ldw, rows, cols, pn, qn, ctx->tt.p,
+                           ldh, HCT_B200_F16, s, err);
+        if (rc) return rc;
+        return fdct_axis(ctx, ctx->tt.as<half_bits>(), ldh, cols, rows, pm, qm, d_out, cols,
+                         out_dtype, s, err);
+    }
     const Basis *bw = nullptr, *bh = nullptr;
     int rc = get_basis(ctx, cols, &bw, s, err);
     if (rc) return rc;
@@ -421,6 +525,13 @@ int hct_b200_ctx_reserve(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols) {
     const uint64_t total = rows * cols;
     hct_b200_error e;
     return reserve_spectral(ctx, rows, cols, (total + 7) / 8 + total, &e);
+}
+
+int hct_b200_ctx_set_idct(hct_b200_ctx *ctx, int mode) {
+    if (!ctx || (mode != HCT_B200_IDCT_AUTO && mode != HCT_B200_IDCT_DENSE))
+        return HCT_B200_ERR_INVALID_ARGUMENT;
+    ctx->idct_mode = mode;
+    return HCT_B200_OK;
 }
 
 int hct_b200_ctx_profile(hct_b200_ctx *ctx, int enable) {

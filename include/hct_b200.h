@@ -122,6 +122,16 @@ int hct_b200_ctx_reserve(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols);
 const char *hct_b200_status_string(int code);
 int hct_b200_abi_version(void);
 
+/* How the context computes the IDCT.  AUTO (default) uses the factored
+ * transform (a Makhoul pack pass and two short tcgen05 DFT contractions per
+ * axis; O(n) tensor-core FLOPs per element, HBM-bound) whenever both axis
+ * lengths factor as 2*P*Q with P, Q multiples of 4 up to 128, and the dense
+ * contraction against the full DCT basis otherwise; DENSE always uses the
+ * dense contraction.  Both compute haagenti_core::dct::idct_2d
+ * (crates/haagenti-core/src/dct.rs:311-337). */
+enum { HCT_B200_IDCT_AUTO = 0, HCT_B200_IDCT_DENSE = 1 };
+int hct_b200_ctx_set_idct(hct_b200_ctx *ctx, int mode);
+
 /* Per-kernel timing of the context's own launches, for roofline reports.
  * With profiling enabled every kernel launch made through the context is
  * bracketed by CUDA events recorded on its launch stream; _read synchronises

@@ -1,0 +1,80 @@
+"""The factored IDCT (Makhoul pack + two tcgen05 DFT stages per axis) against
+the oracle, the f64 truth and the dense-basis contraction.  Tolerance as in
+test_gpu_idct_hct.py: max-abs <= 1e-3, cosine >= 0.99999."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 1e-3
+MIN_COS = 0.99999
+
+
+def _cos(a, b):
+    a = a.astype(np.float64).ravel()
+    b = b.astype(np.float64).ravel()
+    return float((a * b).sum() / np.sqrt((a * a).sum() * (b * b).sum()))
+
+
+def _check(got, ref, tag):
+    err = float(np.abs(got.astype(np.float64) - ref.astype(np.float64)).max())
+    cos = _cos(got, ref)
+    assert err <= MAX_ABS and cos >= MIN_COS, f"{tag}: max-abs {err:.3e} cos {cos:.8f}"
+
+
+def _coeffs(orc, shape, seed):
+    from oracle import hct as OH
+
+    return orc.dct_2d(OH.gen_weight(shape, seed).reshape(shape))
+
+
+@pytest.fixture(scope="module")
+def ctxs(hb):
+    auto = hb.Context(0)
+    dense = hb.Context(0)
+    dense.set_idct(hb.IDCT_DENSE)
+    return auto, dense
+
+
+@pytest.mark.parametrize("shape", [(32, 32), (64, 128), (128, 96), (1024, 1024), (1, 8192),
+                                   (8192, 1), (1024, 8192), (8192, 8192)])
+def test_factored_vs_oracle_truth_and_dense(hb, orc, dev, ctxs, shape):
+    import torch
+
+    auto, dense = ctxs
+    c = _coeffs(orc, shape, 7 + sum(shape))
+    x = torch.from_numpy(c).to(dev)
+    got = hb.idct_2d(x, ctx=auto).cpu().numpy()
+    ref = orc.idct_2d(c)
+    _check(got, ref, f"{shape} factored vs oracle f32")
+    if c.size <= 1 << 22:
+        _check(got, orc.idct_2d_f64_truth(c), f"{shape} factored vs f64")
+    d = hb.idct_2d(x, ctx=dense).cpu().numpy()
+    _check(got, d, f"{shape} factored vs dense")
+
+
+def test_factored_full_gate_shape(hb, dev, ctxs):
+    """28672 x 8192 (gate/up, P x Q = 112 x 128 along rows): dense vs factored, Parseval."""
+    import torch
+
+    auto, dense = ctxs
+    g = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn(28672, 8192, device=dev, generator=g) * 0.02
+    a = hb.idct_2d(x, ctx=auto)
+    assert abs(a.double().norm().item() / x.double().norm().item() - 1) < 1e-4
+    d = hb.idct_2d(x, ctx=dense)
+    diff = (a - d).abs().max().item()
+    assert diff < MAX_ABS, diff
+    cos = torch.nn.functional.cosine_similarity(a.double().flatten(), d.double().flatten(), dim=0)
+    assert cos.item() >= MIN_COS
+
+
+@pytest.mark.parametrize("shape", [(1024, 8192), (8192, 1024), (4096, 14336)])
+def test_factored_hct_decode(hb, orc, shape):
+    from oracle import hct as OH
+
+    w = OH.gen_weight(shape, 40)
+    f = OH.encode_spectral_q4(w)
+    ref = OH.decode_spectral_q4_cpu(f)
+    got = hb.HctReader(f).decode(hb.F32).cpu().numpy()
+    _check(got, ref, f"hct {shape}")
