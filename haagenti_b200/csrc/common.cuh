@@ -79,6 +79,17 @@ cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t 
                                 uint32_t P, uint32_t Q, const float *d_tables, half_bits *d_out,
                                 cudaStream_t s);
 cudaError_t launch_pack_tables(uint32_t L, float *d_tables, cudaStream_t s);
+// Rank directory of a spectral payload: per-1024-bit chunk exclusive popcount
+// prefix in d_chunk, meta[0] = k, meta[1] = nibble offset, meta[2] = short.
+cudaError_t launch_spectral_rank(const uint8_t *d_payload, size_t payload_len, uint64_t total,
+                                 uint32_t *d_chunk, uint64_t *d_meta, int *d_flag, cudaStream_t s);
+// Row pack straight from a spectral payload (rows of length L, row-major
+// bitmap), after launch_spectral_rank.  Needs spectral_pack_supported(L).
+bool spectral_pack_supported(uint64_t L);
+cudaError_t launch_spectral_pack(const uint8_t *d_payload, uint64_t bmb, const uint32_t *d_chunk,
+                                 const uint64_t *d_meta, uint64_t batch, uint32_t L, uint32_t P,
+                                 uint32_t Q, const float *d_tables, half_bits *d_out,
+                                 cudaStream_t s);
 // realified n-point inverse-DFT matrix, 2n x 2n fp16 (rows_pad x ld).
 cudaError_t launch_dft_matrix(uint32_t n, uint32_t rows_pad, uint32_t ld, half_bits *d_out,
                               cudaStream_t s);

@@ -1,5 +1,5 @@
 // Factored DCT-III: the IDCT along one axis as a pack pass plus two short
-// tensor-core DFT stages (the stages run on umma_gemm_kernel, modes 2 and 3).
+// tensor-core DFT stages (the stages run on dft_stage_kernel, idct_gemm.cu).
 //
 // For a row c[0..L) (L even, H = L/2 = P*Q) the orthonormal DCT-III
 // x[n] = sum_k alpha(k) c[k] cos(pi (2n+1) k / 2L) is computed as
@@ -23,6 +23,12 @@
 //   stage 2 G  rows (m1, b), K=2Q   -> Y  [n][b]              (transposed)
 // so two applications (rows, then the rows of the transposed result) give
 // the 2-D transform X = A_M F A_N^T with the output in row-major order.
+//
+// The pack is written with the combined coefficients
+//   alpha_k = w_k' e^{i pi k / 2L} (1 + i e^{2 pi i k / L}),  w_0' = 1/sqrt(2), w_k' = 1/2
+//   beta_k  = 1/2 e^{i pi (k+H) / 2L} (1 - i e^{2 pi i k / L})
+//   Z[k]    = alpha_k (c[k] - i c[L-k]) + beta_k (c[H+k] - i c[H-k])
+// (one float4 per k, computed once per length in f64).
 #include <cuda_fp16.h>
 
 #include <cmath>
@@ -36,39 +42,55 @@ __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_
 __device__ __forceinline__ uint16_t f2h(float v) { return __half_as_ushort(__float2half_rn(v)); }
 
 // Shared-memory index of row element k: two fp16 of padding every 64
-// elements, so reads at stride Q (a multiple of 4) spread over the banks.
+// elements, so accesses at stride 64 (and at stride Q) spread over the banks.
 __device__ __forceinline__ uint32_t pad_idx(uint32_t k) { return k + 2 * (k >> 6); }
-
-// Shared-memory word index of Z[k] in the transpose buffer (one pad word per
-// 64 words, so the stride-Q reads of the output phase spread over the banks).
+// Word index of Z[k] in the transpose buffer (one pad word per 64 words).
 __device__ __forceinline__ uint32_t zpad_idx(uint32_t k) { return k + (k >> 6); }
 
-// One CTA per row (grid-stride over the batch), three phases:
-//  1. the row is staged in shared memory (fp16, coalesced 16-byte loads);
-//  2. Z[k] for k < H is computed in natural order (c[k], c[L-k], c[H+k],
-//     c[H-k]; twiddle ta[k] = e^{i pi k / 2L} read coalesced; e^{i pi (k+H)/2L}
-//     = ta[k] e^{i pi/4}; e^{2 pi i k / L} = ta[k]^4) into a second buffer;
-//  3. Z is written out in (k2, k1) order, k = Q k1 + k2, k1 fastest, one warp
-//     per k2 row, as 4-byte fp16 pairs.
+__host__ __device__ __forceinline__ uint32_t srow_halves(uint32_t L) {
+    return (L + 2 * (L >> 6) + 8) & ~7u;
+}
+__host__ __device__ __forceinline__ uint32_t zbuf_words(uint32_t L) {
+    return (L / 2 + (L / 2 >> 6) + 8) & ~7u;
+}
+
+// Pack phases 2 and 3 for one staged row: Z[k] for k < H in natural order
+// (coalesced coefficient loads) into the transpose buffer, then the row of
+// Z written in (k2, k1) order, k = Q k1 + k2, one warp per k2, 4-byte pairs.
+__device__ __forceinline__ void pack_row(const uint16_t *srow, uint32_t *zbuf,
+                                         const float4 *__restrict__ coef, uint32_t L, uint32_t P,
+                                         uint32_t Q, uint32_t *__restrict__ orow) {
+    const uint32_t H = L / 2;
+    for (uint32_t k = threadIdx.x; k < H; k += blockDim.x) {
+        const float ck = h2f(srow[pad_idx(k)]);
+        const float cLk = k ? h2f(srow[pad_idx(L - k)]) : 0.0f;
+        const float cHk = h2f(srow[pad_idx(H + k)]);
+        const float cHmk = h2f(srow[pad_idx(H - k)]);  // H - k >= 1 for k < H
+        const float4 t = coef[k];                      // (alpha.re, alpha.im, beta.re, beta.im)
+        const float zr = fmaf(t.x, ck, fmaf(t.y, cLk, fmaf(t.z, cHk, t.w * cHmk)));
+        const float zi = fmaf(t.y, ck, fmaf(-t.x, cLk, fmaf(t.w, cHk, -t.z * cHmk)));
+        zbuf[zpad_idx(k)] = (uint32_t)f2h(zr) | ((uint32_t)f2h(zi) << 16);
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    for (uint32_t k2 = warp; k2 < Q; k2 += nwarps)
+        for (uint32_t k1 = lane; k1 < P; k1 += 32) orow[k2 * P + k1] = zbuf[zpad_idx(Q * k1 + k2)];
+}
+
+// Pack of dense fp16 rows (stride ld_in): one CTA per row, the row staged in
+// shared memory with 8 independent 16-byte loads in flight per thread.
 __global__ void __launch_bounds__(512) makhoul_pack_kernel(const uint16_t *__restrict__ in,
                                                            uint64_t ld_in, uint64_t B, uint32_t L,
                                                            uint32_t P, uint32_t Q,
-                                                           const float2 *__restrict__ ta,
-                                                           const float2 *__restrict__ tb,
+                                                           const float4 *__restrict__ coef,
                                                            uint32_t *__restrict__ out) {
     extern __shared__ uint16_t srow[];
-    const uint32_t H = L / 2;
-    uint32_t *zbuf = reinterpret_cast<uint32_t *>(srow + ((pad_idx(L) + 8) & ~7u));
-    const float inv_sqrt2 = 0.70710678118654752440f;
-    const float c45 = 0.70710678118654752440f;  // e^{i pi/4} = (c45, c45)
+    uint32_t *zbuf = reinterpret_cast<uint32_t *>(srow + srow_halves(L));
     const bool vec = ((ld_in & 7) == 0) && (((uintptr_t)in & 15) == 0) && ((L & 7) == 0);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    (void)tb;
     for (uint64_t b = blockIdx.x; b < B; b += gridDim.x) {
         const uint16_t *row = in + b * ld_in;
         __syncthreads();  // previous row fully consumed
         if (vec) {
-            // 8 independent 16-byte loads in flight per thread before any store
             const uint4 *r4 = reinterpret_cast<const uint4 *>(row);
             const uint32_t nv = L / 8;
             for (uint32_t v0 = threadIdx.x; v0 < nv; v0 += 8 * blockDim.x) {
@@ -81,8 +103,7 @@ __global__ void __launch_bounds__(512) makhoul_pack_kernel(const uint16_t *__res
 #pragma unroll
                 for (int u = 0; u < 8; u++) {
                     const uint32_t v = v0 + u * blockDim.x;
-                    if (v < nv) {
-                        // 8 elements never straddle a 64-element pad
+                    if (v < nv) {  // 8 elements never straddle a 64-element pad
                         uint32_t *d = reinterpret_cast<uint32_t *>(srow + pad_idx(8 * v));
                         d[0] = x[u].x;
                         d[1] = x[u].y;
@@ -95,51 +116,148 @@ __global__ void __launch_bounds__(512) makhoul_pack_kernel(const uint16_t *__res
             for (uint32_t k = threadIdx.x; k < L; k += blockDim.x) srow[pad_idx(k)] = row[k];
         }
         __syncthreads();
-        for (uint32_t k = threadIdx.x; k < H; k += blockDim.x) {
-            float ck = h2f(srow[pad_idx(k)]);
-            float cLk = 0.0f, w = 1.0f;
-            if (k == 0) {
-                ck *= inv_sqrt2;
-            } else {
-                cLk = h2f(srow[pad_idx(L - k)]);
-                w = 0.5f;
-            }
-            const float cHk = h2f(srow[pad_idx(H + k)]);
-            const float cHmk = h2f(srow[pad_idx(H - k)]);  // H - k >= 1 for k < H
-            const float2 a = ta[k];
-            const float2 bb = make_float2(c45 * (a.x - a.y), c45 * (a.x + a.y));
-            const float2 a2 = make_float2(a.x * a.x - a.y * a.y, 2.0f * a.x * a.y);
-            const float2 t = make_float2(a2.x * a2.x - a2.y * a2.y, 2.0f * a2.x * a2.y);
-            // V[k] = w (ck - i cLk) e^{i pi k / 2L}
-            const float vr = w * (ck * a.x + cLk * a.y);
-            const float vi = w * (ck * a.y - cLk * a.x);
-            // U = V[k+H] = 1/2 (cHk - i cHmk) e^{i pi (k+H) / 2L}
-            const float ur = 0.5f * (cHk * bb.x + cHmk * bb.y);
-            const float ui = 0.5f * (cHk * bb.y - cHmk * bb.x);
-            // Z = (V + U) + i (V - U) e^{2 pi i k / L}
-            const float dr = vr - ur, di = vi - ui;
-            const float er = dr * t.x - di * t.y, ei = dr * t.y + di * t.x;
-            zbuf[zpad_idx(k)] =
-                (uint32_t)f2h((vr + ur) - ei) | ((uint32_t)f2h((vi + ui) + er) << 16);
-        }
-        __syncthreads();
-        uint32_t *orow = out + b * (uint64_t)H;
-        for (uint32_t k2 = warp; k2 < Q; k2 += nwarps)
-            for (uint32_t k1 = lane; k1 < P; k1 += 32)
-                orow[k2 * P + k1] = zbuf[zpad_idx(Q * k1 + k2)];
+        pack_row(srow, zbuf, coef, L, P, Q, out + b * (uint64_t)(L / 2));
     }
 }
 
-// ta[k] = e^{i pi k / 2L} for k < L; tb[k] = e^{2 pi i k / L} for k < L/2.
-__global__ void pack_tables_kernel(uint32_t L, float2 *ta, float2 *tb) {
-    for (uint32_t k = blockIdx.x * blockDim.x + threadIdx.x; k < L; k += gridDim.x * blockDim.x) {
-        double s, c;
-        sincospi((double)k / (2.0 * (double)L), &s, &c);
-        ta[k] = make_float2((float)c, (float)s);
-        if (k < L / 2) {
-            sincospi(2.0 * (double)k / (double)L, &s, &c);
-            tb[k] = make_float2((float)c, (float)s);
+__device__ __forceinline__ float f16bits_to_f32(uint32_t h) {
+    // exact conversion (also for subnormals) as quantization.rs:166-197
+    uint32_t sign = (h >> 15) & 1u, exp = (h >> 10) & 0x1fu, frac = h & 0x3ffu, out;
+    if (exp == 0) {
+        if (frac == 0) {
+            out = sign << 31;
+        } else {
+            int e = -14;
+            uint32_t f = frac;
+            while ((f & 0x400u) == 0) { f <<= 1; e -= 1; }
+            out = (sign << 31) | ((uint32_t)((e + 127) & 0xff) << 23) | ((f & 0x3ffu) << 13);
         }
+    } else if (exp == 31) {
+        out = (sign << 31) | (0xffu << 23) | (frac << 13);
+    } else {
+        out = (sign << 31) | ((exp - 15 + 127) << 23) | (frac << 13);
+    }
+    return __uint_as_float(out);
+}
+
+// Row pack straight from the spectral payload (bitmap ++ INT4).  Each CTA
+// decodes the coefficients of its row into shared memory and then runs the
+// pack phases:
+//   - the row's bitmap words (two per thread, coalesced) and a block scan of
+//     their popcounts on top of the row's rank (1024-bit chunk prefix from
+//     launch_spectral_rank plus a partial popcount);
+//   - the row's nibble bytes and its FP16 scales (converted to f32) staged in
+//     shared memory, the row itself zero-filled;
+//   - each thread walks the set bits of its two words (__ffs), writing
+//     f32(nibble - 8) * f32(scale) rounded to fp16 at the bit's position.
+// Requires L % 64 == 0 (rows start on a 64-bit bitmap boundary), which every
+// factorable length satisfies.
+constexpr int SPACK_THREADS = 512;
+
+__host__ __device__ __forceinline__ uint32_t spack_nib_bytes(uint32_t L) {
+    return (L / 2 + 16 + 15) & ~15u;
+}
+
+__global__ void __launch_bounds__(SPACK_THREADS) spectral_pack_kernel(
+    const uint8_t *__restrict__ payload, uint64_t bmb, const uint32_t *__restrict__ chunk_base,
+    const uint64_t *__restrict__ meta, uint64_t B, uint32_t L, uint32_t P, uint32_t Q,
+    const float4 *__restrict__ coef, uint32_t *__restrict__ out) {
+    extern __shared__ uint16_t srow[];
+    __shared__ uint32_t warp_tot[SPACK_THREADS / 32];
+    __shared__ uint32_t s_rank_start;
+    const uint32_t row_words = L / 32;
+    uint32_t *zbuf = reinterpret_cast<uint32_t *>(srow + srow_halves(L));
+    uint8_t *nib_s = reinterpret_cast<uint8_t *>(zbuf + zbuf_words(L));
+    float *sc_s = reinterpret_cast<float *>(nib_s + spack_nib_bytes(L));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    const uint64_t k_total = meta[0];
+    const uint8_t *scales = payload + bmb;
+    const uint8_t *nibbles = payload + meta[1];
+    const bool bad = meta[2] != 0;
+    const uint32_t *bm32 = reinterpret_cast<const uint32_t *>(payload);
+
+    for (uint64_t b = blockIdx.x; b < B; b += gridDim.x) {
+        __syncthreads();  // previous row fully consumed
+        const uint64_t word0 = b * row_words;
+        const uint32_t w_a = 2 * threadIdx.x, w_b = w_a + 1;
+        const uint32_t va = w_a < row_words ? bm32[word0 + w_a] : 0u;
+        const uint32_t vb = w_b < row_words ? bm32[word0 + w_b] : 0u;
+        const uint32_t mine = __popc(va) + __popc(vb);
+        uint32_t incl = mine;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+        }
+        if (lane == 31) warp_tot[warp] = incl;
+        if (warp == 0) {
+            const uint64_t c0 = word0 / 32;  // its 1024-bit chunk
+            uint32_t part = 0;
+            for (uint64_t w = c0 * 32 + lane; w < word0; w += 32) part += __popc(bm32[w]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+            if (lane == 0) s_rank_start = chunk_base[c0] + part;
+        }
+        // zero the staged row while the scan settles
+        uint32_t *srow32 = reinterpret_cast<uint32_t *>(srow);
+        for (uint32_t i = threadIdx.x; i < srow_halves(L) / 2; i += blockDim.x) srow32[i] = 0u;
+        __syncthreads();
+        uint32_t before = 0, row_count = 0;
+        for (int w = 0; w < nwarps; w++) {
+            if (w < warp) before += warp_tot[w];
+            row_count += warp_tot[w];
+        }
+        const uint64_t rank0 = s_rank_start;
+        const uint64_t nb0 = rank0 >> 1, nb1 = (rank0 + row_count + 1) >> 1;
+        const uint64_t sb0 = rank0 >> 5, sb1 = row_count ? ((rank0 + row_count - 1) >> 5) + 1 : sb0;
+        if (!bad) {  // a short payload (meta[2]) decodes to zeros, never reads past its end
+            for (uint64_t i = nb0 + threadIdx.x; i < nb1; i += blockDim.x)
+                nib_s[i - nb0] = nibbles[i];
+            for (uint64_t i = sb0 + threadIdx.x; i < sb1; i += blockDim.x)
+                sc_s[i - sb0] = f16bits_to_f32((uint32_t)scales[2 * i] |
+                                               ((uint32_t)scales[2 * i + 1] << 8));
+        }
+        __syncthreads();
+        if (!bad) {
+            uint64_t r = rank0 + before + (incl - mine);
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                uint32_t x = half ? vb : va;
+                const uint32_t base = 32 * (half ? w_b : w_a);
+                while (x) {
+                    const int bit = __ffs(x) - 1;
+                    x &= x - 1;
+                    if (r < k_total) {
+                        const uint32_t byte = nib_s[(r >> 1) - nb0];
+                        const uint32_t nib = (r & 1) ? byte >> 4 : byte & 0xfu;
+                        srow[pad_idx(base + bit)] =
+                            f2h(__fmul_rn((float)((int)nib - 8), sc_s[(r >> 5) - sb0]));
+                    }
+                    r++;
+                }
+            }
+        }
+        __syncthreads();
+        pack_row(srow, zbuf, coef, L, P, Q, out + b * (uint64_t)(L / 2));
+    }
+}
+
+// coef[k] = (alpha_k, beta_k) for k < L/2 (see the file comment), in f64.
+__global__ void pack_tables_kernel(uint32_t L, float4 *coef) {
+    const uint32_t H = L / 2;
+    for (uint32_t k = blockIdx.x * blockDim.x + threadIdx.x; k < H; k += gridDim.x * blockDim.x) {
+        double sa, ca, sb, cb, st, ct;
+        sincospi((double)k / (2.0 * (double)L), &sa, &ca);          // e^{i pi k / 2L}
+        sincospi((double)(k + H) / (2.0 * (double)L), &sb, &cb);    // e^{i pi (k+H) / 2L}
+        sincospi(2.0 * (double)k / (double)L, &st, &ct);            // t = e^{2 pi i k / L}
+        const double w = k == 0 ? 0.70710678118654752440 : 0.5;
+        // alpha = w a (1 + i t) = w a (1 - st + i ct)
+        const double pr = 1.0 - st, pi_ = ct;
+        const double ar = w * (ca * pr - sa * pi_), ai = w * (ca * pi_ + sa * pr);
+        // beta = 1/2 b (1 - i t) = 1/2 b (1 + st - i ct)
+        const double qr = 1.0 + st, qi = -ct;
+        const double br = 0.5 * (cb * qr - sb * qi), bi = 0.5 * (cb * qi + sb * qr);
+        coef[k] = make_float4((float)ar, (float)ai, (float)br, (float)bi);
     }
 }
 
@@ -198,24 +316,43 @@ bool fdct_factor(uint64_t L, uint32_t *P, uint32_t *Q) {
 cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t B, uint32_t L,
                                 uint32_t P, uint32_t Q, const float *d_tables, half_bits *d_out,
                                 cudaStream_t s) {
-    // row (fp16, padded) + Z transpose buffer (u32, padded)
-    const size_t row_elems = ((size_t)L + 2 * (L / 64) + 8 + 7) & ~(size_t)7;
-    const size_t smem = row_elems * sizeof(uint16_t) + ((size_t)L / 2 + L / 128 + 8) * 4;
+    const size_t smem = (size_t)srow_halves(L) * 2 + (size_t)zbuf_words(L) * 4;
     if (smem > 220 * 1024) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(makhoul_pack_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     uint64_t g = B < 148ull * 8 ? B : 148ull * 8;
     if (g < 1) g = 1;
-    const float2 *ta = reinterpret_cast<const float2 *>(d_tables);
-    makhoul_pack_kernel<<<(unsigned)g, 512, smem, s>>>(d_in, ld_in, B, L, P, Q, ta, ta + L,
-                                                       reinterpret_cast<uint32_t *>(d_out));
+    makhoul_pack_kernel<<<(unsigned)g, 512, smem, s>>>(
+        d_in, ld_in, B, L, P, Q, reinterpret_cast<const float4 *>(d_tables),
+        reinterpret_cast<uint32_t *>(d_out));
+    return cudaGetLastError();
+}
+
+bool spectral_pack_supported(uint64_t L) { return L % 64 == 0 && L / 32 <= 2ull * SPACK_THREADS; }
+
+cudaError_t launch_spectral_pack(const uint8_t *d_payload, uint64_t bmb, const uint32_t *d_chunk,
+                                 const uint64_t *d_meta, uint64_t B, uint32_t L, uint32_t P,
+                                 uint32_t Q, const float *d_tables, half_bits *d_out,
+                                 cudaStream_t s) {
+    if (!spectral_pack_supported(L)) return cudaErrorInvalidValue;
+    // dynamic shared memory: row, transpose buffer, nibbles, f32 scales
+    const size_t smem = (size_t)srow_halves(L) * 2 + (size_t)zbuf_words(L) * 4 +
+                        spack_nib_bytes(L) + ((size_t)L / 32 + 4) * 4;
+    if (smem > 220 * 1024) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(spectral_pack_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    uint64_t g = B < 148ull * 4 ? B : 148ull * 4;
+    if (g < 1) g = 1;
+    spectral_pack_kernel<<<(unsigned)g, SPACK_THREADS, smem, s>>>(
+        d_payload, bmb, d_chunk, d_meta, B, L, P, Q, reinterpret_cast<const float4 *>(d_tables),
+        reinterpret_cast<uint32_t *>(d_out));
     return cudaGetLastError();
 }
 
 cudaError_t launch_pack_tables(uint32_t L, float *d_tables, cudaStream_t s) {
-    float2 *ta = reinterpret_cast<float2 *>(d_tables);
-    pack_tables_kernel<<<(L + 255) / 256, 256, 0, s>>>(L, ta, ta + L);
+    pack_tables_kernel<<<(L / 2 + 255) / 256, 256, 0, s>>>(L, reinterpret_cast<float4 *>(d_tables));
     return cudaGetLastError();
 }
 

@@ -290,9 +290,12 @@ int get_twiddle(hct_b200_ctx *ctx, uint32_t H, const float **out, cudaStream_t s
 // One axis of the factored IDCT: rows of length L (fp16, stride ld_in) in
 // `in`, batch rows; the result is written transposed, out[n * ldo + b], in
 // out_dtype (pack -> DFT stage 1 -> DFT stage 2, see fdct.cu).
-int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, uint64_t batch, uint64_t L,
-              uint32_t P, uint32_t Q, void *out, uint64_t ldo, int out_dtype, cudaStream_t s,
-              hct_b200_error *err) {
+// The pack reads dense fp16 rows (`in`, stride ld_in) or, when `payload` is
+// set, decodes the rows straight from a spectral payload whose rank directory
+// launch_spectral_rank has put in ctx->chunk / ctx->meta.
+int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint8_t *payload,
+              uint64_t batch, uint64_t L, uint32_t P, uint32_t Q, void *out, uint64_t ldo,
+              int out_dtype, cudaStream_t s, hct_b200_error *err) {
     const uint32_t H = (uint32_t)(L / 2);
     const half_bits *wp = nullptr, *wq = nullptr;
     const float *tw = nullptr;
@@ -310,9 +313,18 @@ int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, uint64_t b
     int *flag = ctx->flag.as<int>();
     const double elems = (double)batch * (double)L;
     int slot = ctx->prof_begin(s);
-    CK(launch_makhoul_pack(in, ld_in, batch, (uint32_t)L, P, Q, pt->second->as<float>(),
-                           ctx->za.as<half_bits>(), s));
-    ctx->prof_end(slot, PK_PACK, 4.0 * elems, s);
+    if (payload) {
+        const uint64_t bmb = (batch * L + 7) / 8;
+        CK(launch_spectral_pack(payload, bmb, ctx->chunk.as<uint32_t>(), ctx->meta.as<uint64_t>(),
+                                batch, (uint32_t)L, P, Q, pt->second->as<float>(),
+                                ctx->za.as<half_bits>(), s));
+        // bitmap + ~0.3 of the INT4 section read, fp16 pairs written
+        ctx->prof_end(slot, PK_PACK, (double)bmb + 0.17 * elems + 2.0 * elems, s);
+    } else {
+        CK(launch_makhoul_pack(in, ld_in, batch, (uint32_t)L, P, Q, pt->second->as<float>(),
+                               ctx->za.as<half_bits>(), s));
+        ctx->prof_end(slot, PK_PACK, 4.0 * elems, s);
+    }
     GemmArgs g1{ctx->za.as<half_bits>(), wp, batch * Q, 2ull * P, 2ull * P, 2ull * P, 2ull * P,
                 ctx->zb.p, 0, 2, HCT_B200_F16, flag};
     g1.P = P;
@@ -336,22 +348,44 @@ int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, uint64_t b
     return HCT_B200_OK;
 }
 
+// IDCT of a rows x cols coefficient matrix.  The coefficients are either the
+// dense fp16 matrix in ctx->dense (payload == nullptr) or a spectral payload
+// on the device, which is decoded into the first pass of the factored path
+// when the row length allows, and scattered into ctx->dense otherwise.
 int run_idct(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols, void *d_out, int out_dtype,
-             cudaStream_t s, hct_b200_error *err) {
+             cudaStream_t s, hct_b200_error *err, const uint8_t *payload = nullptr,
+             size_t payload_len = 0) {
     const uint64_t ldw = round_up(cols, 8), ldh = round_up(rows, 8);
     int *flag = ctx->flag.as<int>();
     uint32_t pn = 0, qn = 0, pm = 0, qm = 0;
-    if (ctx->idct_mode == HCT_B200_IDCT_AUTO && fdct_factor(cols, &pn, &qn) &&
-        (rows == 1 || fdct_factor(rows, &pm, &qm))) {
+    const bool factored = ctx->idct_mode == HCT_B200_IDCT_AUTO && fdct_factor(cols, &pn, &qn) &&
+                          (rows == 1 || fdct_factor(rows, &pm, &qm));
+    const uint8_t *src = nullptr;
+    if (payload) {
+        const uint64_t total = rows * cols;
+        int slot = ctx->prof_begin(s);
+        if (factored && spectral_pack_supported(cols)) {
+            CK(launch_spectral_rank(payload, payload_len, total, ctx->chunk.as<uint32_t>(),
+                                    ctx->meta.as<uint64_t>(), flag, s));
+            ctx->prof_end(slot, PK_SCATTER, (double)((total + 7) / 8), s);
+            src = payload;
+        } else {
+            CK(launch_spectral_scatter(payload, payload_len, rows, cols, ctx->chunk.as<uint32_t>(),
+                                       ctx->meta.as<uint64_t>(), ctx->dense.as<half_bits>(), ldw,
+                                       flag, s));
+            ctx->prof_end(slot, PK_SCATTER, (double)payload_len + 2.0 * total, s);
+        }
+    }
+    if (factored) {
         // factored path: rows first (output T^T, cols x ldh), then the rows of T^T
         if (rows == 1)
-            return fdct_axis(ctx, ctx->dense.as<half_bits>(), ldw, 1, cols, pn, qn, d_out, 1,
+            return fdct_axis(ctx, ctx->dense.as<half_bits>(), ldw, src, 1, cols, pn, qn, d_out, 1,
                              out_dtype, s, err);
-        int rc = fdct_axis(ctx, ctx->dense.as<half_bits>(), ldw, rows, cols, pn, qn, ctx->tt.p,
-                           ldh, HCT_B200_F16, s, err);
+        int rc = fdct_axis(ctx, ctx->dense.as<half_bits>(), ldw, src, rows, cols, pn, qn,
+                           ctx->tt.p, ldh, HCT_B200_F16, s, err);
         if (rc) return rc;
-        return fdct_axis(ctx, ctx->tt.as<half_bits>(), ldh, cols, rows, pm, qm, d_out, cols,
-                         out_dtype, s, err);
+        return fdct_axis(ctx, ctx->tt.as<half_bits>(), ldh, nullptr, cols, rows, pm, qm, d_out,
+                         cols, out_dtype, s, err);
     }
     const Basis *bw = nullptr, *bh = nullptr;
     int rc = get_basis(ctx, cols, &bw, s, err);
@@ -645,12 +679,7 @@ int hct_b200_spectral_q4_decode(hct_b200_ctx *ctx, const uint8_t *d_payload, siz
     rc = reserve_spectral(ctx, rows, cols, 0, err);
     if (rc) return rc;
     CK(cudaMemsetAsync(ctx->flag.p, 0, sizeof(int), s));
-    int slot = ctx->prof_begin(s);
-    CK(launch_spectral_scatter(d_payload, payload_len, rows, cols, ctx->chunk.as<uint32_t>(),
-                               ctx->meta.as<uint64_t>(), ctx->dense.as<half_bits>(),
-                               round_up(cols, 8), ctx->flag.as<int>(), s));
-    ctx->prof_end(slot, PK_SCATTER, (double)payload_len + 2.0 * total, s);
-    rc = run_idct(ctx, rows, cols, d_out, out_dtype, s, err);
+    rc = run_idct(ctx, rows, cols, d_out, out_dtype, s, err, d_payload, payload_len);
     if (rc) return rc;
     return read_flag(ctx, s, err);
 }
@@ -957,13 +986,7 @@ int hct_b200_reader_decode(hct_b200_reader *r, void *d_out, int out_dtype, void 
     uint64_t rows = r->rows, cols = r->cols;
     if (cols == 1 && rows > 1) std::swap(rows, cols);
     CK(cudaMemsetAsync(ctx->flag.p, 0, sizeof(int), s));
-    int slot = ctx->prof_begin(s);
-    CK(launch_spectral_scatter(ctx->payload.as<uint8_t>(), written, rows, cols,
-                               ctx->chunk.as<uint32_t>(), ctx->meta.as<uint64_t>(),
-                               ctx->dense.as<half_bits>(), round_up(cols, 8), ctx->flag.as<int>(),
-                               s));
-    ctx->prof_end(slot, PK_SCATTER, (double)written + 2.0 * total, s);
-    rc = run_idct(ctx, rows, cols, d_out, out_dtype, s, err);
+    rc = run_idct(ctx, rows, cols, d_out, out_dtype, s, err, ctx->payload.as<uint8_t>(), written);
     if (rc) return rc;
     return read_flag(ctx, s, err);
 }

@@ -174,12 +174,6 @@ __device__ __forceinline__ uint16_t f2bf(float v) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(v));
 }
 
-__device__ __forceinline__ void store_out(void *out, uint64_t idx, float v, int dt) {
-    if (dt == HCT_B200_F32) reinterpret_cast<float *>(out)[idx] = v;
-    else if (dt == HCT_B200_BF16) reinterpret_cast<uint16_t *>(out)[idx] = f2bf(v);
-    else reinterpret_cast<uint16_t *>(out)[idx] = f2h(v);
-}
-
 // Epilogue of the factored-DCT stages for one 32-column chunk of a TMEM row
 // (fp32 accumulator values r[0..31] of D row `row`, columns col0..col0+31).
 //   mode 2 (stage 1): row = (b, k2); column pair (2 m1, 2 m1 + 1) = complex

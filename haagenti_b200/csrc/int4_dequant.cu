@@ -346,6 +346,16 @@ cudaError_t launch_spectral_scatter(const uint8_t *d_payload, size_t payload_len
     return cudaGetLastError();
 }
 
+cudaError_t launch_spectral_rank(const uint8_t *d_payload, size_t payload_len, uint64_t total,
+                                 uint32_t *d_chunk, uint64_t *d_meta, int *d_flag, cudaStream_t s) {
+    const uint64_t bmb = (total + 7) / 8;
+    const uint64_t nchunks = spectral_chunks(total);
+    chunk_popcount_kernel<<<grid_for(nchunks * 32, 256), 256, 0, s>>>(d_payload, bmb, total,
+                                                                      nchunks, d_chunk);
+    chunk_scan_kernel<<<1, 1024, 0, s>>>(d_chunk, nchunks, bmb, payload_len, d_meta, d_flag);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_f32_to_f16_padded(const float *d_in, uint64_t rows, uint64_t cols,
                                      half_bits *d_out, uint64_t ld, cudaStream_t s) {
     f32_to_f16_padded_kernel<<<grid_for(rows * ld, 256), 256, 0, s>>>(d_in, rows, cols, d_out, ld);

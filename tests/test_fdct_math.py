@@ -58,6 +58,24 @@ def test_one_axis_matches_dct_iii(L, P, Q):
     assert np.abs(y.T - ref).max() < 1e-9 * np.sqrt(L)
 
 
+def test_combined_pack_coefficients():
+    """Z[k] = alpha_k (c[k] - i c[L-k]) + beta_k (c[H+k] - i c[H-k]), as pack_tables_kernel."""
+    L, P, Q = 128, 8, 8
+    H = L // 2
+    c = np.random.default_rng(1).standard_normal((2, L))
+    k = np.arange(H)
+    a = np.exp(1j * np.pi * k / (2 * L))
+    b = np.exp(1j * np.pi * (k + H) / (2 * L))
+    t = np.exp(2j * np.pi * k / L)
+    w = np.where(k == 0, 1 / np.sqrt(2.0), 0.5)
+    alpha = w * a * (1 + 1j * t)
+    beta = 0.5 * b * (1 - 1j * t)
+    cL = np.where(k == 0, 0.0, c[:, (L - k) % L])
+    Z = alpha * (c[:, k] - 1j * cL) + beta * (c[:, H + k] - 1j * c[:, H - k])
+    ref = pack(c, P, Q).transpose(0, 2, 1).reshape(2, H)  # back to natural k order
+    np.testing.assert_allclose(Z, ref, atol=1e-12)
+
+
 def test_two_axes_give_idct_2d():
     # rows first (output T^T), then the rows of T^T (output X row-major)
     rng = np.random.default_rng(0)
