@@ -61,7 +61,9 @@ __device__ __forceinline__ void pack_row(const uint16_t *srow, uint32_t *zbuf,
                                          const float4 *__restrict__ coef, uint32_t L, uint32_t P,
                                          uint32_t Q, uint32_t *__restrict__ orow) {
     const uint32_t H = L / 2;
-    for (uint32_t k = threadIdx.x; k < H; k += blockDim.x) {
+    // Z[k] and Z[H-k] read the same four inputs c[k], c[L-k], c[H+k], c[H-k]
+    // (with the roles permuted), so each thread produces both.
+    for (uint32_t k = threadIdx.x; k <= H / 2; k += blockDim.x) {
         const float ck = h2f(srow[pad_idx(k)]);
         const float cLk = k ? h2f(srow[pad_idx(L - k)]) : 0.0f;
         const float cHk = h2f(srow[pad_idx(H + k)]);
@@ -70,6 +72,13 @@ __device__ __forceinline__ void pack_row(const uint16_t *srow, uint32_t *zbuf,
         const float zr = fmaf(t.x, ck, fmaf(t.y, cLk, fmaf(t.z, cHk, t.w * cHmk)));
         const float zi = fmaf(t.y, ck, fmaf(-t.x, cLk, fmaf(t.w, cHk, -t.z * cHmk)));
         zbuf[zpad_idx(k)] = (uint32_t)f2h(zr) | ((uint32_t)f2h(zi) << 16);
+        if (k != 0 && k != H / 2) {
+            // k' = H - k: c[k'] = c[H-k], c[L-k'] = c[H+k], c[H+k'] = c[L-k], c[H-k'] = c[k]
+            const float4 u = coef[H - k];
+            const float yr = fmaf(u.x, cHmk, fmaf(u.y, cHk, fmaf(u.z, cLk, u.w * ck)));
+            const float yi = fmaf(u.y, cHmk, fmaf(-u.x, cHk, fmaf(u.w, cLk, -u.z * ck)));
+            zbuf[zpad_idx(H - k)] = (uint32_t)f2h(yr) | ((uint32_t)f2h(yi) << 16);
+        }
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;

@@ -426,7 +426,8 @@ template <int BN>
 struct StageCfg {
     static constexpr int KB_MAX = BN / 64;           // K <= BN (K = N = 2 * DFT size)
     static constexpr int W_KB_BYTES = BN * BK * 2;   // one 64-column k-block of W
-    static constexpr int RING = BN == 256 ? 5 : 8;
+    // BN = 128: 32 KB of W + 4 x 16 KB ring -> two CTAs per SM
+    static constexpr int RING = BN == 256 ? 5 : 4;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr size_t SMEM_BYTES =
         1024 + (size_t)KB_MAX * W_KB_BYTES + (size_t)RING * A_TILE_BYTES + 256;
@@ -752,7 +753,8 @@ cudaError_t launch_stage(const GemmArgs &a, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     const uint64_t m_tiles = (a.M + BM - 1) / BM;
     if (m_tiles > 0x7fffffffull) return cudaErrorInvalidValue;
-    const uint32_t grid = (uint32_t)std::min<uint64_t>(m_tiles, (uint64_t)sm_count());
+    const uint64_t per_sm = BN == 128 ? 2 : 1;  // shared memory and TMEM allow two 128-wide CTAs
+    const uint32_t grid = (uint32_t)std::min<uint64_t>(m_tiles, per_sm * (uint64_t)sm_count());
     StageParams sp{a.P, a.Q, a.H, 0, a.batch, reinterpret_cast<const float2 *>(a.twiddle), a.scale};
     dft_stage_kernel<BN><<<grid, STAGE_THREADS, SC::SMEM_BYTES, s>>>(
         ta, tb, (uint32_t)a.M, (uint32_t)a.N, (uint32_t)a.K, (uint32_t)m_tiles, a.out, a.ldo,
