@@ -347,6 +347,19 @@ class HctReader:
         _check(rc, err)
         return out
 
+    def decode_async(self, out, out_dtype: int = BF16, stream=None):
+        """Enqueue the full decode into ``out`` with no host sync; call ``wait()`` for the status."""
+        err = L.Error()
+        rc = L.load().hct_b200_reader_decode_async(self._h, out.data_ptr(), out_dtype,
+                                                   _stream_ptr(stream), C.byref(err))
+        _check(rc, err)
+        return out
+
+    def wait(self):
+        """Status of the last ``decode_async`` (raises like ``decode``)."""
+        err = L.Error()
+        _check(L.load().hct_b200_reader_wait(self._h, C.byref(err)), err)
+
     def close(self):
         if getattr(self, "_h", None):
             L.load().hct_b200_reader_close(self._h)

@@ -96,6 +96,8 @@ SIGNATURES = {
     "hct_b200_reader_decompress_all": (C.c_int, [_vp, _vp, _sz, C.POINTER(C.c_size_t), _vp,
                                                  C.POINTER(Error)]),
     "hct_b200_reader_decode": (C.c_int, [_vp, _vp, C.c_int, _vp, C.POINTER(Error)]),
+    "hct_b200_reader_decode_async": (C.c_int, [_vp, _vp, C.c_int, _vp, C.POINTER(Error)]),
+    "hct_b200_reader_wait": (C.c_int, [_vp, C.POINTER(Error)]),
     "hct_b200_reader_close": (None, [_vp]),
 }
 

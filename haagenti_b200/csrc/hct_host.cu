@@ -213,6 +213,17 @@ struct hct_b200_reader {
     std::vector<uint32_t> expected;
     uint64_t rows = 0, cols = 0;
     bool spectral = false;
+    // deferred status of an asynchronous decode (pinned host copies)
+    hct_b200_status *h_status = nullptr;
+    int *h_flag = nullptr;
+    cudaEvent_t done = nullptr;
+    bool pending = false;
+    uint64_t pending_elems = 0;  // INT4 elements a plain decode produced (0 = spectral)
+    ~hct_b200_reader() {
+        if (h_status) cudaFreeHost(h_status);
+        if (h_flag) cudaFreeHost(h_flag);
+        if (done) cudaEventDestroy(done);
+    }
 };
 
 namespace {
@@ -834,6 +845,9 @@ int hct_b200_reader_open(hct_b200_ctx *ctx, const uint8_t *file, size_t file_len
     CK(r->d_data.reserve(r->data_len + 64));
     CK(r->d_blocks.reserve((size_t)std::max<uint32_t>(nb, 1) * sizeof(hct_b200_lz4_block)));
     CK(r->d_status.reserve((size_t)std::max<uint32_t>(nb, 1) * sizeof(hct_b200_status)));
+    CK(cudaMallocHost(&r->h_status, (size_t)std::max<uint32_t>(nb, 1) * sizeof(hct_b200_status)));
+    CK(cudaMallocHost(&r->h_flag, sizeof(int)));
+    CK(cudaEventCreateWithFlags(&r->done, cudaEventDisableTiming));
     std::vector<hct_b200_lz4_block> blocks(nb);
     for (uint32_t i = 0; i < nb; i++) {
         blocks[i].src_off = r->offsets[i];
@@ -952,16 +966,58 @@ int hct_b200_reader_decode(hct_b200_reader *r, void *d_out, int out_dtype, void 
         set_err(err, HCT_B200_ERR_UNSUPPORTED, -1, 0, 0, 0, "only I4 tensors are decoded");
         return HCT_B200_ERR_UNSUPPORTED;
     }
+    int rc = hct_b200_reader_decode_async(r, d_out, out_dtype, stream, err);
+    if (rc) return rc;
+    return hct_b200_reader_wait(r, err);
+}
+
+// The whole decode is enqueued on `stream` with no host synchronisation:
+// LZ4 writes its per-block statuses, the payload is decoded on the
+// assumption that every block is complete, and the statuses and the device
+// flag are copied to pinned host memory behind the kernels.
+// hct_b200_reader_wait then reports exactly what hct_b200_reader_decode
+// would have (the output is undefined when it reports an error).
+int hct_b200_reader_decode_async(hct_b200_reader *r, void *d_out, int out_dtype, void *stream,
+                                 hct_b200_error *err) {
+    clear_err(err);
+    if (!r || !d_out) {
+        set_err(err, HCT_B200_ERR_INVALID_ARGUMENT, -1, 0, 0, 0, "null argument");
+        return HCT_B200_ERR_INVALID_ARGUMENT;
+    }
+    if (out_dtype < HCT_B200_F32 || out_dtype > HCT_B200_BF16) {
+        set_err(err, HCT_B200_ERR_INVALID_ARGUMENT, -1, 0, 0, 0, "bad output dtype");
+        return HCT_B200_ERR_INVALID_ARGUMENT;
+    }
+    if (r->hdr.algorithm != 0) {
+        set_err(err, HCT_B200_ERR_UNSUPPORTED, -1, 0, 0, 0, "only LZ4 containers are decoded");
+        return HCT_B200_ERR_UNSUPPORTED;
+    }
+    if (r->hdr.dtype != 4) {
+        set_err(err, HCT_B200_ERR_UNSUPPORTED, -1, 0, 0, 0, "only I4 tensors are decoded");
+        return HCT_B200_ERR_UNSUPPORTED;
+    }
     hct_b200_ctx *ctx = r->ctx;
     int rc = ensure_device(ctx);
     if (rc) return rc;
     cudaStream_t s = (cudaStream_t)stream;
-    size_t written = 0;
-    rc = reader_lz4(r, ctx->payload.as<uint8_t>(), ctx->payload.cap, &written, s, err);
-    if (rc) return rc;
+    const uint32_t nb = r->hdr.num_blocks;
+    if (ctx->payload.cap < r->hdr.original_size) {
+        set_err(err, HCT_B200_ERR_BUFFER_TOO_SMALL, -1, 0, r->hdr.original_size, ctx->payload.cap,
+                "context payload scratch too small");
+        return HCT_B200_ERR_BUFFER_TOO_SMALL;
+    }
+    CK(cudaMemsetAsync(ctx->flag.p, 0, sizeof(int), s));
+    if (nb) {
+        int slot = ctx->prof_begin(s);
+        CK(launch_lz4_blocks(r->d_data.as<uint8_t>(), r->d_blocks.as<hct_b200_lz4_block>(), nb,
+                             ctx->payload.as<uint8_t>(), r->d_status.as<hct_b200_status>(), s));
+        ctx->prof_end(slot, PK_LZ4, (double)r->hdr.compressed_size + (double)r->hdr.original_size,
+                      s);
+    }
     const uint64_t total = r->rows * r->cols;
-    if (total == 0) return HCT_B200_OK;
-    if (!r->spectral) {
+    const size_t written = r->hdr.original_size;  // verified against the statuses in _wait
+    r->pending_elems = 0;
+    if (total && !r->spectral) {
         // plain INT4 weights (examples/safetensors_to_int4_hct.rs:241-284)
         size_t n = 0;
         int slot = ctx->prof_begin(s);
@@ -970,25 +1026,53 @@ int hct_b200_reader_decode(hct_b200_reader *r, void *d_out, int out_dtype, void 
         ctx->prof_end(slot, PK_DEQUANT, (double)written + (out_dtype == HCT_B200_F32 ? 4.0 : 2.0) * n,
                       s);
         if (rc) return rc;
-        if (n != total) {
-            set_err(err, HCT_B200_ERR_SIZE_MISMATCH, -1, 0, total, n,
-                    "INT4 payload holds %zu of %llu elements", n, (unsigned long long)total);
-            return HCT_B200_ERR_SIZE_MISMATCH;
-        }
-        CK(cudaStreamSynchronize(s));
-        return HCT_B200_OK;
+        r->pending_elems = n;
+    } else if (total) {
+        uint64_t rows = r->rows, cols = r->cols;
+        if (cols == 1 && rows > 1) std::swap(rows, cols);
+        rc = run_idct(ctx, rows, cols, d_out, out_dtype, s, err, ctx->payload.as<uint8_t>(),
+                      written);
+        if (rc) return rc;
     }
-    if (written != r->hdr.original_size) {
-        set_err(err, HCT_B200_ERR_SIZE_MISMATCH, -1, 0, r->hdr.original_size, written,
-                "spectral payload truncated");
+    if (nb)
+        CK(cudaMemcpyAsync(r->h_status, r->d_status.p, nb * sizeof(hct_b200_status),
+                           cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(r->h_flag, ctx->flag.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CK(cudaEventRecord(r->done, s));
+    r->pending = true;
+    return HCT_B200_OK;
+}
+
+int hct_b200_reader_wait(hct_b200_reader *r, hct_b200_error *err) {
+    clear_err(err);
+    if (!r) return HCT_B200_ERR_INVALID_ARGUMENT;
+    if (!r->pending) return HCT_B200_OK;
+    r->pending = false;
+    CK(cudaEventSynchronize(r->done));
+    const uint32_t nb = r->hdr.num_blocks;
+    std::vector<hct_b200_status> st(r->h_status, r->h_status + nb);
+    int rc = check_block_status(st, err);
+    if (rc) return rc;
+    uint64_t got = 0;
+    for (uint32_t i = 0; i < nb; i++) got += st[i].written;
+    if (got != r->hdr.original_size) {
+        set_err(err, HCT_B200_ERR_SIZE_MISMATCH, -1, 0, r->hdr.original_size, got,
+                "decompressed payload holds %llu of %llu bytes", (unsigned long long)got,
+                (unsigned long long)r->hdr.original_size);
         return HCT_B200_ERR_SIZE_MISMATCH;
     }
-    uint64_t rows = r->rows, cols = r->cols;
-    if (cols == 1 && rows > 1) std::swap(rows, cols);
-    CK(cudaMemsetAsync(ctx->flag.p, 0, sizeof(int), s));
-    rc = run_idct(ctx, rows, cols, d_out, out_dtype, s, err, ctx->payload.as<uint8_t>(), written);
-    if (rc) return rc;
-    return read_flag(ctx, s, err);
+    const uint64_t total = r->rows * r->cols;
+    if (!r->spectral && r->pending_elems != total) {
+        set_err(err, HCT_B200_ERR_SIZE_MISMATCH, -1, 0, total, r->pending_elems,
+                "INT4 payload holds %llu of %llu elements", (unsigned long long)r->pending_elems,
+                (unsigned long long)total);
+        return HCT_B200_ERR_SIZE_MISMATCH;
+    }
+    if (*r->h_flag) {
+        set_err(err, *r->h_flag, -1, 0, 0, 0, "%s", hct_b200_status_string(*r->h_flag));
+        return *r->h_flag;
+    }
+    return HCT_B200_OK;
 }
 
 void hct_b200_reader_close(hct_b200_reader *r) {

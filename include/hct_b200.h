@@ -257,6 +257,16 @@ int hct_b200_reader_decompress_all(hct_b200_reader *r, uint8_t *d_out, size_t ou
  *     LZ4 -> dequantize_int4. */
 int hct_b200_reader_decode(hct_b200_reader *r, void *d_out, int out_dtype, void *stream,
                            hct_b200_error *err);
+/* hct_b200_reader_decode split in two: _async enqueues the whole decode on
+ * `stream` without any host synchronisation (per-block statuses and the
+ * device error flag are copied to pinned host memory behind the kernels);
+ * _wait synchronises on that copy and returns what hct_b200_reader_decode
+ * would have returned.  d_out is undefined when _wait reports an error.
+ * Asynchronous decodes through one context share its scratch and must be
+ * issued on one stream. */
+int hct_b200_reader_decode_async(hct_b200_reader *r, void *d_out, int out_dtype, void *stream,
+                                 hct_b200_error *err);
+int hct_b200_reader_wait(hct_b200_reader *r, hct_b200_error *err);
 void hct_b200_reader_close(hct_b200_reader *r);
 
 #ifdef __cplusplus

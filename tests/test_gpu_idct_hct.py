@@ -171,3 +171,27 @@ def test_container_errors(hb, orc):
     with pytest.raises(hb.CorruptedData, match="zero offset") as ei:
         hb.HctReader(bytes(g)).decode(hb.F32)
     assert ei.value.block == 0
+    # the asynchronous form reports the same error from wait()
+    import torch
+
+    r = hb.HctReader(bytes(g))
+    out = torch.empty(r.shape, dtype=torch.float32, device="cuda")
+    r.decode_async(out, hb.F32)
+    with pytest.raises(hb.CorruptedData, match="zero offset"):
+        r.wait()
+
+
+def test_async_decode_matches_sync(hb, orc):
+    import torch
+    from oracle import hct as OH
+
+    files = [OH.encode_spectral_q4(OH.gen_weight(s, 50 + i)) for i, s in
+             enumerate([(256, 512), (64, 1024), (512, 256)])]
+    readers = [hb.HctReader(f) for f in files]
+    outs = [torch.empty(r.shape, dtype=torch.float32, device="cuda") for r in readers]
+    for r, o in zip(readers, outs):
+        r.decode_async(o, hb.F32)
+    for r in readers:
+        r.wait()
+    for r, o in zip(readers, outs):
+        assert torch.equal(o, r.decode(hb.F32))
