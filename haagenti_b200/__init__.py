@@ -316,7 +316,11 @@ class HctReader:
         return self.header()["shape"]
 
     def upload(self, file, stream=None):
-        """Re-upload the compressed data of a same-layout file (stream-ordered)."""
+        """Re-upload the compressed data of a same-layout file (stream-ordered).
+
+        The copy may run on its own stream: it waits for the previous decode
+        of this reader to finish reading the buffer, and the next decode waits
+        for the copy, with no host synchronisation."""
         f = _as_host_u8(file) if not isinstance(file, np.ndarray) else file
         _check(L.load().hct_b200_reader_upload(self._h, f.ctypes.data, f.size, _stream_ptr(stream)))
 

@@ -148,12 +148,15 @@ enum ProfKind {
     PK_GEMM = 2,
     PK_DEQUANT = 3,
     PK_PACK = 4,
-    PK_DFT = 5,
-    PK_COUNT = 6
+    PK_DFT1 = 5,
+    PK_RANK = 6,
+    PK_SPACK = 7,
+    PK_DFT2 = 8,
+    PK_COUNT = 9
 };
-static const char *const kProfNames[PK_COUNT] = {"lz4_decode_blocks", "spectral_scatter",
-                                                 "umma_gemm",         "dequant_int4",
-                                                 "makhoul_pack",      "dft_stage"};
+static const char *const kProfNames[PK_COUNT] = {
+    "lz4_decode_blocks", "spectral_scatter", "umma_gemm",     "dequant_int4", "makhoul_pack",
+    "dft_stage1",        "spectral_rank",    "spectral_pack", "dft_stage2"};
 struct ProfRec {
     int kind;
     cudaEvent_t a, b;
@@ -219,10 +222,27 @@ struct hct_b200_reader {
     cudaEvent_t done = nullptr;
     bool pending = false;
     uint64_t pending_elems = 0;  // INT4 elements a plain decode produced (0 = spectral)
+    // Cross-stream ordering of d_data: an upload on any stream waits for the
+    // last LZ4 launch that read the buffer (data_free), and an LZ4 launch
+    // waits for the last upload (uploaded).  Uploads on a copy stream thus
+    // overlap the decode of other tensors without host synchronisation.
+    cudaEvent_t uploaded = nullptr, data_free = nullptr;
+    bool upload_pending = false, read_pending = false;
     ~hct_b200_reader() {
         if (h_status) cudaFreeHost(h_status);
         if (h_flag) cudaFreeHost(h_flag);
         if (done) cudaEventDestroy(done);
+        if (uploaded) cudaEventDestroy(uploaded);
+        if (data_free) cudaEventDestroy(data_free);
+    }
+    // stream s is about to read d_data (LZ4)
+    cudaError_t before_read(cudaStream_t s) {
+        return upload_pending ? cudaStreamWaitEvent(s, uploaded, 0) : cudaSuccess;
+    }
+    // stream s has enqueued its last read of d_data
+    cudaError_t after_read(cudaStream_t s) {
+        read_pending = true;
+        return cudaEventRecord(data_free, s);
     }
 };
 
@@ -330,7 +350,7 @@ int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint
                                 batch, (uint32_t)L, P, Q, pt->second->as<float>(),
                                 ctx->za.as<half_bits>(), s));
         // bitmap + ~0.3 of the INT4 section read, fp16 pairs written
-        ctx->prof_end(slot, PK_PACK, (double)bmb + 0.17 * elems + 2.0 * elems, s);
+        ctx->prof_end(slot, PK_SPACK, (double)bmb + 0.17 * elems + 2.0 * elems, s);
     } else {
         CK(launch_makhoul_pack(in, ld_in, batch, (uint32_t)L, P, Q, pt->second->as<float>(),
                                ctx->za.as<half_bits>(), s));
@@ -345,7 +365,7 @@ int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint
     g1.twiddle = tw;
     slot = ctx->prof_begin(s);
     CK(launch_umma_gemm(g1, s));
-    ctx->prof_end(slot, PK_DFT, 4.0 * elems, s);
+    ctx->prof_end(slot, PK_DFT1, 4.0 * elems, s);
     GemmArgs g2{ctx->zb.as<half_bits>(), wq, (uint64_t)P * batch, 2ull * Q, 2ull * Q, 2ull * Q,
                 2ull * Q, out, ldo, 3, out_dtype, flag};
     g2.P = P;
@@ -355,7 +375,7 @@ int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint
     g2.scale = (float)std::sqrt(2.0 / (double)L);
     slot = ctx->prof_begin(s);
     CK(launch_umma_gemm(g2, s));
-    ctx->prof_end(slot, PK_DFT, (2.0 + (out_dtype == HCT_B200_F32 ? 4.0 : 2.0)) * elems, s);
+    ctx->prof_end(slot, PK_DFT2, (2.0 + (out_dtype == HCT_B200_F32 ? 4.0 : 2.0)) * elems, s);
     return HCT_B200_OK;
 }
 
@@ -378,7 +398,7 @@ int run_idct(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols, void *d_out, int o
         if (factored && spectral_pack_supported(cols)) {
             CK(launch_spectral_rank(payload, payload_len, total, ctx->chunk.as<uint32_t>(),
                                     ctx->meta.as<uint64_t>(), flag, s));
-            ctx->prof_end(slot, PK_SCATTER, (double)((total + 7) / 8), s);
+            ctx->prof_end(slot, PK_RANK, (double)((total + 7) / 8), s);
             src = payload;
         } else {
             CK(launch_spectral_scatter(payload, payload_len, rows, cols, ctx->chunk.as<uint32_t>(),
@@ -848,6 +868,8 @@ int hct_b200_reader_open(hct_b200_ctx *ctx, const uint8_t *file, size_t file_len
     CK(cudaMallocHost(&r->h_status, (size_t)std::max<uint32_t>(nb, 1) * sizeof(hct_b200_status)));
     CK(cudaMallocHost(&r->h_flag, sizeof(int)));
     CK(cudaEventCreateWithFlags(&r->done, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&r->uploaded, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&r->data_free, cudaEventDisableTiming));
     std::vector<hct_b200_lz4_block> blocks(nb);
     for (uint32_t i = 0; i < nb; i++) {
         blocks[i].src_off = r->offsets[i];
@@ -877,9 +899,15 @@ int hct_b200_reader_open(hct_b200_ctx *ctx, const uint8_t *file, size_t file_len
 int hct_b200_reader_upload(hct_b200_reader *r, const uint8_t *file, size_t file_len, void *stream) {
     if (!r || !file) return HCT_B200_ERR_INVALID_ARGUMENT;
     if (file_len != r->data_offset + r->data_len) return HCT_B200_ERR_SIZE_MISMATCH;
-    cudaError_t e = cudaMemcpyAsync(r->d_data.p, file + r->data_offset, r->data_len,
-                                    cudaMemcpyHostToDevice, (cudaStream_t)stream);
-    return cuda_code(e);
+    const cudaStream_t s = (cudaStream_t)stream;
+    hct_b200_error *err = nullptr;  // this entry point reports the status code only
+    int rc = ensure_device(r->ctx);
+    if (rc) return rc;
+    if (r->read_pending) CK(cudaStreamWaitEvent(s, r->data_free, 0));
+    CK(cudaMemcpyAsync(r->d_data.p, file + r->data_offset, r->data_len, cudaMemcpyHostToDevice, s));
+    CK(cudaEventRecord(r->uploaded, s));
+    r->upload_pending = true;
+    return HCT_B200_OK;
 }
 
 int hct_b200_reader_header(const hct_b200_reader *r, hct_b200_header *out) {
@@ -905,10 +933,12 @@ int reader_lz4(hct_b200_reader *r, uint8_t *d_dst, size_t cap, size_t *written, 
     }
     *written = 0;
     if (nb == 0) return HCT_B200_OK;
+    CK(r->before_read(s));
     int slot = r->ctx->prof_begin(s);
     CK(launch_lz4_blocks(r->d_data.as<uint8_t>(), r->d_blocks.as<hct_b200_lz4_block>(), nb, d_dst,
                          r->d_status.as<hct_b200_status>(), s));
     r->ctx->prof_end(slot, PK_LZ4, (double)r->hdr.compressed_size + (double)r->hdr.original_size, s);
+    CK(r->after_read(s));
     std::vector<hct_b200_status> st(nb);
     CK(cudaMemcpyAsync(st.data(), r->d_status.p, nb * sizeof(hct_b200_status),
                        cudaMemcpyDeviceToHost, s));
@@ -1008,11 +1038,13 @@ int hct_b200_reader_decode_async(hct_b200_reader *r, void *d_out, int out_dtype,
     }
     CK(cudaMemsetAsync(ctx->flag.p, 0, sizeof(int), s));
     if (nb) {
+        CK(r->before_read(s));
         int slot = ctx->prof_begin(s);
         CK(launch_lz4_blocks(r->d_data.as<uint8_t>(), r->d_blocks.as<hct_b200_lz4_block>(), nb,
                              ctx->payload.as<uint8_t>(), r->d_status.as<hct_b200_status>(), s));
         ctx->prof_end(slot, PK_LZ4, (double)r->hdr.compressed_size + (double)r->hdr.original_size,
                       s);
+        CK(r->after_read(s));
     }
     const uint64_t total = r->rows * r->cols;
     const size_t written = r->hdr.original_size;  // verified against the statuses in _wait

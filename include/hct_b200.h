@@ -241,7 +241,11 @@ int hct_b200_spectral_q4_decode_noalloc(const uint8_t *d_payload, size_t payload
 int hct_b200_reader_open(hct_b200_ctx *ctx, const uint8_t *file, size_t file_len,
                          int validate_checksums, hct_b200_reader **out, hct_b200_error *err);
 /* Re-upload the compressed data of a file with the same layout into an open
- * reader (stream-ordered H2D copy; pinned host memory makes it asynchronous). */
+ * reader (stream-ordered H2D copy; pinned host memory makes it asynchronous).
+ * The reader orders its device buffer across streams by itself: the copy
+ * waits for the last decode that read the buffer, and the next decode on any
+ * stream waits for the copy, so uploads may run on a copy stream while other
+ * tensors decode. */
 int hct_b200_reader_upload(hct_b200_reader *r, const uint8_t *file, size_t file_len, void *stream);
 int hct_b200_reader_header(const hct_b200_reader *r, hct_b200_header *out);
 uint32_t hct_b200_reader_num_blocks(const hct_b200_reader *r);

@@ -195,3 +195,36 @@ def test_async_decode_matches_sync(hb, orc):
         r.wait()
     for r, o in zip(readers, outs):
         assert torch.equal(o, r.decode(hb.F32))
+
+
+def test_upload_on_copy_stream_is_ordered(hb, orc):
+    """upload() on a second stream waits for the previous decode's read of the
+    buffer, and the next decode waits for the upload (no host sync between)."""
+    import torch
+    from oracle import hct as OH
+
+    f = OH.encode_spectral_q4(OH.gen_weight((256, 1024), 77))
+    ref = hb.HctReader(f).decode(hb.F32)
+    r = hb.HctReader(f)
+    hdr_len = len(f) - len(OH.parse_hct(f).data)
+    zeros = bytes(f[:hdr_len]) + bytes(len(f) - hdr_len)  # same layout, data all zero
+    pinned_f = torch.empty(len(f), dtype=torch.uint8, pin_memory=True)
+    pinned_f.numpy()[:] = np.frombuffer(f, np.uint8)
+    pinned_z = torch.empty(len(f), dtype=torch.uint8, pin_memory=True)
+    pinned_z.numpy()[:] = np.frombuffer(zeros, np.uint8)
+    comp, copy = torch.cuda.current_stream(), torch.cuda.Stream()
+    out1 = torch.empty_like(ref)
+    out2 = torch.empty_like(ref)
+    out3 = torch.empty_like(ref)
+    for _ in range(3):
+        r.decode_async(out1, hb.F32, stream=comp)
+        r.upload(pinned_z.numpy(), stream=copy)  # must not overwrite the data under decode 1
+        r.wait()
+        assert torch.equal(out1, ref)
+        r.decode_async(out2, hb.F32, stream=comp)  # must see the zeros: a zero LZ4 offset
+        with pytest.raises(hb.CorruptedData, match="zero offset"):
+            r.wait()
+        r.upload(pinned_f.numpy(), stream=copy)
+        r.decode_async(out3, hb.F32, stream=comp)
+        r.wait()
+        assert torch.equal(out3, ref)
