@@ -24,11 +24,25 @@ cudaError_t launch_dequant_int4(const uint8_t *d_data, size_t data_len, size_t n
                                 size_t num_elements, void *d_out, int out_dtype, cudaStream_t s);
 
 // Number of 1024-bit chunks the spectral scatter scans.
-inline uint64_t spectral_chunks(uint64_t total) { return (total + 1023) / 1024; }
+__host__ __device__ inline constexpr uint64_t spectral_chunks(uint64_t total) {
+    return (total + 1023) / 1024;
+}
+// Rank directory of the bitmap (launch_spectral_rank): d_chunk[c] is the
+// popcount of the chunks before c within its group of RANK_GROUP chunks, and
+// the group prefixes follow at d_chunk + rank_group_offset(total), so the
+// rank of chunk c is d_chunk[c] + d_chunk[rank_group_offset + c / RANK_GROUP].
+constexpr uint64_t RANK_GROUP = 256;
+__host__ __device__ inline constexpr uint64_t rank_group_offset(uint64_t total) {
+    return (spectral_chunks(total) + RANK_GROUP - 1) / RANK_GROUP * RANK_GROUP;
+}
+// u32 words of the rank directory for a bitmap of `total` bits.
+__host__ __device__ inline constexpr uint64_t rank_dir_words(uint64_t total) {
+    return rank_group_offset(total) + spectral_chunks(total) / RANK_GROUP + 2;
+}
 
 // Spectral payload (bitmap ++ INT4) -> dense fp16 coefficients, row stride ld
 // (ld >= cols, pad columns written as zero).  Scratch: d_chunk holds
-// spectral_chunks(total)+1 u32, d_meta 4 u64 (meta[0] = popcount k).
+// rank_dir_words(total) u32, d_meta 4 u64 (meta[0] = popcount k).
 cudaError_t launch_spectral_scatter(const uint8_t *d_payload, size_t payload_len, uint64_t rows,
                                     uint64_t cols, uint32_t *d_chunk, uint64_t *d_meta,
                                     half_bits *d_dense, uint64_t ld, int *d_flag, cudaStream_t s);
@@ -74,13 +88,15 @@ cudaError_t launch_umma_gemm(const GemmArgs &args, cudaStream_t s);
 // L even, H = L/2 = P*Q with P, Q multiples of 4 and <= 128.
 bool fdct_factor(uint64_t L, uint32_t *P, uint32_t *Q);
 // rows of length L (fp16, stride ld_in) -> Z[b][k2][k1] complex fp16 pairs.
-// d_tables: the 3L/2 complex fp32 twiddles written by launch_pack_tables(L).
+// d_tables: the per-k pack coefficients written by launch_pack_tables(L, P, Q).
 cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t batch, uint32_t L,
                                 uint32_t P, uint32_t Q, const float *d_tables, half_bits *d_out,
                                 cudaStream_t s);
-cudaError_t launch_pack_tables(uint32_t L, float *d_tables, cudaStream_t s);
-// Rank directory of a spectral payload: per-1024-bit chunk exclusive popcount
-// prefix in d_chunk, meta[0] = k, meta[1] = nibble offset, meta[2] = short.
+// L/2 float4 (alpha_k, beta_k) in (k2, k1) order, k = Q k1 + k2 (P Q = L/2).
+cudaError_t launch_pack_tables(uint32_t L, uint32_t P, uint32_t Q, float *d_tables,
+                               cudaStream_t s);
+// Rank directory of a spectral payload (layout at spectral_chunks above) in
+// d_chunk, meta[0] = k, meta[1] = nibble offset, meta[2] = short.
 cudaError_t launch_spectral_rank(const uint8_t *d_payload, size_t payload_len, uint64_t total,
                                  uint32_t *d_chunk, uint64_t *d_meta, int *d_flag, cudaStream_t s);
 // Row pack straight from a spectral payload (rows of length L, row-major

@@ -42,76 +42,81 @@ __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_
 __device__ __forceinline__ uint16_t f2h(float v) { return __half_as_ushort(__float2half_rn(v)); }
 
 // Shared-memory index of row element k: two fp16 of padding every 64
-// elements, so accesses at stride 64 (and at stride Q) spread over the banks.
+// elements, so the pack's reads at stride Q (lanes = consecutive k1) spread
+// over the banks.
 __device__ __forceinline__ uint32_t pad_idx(uint32_t k) { return k + 2 * (k >> 6); }
-// Word index of Z[k] in the transpose buffer (one pad word per 64 words).
-__device__ __forceinline__ uint32_t zpad_idx(uint32_t k) { return k + (k >> 6); }
 
 __host__ __device__ __forceinline__ uint32_t srow_halves(uint32_t L) {
     return (L + 2 * (L >> 6) + 8) & ~7u;
 }
-__host__ __device__ __forceinline__ uint32_t zbuf_words(uint32_t L) {
-    return (L / 2 + (L / 2 >> 6) + 8) & ~7u;
+
+__device__ __forceinline__ uint32_t pack_z(float re, float im) {
+    const __half2 h = __floats2half2_rn(re, im);
+    return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-// Pack phases 2 and 3 for one staged row: Z[k] for k < H in natural order
-// (coalesced coefficient loads) into the transpose buffer, then the row of
-// Z written in (k2, k1) order, k = Q k1 + k2, one warp per k2, 4-byte pairs.
-__device__ __forceinline__ void pack_row(const uint16_t *srow, uint32_t *zbuf,
-                                         const float4 *__restrict__ coef, uint32_t L, uint32_t P,
-                                         uint32_t Q, uint32_t *__restrict__ orow) {
+// Pack of one staged row, written straight to the output row in (k2, k1)
+// order, k = Q k1 + k2: warp w takes the k2 rows w, w + nwarps, ... <= Q/2 and
+// lane l the k1 = l, l + 32, ...; each item also produces its partner H - k,
+// which reads the same four inputs c[k], c[L-k], c[H+k], c[H-k] with the
+// roles permuted and lies at k2' = Q - k2, k1' = P - 1 - k1 (k2 > 0) or
+// k2' = 0, k1' = P - k1 (k2 = 0).  coefT holds (alpha_k, beta_k) in the same
+// (k2, k1) order, so every global access of a warp is contiguous.
+__device__ __forceinline__ void pack_row(const uint16_t *srow, const float4 *__restrict__ coefT,
+                                         uint32_t L, uint32_t P, uint32_t Q,
+                                         uint32_t *__restrict__ orow) {
     const uint32_t H = L / 2;
-    // Z[k] and Z[H-k] read the same four inputs c[k], c[L-k], c[H+k], c[H-k]
-    // (with the roles permuted), so each thread produces both.
-    for (uint32_t k = threadIdx.x; k <= H / 2; k += blockDim.x) {
-        const float ck = h2f(srow[pad_idx(k)]);
-        const float cLk = k ? h2f(srow[pad_idx(L - k)]) : 0.0f;
-        const float cHk = h2f(srow[pad_idx(H + k)]);
-        const float cHmk = h2f(srow[pad_idx(H - k)]);  // H - k >= 1 for k < H
-        const float4 t = coef[k];                      // (alpha.re, alpha.im, beta.re, beta.im)
-        const float zr = fmaf(t.x, ck, fmaf(t.y, cLk, fmaf(t.z, cHk, t.w * cHmk)));
-        const float zi = fmaf(t.y, ck, fmaf(-t.x, cLk, fmaf(t.w, cHk, -t.z * cHmk)));
-        zbuf[zpad_idx(k)] = (uint32_t)f2h(zr) | ((uint32_t)f2h(zi) << 16);
-        if (k != 0 && k != H / 2) {
-            // k' = H - k: c[k'] = c[H-k], c[L-k'] = c[H+k], c[H+k'] = c[L-k], c[H-k'] = c[k]
-            const float4 u = coef[H - k];
-            const float yr = fmaf(u.x, cHmk, fmaf(u.y, cHk, fmaf(u.z, cLk, u.w * ck)));
-            const float yi = fmaf(u.y, cHmk, fmaf(-u.x, cHk, fmaf(u.w, cLk, -u.z * ck)));
-            zbuf[zpad_idx(H - k)] = (uint32_t)f2h(yr) | ((uint32_t)f2h(yi) << 16);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    for (uint32_t k2 = warp; 2 * k2 <= Q; k2 += nwarps) {
+        const uint32_t k1_end = k2 == 0 ? P / 2 + 1 : (2 * k2 == Q ? P / 2 : P);
+        for (uint32_t k1 = lane; k1 < k1_end; k1 += 32) {
+            const uint32_t k = Q * k1 + k2;
+            const float ck = h2f(srow[pad_idx(k)]);
+            const float cLk = k ? h2f(srow[pad_idx(L - k)]) : 0.0f;
+            const float cHk = h2f(srow[pad_idx(H + k)]);
+            const float cHmk = h2f(srow[pad_idx(H - k)]);  // H - k >= 1 for k < H
+            const float4 t = coefT[k2 * P + k1];            // (alpha.re, alpha.im, beta.re, beta.im)
+            const float zr = fmaf(t.x, ck, fmaf(t.y, cLk, fmaf(t.z, cHk, t.w * cHmk)));
+            const float zi = fmaf(t.y, ck, fmaf(-t.x, cLk, fmaf(t.w, cHk, -t.z * cHmk)));
+            orow[k2 * P + k1] = pack_z(zr, zi);
+            if (k != 0 && 2 * k != H) {
+                // k' = H - k: c[k'] = c[H-k], c[L-k'] = c[H+k], c[H+k'] = c[L-k], c[H-k'] = c[k]
+                const uint32_t j = k2 == 0 ? P - k1 : (Q - k2) * P + (P - 1 - k1);
+                const float4 u = coefT[j];
+                const float yr = fmaf(u.x, cHmk, fmaf(u.y, cHk, fmaf(u.z, cLk, u.w * ck)));
+                const float yi = fmaf(u.y, cHmk, fmaf(-u.x, cHk, fmaf(u.w, cLk, -u.z * ck)));
+                orow[j] = pack_z(yr, yi);
+            }
         }
     }
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    for (uint32_t k2 = warp; k2 < Q; k2 += nwarps)
-        for (uint32_t k1 = lane; k1 < P; k1 += 32) orow[k2 * P + k1] = zbuf[zpad_idx(Q * k1 + k2)];
 }
 
 // Pack of dense fp16 rows (stride ld_in): one CTA per row, the row staged in
-// shared memory with 8 independent 16-byte loads in flight per thread.
-__global__ void __launch_bounds__(512) makhoul_pack_kernel(const uint16_t *__restrict__ in,
-                                                           uint64_t ld_in, uint64_t B, uint32_t L,
-                                                           uint32_t P, uint32_t Q,
-                                                           const float4 *__restrict__ coef,
-                                                           uint32_t *__restrict__ out) {
+// shared memory with up to 4 independent 16-byte loads in flight per thread.
+// THREADS = 256 with 5 CTAs per SM for rows up to 16384 elements, 512 with 2
+// beyond (the staged row then takes up to 57 KB).
+template <int THREADS, int MIN_CTAS>
+__global__ void __launch_bounds__(THREADS, MIN_CTAS) makhoul_pack_kernel(
+    const uint16_t *__restrict__ in, uint64_t ld_in, uint64_t B, uint32_t L, uint32_t P,
+    uint32_t Q, const float4 *__restrict__ coefT, uint32_t *__restrict__ out) {
     extern __shared__ uint16_t srow[];
-    uint32_t *zbuf = reinterpret_cast<uint32_t *>(srow + srow_halves(L));
     const bool vec = ((ld_in & 7) == 0) && (((uintptr_t)in & 15) == 0) && ((L & 7) == 0);
+    const uint32_t nv = L / 8;
     for (uint64_t b = blockIdx.x; b < B; b += gridDim.x) {
         const uint16_t *row = in + b * ld_in;
         __syncthreads();  // previous row fully consumed
         if (vec) {
             const uint4 *r4 = reinterpret_cast<const uint4 *>(row);
-            const uint32_t nv = L / 8;
-            for (uint32_t v0 = threadIdx.x; v0 < nv; v0 += 8 * blockDim.x) {
-                uint4 x[8];
+            for (uint32_t v0 = threadIdx.x; v0 < nv; v0 += 4 * THREADS) {
+                uint4 x[4];
 #pragma unroll
-                for (int u = 0; u < 8; u++) {
-                    const uint32_t v = v0 + u * blockDim.x;
-                    if (v < nv) x[u] = r4[v];
+                for (int u = 0; u < 4; u++) {
+                    const uint32_t v = v0 + u * THREADS;
+                    if (v < nv) x[u] = __ldg(r4 + v);
                 }
 #pragma unroll
-                for (int u = 0; u < 8; u++) {
-                    const uint32_t v = v0 + u * blockDim.x;
+                for (int u = 0; u < 4; u++) {
+                    const uint32_t v = v0 + u * THREADS;
                     if (v < nv) {  // 8 elements never straddle a 64-element pad
                         uint32_t *d = reinterpret_cast<uint32_t *>(srow + pad_idx(8 * v));
                         d[0] = x[u].x;
@@ -122,10 +127,10 @@ __global__ void __launch_bounds__(512) makhoul_pack_kernel(const uint16_t *__res
                 }
             }
         } else {
-            for (uint32_t k = threadIdx.x; k < L; k += blockDim.x) srow[pad_idx(k)] = row[k];
+            for (uint32_t k = threadIdx.x; k < L; k += THREADS) srow[pad_idx(k)] = row[k];
         }
         __syncthreads();
-        pack_row(srow, zbuf, coef, L, P, Q, out + b * (uint64_t)(L / 2));
+        pack_row(srow, coefT, L, P, Q, out + b * (uint64_t)(L / 2));
     }
 }
 
@@ -153,8 +158,8 @@ __device__ __forceinline__ float f16bits_to_f32(uint32_t h) {
 // decodes the coefficients of its row into shared memory and then runs the
 // pack phases:
 //   - the row's bitmap words (two per thread, coalesced) and a block scan of
-//     their popcounts on top of the row's rank (1024-bit chunk prefix from
-//     launch_spectral_rank plus a partial popcount);
+//     their popcounts on top of the row's rank (the rank directory of
+//     launch_spectral_rank for its 1024-bit chunk plus a partial popcount);
 //   - the row's nibble bytes and its FP16 scales (converted to f32) staged in
 //     shared memory, the row itself zero-filled;
 //   - each thread walks the set bits of its two words (__ffs), writing
@@ -167,16 +172,15 @@ __host__ __device__ __forceinline__ uint32_t spack_nib_bytes(uint32_t L) {
     return (L / 2 + 16 + 15) & ~15u;
 }
 
-__global__ void __launch_bounds__(SPACK_THREADS) spectral_pack_kernel(
+__global__ void __launch_bounds__(SPACK_THREADS, 3) spectral_pack_kernel(
     const uint8_t *__restrict__ payload, uint64_t bmb, const uint32_t *__restrict__ chunk_base,
-    const uint64_t *__restrict__ meta, uint64_t B, uint32_t L, uint32_t P, uint32_t Q,
-    const float4 *__restrict__ coef, uint32_t *__restrict__ out) {
+    uint64_t group_off, const uint64_t *__restrict__ meta, uint64_t B, uint32_t L, uint32_t P,
+    uint32_t Q, const float4 *__restrict__ coef, uint32_t *__restrict__ out) {
     extern __shared__ uint16_t srow[];
     __shared__ uint32_t warp_tot[SPACK_THREADS / 32];
     __shared__ uint32_t s_rank_start;
     const uint32_t row_words = L / 32;
-    uint32_t *zbuf = reinterpret_cast<uint32_t *>(srow + srow_halves(L));
-    uint8_t *nib_s = reinterpret_cast<uint8_t *>(zbuf + zbuf_words(L));
+    uint8_t *nib_s = reinterpret_cast<uint8_t *>(srow + srow_halves(L));
     float *sc_s = reinterpret_cast<float *>(nib_s + spack_nib_bytes(L));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
     const uint64_t k_total = meta[0];
@@ -205,7 +209,8 @@ __global__ void __launch_bounds__(SPACK_THREADS) spectral_pack_kernel(
             for (uint64_t w = c0 * 32 + lane; w < word0; w += 32) part += __popc(bm32[w]);
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-            if (lane == 0) s_rank_start = chunk_base[c0] + part;
+            if (lane == 0)
+                s_rank_start = chunk_base[c0] + chunk_base[group_off + c0 / RANK_GROUP] + part;
         }
         // zero the staged row while the scan settles
         uint32_t *srow32 = reinterpret_cast<uint32_t *>(srow);
@@ -247,12 +252,13 @@ __global__ void __launch_bounds__(SPACK_THREADS) spectral_pack_kernel(
             }
         }
         __syncthreads();
-        pack_row(srow, zbuf, coef, L, P, Q, out + b * (uint64_t)(L / 2));
+        pack_row(srow, coef, L, P, Q, out + b * (uint64_t)(L / 2));
     }
 }
 
-// coef[k] = (alpha_k, beta_k) for k < L/2 (see the file comment), in f64.
-__global__ void pack_tables_kernel(uint32_t L, float4 *coef) {
+// coefT[k2 * P + k1] = (alpha_k, beta_k), k = Q k1 + k2 < L/2 (see the file
+// comment), in f64.
+__global__ void pack_tables_kernel(uint32_t L, uint32_t P, uint32_t Q, float4 *coefT) {
     const uint32_t H = L / 2;
     for (uint32_t k = blockIdx.x * blockDim.x + threadIdx.x; k < H; k += gridDim.x * blockDim.x) {
         double sa, ca, sb, cb, st, ct;
@@ -266,7 +272,7 @@ __global__ void pack_tables_kernel(uint32_t L, float4 *coef) {
         // beta = 1/2 b (1 - i t) = 1/2 b (1 + st - i ct)
         const double qr = 1.0 + st, qi = -ct;
         const double br = 0.5 * (cb * qr - sb * qi), bi = 0.5 * (cb * qi + sb * qr);
-        coef[k] = make_float4((float)ar, (float)ai, (float)br, (float)bi);
+        coefT[(k % Q) * P + k / Q] = make_float4((float)ar, (float)ai, (float)br, (float)bi);
     }
 }
 
@@ -325,16 +331,19 @@ bool fdct_factor(uint64_t L, uint32_t *P, uint32_t *Q) {
 cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t B, uint32_t L,
                                 uint32_t P, uint32_t Q, const float *d_tables, half_bits *d_out,
                                 cudaStream_t s) {
-    const size_t smem = (size_t)srow_halves(L) * 2 + (size_t)zbuf_words(L) * 4;
+    const size_t smem = (size_t)srow_halves(L) * 2;
     if (smem > 220 * 1024) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(makhoul_pack_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const bool small = L <= 16384;
+    auto kern = small ? makhoul_pack_kernel<256, 5> : makhoul_pack_kernel<512, 2>;
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    uint64_t g = B < 148ull * 8 ? B : 148ull * 8;
+    const uint64_t per_sm = small ? 5 : 2;
+    uint64_t g = B < 148ull * per_sm ? B : 148ull * per_sm;
     if (g < 1) g = 1;
-    makhoul_pack_kernel<<<(unsigned)g, 512, smem, s>>>(
-        d_in, ld_in, B, L, P, Q, reinterpret_cast<const float4 *>(d_tables),
-        reinterpret_cast<uint32_t *>(d_out));
+    kern<<<(unsigned)g, small ? 256 : 512, smem, s>>>(d_in, ld_in, B, L, P, Q,
+                                                      reinterpret_cast<const float4 *>(d_tables),
+                                                      reinterpret_cast<uint32_t *>(d_out));
     return cudaGetLastError();
 }
 
@@ -345,9 +354,8 @@ cudaError_t launch_spectral_pack(const uint8_t *d_payload, uint64_t bmb, const u
                                  uint32_t Q, const float *d_tables, half_bits *d_out,
                                  cudaStream_t s) {
     if (!spectral_pack_supported(L)) return cudaErrorInvalidValue;
-    // dynamic shared memory: row, transpose buffer, nibbles, f32 scales
-    const size_t smem = (size_t)srow_halves(L) * 2 + (size_t)zbuf_words(L) * 4 +
-                        spack_nib_bytes(L) + ((size_t)L / 32 + 4) * 4;
+    // dynamic shared memory: row, nibbles, f32 scales
+    const size_t smem = (size_t)srow_halves(L) * 2 + spack_nib_bytes(L) + ((size_t)L / 32 + 4) * 4;
     if (smem > 220 * 1024) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(spectral_pack_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -355,13 +363,16 @@ cudaError_t launch_spectral_pack(const uint8_t *d_payload, uint64_t bmb, const u
     uint64_t g = B < 148ull * 4 ? B : 148ull * 4;
     if (g < 1) g = 1;
     spectral_pack_kernel<<<(unsigned)g, SPACK_THREADS, smem, s>>>(
-        d_payload, bmb, d_chunk, d_meta, B, L, P, Q, reinterpret_cast<const float4 *>(d_tables),
-        reinterpret_cast<uint32_t *>(d_out));
+        d_payload, bmb, d_chunk, rank_group_offset(B * (uint64_t)L), d_meta, B, L, P, Q,
+        reinterpret_cast<const float4 *>(d_tables), reinterpret_cast<uint32_t *>(d_out));
     return cudaGetLastError();
 }
 
-cudaError_t launch_pack_tables(uint32_t L, float *d_tables, cudaStream_t s) {
-    pack_tables_kernel<<<(L / 2 + 255) / 256, 256, 0, s>>>(L, reinterpret_cast<float4 *>(d_tables));
+cudaError_t launch_pack_tables(uint32_t L, uint32_t P, uint32_t Q, float *d_tables,
+                               cudaStream_t s) {
+    if ((uint64_t)P * Q != L / 2) return cudaErrorInvalidValue;
+    pack_tables_kernel<<<(L / 2 + 255) / 256, 256, 0, s>>>(L, P, Q,
+                                                            reinterpret_cast<float4 *>(d_tables));
     return cudaGetLastError();
 }
 

@@ -284,7 +284,7 @@ int reserve_spectral(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols, size_t pay
     CK(ctx->tt.reserve(cols * round_up(rows, 8) * 2 + 16));
     CK(ctx->za.reserve(rows * cols * 2 + 16));
     CK(ctx->zb.reserve(rows * cols * 2 + 16));
-    CK(ctx->chunk.reserve((spectral_chunks(rows * cols) + 1) * sizeof(uint32_t)));
+    CK(ctx->chunk.reserve(rank_dir_words(rows * cols) * sizeof(uint32_t)));
     CK(ctx->meta.reserve(4 * sizeof(uint64_t)));
     CK(ctx->flag.reserve(sizeof(int)));
     return HCT_B200_OK;
@@ -338,7 +338,7 @@ int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint
     if (pt == ctx->pack_tabs.end()) {
         auto b = std::make_unique<DevBuf>();
         CK(b->reserve((size_t)L * 12));
-        CK(launch_pack_tables((uint32_t)L, b->as<float>(), s));
+        CK(launch_pack_tables((uint32_t)L, P, Q, b->as<float>(), s));
         pt = ctx->pack_tabs.emplace((uint32_t)L, std::move(b)).first;
     }
     int *flag = ctx->flag.as<int>();

@@ -36,7 +36,7 @@ constexpr uint64_t NOALLOC_MAX_ELEMS = NOALLOC_MAX_DIM * NOALLOC_MAX_DIM;
 constexpr size_t OFF_FLAG = 0;
 constexpr size_t OFF_META = 256;
 constexpr size_t OFF_CHUNK = 512;
-constexpr size_t CHUNK_BYTES = ((NOALLOC_MAX_ELEMS / 1024 + 1) * 4 + 255) / 256 * 256;
+constexpr size_t CHUNK_BYTES = (hct::rank_dir_words(NOALLOC_MAX_ELEMS) * 4 + 255) / 256 * 256;
 constexpr size_t MAT_BYTES = NOALLOC_MAX_ELEMS * 2;  // one fp16 matrix, <= 2048 x 2048
 constexpr size_t OFF_BASIS_W = OFF_CHUNK + CHUNK_BYTES;
 constexpr size_t OFF_BASIS_H = OFF_BASIS_W + MAT_BYTES;

@@ -137,23 +137,51 @@ __device__ __forceinline__ uint32_t bitmap_word(const uint8_t *bm, uint64_t bmb,
     return v;
 }
 
-// Popcount of each 1024-bit chunk: one warp per chunk.
-__global__ void __launch_bounds__(256) chunk_popcount_kernel(const uint8_t *__restrict__ bm,
-                                                             uint64_t bmb, uint64_t total,
-                                                             uint64_t nchunks,
-                                                             uint32_t *__restrict__ counts) {
-    const int lane = threadIdx.x & 31;
-    const uint64_t warps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
-    for (uint64_t c = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; c < nchunks;
-         c += warps) {
-        uint32_t p = __popc(bitmap_word(bm, bmb, total, 32 * c + lane));
+// Rank directory, level 1: one CTA per group of RANK_GROUP chunks, one
+// thread per 1024-bit chunk (eight 16-byte loads), a block scan of the
+// popcounts; writes each chunk's prefix within its group and the group total.
+constexpr int RANK_THREADS = (int)RANK_GROUP;
+
+__global__ void __launch_bounds__(RANK_THREADS) chunk_rank_kernel(
+    const uint8_t *__restrict__ bm, uint64_t bmb, uint64_t total, uint64_t nchunks,
+    uint32_t *__restrict__ local, uint32_t *__restrict__ group_tot) {
+    __shared__ uint32_t warp_tot[RANK_THREADS / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint64_t c = (uint64_t)blockIdx.x * RANK_THREADS + threadIdx.x;
+    uint32_t cnt = 0;
+    if (c < nchunks) {
+        if (128 * (c + 1) <= bmb && 1024 * (c + 1) <= total) {
+            const uint4 *p = reinterpret_cast<const uint4 *>(bm + 128 * c);
+            uint4 v[8];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
-        if (lane == 0) counts[c] = p;
+            for (int j = 0; j < 8; j++) v[j] = __ldg(p + j);
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                cnt += __popc(v[j].x) + __popc(v[j].y) + __popc(v[j].z) + __popc(v[j].w);
+        } else {
+            for (int j = 0; j < 32; j++) cnt += __popc(bitmap_word(bm, bmb, total, 32 * c + j));
+        }
     }
+    uint32_t incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    uint32_t before = 0, sum = 0;
+#pragma unroll
+    for (int w = 0; w < RANK_THREADS / 32; w++) {
+        const uint32_t t = warp_tot[w];
+        before += w < warp ? t : 0u;
+        sum += t;
+    }
+    if (c < nchunks) local[c] = before + incl - cnt;
+    if (threadIdx.x == 0) group_tot[blockIdx.x] = sum;
 }
 
-// Exclusive scan of the chunk counts in place (single CTA of 1024 threads);
+// Exclusive scan of the group totals in place (single CTA of 1024 threads);
 // meta[0] = total popcount k, meta[1] = nibble section offset, meta[2] =
 // 1 if the payload is too short for k coefficients.
 __global__ void __launch_bounds__(1024) chunk_scan_kernel(uint32_t *__restrict__ counts,
@@ -221,7 +249,8 @@ __global__ void __launch_bounds__(1024) chunk_scan_kernel(uint32_t *__restrict__
 // 4 passes, so a warp writes 256 contiguous fp16 per pass.
 __global__ void __launch_bounds__(256) spectral_scatter_kernel(
     const uint8_t *__restrict__ payload, uint64_t bmb, uint64_t total, uint64_t cols,
-    uint64_t nchunks, const uint32_t *__restrict__ chunk_base, const uint64_t *__restrict__ meta,
+    uint64_t nchunks, const uint32_t *__restrict__ chunk_base,
+    const uint32_t *__restrict__ group_base, const uint64_t *__restrict__ meta,
     uint16_t *__restrict__ dense, uint64_t ld, bool vec_rows) {
     const int lane = threadIdx.x & 31;
     const uint64_t k = meta[0];
@@ -239,7 +268,8 @@ __global__ void __launch_bounds__(256) spectral_scatter_kernel(
             uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
             if (lane >= o) incl += t;
         }
-        const uint64_t wrank = (uint64_t)chunk_base[c] + (incl - pc);
+        const uint64_t wrank =
+            (uint64_t)chunk_base[c] + group_base[c / RANK_GROUP] + (incl - pc);
 #pragma unroll
         for (int pass = 0; pass < 4; pass++) {
             const int src_lane = pass * 8 + (lane >> 2);      // word holding my 8 bits
@@ -337,12 +367,12 @@ cudaError_t launch_spectral_scatter(const uint8_t *d_payload, size_t payload_len
         cudaError_t e = cudaMemset2DAsync(d_dense + cols, ld * 2, 0, (ld - cols) * 2, rows, s);
         if (e != cudaSuccess) return e;
     }
-    chunk_popcount_kernel<<<grid_for(nchunks * 32, 256), 256, 0, s>>>(d_payload, bmb, total,
-                                                                      nchunks, d_chunk);
-    chunk_scan_kernel<<<1, 1024, 0, s>>>(d_chunk, nchunks, bmb, payload_len, d_meta, d_flag);
+    cudaError_t e = launch_spectral_rank(d_payload, payload_len, total, d_chunk, d_meta, d_flag, s);
+    if (e != cudaSuccess) return e;
     const bool vec_rows = (cols % 8 == 0) && (ld % 8 == 0) && (((uintptr_t)d_dense & 15u) == 0);
     spectral_scatter_kernel<<<grid_for(nchunks * 32, 256), 256, 0, s>>>(
-        d_payload, bmb, total, cols, nchunks, d_chunk, d_meta, d_dense, ld, vec_rows);
+        d_payload, bmb, total, cols, nchunks, d_chunk, d_chunk + rank_group_offset(total), d_meta,
+        d_dense, ld, vec_rows);
     return cudaGetLastError();
 }
 
@@ -350,9 +380,11 @@ cudaError_t launch_spectral_rank(const uint8_t *d_payload, size_t payload_len, u
                                  uint32_t *d_chunk, uint64_t *d_meta, int *d_flag, cudaStream_t s) {
     const uint64_t bmb = (total + 7) / 8;
     const uint64_t nchunks = spectral_chunks(total);
-    chunk_popcount_kernel<<<grid_for(nchunks * 32, 256), 256, 0, s>>>(d_payload, bmb, total,
-                                                                      nchunks, d_chunk);
-    chunk_scan_kernel<<<1, 1024, 0, s>>>(d_chunk, nchunks, bmb, payload_len, d_meta, d_flag);
+    const uint64_t groups = (nchunks + RANK_GROUP - 1) / RANK_GROUP;
+    uint32_t *group = d_chunk + rank_group_offset(total);
+    chunk_rank_kernel<<<(unsigned)(groups ? groups : 1), RANK_THREADS, 0, s>>>(
+        d_payload, bmb, total, nchunks, d_chunk, group);
+    chunk_scan_kernel<<<1, 1024, 0, s>>>(group, groups, bmb, payload_len, d_meta, d_flag);
     return cudaGetLastError();
 }
 
