@@ -134,42 +134,34 @@ __global__ void __launch_bounds__(THREADS, MIN_CTAS) makhoul_pack_kernel(
     }
 }
 
-__device__ __forceinline__ float f16bits_to_f32(uint32_t h) {
-    // exact conversion (also for subnormals) as quantization.rs:166-197
-    uint32_t sign = (h >> 15) & 1u, exp = (h >> 10) & 0x1fu, frac = h & 0x3ffu, out;
-    if (exp == 0) {
-        if (frac == 0) {
-            out = sign << 31;
-        } else {
-            int e = -14;
-            uint32_t f = frac;
-            while ((f & 0x400u) == 0) { f <<= 1; e -= 1; }
-            out = (sign << 31) | ((uint32_t)((e + 127) & 0xff) << 23) | ((f & 0x3ffu) << 13);
-        }
-    } else if (exp == 31) {
-        out = (sign << 31) | (0xffu << 23) | (frac << 13);
-    } else {
-        out = (sign << 31) | ((exp - 15 + 127) << 23) | (frac << 13);
-    }
-    return __uint_as_float(out);
-}
-
 // Row pack straight from the spectral payload (bitmap ++ INT4).  Each CTA
 // decodes the coefficients of its row into shared memory and then runs the
-// pack phases:
-//   - the row's bitmap words (two per thread, coalesced) and a block scan of
-//     their popcounts on top of the row's rank (the rank directory of
-//     launch_spectral_rank for its 1024-bit chunk plus a partial popcount);
-//   - the row's nibble bytes and its FP16 scales (converted to f32) staged in
-//     shared memory, the row itself zero-filled;
-//   - each thread walks the set bits of its two words (__ffs), writing
-//     f32(nibble - 8) * f32(scale) rounded to fp16 at the bit's position.
-// Requires L % 64 == 0 (rows start on a 64-bit bitmap boundary), which every
-// factorable length satisfies.
+// pack:
+//   A. warp w takes the 64-bit bitmap words [w * spw, (w + 1) * spw) of the
+//      row, one per lane, and a warp scan of their popcounts; warp 0 adds
+//      up the row's rank (the rank directory of launch_spectral_rank for its
+//      1024-bit chunk plus a partial popcount);
+//   B. the row's coefficients in rank order are staged in shared memory:
+//      fp16((nibble - 8) * scale) per set bit when the row has at most L/2
+//      of them, else the raw nibble bytes and the f32 scales;
+//   C. each warp expands its words, 64 elements per step, lane l writing
+//      elements (2l, 2l + 1) of the word as one fp16 pair (zero where the
+//      bit is clear; the rank is the word's rank plus a masked popcount).
+// Requires L % 64 == 0 (rows start on a 64-bit bitmap boundary) and
+// L / 64 <= 32 * SPACK_WARPS.
 constexpr int SPACK_THREADS = 512;
+constexpr int SPACK_WARPS = SPACK_THREADS / 32;
 
-__host__ __device__ __forceinline__ uint32_t spack_nib_bytes(uint32_t L) {
-    return (L / 2 + 16 + 15) & ~15u;
+// bytes of the staging area behind the row: L/2 fp16 values, or L/2
+// nibble bytes (+ 16 slack) and L/32 + 4 f32 scales
+__host__ __device__ __forceinline__ uint32_t spack_stage_bytes(uint32_t L) {
+    const uint32_t vals = L, raw = ((L / 2 + 16 + 15) & ~15u) + (L / 32 + 4) * 4;
+    return vals > raw ? vals : raw;
+}
+
+__device__ __forceinline__ float deq_nibble(uint32_t byte, uint64_t r, float scale) {
+    const uint32_t nib = (r & 1) ? byte >> 4 : byte & 0xfu;
+    return __fmul_rn((float)((int)nib - 8), scale);
 }
 
 __global__ void __launch_bounds__(SPACK_THREADS, 3) spectral_pack_kernel(
@@ -177,26 +169,31 @@ __global__ void __launch_bounds__(SPACK_THREADS, 3) spectral_pack_kernel(
     uint64_t group_off, const uint64_t *__restrict__ meta, uint64_t B, uint32_t L, uint32_t P,
     uint32_t Q, const float4 *__restrict__ coef, uint32_t *__restrict__ out) {
     extern __shared__ uint16_t srow[];
-    __shared__ uint32_t warp_tot[SPACK_THREADS / 32];
+    __shared__ uint32_t warp_tot[SPACK_WARPS];
     __shared__ uint32_t s_rank_start;
-    const uint32_t row_words = L / 32;
-    uint8_t *nib_s = reinterpret_cast<uint8_t *>(srow + srow_halves(L));
-    float *sc_s = reinterpret_cast<float *>(nib_s + spack_nib_bytes(L));
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    const uint64_t k_total = meta[0];
+    uint8_t *stage = reinterpret_cast<uint8_t *>(srow + srow_halves(L));
+    uint16_t *vals_s = reinterpret_cast<uint16_t *>(stage);
+    uint8_t *nib_s = stage;
+    float *sc_s = reinterpret_cast<float *>(stage + ((L / 2 + 16 + 15) & ~15u));
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t segs = L / 64;
+    const uint32_t spw = (segs + SPACK_WARPS - 1) / SPACK_WARPS;
+    const uint32_t seg0 = warp * spw;
+    const uint32_t nseg = seg0 < segs ? min(spw, segs - seg0) : 0u;
     const uint8_t *scales = payload + bmb;
     const uint8_t *nibbles = payload + meta[1];
     const bool bad = meta[2] != 0;
+    const uint64_t *bm64 = reinterpret_cast<const uint64_t *>(payload);
     const uint32_t *bm32 = reinterpret_cast<const uint32_t *>(payload);
+    const uint32_t pair_shift = 2 * lane;
+    const uint64_t below = (1ull << pair_shift) - 1ull;  // bits of the elements before 2l
 
     for (uint64_t b = blockIdx.x; b < B; b += gridDim.x) {
         __syncthreads();  // previous row fully consumed
-        const uint64_t word0 = b * row_words;
-        const uint32_t w_a = 2 * threadIdx.x, w_b = w_a + 1;
-        const uint32_t va = w_a < row_words ? bm32[word0 + w_a] : 0u;
-        const uint32_t vb = w_b < row_words ? bm32[word0 + w_b] : 0u;
-        const uint32_t mine = __popc(va) + __popc(vb);
-        uint32_t incl = mine;
+        // A. bitmap words and their ranks
+        const uint64_t mw = lane < nseg ? bm64[b * segs + seg0 + lane] : 0ull;
+        const uint32_t cnt = __popcll(mw);
+        uint32_t incl = cnt;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
@@ -204,6 +201,7 @@ __global__ void __launch_bounds__(SPACK_THREADS, 3) spectral_pack_kernel(
         }
         if (lane == 31) warp_tot[warp] = incl;
         if (warp == 0) {
+            const uint64_t word0 = b * (uint64_t)(L / 32);
             const uint64_t c0 = word0 / 32;  // its 1024-bit chunk
             uint32_t part = 0;
             for (uint64_t w = c0 * 32 + lane; w < word0; w += 32) part += __popc(bm32[w]);
@@ -212,44 +210,68 @@ __global__ void __launch_bounds__(SPACK_THREADS, 3) spectral_pack_kernel(
             if (lane == 0)
                 s_rank_start = chunk_base[c0] + chunk_base[group_off + c0 / RANK_GROUP] + part;
         }
-        // zero the staged row while the scan settles
-        uint32_t *srow32 = reinterpret_cast<uint32_t *>(srow);
-        for (uint32_t i = threadIdx.x; i < srow_halves(L) / 2; i += blockDim.x) srow32[i] = 0u;
         __syncthreads();
-        uint32_t before = 0, row_count = 0;
-        for (int w = 0; w < nwarps; w++) {
-            if (w < warp) before += warp_tot[w];
-            row_count += warp_tot[w];
-        }
-        const uint64_t rank0 = s_rank_start;
-        const uint64_t nb0 = rank0 >> 1, nb1 = (rank0 + row_count + 1) >> 1;
-        const uint64_t sb0 = rank0 >> 5, sb1 = row_count ? ((rank0 + row_count - 1) >> 5) + 1 : sb0;
-        if (!bad) {  // a short payload (meta[2]) decodes to zeros, never reads past its end
-            for (uint64_t i = nb0 + threadIdx.x; i < nb1; i += blockDim.x)
-                nib_s[i - nb0] = nibbles[i];
-            for (uint64_t i = sb0 + threadIdx.x; i < sb1; i += blockDim.x)
-                sc_s[i - sb0] = f16bits_to_f32((uint32_t)scales[2 * i] |
-                                               ((uint32_t)scales[2 * i + 1] << 8));
-        }
-        __syncthreads();
-        if (!bad) {
-            uint64_t r = rank0 + before + (incl - mine);
+        // rank of this warp's first bit within the row, and the row's count
+        const uint32_t wt = lane < SPACK_WARPS ? warp_tot[lane] : 0u;
+        uint32_t wincl = wt;
 #pragma unroll
-            for (int half = 0; half < 2; half++) {
-                uint32_t x = half ? vb : va;
-                const uint32_t base = 32 * (half ? w_b : w_a);
-                while (x) {
-                    const int bit = __ffs(x) - 1;
-                    x &= x - 1;
-                    if (r < k_total) {
-                        const uint32_t byte = nib_s[(r >> 1) - nb0];
-                        const uint32_t nib = (r & 1) ? byte >> 4 : byte & 0xfu;
-                        srow[pad_idx(base + bit)] =
-                            f2h(__fmul_rn((float)((int)nib - 8), sc_s[(r >> 5) - sb0]));
-                    }
-                    r++;
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xffffffffu, wincl, o);
+            if (lane >= o) wincl += t;
+        }
+        const uint32_t before = __shfl_sync(0xffffffffu, wincl - wt, warp);
+        const uint32_t row_count = __shfl_sync(0xffffffffu, wincl, SPACK_WARPS - 1);
+        const uint64_t rank0 = s_rank_start;
+        const bool packed_vals = 2 * row_count <= L;
+        const uint64_t nb0 = rank0 >> 1, sb0 = rank0 >> 5;
+        // B. stage the row's coefficients (rank order); a short payload
+        // (meta[2]) decodes to zeros and never reads past its end
+        if (!bad) {
+            if (packed_vals) {
+#pragma unroll 4
+                for (uint32_t i = threadIdx.x; i < row_count; i += SPACK_THREADS) {
+                    const uint64_t r = rank0 + i;
+                    const uint32_t sh = (uint32_t)scales[2 * (r >> 5)] |
+                                        ((uint32_t)scales[2 * (r >> 5) + 1] << 8);
+                    const float v = deq_nibble(nibbles[r >> 1], r,
+                                               __half2float(__ushort_as_half((uint16_t)sh)));
+                    vals_s[i] = f2h(v);
                 }
+            } else {
+                const uint64_t nb1 = (rank0 + row_count + 1) >> 1;
+                const uint64_t sb1 = row_count ? ((rank0 + row_count - 1) >> 5) + 1 : sb0;
+                for (uint64_t i = nb0 + threadIdx.x; i < nb1; i += SPACK_THREADS)
+                    nib_s[i - nb0] = nibbles[i];
+                for (uint64_t i = sb0 + threadIdx.x; i < sb1; i += SPACK_THREADS)
+                    sc_s[i - sb0] = __half2float(__ushort_as_half(
+                        (uint16_t)((uint32_t)scales[2 * i] | ((uint32_t)scales[2 * i + 1] << 8))));
             }
+        }
+        __syncthreads();
+        // C. expand this warp's words into the staged row
+        const uint32_t wrank = before + incl - cnt;  // rank of my word within the row
+        uint32_t *dst = reinterpret_cast<uint32_t *>(srow + pad_idx(64 * seg0 + pair_shift));
+        for (uint32_t i = 0; i < nseg; i++, dst += 33) {  // 64 elements + 2 pad halves
+            const uint64_t w = __shfl_sync(0xffffffffu, mw, i);
+            const uint32_t r = __shfl_sync(0xffffffffu, wrank, i) + __popcll(w & below);
+            const uint32_t m2 = (uint32_t)(w >> pair_shift) & 3u;
+            uint32_t pair = 0;
+            if (!bad && m2) {
+                const uint32_t r1 = r + (m2 & 1u);
+                float v0 = 0.0f, v1 = 0.0f;
+                if (packed_vals) {
+                    if (m2 & 1u) v0 = h2f(vals_s[r]);
+                    if (m2 & 2u) v1 = h2f(vals_s[r1]);
+                } else {
+                    const uint64_t g0 = rank0 + r, g1 = rank0 + r1;
+                    if (m2 & 1u) v0 = h2f(f2h(deq_nibble(nib_s[(g0 >> 1) - nb0], g0,
+                                                          sc_s[(g0 >> 5) - sb0])));
+                    if (m2 & 2u) v1 = h2f(f2h(deq_nibble(nib_s[(g1 >> 1) - nb0], g1,
+                                                          sc_s[(g1 >> 5) - sb0])));
+                }
+                pair = pack_z(v0, v1);
+            }
+            *dst = pair;
         }
         __syncthreads();
         pack_row(srow, coef, L, P, Q, out + b * (uint64_t)(L / 2));
@@ -347,15 +369,17 @@ cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t 
     return cudaGetLastError();
 }
 
-bool spectral_pack_supported(uint64_t L) { return L % 64 == 0 && L / 32 <= 2ull * SPACK_THREADS; }
+bool spectral_pack_supported(uint64_t L) {
+    return L % 64 == 0 && L / 64 <= 32ull * SPACK_WARPS;
+}
 
 cudaError_t launch_spectral_pack(const uint8_t *d_payload, uint64_t bmb, const uint32_t *d_chunk,
                                  const uint64_t *d_meta, uint64_t B, uint32_t L, uint32_t P,
                                  uint32_t Q, const float *d_tables, half_bits *d_out,
                                  cudaStream_t s) {
     if (!spectral_pack_supported(L)) return cudaErrorInvalidValue;
-    // dynamic shared memory: row, nibbles, f32 scales
-    const size_t smem = (size_t)srow_halves(L) * 2 + spack_nib_bytes(L) + ((size_t)L / 32 + 4) * 4;
+    // dynamic shared memory: the row and its staged coefficients
+    const size_t smem = (size_t)srow_halves(L) * 2 + spack_stage_bytes(L);
     if (smem > 220 * 1024) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(spectral_pack_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -78,3 +78,20 @@ def test_factored_hct_decode(hb, orc, shape):
     ref = OH.decode_spectral_q4_cpu(f)
     got = hb.HctReader(f).decode(hb.F32).cpu().numpy()
     _check(got, ref, f"hct {shape}")
+
+
+@pytest.mark.parametrize("retention", [0.02, 0.3, 0.6, 0.95, 1.0])
+def test_factored_hct_decode_retention(hb, orc, retention):
+    """Rows with few and with more than L/2 retained coefficients: the fused
+    row pack stages fp16 values for sparse rows and raw nibbles for dense ones."""
+    from oracle import hct as OH
+
+    shape = (192, 2048)
+    w = OH.gen_weight(shape, 41)
+    f = OH.encode_spectral_q4(w, retention=retention)
+    ref = OH.decode_spectral_q4_cpu(f)
+    for dt, tol in ((hb.F32, 0.0), (hb.BF16, 2.0 ** -8)):
+        got = hb.HctReader(f).decode(dt).float().cpu().numpy()
+        err = np.abs(got.astype(np.float64) - ref.astype(np.float64))
+        assert (err <= MAX_ABS + tol * np.abs(ref)).all(), f"retention {retention}: {err.max():.3e}"
+        assert _cos(got, ref) >= MIN_COS
