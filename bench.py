@@ -468,7 +468,8 @@ def bench_lz4(H, torch, dev, stream, args):
 
     def launch():
         rc = lib.hct_b200_lz4_decompress_blocks(d_src.data_ptr(), d_blk.data_ptr(), nb,
-                                                d_dst.data_ptr(), d_st.data_ptr(), sp)
+                                                d_dst.data_ptr(), d_st.data_ptr(),
+                                                int(lens.max()), sp)
         assert rc == 0
 
     for _ in range(3):

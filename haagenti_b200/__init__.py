@@ -208,12 +208,14 @@ class Lz4Decompressor:
                 if size > 256 * 1024 * 1024:
                     raise CorruptedData(L.CORRUPTED, "corrupted data: decompressed size exceeds limit")
 
-    def decompress_blocks(self, d_src, blocks: np.ndarray, d_dst, stream=None):
+    def decompress_blocks(self, d_src, blocks: np.ndarray, d_dst, stream=None, staged=True):
         """Batched block decode on device buffers.
 
         ``blocks`` is a structured array of (src_off, dst_off, src_len, dst_cap,
         out_size) rows; returns the per-block status array (code, position,
-        provided, written), synchronising the stream.
+        provided, written), synchronising the stream.  The largest src_len is
+        passed as the kernel's size bound (``staged=False`` passes none, which
+        selects the variant that parses straight from device memory).
         """
         torch = _torch()
         blk = np.zeros(len(blocks), dtype=[("src_off", "<u8"), ("dst_off", "<u8"),
@@ -224,9 +226,10 @@ class Lz4Decompressor:
         dev = d_src.device
         d_blk = torch.from_numpy(blk.view(np.uint8).copy()).to(dev)
         d_st = torch.zeros(len(blocks) * 32, dtype=torch.uint8, device=dev)
+        bound = int(blk["src_len"].max()) if staged and len(blk) else 0
         _check(L.load().hct_b200_lz4_decompress_blocks(
             d_src.data_ptr(), d_blk.data_ptr(), len(blocks), d_dst.data_ptr(), d_st.data_ptr(),
-            _stream_ptr(stream)))
+            bound, _stream_ptr(stream)))
         st = d_st.cpu().numpy().view([("code", "<i4"), ("reserved", "<i4"), ("position", "<u8"),
                                        ("provided", "<u8"), ("written", "<u8")])
         return st

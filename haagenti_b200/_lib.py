@@ -78,7 +78,8 @@ SIGNATURES = {
                                                C.POINTER(C.c_uint32)]),
     "hct_b200_quantize_int4": (C.c_int, [_vp, _sz, _u8p]),
     "hct_b200_spectral_select": (C.c_int, [_vp, _sz, _sz, _u8p, _vp, C.POINTER(C.c_size_t)]),
-    "hct_b200_lz4_decompress_blocks": (C.c_int, [_vp, _vp, C.c_uint32, _vp, _vp, _vp]),
+    "hct_b200_lz4_decompress_blocks": (C.c_int, [_vp, _vp, C.c_uint32, _vp, _vp, C.c_uint64,
+                                                 _vp]),
     "hct_b200_lz4_decompress_with_size": (C.c_int, [_vp, _u8p, _sz, _sz, _u8p,
                                                     C.POINTER(C.c_size_t), C.POINTER(Error)]),
     "hct_b200_lz4_decompress_to": (C.c_int, [_vp, _u8p, _sz, _u8p, _sz,

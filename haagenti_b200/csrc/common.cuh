@@ -13,9 +13,12 @@ namespace hct {
 using half_bits = uint16_t;
 
 // ---- LZ4 (lz4_decode.cu) -----------------------------------------------
+// max_src_len: an upper bound of the blocks' compressed lengths when the
+// caller knows one (0 = unknown); bounds up to the LZ4 bound of a 16 KiB
+// block select the variant that stages each compressed block in shared memory.
 cudaError_t launch_lz4_blocks(const uint8_t *d_src, const hct_b200_lz4_block *d_blocks,
                               uint32_t n, uint8_t *d_dst, hct_b200_status *d_status,
-                              cudaStream_t s);
+                              cudaStream_t s, uint64_t max_src_len = 0);
 
 // ---- INT4 / spectral scatter (int4_dequant.cu) -------------------------
 // n_written elements are produced (the reference's short-input rule is

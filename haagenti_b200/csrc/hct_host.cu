@@ -212,6 +212,7 @@ struct hct_b200_reader {
     std::vector<uint64_t> checksums;
     size_t data_offset = 0;  // within the file
     size_t data_len = 0;
+    uint64_t max_block = 0;  // largest compressed block
     DevBuf d_data, d_blocks, d_status;
     std::vector<uint32_t> expected;
     uint64_t rows = 0, cols = 0;
@@ -635,11 +636,11 @@ int hct_b200_ctx_profile_read(hct_b200_ctx *ctx, hct_b200_kernel_stats *out, int
 
 int hct_b200_lz4_decompress_blocks(const uint8_t *d_src, const hct_b200_lz4_block *d_blocks,
                                    uint32_t num_blocks, uint8_t *d_dst, hct_b200_status *d_status,
-                                   void *stream) {
+                                   uint64_t max_src_len, void *stream) {
     if (num_blocks == 0) return HCT_B200_OK;
     if (!d_src || !d_blocks || !d_dst || !d_status) return HCT_B200_ERR_INVALID_ARGUMENT;
     return cuda_code(launch_lz4_blocks(d_src, d_blocks, num_blocks, d_dst, d_status,
-                                       (cudaStream_t)stream));
+                                       (cudaStream_t)stream, max_src_len));
 }
 
 int hct_b200_lz4_decompress_with_size(hct_b200_ctx *ctx, const uint8_t *in, size_t in_len,
@@ -803,6 +804,7 @@ int hct_b200_reader_open(hct_b200_ctx *ctx, const uint8_t *file, size_t file_len
         const uint8_t *e = file + pos + (size_t)i * ent;
         r->offsets[i] = rd32(e);
         r->sizes[i] = rd32(e + 4);
+        r->max_block = std::max<uint64_t>(r->max_block, r->sizes[i]);
         if (sums) r->checksums[i] = rd64(e + 8);
     }
     pos += (size_t)nb * ent;
@@ -936,7 +938,7 @@ int reader_lz4(hct_b200_reader *r, uint8_t *d_dst, size_t cap, size_t *written, 
     CK(r->before_read(s));
     int slot = r->ctx->prof_begin(s);
     CK(launch_lz4_blocks(r->d_data.as<uint8_t>(), r->d_blocks.as<hct_b200_lz4_block>(), nb, d_dst,
-                         r->d_status.as<hct_b200_status>(), s));
+                         r->d_status.as<hct_b200_status>(), s, r->max_block));
     r->ctx->prof_end(slot, PK_LZ4, (double)r->hdr.compressed_size + (double)r->hdr.original_size, s);
     CK(r->after_read(s));
     std::vector<hct_b200_status> st(nb);
@@ -1041,7 +1043,8 @@ int hct_b200_reader_decode_async(hct_b200_reader *r, void *d_out, int out_dtype,
         CK(r->before_read(s));
         int slot = ctx->prof_begin(s);
         CK(launch_lz4_blocks(r->d_data.as<uint8_t>(), r->d_blocks.as<hct_b200_lz4_block>(), nb,
-                             ctx->payload.as<uint8_t>(), r->d_status.as<hct_b200_status>(), s));
+                             ctx->payload.as<uint8_t>(), r->d_status.as<hct_b200_status>(), s,
+                             r->max_block));
         ctx->prof_end(slot, PK_LZ4, (double)r->hdr.compressed_size + (double)r->hdr.original_size,
                       s);
         CK(r->after_read(s));

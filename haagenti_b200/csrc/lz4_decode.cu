@@ -16,6 +16,13 @@
 // Every read is checked against the block's compressed length and every
 // write against its capacity before it happens: a corrupt block ends with a
 // status, never with an out-of-range access or a trap.
+//
+// Staged variant (container blocks of at most LZ4_STAGE_MAX compressed
+// bytes): the warp first pulls its whole compressed block into shared memory
+// with 16-byte cp.async copies (the block's bytes all in flight at once, no
+// registers held), then parses it and copies its literals from shared
+// memory, so the serial token walk costs shared-memory latency instead of
+// one DRAM round trip per step.
 #include "common.cuh"
 
 namespace hct {
@@ -97,9 +104,43 @@ __device__ __forceinline__ void warp_copy(uint8_t *dst, const uint8_t *src, uint
     if (lane < (int)tail) dst[nw * 4 + lane] = src[nw * 4 + lane];
 }
 
+// staged compressed bytes per warp: the LZ4 bound of a 16 KiB block
+// (16384 + 16384 / 255 + 16 = 16464), rounded up
+constexpr uint32_t LZ4_STAGE_MAX = 16512;
+constexpr uint32_t LZ4_STAGE_BYTES = LZ4_STAGE_MAX + 32;  // + alignment slack
+constexpr int LZ4_STAGED_WARPS = 4;                   // warps per CTA of the staged variant
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+}
+
+// Copies in[0, len) into stage + (in & 15) and returns that pointer: bytes
+// up to the first 16-byte boundary and after the last one one by one, the
+// aligned body with cp.async (no byte outside [in, in + len) is read).
+__device__ __forceinline__ const uint8_t *stage_block(uint8_t *stage, const uint8_t *in,
+                                                     uint64_t len, int lane) {
+    const uint32_t mis = (uint32_t)((uintptr_t)in & 15u);
+    uint8_t *s = stage + mis;
+    uint64_t head = (16u - mis) & 15u;
+    if (head > len) head = len;
+    const uint64_t body_end = head + ((len - head) & ~15ull);
+    if ((uint64_t)lane < head) s[lane] = in[lane];
+    if ((uint64_t)lane < len - body_end) s[body_end + lane] = in[body_end + lane];
+    for (uint64_t j = head + 16ull * lane; j < body_end; j += 512) cp_async16(s + j, in + j);
+    cp_async_wait_all();
+    __syncwarp();
+    return s;
+}
+
+template <bool STAGED>
 __global__ void __launch_bounds__(256) lz4_decode_blocks_kernel(
     const uint8_t *__restrict__ src, const hct_b200_lz4_block *__restrict__ blocks,
     uint32_t nblocks, uint8_t *dst, hct_b200_status *__restrict__ status) {
+    extern __shared__ __align__(16) uint8_t lz4_stage[];
     const int lane = threadIdx.x & 31;
     const uint32_t warps_per_grid = (gridDim.x * blockDim.x) >> 5;
     for (uint32_t bi = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; bi < nblocks;
@@ -108,6 +149,10 @@ __global__ void __launch_bounds__(256) lz4_decode_blocks_kernel(
         const uint8_t *in = src + b.src_off;
         uint8_t *out = dst + b.dst_off;
         const uint64_t in_len = b.src_len, cap = b.dst_cap, osz = b.out_size;
+        if (STAGED && in_len <= LZ4_STAGE_MAX) {
+            __syncwarp();  // the previous block's reads of the stage are done
+            in = stage_block(lz4_stage + (threadIdx.x >> 5) * LZ4_STAGE_BYTES, in, in_len, lane);
+        }
         uint64_t ip = 0, op = 0;
         int code = HCT_B200_OK;
         uint64_t epos = 0, eprov = 0;
@@ -184,13 +229,25 @@ __global__ void __launch_bounds__(256) lz4_decode_blocks_kernel(
 
 cudaError_t launch_lz4_blocks(const uint8_t *d_src, const hct_b200_lz4_block *d_blocks,
                               uint32_t n, uint8_t *d_dst, hct_b200_status *d_status,
-                              cudaStream_t s) {
+                              cudaStream_t s, uint64_t max_src_len) {
     if (n == 0) return cudaSuccess;
+    if (max_src_len != 0 && max_src_len <= LZ4_STAGE_MAX) {
+        // staged: 4 warps and 64 KiB of shared memory per CTA, 3 CTAs per SM
+        const size_t smem = (size_t)LZ4_STAGED_WARPS * LZ4_STAGE_BYTES;
+        cudaError_t e = cudaFuncSetAttribute(lz4_decode_blocks_kernel<true>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        uint64_t ctas = (n + LZ4_STAGED_WARPS - 1) / LZ4_STAGED_WARPS;
+        if (ctas > 148ull * 3) ctas = 148ull * 3;
+        lz4_decode_blocks_kernel<true><<<(unsigned)ctas, 32 * LZ4_STAGED_WARPS, smem, s>>>(
+            d_src, d_blocks, n, d_dst, d_status);
+        return cudaGetLastError();
+    }
     const int threads = 256;  // 8 warps = 8 blocks per CTA
     uint64_t ctas = (n + 7) / 8;
     if (ctas > 148ull * 64) ctas = 148ull * 64;
-    lz4_decode_blocks_kernel<<<(unsigned)ctas, threads, 0, s>>>(d_src, d_blocks, n, d_dst,
-                                                                d_status);
+    lz4_decode_blocks_kernel<false><<<(unsigned)ctas, threads, 0, s>>>(d_src, d_blocks, n, d_dst,
+                                                                       d_status);
     return cudaGetLastError();
 }
 

@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define HCT_B200_ABI_VERSION 1
+#define HCT_B200_ABI_VERSION 2
 
 /* ---- status codes ------------------------------------------------------ */
 enum {
@@ -135,10 +135,11 @@ int hct_b200_ctx_set_idct(hct_b200_ctx *ctx, int mode);
 /* Per-kernel timing of the context's own launches, for roofline reports.
  * With profiling enabled every kernel launch made through the context is
  * bracketed by CUDA events recorded on its launch stream; _read synchronises
- * those events and returns one entry per kernel kind (lz4_decode_blocks,
- * spectral_scatter, umma_gemm, dequant_int4).  `work` is the algorithmic
- * work summed over launches: FLOPs (2*M*N*K) for umma_gemm, bytes read +
- * written for the others.  No reference counterpart (the reference keeps
+ * those events and returns one entry per kernel kind that ran
+ * (lz4_decode_blocks, spectral_scatter, umma_gemm, dequant_int4,
+ * makhoul_pack, dft_stage1, spectral_rank, spectral_pack, dft_stage2).
+ * `work` is the algorithmic work summed over launches: FLOPs (2*M*N*K) for
+ * umma_gemm, bytes read + written for the others.  No reference counterpart (the reference keeps
  * ad-hoc DecompressStats, crates/haagenti-cuda/src/decompress.rs:55-94). */
 typedef struct {
     char name[32];
@@ -154,10 +155,15 @@ int hct_b200_ctx_profile_read(hct_b200_ctx *ctx, hct_b200_kernel_stats *out, int
  * Batched form of block::decompress_block (crates/haagenti-lz4/src/block.rs:261),
  * one warp per independent block.  Results are exact: byte-for-byte output and
  * the same error variant/position as the reference for every block.
+ * max_src_len is an upper bound of the blocks' src_len when the caller knows
+ * one, else 0; a bound up to the LZ4 bound of a 16 KiB block (16464) lets the
+ * kernel stage each compressed block in shared memory (the layout the HCT
+ * container uses).  A wrong bound never affects results, only the variant.
  * Stream-ordered; d_status is written when the kernel completes. */
 int hct_b200_lz4_decompress_blocks(const uint8_t *d_src, const hct_b200_lz4_block *d_blocks,
                                    uint32_t num_blocks, uint8_t *d_dst,
-                                   hct_b200_status *d_status, void *stream);
+                                   hct_b200_status *d_status, uint64_t max_src_len,
+                                   void *stream);
 
 /* Lz4Decompressor::decompress_with_size (crates/haagenti-lz4/src/decompress.rs:63-68)
  * on host buffers: `out` must hold output_size bytes; *written = truncated length. */

@@ -49,7 +49,7 @@ def test_struct_layouts_match_header(tmp_path):
 
 def test_status_strings_and_abi():
     lib = L.load()
-    assert lib.hct_b200_abi_version() == 1
+    assert lib.hct_b200_abi_version() == 2
     assert lib.hct_b200_status_string(L.BUFFER_TOO_SMALL) == b"buffer too small"
     assert lib.hct_b200_status_string(L.ZERO_OFFSET).endswith(b"invalid zero offset")
 

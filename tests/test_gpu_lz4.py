@@ -62,7 +62,8 @@ def test_error_semantics_match_oracle(hb, orc, golden):
             assert e.required == case["position"] and e.provided == case["provided"]
 
 
-def test_batched_blocks_error_cases_device_api(hb, orc, golden, dev):
+@pytest.mark.parametrize("staged", [True, False])
+def test_batched_blocks_error_cases_device_api(hb, orc, golden, dev, staged):
     import torch
 
     cases = golden["lz4_errors"]
@@ -71,7 +72,7 @@ def test_batched_blocks_error_cases_device_api(hb, orc, golden, dev):
                               [c["capacity"] for c in cases], [c["output_size"] for c in cases])
     src = torch.from_numpy(np.frombuffer(b"".join(comps) + b"\0" * 16, np.uint8).copy()).to(dev)
     dst = torch.zeros(max(dsz, 1) + 16, dtype=torch.uint8, device=dev)
-    st = hb.Lz4Decompressor().decompress_blocks(src, d, dst)
+    st = hb.Lz4Decompressor().decompress_blocks(src, d, dst, staged=staged)
     for i, c in enumerate(cases):
         assert st["code"][i] == c["code"], c["name"]
         assert st["written"][i] == c["written"], c["name"]
@@ -101,7 +102,8 @@ def _mixed_payloads(rng, count, max_len=70000):
     return out
 
 
-def test_random_batches_bit_exact(hb, orc, dev):
+@pytest.mark.parametrize("staged", [True, False])
+def test_random_batches_bit_exact(hb, orc, dev, staged):
     import torch
 
     rng = np.random.default_rng(11)
@@ -110,13 +112,14 @@ def test_random_batches_bit_exact(hb, orc, dev):
     d, ssz, dsz = _blocks_for(payloads, comps)
     src = torch.from_numpy(np.frombuffer(b"".join(comps), np.uint8).copy()).to(dev)
     dst = torch.zeros(dsz + 16, dtype=torch.uint8, device=dev)
-    st = hb.Lz4Decompressor().decompress_blocks(src, d, dst)
+    st = hb.Lz4Decompressor().decompress_blocks(src, d, dst, staged=staged)
     assert (st["code"] == 0).all()
     assert (st["written"] == np.array([len(p) for p in payloads])).all()
     assert dst[:dsz].cpu().numpy().tobytes() == b"".join(payloads)
 
 
-def test_corrupted_random_blocks_match_oracle(hb, orc, dev):
+@pytest.mark.parametrize("staged", [True, False])
+def test_corrupted_random_blocks_match_oracle(hb, orc, dev, staged):
     """Bit flips / truncations: same status as the oracle, same bytes when Ok."""
     import torch
 
@@ -137,7 +140,7 @@ def test_corrupted_random_blocks_match_oracle(hb, orc, dev):
     ref_out, ref_st = orc.lz4_decompress_batch(srcnp, d.astype(orc.BLOCK_DESC), dsz)
     src = torch.from_numpy(srcnp.copy()).to(dev)
     dst = torch.zeros(dsz + 16, dtype=torch.uint8, device=dev)
-    st = hb.Lz4Decompressor().decompress_blocks(src, d, dst)
+    st = hb.Lz4Decompressor().decompress_blocks(src, d, dst, staged=staged)
     got = dst[:dsz].cpu().numpy()
     assert np.array_equal(st["code"], ref_st["code"])
     err = ref_st["code"] != 0
