@@ -10,19 +10,21 @@
 // is wide: 255-run length extensions are scanned 32 bytes at a time with a
 // ballot, literal runs and non-overlapping matches are copied as aligned
 // 32-bit words (funnel-shifted from an unaligned source), and overlapping
-// matches are expanded as out[p + i] = out[p - off + i % off], which only
-// reads bytes that were written before the match started.
+// matches (out[p] = out[p - off]) are expanded from the period held in
+// registers when off <= 32, else by copying the first period and doubling
+// the copied prefix; no copy reads a byte that it writes.
 //
 // Every read is checked against the block's compressed length and every
 // write against its capacity before it happens: a corrupt block ends with a
 // status, never with an out-of-range access or a trap.
 //
-// Staged variant (container blocks of at most LZ4_STAGE_MAX compressed
-// bytes): the warp first pulls its whole compressed block into shared memory
-// with 16-byte cp.async copies (the block's bytes all in flight at once, no
-// registers held), then parses it and copies its literals from shared
-// memory, so the serial token walk costs shared-memory latency instead of
-// one DRAM round trip per step.
+// Staged variant (container blocks: at most LZ4_STAGE_MAX compressed and
+// LZ4_OUT_MAX decompressed bytes): the warp first pulls its whole compressed
+// block into shared memory with 16-byte cp.async copies (all of its bytes in
+// flight at once, no registers held), decodes it into a shared-memory output
+// buffer -- token walk, literal copies and match sources all at
+// shared-memory latency, and the warp barriers between steps drain no
+// global stores -- and finally writes the block out with 16-byte stores.
 #include "common.cuh"
 
 namespace hct {
@@ -108,7 +110,10 @@ __device__ __forceinline__ void warp_copy(uint8_t *dst, const uint8_t *src, uint
 // (16384 + 16384 / 255 + 16 = 16464), rounded up
 constexpr uint32_t LZ4_STAGE_MAX = 16512;
 constexpr uint32_t LZ4_STAGE_BYTES = LZ4_STAGE_MAX + 32;  // + alignment slack
-constexpr int LZ4_STAGED_WARPS = 4;                   // warps per CTA of the staged variant
+constexpr uint32_t LZ4_OUT_MAX = 16384;                  // staged decompressed bytes per warp
+constexpr uint32_t LZ4_OUT_BYTES = LZ4_OUT_MAX + 32;
+constexpr uint32_t LZ4_SLOT_BYTES = LZ4_STAGE_BYTES + LZ4_OUT_BYTES;
+constexpr int LZ4_STAGED_WARPS = 2;  // warps per CTA: 64 KiB of shared memory, 3 CTAs per SM
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
@@ -136,6 +141,51 @@ __device__ __forceinline__ const uint8_t *stage_block(uint8_t *stage, const uint
     return s;
 }
 
+// Overlapping match with period off <= 32: o[p] = o[p - off] for p < ml.
+// Lane r holds the period's byte r (read once, written before the match);
+// every output byte is a shuffle of it, stored 4 bytes per lane from the
+// first 4-byte boundary, so the expansion reads no memory it writes.
+__device__ __forceinline__ void expand_short_period(uint8_t *o, uint32_t off, uint64_t ml,
+                                                    int lane) {
+    const uint32_t pv = (uint32_t)lane < off ? (uint32_t)o[(int64_t)lane - (int64_t)off] : 0u;
+    uint64_t head = (4u - ((uintptr_t)o & 3u)) & 3u;
+    if (head > ml) head = ml;
+    const uint32_t hb = __shfl_sync(FULL, pv, (uint32_t)lane % off);
+    if ((uint64_t)lane < head) o[lane] = (uint8_t)hb;
+    const uint64_t nw = (ml - head) >> 2;
+    uint32_t *dw = reinterpret_cast<uint32_t *>(o + head);
+    uint32_t r = (uint32_t)((head + 4ull * (uint32_t)lane) % off);  // period index of my word
+    const uint32_t step = 128u % off;                                 // 32 words per iteration
+    for (uint64_t j0 = 0; j0 < nw; j0 += 32) {
+        const uint32_t r1 = r + 1 == off ? 0u : r + 1;
+        const uint32_t r2 = r1 + 1 == off ? 0u : r1 + 1;
+        const uint32_t r3 = r2 + 1 == off ? 0u : r2 + 1;
+        const uint32_t b0 = __shfl_sync(FULL, pv, r);
+        const uint32_t b1 = __shfl_sync(FULL, pv, r1);
+        const uint32_t b2 = __shfl_sync(FULL, pv, r2);
+        const uint32_t b3 = __shfl_sync(FULL, pv, r3);
+        if (j0 + lane < nw) dw[j0 + lane] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        r += step;
+        if (r >= off) r -= off;
+    }
+    const uint64_t t0 = head + 4 * nw;  // fewer than 4 bytes remain
+    const uint32_t tb = __shfl_sync(FULL, pv, (uint32_t)((t0 + (uint32_t)lane) % off));
+    if ((uint64_t)lane < ml - t0) o[t0 + lane] = (uint8_t)tb;
+}
+
+// Writes the staged output sout[0, n) to gdst[0, n); sout and gdst agree
+// modulo 16, so the body moves as aligned 16-byte words.
+__device__ __forceinline__ void store_block(uint8_t *gdst, const uint8_t *sout, uint64_t n,
+                                            int lane) {
+    uint64_t head = (16u - ((uintptr_t)gdst & 15u)) & 15u;
+    if (head > n) head = n;
+    const uint64_t body_end = head + ((n - head) & ~15ull);
+    if ((uint64_t)lane < head) gdst[lane] = sout[lane];
+    if ((uint64_t)lane < n - body_end) gdst[body_end + lane] = sout[body_end + lane];
+    for (uint64_t j = head + 16ull * lane; j < body_end; j += 512)
+        *reinterpret_cast<uint4 *>(gdst + j) = *reinterpret_cast<const uint4 *>(sout + j);
+}
+
 template <bool STAGED>
 __global__ void __launch_bounds__(256) lz4_decode_blocks_kernel(
     const uint8_t *__restrict__ src, const hct_b200_lz4_block *__restrict__ blocks,
@@ -149,9 +199,13 @@ __global__ void __launch_bounds__(256) lz4_decode_blocks_kernel(
         const uint8_t *in = src + b.src_off;
         uint8_t *out = dst + b.dst_off;
         const uint64_t in_len = b.src_len, cap = b.dst_cap, osz = b.out_size;
-        if (STAGED && in_len <= LZ4_STAGE_MAX) {
-            __syncwarp();  // the previous block's reads of the stage are done
-            in = stage_block(lz4_stage + (threadIdx.x >> 5) * LZ4_STAGE_BYTES, in, in_len, lane);
+        uint8_t *const gout = out;
+        const bool staged = STAGED && in_len <= LZ4_STAGE_MAX && cap <= LZ4_OUT_MAX;
+        if (staged) {
+            uint8_t *slot = lz4_stage + (threadIdx.x >> 5) * LZ4_SLOT_BYTES;
+            __syncwarp();  // the previous block's reads of the slot are done
+            in = stage_block(slot, in, in_len, lane);
+            out = slot + LZ4_STAGE_BYTES + ((uintptr_t)gout & 15u);
         }
         uint64_t ip = 0, op = 0;
         int code = HCT_B200_OK;
@@ -173,7 +227,11 @@ __global__ void __launch_bounds__(256) lz4_decode_blocks_kernel(
                 if (op + lit > cap) {
                     code = HCT_B200_ERR_BUFFER_TOO_SMALL; epos = op + lit; eprov = cap; break;
                 }
-                warp_copy(out + op, in + ip, lit, lane);
+                if (lit <= 32) {  // short run: one byte per lane
+                    if ((uint64_t)lane < lit) out[op + lane] = in[ip + lane];
+                } else {
+                    warp_copy(out + op, in + ip, lit, lane);
+                }
                 ip += lit;
                 op += lit;
             }
@@ -195,22 +253,31 @@ __global__ void __launch_bounds__(256) lz4_decode_blocks_kernel(
             }
             __syncwarp();  // earlier output visible to every lane
             uint8_t *o = out + op;
-            if (offset >= ml) {
+            if (offset >= ml && ml <= 32) {  // short, non-overlapping: one byte per lane
+                if ((uint64_t)lane < ml) o[lane] = o[(int64_t)lane - (int64_t)offset];
+            } else if (offset >= ml) {
                 warp_copy(o, o - offset, ml, lane);
+            } else if (offset <= 32) {
+                expand_short_period(o, (uint32_t)offset, ml, lane);
             } else {
-                const uint8_t *m = o - offset;
-                // i % offset advanced incrementally: step 32 mod offset
-                const uint32_t off32 = (uint32_t)offset;
-                const uint32_t step = 32u % off32;
-                uint32_t r = (uint32_t)lane % off32;
-                for (uint64_t i = lane; i < ml; i += 32) {
-                    o[i] = m[r];
-                    r += step;
-                    if (r >= off32) r -= off32;
+                // the match is periodic with period offset: copy the first
+                // period (it only reads bytes before o), then double the
+                // copied prefix; every copy reads bytes written before it
+                warp_copy(o, o - offset, offset, lane);
+                uint64_t done = offset;
+                while (done < ml) {
+                    __syncwarp();
+                    const uint64_t n = done < ml - done ? done : ml - done;
+                    warp_copy(o + done, o, n, lane);
+                    done += n;
                 }
             }
             __syncwarp();
             op += ml;
+        }
+        if (staged) {
+            __syncwarp();
+            store_block(gout, out, op, lane);
         }
         if (lane == 0) {
             hct_b200_status s;
@@ -232,8 +299,8 @@ cudaError_t launch_lz4_blocks(const uint8_t *d_src, const hct_b200_lz4_block *d_
                               cudaStream_t s, uint64_t max_src_len) {
     if (n == 0) return cudaSuccess;
     if (max_src_len != 0 && max_src_len <= LZ4_STAGE_MAX) {
-        // staged: 4 warps and 64 KiB of shared memory per CTA, 3 CTAs per SM
-        const size_t smem = (size_t)LZ4_STAGED_WARPS * LZ4_STAGE_BYTES;
+        // staged: 2 warps and 64 KiB of shared memory per CTA, 3 CTAs per SM
+        const size_t smem = (size_t)LZ4_STAGED_WARPS * LZ4_SLOT_BYTES;
         cudaError_t e = cudaFuncSetAttribute(lz4_decode_blocks_kernel<true>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;

@@ -174,3 +174,58 @@ def test_config2_lz4_256mib_roundtrip(hb, orc, dev):
     st = hb.Lz4Decompressor().decompress_blocks(src, d, dst)
     assert (st["code"] == 0).all() and (st["written"] == 65536).all()
     assert torch.equal(dst, torch.from_numpy(raw).to(dev))
+
+
+def _lz4_len(n: int) -> bytes:
+    out = bytearray()
+    while n >= 255:
+        out.append(255)
+        n -= 255
+    out.append(n)
+    return bytes(out)
+
+
+def _lz4_seq(lits: bytes, offset: int = 0, ml: int = 0) -> bytes:
+    """One LZ4 sequence; offset == 0 makes it the literal-only last sequence."""
+    ln = len(lits)
+    mcode = ml - 4 if offset else 0
+    tok = (min(ln, 15) << 4) | min(mcode, 15)
+    out = bytearray([tok])
+    if ln >= 15:
+        out += _lz4_len(ln - 15)
+    out += lits
+    if offset:
+        out += offset.to_bytes(2, "little")
+        if mcode >= 15:
+            out += _lz4_len(mcode - 15)
+    return bytes(out)
+
+
+@pytest.mark.parametrize("staged", [True, False])
+def test_overlapping_matches_all_periods(hb, orc, dev, staged):
+    """Crafted blocks whose matches overlap their source (offset < length) for
+    periods 1..40 and large ones, at every output alignment: same bytes as the oracle."""
+    import torch
+
+    rng = np.random.default_rng(13)
+    comps, sizes = [], []
+    for period in list(range(1, 41)) + [63, 64, 65, 100, 255, 1000, 4097]:
+        for lead in range(4):  # output alignment of the match
+            lits = rng.integers(0, 256, lead + period, dtype=np.uint8).tobytes()
+            # lead 3: outputs beyond 16 KiB from a small block (the staged
+            # kernel decodes those straight in device memory)
+            ml = int(rng.integers(period + 1, 9000 if lead < 3 else 60000))
+            tail = rng.integers(0, 256, int(rng.integers(5, 40)), dtype=np.uint8).tobytes()
+            blk = _lz4_seq(lits, period, ml) + _lz4_seq(tail)
+            comps.append(blk)
+            sizes.append(len(lits) + ml + len(tail))
+    d, ssz, dsz = _blocks_for([b"\0" * n for n in sizes], comps)
+    srcnp = np.frombuffer(b"".join(comps), np.uint8)
+    ref_out, ref_st = orc.lz4_decompress_batch(srcnp, d.astype(orc.BLOCK_DESC), dsz)
+    assert (ref_st["code"] == 0).all()
+    src = torch.from_numpy(srcnp.copy()).to(dev)
+    dst = torch.zeros(dsz + 16, dtype=torch.uint8, device=dev)
+    st = hb.Lz4Decompressor().decompress_blocks(src, d, dst, staged=staged)
+    assert (st["code"] == 0).all()
+    assert np.array_equal(st["written"], ref_st["written"])
+    assert np.array_equal(dst[:dsz].cpu().numpy(), ref_out[:dsz])
