@@ -166,7 +166,10 @@ struct ProfRec {
 struct hct_b200_ctx {
     int device = 0;
     cudaStream_t stream = nullptr;  // used by the host-buffer entry points
-    DevBuf payload, dense, tt, chunk, meta, flag;
+    // front-end stream of the readers' asynchronous decodes (LZ4 + bitmap
+    // rank), so that a tensor's front end overlaps the IDCT of the previous one
+    cudaStream_t side = nullptr;
+    DevBuf dense, tt, chunk, meta, flag;
     DevBuf za, zb;  // factored-IDCT intermediates (rows*cols fp16 each)
     DevBuf io_in, io_out, io_blk, io_status;
     std::map<uint64_t, std::unique_ptr<Basis>> bases;
@@ -229,12 +232,20 @@ struct hct_b200_reader {
     // overlap the decode of other tensors without host synchronisation.
     cudaEvent_t uploaded = nullptr, data_free = nullptr;
     bool upload_pending = false, read_pending = false;
+    // the reader's own decoded payload, rank directory and error flag: the
+    // front end of decode_async fills them on ctx->side (front_done), the back
+    // end consumes them on the caller's stream (back_done)
+    DevBuf d_payload, d_chunk, d_meta, d_flag;
+    cudaEvent_t front_done = nullptr, back_done = nullptr;
+    bool back_pending = false;
     ~hct_b200_reader() {
         if (h_status) cudaFreeHost(h_status);
         if (h_flag) cudaFreeHost(h_flag);
         if (done) cudaEventDestroy(done);
         if (uploaded) cudaEventDestroy(uploaded);
         if (data_free) cudaEventDestroy(data_free);
+        if (front_done) cudaEventDestroy(front_done);
+        if (back_done) cudaEventDestroy(back_done);
     }
     // stream s is about to read d_data (LZ4)
     cudaError_t before_read(cudaStream_t s) {
@@ -278,9 +289,8 @@ int get_basis(hct_b200_ctx *ctx, uint64_t n, const Basis **out, cudaStream_t s,
     return HCT_B200_OK;
 }
 
-int reserve_spectral(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols, size_t payload_bytes,
+int reserve_spectral(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols,
                      hct_b200_error *err) {
-    CK(ctx->payload.reserve(payload_bytes + 64));
     CK(ctx->dense.reserve(rows * round_up(cols, 8) * 2 + 16));
     CK(ctx->tt.reserve(cols * round_up(rows, 8) * 2 + 16));
     CK(ctx->za.reserve(rows * cols * 2 + 16));
@@ -319,15 +329,42 @@ int get_twiddle(hct_b200_ctx *ctx, uint32_t H, const float **out, cudaStream_t s
     return HCT_B200_OK;
 }
 
+// Where a decode keeps the rank directory of its spectral payload and its
+// device error flag: the context's scratch for the one-shot entry points, a
+// reader's own buffers for its asynchronous decode (ranked = the directory
+// was already built by the reader's front end).
+struct RankDir {
+    uint32_t *chunk;
+    uint64_t *meta;
+    int *flag;
+    bool ranked;
+};
+
+RankDir ctx_rank_dir(hct_b200_ctx *ctx) {
+    return RankDir{ctx->chunk.as<uint32_t>(), ctx->meta.as<uint64_t>(), ctx->flag.as<int>(), false};
+}
+
+// Whether run_idct takes the factored path for a rows x cols matrix, and
+// whether it then decodes a spectral payload straight into the row pack.
+bool idct_factored(const hct_b200_ctx *ctx, uint64_t rows, uint64_t cols, uint32_t *pn,
+                   uint32_t *qn, uint32_t *pm, uint32_t *qm) {
+    return ctx->idct_mode == HCT_B200_IDCT_AUTO && fdct_factor(cols, pn, qn) &&
+           (rows == 1 || fdct_factor(rows, pm, qm));
+}
+bool spectral_fused(const hct_b200_ctx *ctx, uint64_t rows, uint64_t cols) {
+    uint32_t a, b, c, d;
+    return idct_factored(ctx, rows, cols, &a, &b, &c, &d) && spectral_pack_supported(cols);
+}
+
 // One axis of the factored IDCT: rows of length L (fp16, stride ld_in) in
 // `in`, batch rows; the result is written transposed, out[n * ldo + b], in
 // out_dtype (pack -> DFT stage 1 -> DFT stage 2, see fdct.cu).
 // The pack reads dense fp16 rows (`in`, stride ld_in) or, when `payload` is
 // set, decodes the rows straight from a spectral payload whose rank directory
-// launch_spectral_rank has put in ctx->chunk / ctx->meta.
+// launch_spectral_rank has put in dir.chunk / dir.meta.
 int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint8_t *payload,
-              uint64_t batch, uint64_t L, uint32_t P, uint32_t Q, void *out, uint64_t ldo,
-              int out_dtype, cudaStream_t s, hct_b200_error *err) {
+              const RankDir &dir, uint64_t batch, uint64_t L, uint32_t P, uint32_t Q, void *out,
+              uint64_t ldo, int out_dtype, cudaStream_t s, hct_b200_error *err) {
     const uint32_t H = (uint32_t)(L / 2);
     const half_bits *wp = nullptr, *wq = nullptr;
     const float *tw = nullptr;
@@ -342,12 +379,12 @@ int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint
         CK(launch_pack_tables((uint32_t)L, P, Q, b->as<float>(), s));
         pt = ctx->pack_tabs.emplace((uint32_t)L, std::move(b)).first;
     }
-    int *flag = ctx->flag.as<int>();
+    int *flag = dir.flag;
     const double elems = (double)batch * (double)L;
     int slot = ctx->prof_begin(s);
     if (payload) {
         const uint64_t bmb = (batch * L + 7) / 8;
-        CK(launch_spectral_pack(payload, bmb, ctx->chunk.as<uint32_t>(), ctx->meta.as<uint64_t>(),
+        CK(launch_spectral_pack(payload, bmb, dir.chunk, dir.meta,
                                 batch, (uint32_t)L, P, Q, pt->second->as<float>(),
                                 ctx->za.as<half_bits>(), s));
         // bitmap + ~0.3 of the INT4 section read, fp16 pairs written
@@ -386,38 +423,39 @@ int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint
 // when the row length allows, and scattered into ctx->dense otherwise.
 int run_idct(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols, void *d_out, int out_dtype,
              cudaStream_t s, hct_b200_error *err, const uint8_t *payload = nullptr,
-             size_t payload_len = 0) {
+             size_t payload_len = 0, const RankDir *dir_in = nullptr) {
     const uint64_t ldw = round_up(cols, 8), ldh = round_up(rows, 8);
-    int *flag = ctx->flag.as<int>();
+    const RankDir dir = dir_in ? *dir_in : ctx_rank_dir(ctx);
+    int *flag = dir.flag;
     uint32_t pn = 0, qn = 0, pm = 0, qm = 0;
-    const bool factored = ctx->idct_mode == HCT_B200_IDCT_AUTO && fdct_factor(cols, &pn, &qn) &&
-                          (rows == 1 || fdct_factor(rows, &pm, &qm));
+    const bool factored = idct_factored(ctx, rows, cols, &pn, &qn, &pm, &qm);
     const uint8_t *src = nullptr;
     if (payload) {
         const uint64_t total = rows * cols;
-        int slot = ctx->prof_begin(s);
         if (factored && spectral_pack_supported(cols)) {
-            CK(launch_spectral_rank(payload, payload_len, total, ctx->chunk.as<uint32_t>(),
-                                    ctx->meta.as<uint64_t>(), flag, s));
-            ctx->prof_end(slot, PK_RANK, (double)((total + 7) / 8), s);
+            if (!dir.ranked) {
+                int slot = ctx->prof_begin(s);
+                CK(launch_spectral_rank(payload, payload_len, total, dir.chunk, dir.meta, flag, s));
+                ctx->prof_end(slot, PK_RANK, (double)((total + 7) / 8), s);
+            }
             src = payload;
         } else {
-            CK(launch_spectral_scatter(payload, payload_len, rows, cols, ctx->chunk.as<uint32_t>(),
-                                       ctx->meta.as<uint64_t>(), ctx->dense.as<half_bits>(), ldw,
-                                       flag, s));
+            int slot = ctx->prof_begin(s);
+            CK(launch_spectral_scatter(payload, payload_len, rows, cols, dir.chunk, dir.meta,
+                                       ctx->dense.as<half_bits>(), ldw, flag, s));
             ctx->prof_end(slot, PK_SCATTER, (double)payload_len + 2.0 * total, s);
         }
     }
     if (factored) {
         // factored path: rows first (output T^T, cols x ldh), then the rows of T^T
         if (rows == 1)
-            return fdct_axis(ctx, ctx->dense.as<half_bits>(), ldw, src, 1, cols, pn, qn, d_out, 1,
-                             out_dtype, s, err);
-        int rc = fdct_axis(ctx, ctx->dense.as<half_bits>(), ldw, src, rows, cols, pn, qn,
+            return fdct_axis(ctx, ctx->dense.as<half_bits>(), ldw, src, dir, 1, cols, pn, qn, d_out,
+                             1, out_dtype, s, err);
+        int rc = fdct_axis(ctx, ctx->dense.as<half_bits>(), ldw, src, dir, rows, cols, pn, qn,
                            ctx->tt.p, ldh, HCT_B200_F16, s, err);
         if (rc) return rc;
-        return fdct_axis(ctx, ctx->tt.as<half_bits>(), ldh, nullptr, cols, rows, pm, qm, d_out,
-                         cols, out_dtype, s, err);
+        return fdct_axis(ctx, ctx->tt.as<half_bits>(), ldh, nullptr, dir, cols, rows, pm, qm,
+                         d_out, cols, out_dtype, s, err);
     }
     const Basis *bw = nullptr, *bh = nullptr;
     int rc = get_basis(ctx, cols, &bw, s, err);
@@ -564,8 +602,14 @@ int hct_b200_ctx_create(int device, hct_b200_ctx **out) {
         delete c;
         return HCT_B200_ERR_CUDA;
     }
+    if (cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking) != cudaSuccess) {
+        cudaStreamDestroy(c->stream);
+        delete c;
+        return HCT_B200_ERR_CUDA;
+    }
     if (c->flag.reserve(sizeof(int)) != cudaSuccess || c->meta.reserve(32) != cudaSuccess) {
         cudaStreamDestroy(c->stream);
+        cudaStreamDestroy(c->side);
         delete c;
         return HCT_B200_ERR_OUT_OF_MEMORY;
     }
@@ -581,6 +625,7 @@ void hct_b200_ctx_destroy(hct_b200_ctx *ctx) {
     ctx->bases.clear();
     for (cudaEvent_t e : ctx->event_pool) cudaEventDestroy(e);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    if (ctx->side) cudaStreamDestroy(ctx->side);
     delete ctx;
 }
 
@@ -588,9 +633,8 @@ int hct_b200_ctx_reserve(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols) {
     if (!ctx) return HCT_B200_ERR_INVALID_ARGUMENT;
     int rc = ensure_device(ctx);
     if (rc) return rc;
-    const uint64_t total = rows * cols;
     hct_b200_error e;
-    return reserve_spectral(ctx, rows, cols, (total + 7) / 8 + total, &e);
+    return reserve_spectral(ctx, rows, cols, &e);
 }
 
 int hct_b200_ctx_set_idct(hct_b200_ctx *ctx, int mode) {
@@ -683,7 +727,7 @@ int hct_b200_idct_2d(hct_b200_ctx *ctx, const float *d_in, void *d_out, int out_
     cudaStream_t s = (cudaStream_t)stream;
     uint64_t rows = height, cols = width;
     if (cols == 1 && rows > 1) std::swap(rows, cols);  // a column vector: one row transform
-    rc = reserve_spectral(ctx, rows, cols, 0, err);
+    rc = reserve_spectral(ctx, rows, cols, err);
     if (rc) return rc;
     CK(cudaMemsetAsync(ctx->flag.p, 0, sizeof(int), s));
     CK(launch_f32_to_f16_padded(d_in, rows, cols, ctx->dense.as<half_bits>(), round_up(cols, 8), s));
@@ -708,7 +752,7 @@ int hct_b200_spectral_q4_decode(hct_b200_ctx *ctx, const uint8_t *d_payload, siz
     if (cols == 1 && rows > 1) std::swap(rows, cols);
     const uint64_t total = rows * cols;
     if (payload_len < (total + 7) / 8) return HCT_B200_ERR_SIZE_MISMATCH;
-    rc = reserve_spectral(ctx, rows, cols, 0, err);
+    rc = reserve_spectral(ctx, rows, cols, err);
     if (rc) return rc;
     CK(cudaMemsetAsync(ctx->flag.p, 0, sizeof(int), s));
     rc = run_idct(ctx, rows, cols, d_out, out_dtype, s, err, d_payload, payload_len);
@@ -872,6 +916,13 @@ int hct_b200_reader_open(hct_b200_ctx *ctx, const uint8_t *file, size_t file_len
     CK(cudaEventCreateWithFlags(&r->done, cudaEventDisableTiming));
     CK(cudaEventCreateWithFlags(&r->uploaded, cudaEventDisableTiming));
     CK(cudaEventCreateWithFlags(&r->data_free, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&r->front_done, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&r->back_done, cudaEventDisableTiming));
+    CK(r->d_payload.reserve(h.original_size + 64));
+    CK(r->d_meta.reserve(4 * sizeof(uint64_t)));
+    CK(r->d_flag.reserve(sizeof(int)));
+    if (h.dtype == 4 && r->spectral)
+        CK(r->d_chunk.reserve(rank_dir_words(rows * cols) * sizeof(uint32_t)));
     std::vector<hct_b200_lz4_block> blocks(nb);
     for (uint32_t i = 0; i < nb; i++) {
         blocks[i].src_off = r->offsets[i];
@@ -887,11 +938,11 @@ int hct_b200_reader_open(hct_b200_ctx *ctx, const uint8_t *file, size_t file_len
         CK(cudaMemcpyAsync(r->d_blocks.p, blocks.data(), nb * sizeof(hct_b200_lz4_block),
                            cudaMemcpyHostToDevice, s));
     if (h.dtype == 4 && r->spectral) {
-        rc = reserve_spectral(ctx, rows, cols, h.original_size, err);
+        // the back end's matrices live in the context (the payload in the reader)
+        uint64_t rr = rows, cc = cols;
+        if (cc == 1 && rr > 1) std::swap(rr, cc);
+        rc = reserve_spectral(ctx, rr, cc, err);
         if (rc) return rc;
-    } else {
-        CK(ctx->payload.reserve(h.original_size + 64));
-        CK(ctx->flag.reserve(sizeof(int)));
     }
     CK(cudaStreamSynchronize(s));
     *out = r.release();
@@ -935,6 +986,7 @@ int reader_lz4(hct_b200_reader *r, uint8_t *d_dst, size_t cap, size_t *written, 
     }
     *written = 0;
     if (nb == 0) return HCT_B200_OK;
+    if (r->back_pending) CK(cudaStreamWaitEvent(s, r->back_done, 0));  // d_status in use
     CK(r->before_read(s));
     int slot = r->ctx->prof_begin(s);
     CK(launch_lz4_blocks(r->d_data.as<uint8_t>(), r->d_blocks.as<hct_b200_lz4_block>(), nb, d_dst,
@@ -1003,12 +1055,18 @@ int hct_b200_reader_decode(hct_b200_reader *r, void *d_out, int out_dtype, void 
     return hct_b200_reader_wait(r, err);
 }
 
-// The whole decode is enqueued on `stream` with no host synchronisation:
-// LZ4 writes its per-block statuses, the payload is decoded on the
-// assumption that every block is complete, and the statuses and the device
-// flag are copied to pinned host memory behind the kernels.
-// hct_b200_reader_wait then reports exactly what hct_b200_reader_decode
-// would have (the output is undefined when it reports an error).
+// The whole decode is enqueued with no host synchronisation, in two parts:
+//  - front end on the context's side stream: LZ4 into the reader's payload
+//    (per-block statuses) and, for a spectral tensor decoded through the
+//    fused row pack, the payload's rank directory;
+//  - back end on `stream`, after the front end: INT4 dequantisation or the
+//    IDCT, then the statuses and the device flag copied to pinned host
+//    memory.
+// Consecutive decodes of different readers thus overlap one tensor's front
+// end with the previous tensor's back end; a reader's next front end waits
+// for its previous back end.  hct_b200_reader_wait then reports exactly what
+// hct_b200_reader_decode would have (the output is undefined when it reports
+// an error).
 int hct_b200_reader_decode_async(hct_b200_reader *r, void *d_out, int out_dtype, void *stream,
                                  hct_b200_error *err) {
     clear_err(err);
@@ -1031,49 +1089,58 @@ int hct_b200_reader_decode_async(hct_b200_reader *r, void *d_out, int out_dtype,
     hct_b200_ctx *ctx = r->ctx;
     int rc = ensure_device(ctx);
     if (rc) return rc;
-    cudaStream_t s = (cudaStream_t)stream;
+    const cudaStream_t s = (cudaStream_t)stream, fs = ctx->side;
     const uint32_t nb = r->hdr.num_blocks;
-    if (ctx->payload.cap < r->hdr.original_size) {
-        set_err(err, HCT_B200_ERR_BUFFER_TOO_SMALL, -1, 0, r->hdr.original_size, ctx->payload.cap,
-                "context payload scratch too small");
-        return HCT_B200_ERR_BUFFER_TOO_SMALL;
-    }
-    CK(cudaMemsetAsync(ctx->flag.p, 0, sizeof(int), s));
-    if (nb) {
-        CK(r->before_read(s));
-        int slot = ctx->prof_begin(s);
-        CK(launch_lz4_blocks(r->d_data.as<uint8_t>(), r->d_blocks.as<hct_b200_lz4_block>(), nb,
-                             ctx->payload.as<uint8_t>(), r->d_status.as<hct_b200_status>(), s,
-                             r->max_block));
-        ctx->prof_end(slot, PK_LZ4, (double)r->hdr.compressed_size + (double)r->hdr.original_size,
-                      s);
-        CK(r->after_read(s));
-    }
     const uint64_t total = r->rows * r->cols;
+    uint64_t rows = r->rows, cols = r->cols;
+    if (cols == 1 && rows > 1) std::swap(rows, cols);
+    uint8_t *payload = r->d_payload.as<uint8_t>();
     const size_t written = r->hdr.original_size;  // verified against the statuses in _wait
+    RankDir dir{r->d_chunk.as<uint32_t>(), r->d_meta.as<uint64_t>(), r->d_flag.as<int>(), false};
+
+    // ---- front end (side stream)
+    if (r->back_pending) CK(cudaStreamWaitEvent(fs, r->back_done, 0));
+    CK(cudaMemsetAsync(r->d_flag.p, 0, sizeof(int), fs));
+    if (nb) {
+        CK(r->before_read(fs));
+        int slot = ctx->prof_begin(fs);
+        CK(launch_lz4_blocks(r->d_data.as<uint8_t>(), r->d_blocks.as<hct_b200_lz4_block>(), nb,
+                             payload, r->d_status.as<hct_b200_status>(), fs, r->max_block));
+        ctx->prof_end(slot, PK_LZ4, (double)r->hdr.compressed_size + (double)r->hdr.original_size,
+                      fs);
+        CK(r->after_read(fs));
+    }
+    if (total && r->spectral && spectral_fused(ctx, rows, cols)) {
+        int slot = ctx->prof_begin(fs);
+        CK(launch_spectral_rank(payload, written, total, dir.chunk, dir.meta, dir.flag, fs));
+        ctx->prof_end(slot, PK_RANK, (double)((total + 7) / 8), fs);
+        dir.ranked = true;
+    }
+    CK(cudaEventRecord(r->front_done, fs));
+
+    // ---- back end (caller's stream)
+    CK(cudaStreamWaitEvent(s, r->front_done, 0));
     r->pending_elems = 0;
     if (total && !r->spectral) {
         // plain INT4 weights (examples/safetensors_to_int4_hct.rs:241-284)
         size_t n = 0;
         int slot = ctx->prof_begin(s);
-        rc = hct_b200_dequantize_int4(ctx->payload.as<uint8_t>(), written, total, d_out, out_dtype,
-                                      &n, s);
+        rc = hct_b200_dequantize_int4(payload, written, total, d_out, out_dtype, &n, s);
         ctx->prof_end(slot, PK_DEQUANT, (double)written + (out_dtype == HCT_B200_F32 ? 4.0 : 2.0) * n,
                       s);
         if (rc) return rc;
         r->pending_elems = n;
     } else if (total) {
-        uint64_t rows = r->rows, cols = r->cols;
-        if (cols == 1 && rows > 1) std::swap(rows, cols);
-        rc = run_idct(ctx, rows, cols, d_out, out_dtype, s, err, ctx->payload.as<uint8_t>(),
-                      written);
+        rc = run_idct(ctx, rows, cols, d_out, out_dtype, s, err, payload, written, &dir);
         if (rc) return rc;
     }
     if (nb)
         CK(cudaMemcpyAsync(r->h_status, r->d_status.p, nb * sizeof(hct_b200_status),
                            cudaMemcpyDeviceToHost, s));
-    CK(cudaMemcpyAsync(r->h_flag, ctx->flag.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CK(cudaMemcpyAsync(r->h_flag, r->d_flag.p, sizeof(int), cudaMemcpyDeviceToHost, s));
     CK(cudaEventRecord(r->done, s));
+    CK(cudaEventRecord(r->back_done, s));
+    r->back_pending = true;
     r->pending = true;
     return HCT_B200_OK;
 }
