@@ -268,6 +268,7 @@ def run_b200(args):
             dist.barrier()
 
     import haagenti_b200 as H
+    from haagenti_b200 import shard
 
     files = layer_files(local, world, barrier)
     ctx = H.Context(local)
@@ -309,10 +310,7 @@ def run_b200(args):
     ms_total = e0.elapsed_time(e1)
     ks = kernel_stats(H, ctx)
     set_profiling(ctx, False)
-    t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_total = float(t.item())
+    ms_total = shard.max_over_ranks(ms_total, dev)
     ms_step = ms_total / args.steps
     value = world * out_bytes / (ms_step / 1e3) / 1e9
 
@@ -346,10 +344,7 @@ def run_b200(args):
     e1.record(stream)
     torch.cuda.synchronize(dev)
     barrier()
-    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_ms = float(t.item()) / args.steps
+    e2e_ms = shard.max_over_ranks(e0.elapsed_time(e1), dev) / args.steps
     h2d = sum(_data_len(files[n]) for n, _, _ in TENS)  # compressed data sections
     d2h = sum(32 * readers[n].num_blocks() + 4 for n in readers)
     e2e_value = world * out_bytes / (e2e_ms / 1e3) / 1e9
