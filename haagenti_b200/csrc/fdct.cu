@@ -62,31 +62,43 @@ __device__ __forceinline__ uint32_t pack_z(float re, float im) {
 // roles permuted and lies at k2' = Q - k2, k1' = P - 1 - k1 (k2 > 0) or
 // k2' = 0, k1' = P - k1 (k2 = 0).  coefT holds (alpha_k, beta_k) in the same
 // (k2, k1) order, so every global access of a warp is contiguous.
+// srow[pad_idx(L)] must hold zero: it is c[L] of the k = 0 term.  Along a
+// lane's k1 = l, l + 32, ... every index moves by a constant (32 Q is a
+// multiple of 64, so pad_idx(k + 32 Q) = pad_idx(k) + 33 Q).
 __device__ __forceinline__ void pack_row(const uint16_t *srow, const float4 *__restrict__ coefT,
                                          uint32_t L, uint32_t P, uint32_t Q,
                                          uint32_t *__restrict__ orow) {
     const uint32_t H = L / 2;
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    const uint32_t sstep = 33 * Q;
     for (uint32_t k2 = warp; 2 * k2 <= Q; k2 += nwarps) {
         const uint32_t k1_end = k2 == 0 ? P / 2 + 1 : (2 * k2 == Q ? P / 2 : P);
+        const uint32_t k = Q * lane + k2;
+        uint32_t ia = pad_idx(k), ib = pad_idx(L - k), ic = pad_idx(H + k), id = pad_idx(H - k);
+        uint32_t io = k2 * P + lane;
+        uint32_t jo = k2 == 0 ? P - lane : (Q - k2) * P + (P - 1 - lane);
         for (uint32_t k1 = lane; k1 < k1_end; k1 += 32) {
-            const uint32_t k = Q * k1 + k2;
-            const float ck = h2f(srow[pad_idx(k)]);
-            const float cLk = k ? h2f(srow[pad_idx(L - k)]) : 0.0f;
-            const float cHk = h2f(srow[pad_idx(H + k)]);
-            const float cHmk = h2f(srow[pad_idx(H - k)]);  // H - k >= 1 for k < H
-            const float4 t = coefT[k2 * P + k1];            // (alpha.re, alpha.im, beta.re, beta.im)
+            const float ck = h2f(srow[ia]);
+            const float cLk = h2f(srow[ib]);
+            const float cHk = h2f(srow[ic]);
+            const float cHmk = h2f(srow[id]);  // H - k >= 1 for k < H
+            const float4 t = coefT[io];        // (alpha.re, alpha.im, beta.re, beta.im)
             const float zr = fmaf(t.x, ck, fmaf(t.y, cLk, fmaf(t.z, cHk, t.w * cHmk)));
             const float zi = fmaf(t.y, ck, fmaf(-t.x, cLk, fmaf(t.w, cHk, -t.z * cHmk)));
-            orow[k2 * P + k1] = pack_z(zr, zi);
-            if (k != 0 && 2 * k != H) {
+            orow[io] = pack_z(zr, zi);
+            if (k2 != 0 || (k1 != 0 && 2 * k1 != P)) {  // k != 0 and k != H/2
                 // k' = H - k: c[k'] = c[H-k], c[L-k'] = c[H+k], c[H+k'] = c[L-k], c[H-k'] = c[k]
-                const uint32_t j = k2 == 0 ? P - k1 : (Q - k2) * P + (P - 1 - k1);
-                const float4 u = coefT[j];
+                const float4 u = coefT[jo];
                 const float yr = fmaf(u.x, cHmk, fmaf(u.y, cHk, fmaf(u.z, cLk, u.w * ck)));
                 const float yi = fmaf(u.y, cHmk, fmaf(-u.x, cHk, fmaf(u.w, cLk, -u.z * ck)));
-                orow[j] = pack_z(yr, yi);
+                orow[jo] = pack_z(yr, yi);
             }
+            ia += sstep;
+            ib -= sstep;
+            ic += sstep;
+            id -= sstep;
+            io += 32;
+            jo -= 32;
         }
     }
 }
@@ -102,6 +114,7 @@ __global__ void __launch_bounds__(THREADS, MIN_CTAS) makhoul_pack_kernel(
     extern __shared__ uint16_t srow[];
     const bool vec = ((ld_in & 7) == 0) && (((uintptr_t)in & 15) == 0) && ((L & 7) == 0);
     const uint32_t nv = L / 8;
+    if (threadIdx.x == 0) srow[pad_idx(L)] = 0;  // c[L] = 0 (never overwritten)
     for (uint64_t b = blockIdx.x; b < B; b += gridDim.x) {
         const uint16_t *row = in + b * ld_in;
         __syncthreads();  // previous row fully consumed
@@ -187,6 +200,7 @@ __global__ void __launch_bounds__(SPACK_THREADS, 3) spectral_pack_kernel(
     const uint32_t *bm32 = reinterpret_cast<const uint32_t *>(payload);
     const uint32_t pair_shift = 2 * lane;
     const uint64_t below = (1ull << pair_shift) - 1ull;  // bits of the elements before 2l
+    if (threadIdx.x == 0) srow[pad_idx(L)] = 0;  // c[L] = 0 (never overwritten)
 
     for (uint64_t b = blockIdx.x; b < B; b += gridDim.x) {
         __syncthreads();  // previous row fully consumed
