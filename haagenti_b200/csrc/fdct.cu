@@ -150,25 +150,27 @@ __global__ void __launch_bounds__(THREADS, MIN_CTAS) makhoul_pack_kernel(
 // Row pack straight from the spectral payload (bitmap ++ INT4).  Each CTA
 // decodes the coefficients of its row into shared memory and then runs the
 // pack:
-//   A. warp w takes the 64-bit bitmap words [w * spw, (w + 1) * spw) of the
-//      row, one per lane, and a warp scan of their popcounts; warp 0 adds
-//      up the row's rank (the rank directory of launch_spectral_rank for its
+//   A. warp w takes a run of the row's 64-bit bitmap words (a multiple of 4,
+//      one per lane) and a warp scan of their popcounts; warp 0 adds up the
+//      row's rank (the rank directory of launch_spectral_rank for its
 //      1024-bit chunk plus a partial popcount);
 //   B. the row's coefficients in rank order are staged in shared memory:
-//      fp16((nibble - 8) * scale) per set bit when the row has at most L/2
-//      of them, else the raw nibble bytes and the f32 scales;
-//   C. each warp expands its words, 64 elements per step, lane l writing
-//      elements (2l, 2l + 1) of the word as one fp16 pair (zero where the
-//      bit is clear; the rank is the word's rank plus a masked popcount).
+//      fp16((nibble - 8) * scale) per set bit, four ranks per thread and
+//      step (one 16-bit nibble load, one scale) when the row has at most L/2
+//      of them; else the raw nibble bytes and the f32 scales;
+//   C. each warp expands its words 256 elements per step: lane l takes bitmap
+//      byte l of four consecutive words and writes its 8 elements (zero where
+//      the bit is clear) as four 32-bit words, which the one-word pad per 64
+//      elements spreads over all 32 banks.
 // Requires L % 64 == 0 (rows start on a 64-bit bitmap boundary) and
 // L / 64 <= 32 * SPACK_WARPS.
 constexpr int SPACK_THREADS = 512;
 constexpr int SPACK_WARPS = SPACK_THREADS / 32;
 
-// bytes of the staging area behind the row: L/2 fp16 values, or L/2
+// bytes of the staging area behind the row: L/2 + 8 fp16 values, or L/2
 // nibble bytes (+ 16 slack) and L/32 + 4 f32 scales
 __host__ __device__ __forceinline__ uint32_t spack_stage_bytes(uint32_t L) {
-    const uint32_t vals = L, raw = ((L / 2 + 16 + 15) & ~15u) + (L / 32 + 4) * 4;
+    const uint32_t vals = L + 16, raw = ((L / 2 + 16 + 15) & ~15u) + (L / 32 + 4) * 4;
     return vals > raw ? vals : raw;
 }
 
@@ -188,18 +190,25 @@ __global__ void __launch_bounds__(SPACK_THREADS, 3) spectral_pack_kernel(
     uint16_t *vals_s = reinterpret_cast<uint16_t *>(stage);
     uint8_t *nib_s = stage;
     float *sc_s = reinterpret_cast<float *>(stage + ((L / 2 + 16 + 15) & ~15u));
+    uint32_t *srow32 = reinterpret_cast<uint32_t *>(srow);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t segs = L / 64;
-    const uint32_t spw = (segs + SPACK_WARPS - 1) / SPACK_WARPS;
+    const uint32_t spw = ((segs + SPACK_WARPS - 1) / SPACK_WARPS + 3) & ~3u;  // <= 32
     const uint32_t seg0 = warp * spw;
     const uint32_t nseg = seg0 < segs ? min(spw, segs - seg0) : 0u;
+    const uint64_t k_total = meta[0];
+    const uint64_t nib_len = (k_total + 1) >> 1;  // bytes of the nibble section
     const uint8_t *scales = payload + bmb;
     const uint8_t *nibbles = payload + meta[1];
     const bool bad = meta[2] != 0;
     const uint64_t *bm64 = reinterpret_cast<const uint64_t *>(payload);
     const uint32_t *bm32 = reinterpret_cast<const uint32_t *>(payload);
+    // expand geometry of this lane: byte (lane & 7) of word (lane >> 3) of a span
+    const uint32_t sub = lane >> 3, bshift = 8 * (lane & 7);
+    const uint64_t below8 = (1ull << bshift) - 1ull;
+    // raw-nibble expand (rows over half full): elements (2l, 2l + 1) of a word
     const uint32_t pair_shift = 2 * lane;
-    const uint64_t below = (1ull << pair_shift) - 1ull;  // bits of the elements before 2l
+    const uint64_t below2 = (1ull << pair_shift) - 1ull;
     if (threadIdx.x == 0) srow[pad_idx(L)] = 0;  // c[L] = 0 (never overwritten)
 
     for (uint64_t b = blockIdx.x; b < B; b += gridDim.x) {
@@ -237,19 +246,27 @@ __global__ void __launch_bounds__(SPACK_THREADS, 3) spectral_pack_kernel(
         const uint32_t row_count = __shfl_sync(0xffffffffu, wincl, SPACK_WARPS - 1);
         const uint64_t rank0 = s_rank_start;
         const bool packed_vals = 2 * row_count <= L;
+        const uint64_t a4 = rank0 & ~3ull;  // vals_s[i] holds rank a4 + i
         const uint64_t nb0 = rank0 >> 1, sb0 = rank0 >> 5;
         // B. stage the row's coefficients (rank order); a short payload
         // (meta[2]) decodes to zeros and never reads past its end
         if (!bad) {
             if (packed_vals) {
-#pragma unroll 4
-                for (uint32_t i = threadIdx.x; i < row_count; i += SPACK_THREADS) {
-                    const uint64_t r = rank0 + i;
-                    const uint32_t sh = (uint32_t)scales[2 * (r >> 5)] |
-                                        ((uint32_t)scales[2 * (r >> 5) + 1] << 8);
-                    const float v = deq_nibble(nibbles[r >> 1], r,
-                                               __half2float(__ushort_as_half((uint16_t)sh)));
-                    vals_s[i] = f2h(v);
+                const uint32_t ngroups = (uint32_t)((rank0 + row_count + 3 - a4) >> 2);
+                for (uint32_t g = threadIdx.x; g < ngroups; g += SPACK_THREADS) {
+                    const uint64_t r = a4 + 4ull * g;  // a multiple of 4, below k_total
+                    const uint64_t nb = r >> 1;        // even: a 16-bit aligned pair
+                    uint32_t nib4;
+                    if (nb + 1 < nib_len) nib4 = *reinterpret_cast<const uint16_t *>(nibbles + nb);
+                    else nib4 = nb < nib_len ? (uint32_t)nibbles[nb] : 0u;
+                    const float sc = __half2float(__ushort_as_half(
+                        *reinterpret_cast<const uint16_t *>(scales + 2 * (r >> 5))));
+                    float v[4];
+#pragma unroll
+                    for (int t = 0; t < 4; t++)
+                        v[t] = __fmul_rn((float)((int)((nib4 >> (4 * t)) & 0xfu) - 8), sc);
+                    *reinterpret_cast<uint2 *>(vals_s + 4 * g) =
+                        make_uint2(pack_z(v[0], v[1]), pack_z(v[2], v[3]));
                 }
             } else {
                 const uint64_t nb1 = (rank0 + row_count + 1) >> 1;
@@ -264,28 +281,46 @@ __global__ void __launch_bounds__(SPACK_THREADS, 3) spectral_pack_kernel(
         __syncthreads();
         // C. expand this warp's words into the staged row
         const uint32_t wrank = before + incl - cnt;  // rank of my word within the row
-        uint32_t *dst = reinterpret_cast<uint32_t *>(srow + pad_idx(64 * seg0 + pair_shift));
-        for (uint32_t i = 0; i < nseg; i++, dst += 33) {  // 64 elements + 2 pad halves
-            const uint64_t w = __shfl_sync(0xffffffffu, mw, i);
-            const uint32_t r = __shfl_sync(0xffffffffu, wrank, i) + __popcll(w & below);
-            const uint32_t m2 = (uint32_t)(w >> pair_shift) & 3u;
-            uint32_t pair = 0;
-            if (!bad && m2) {
-                const uint32_t r1 = r + (m2 & 1u);
-                float v0 = 0.0f, v1 = 0.0f;
-                if (packed_vals) {
-                    if (m2 & 1u) v0 = h2f(vals_s[r]);
-                    if (m2 & 2u) v1 = h2f(vals_s[r1]);
-                } else {
-                    const uint64_t g0 = rank0 + r, g1 = rank0 + r1;
-                    if (m2 & 1u) v0 = h2f(f2h(deq_nibble(nib_s[(g0 >> 1) - nb0], g0,
-                                                          sc_s[(g0 >> 5) - sb0])));
-                    if (m2 & 2u) v1 = h2f(f2h(deq_nibble(nib_s[(g1 >> 1) - nb0], g1,
-                                                          sc_s[(g1 >> 5) - sb0])));
+        if (packed_vals) {
+            const uint32_t roff = (uint32_t)(rank0 - a4);
+            uint32_t *dst = srow32 + 33 * (seg0 + sub) + 4 * (lane & 7);
+            const uint32_t nspan = (nseg + 3) >> 2;  // nseg <= 32: s stays below 32
+            for (uint32_t i = 0; i < nspan; i++, dst += 132) {  // 4 x (64 elements + pad)
+                const uint32_t s = 4 * i + sub;
+                const uint64_t w = __shfl_sync(0xffffffffu, mw, s);
+                const uint32_t wr = __shfl_sync(0xffffffffu, wrank, s);
+                if (s < nseg) {
+                    const uint32_t byte = bad ? 0u : (uint32_t)(w >> bshift) & 0xffu;
+                    uint32_t r = wr + roff + __popcll(w & below8);
+                    uint32_t h[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const uint32_t bit = (byte >> j) & 1u;
+                        h[j] = bit ? (uint32_t)vals_s[r] : 0u;
+                        r += bit;
+                    }
+                    dst[0] = h[0] | (h[1] << 16);
+                    dst[1] = h[2] | (h[3] << 16);
+                    dst[2] = h[4] | (h[5] << 16);
+                    dst[3] = h[6] | (h[7] << 16);
                 }
-                pair = pack_z(v0, v1);
             }
-            *dst = pair;
+        } else {
+            uint32_t *dst = srow32 + 33 * seg0 + lane;  // 64 elements + 2 pad halves per word
+            for (uint32_t i = 0; i < nseg; i++, dst += 33) {
+                const uint64_t w = __shfl_sync(0xffffffffu, mw, i);
+                const uint32_t r = __shfl_sync(0xffffffffu, wrank, i) + __popcll(w & below2);
+                const uint32_t m2 = (uint32_t)(w >> pair_shift) & 3u;
+                uint32_t pair = 0;
+                if (!bad && m2) {
+                    const uint64_t g0 = rank0 + r, g1 = g0 + (m2 & 1u);
+                    float v0 = 0.0f, v1 = 0.0f;
+                    if (m2 & 1u) v0 = deq_nibble(nib_s[(g0 >> 1) - nb0], g0, sc_s[(g0 >> 5) - sb0]);
+                    if (m2 & 2u) v1 = deq_nibble(nib_s[(g1 >> 1) - nb0], g1, sc_s[(g1 >> 5) - sb0]);
+                    pair = pack_z(v0, v1);
+                }
+                *dst = pair;
+            }
         }
         __syncthreads();
         pack_row(srow, coef, L, P, Q, out + b * (uint64_t)(L / 2));
