@@ -19,6 +19,13 @@
 //           is released to the producer by tcgen05.commit on "empty";
 //   warps 2-5 epilogue: tcgen05.ld of the fp32 accumulator (TMEM lanes =
 //           tile rows), conversion and global stores.
+// The factored IDCT's two DFT stages (fdct.cu) run on dft_stage_t_kernel,
+// a persistent variant: the DFT matrix stays resident in shared memory as
+// the A operand, 128-row data tiles stream in as the B operand, TMEM is
+// double-buffered so the epilogue of one tile overlaps the MMAs of the next,
+// and 8 epilogue warps write each output as contiguous runs through a
+// per-warp shared-memory transpose.
+//
 // Every mbarrier wait is bounded (iteration count and %globaltimer); an
 // expired wait raises HCT_B200_ERR_TIMEOUT in the device flag, the CTA
 // drains its own in-flight copies and MMAs (again bounded), frees TMEM and
@@ -56,7 +63,7 @@ struct Cfg {
 // Extra epilogue parameters of the factored-DCT stages (modes 2 and 3).
 struct StageParams {
     uint32_t P, Q, H;
-    uint32_t pad;
+    uint32_t vec_out;  // output rows may be written with 16-byte stores
     uint64_t batch;
     const float2 *twiddle;
     float scale;
@@ -172,66 +179,6 @@ __device__ __forceinline__ void raise_timeout(int *flag, SmemCtl *ctl) {
 __device__ __forceinline__ uint16_t f2h(float v) { return __half_as_ushort(__float2half_rn(v)); }
 __device__ __forceinline__ uint16_t f2bf(float v) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(v));
-}
-
-// Epilogue of the factored-DCT stages for one 32-column chunk of a TMEM row
-// (fp32 accumulator values r[0..31] of D row `row`, columns col0..col0+31).
-//   mode 2 (stage 1): row = (b, k2); column pair (2 m1, 2 m1 + 1) = complex
-//           output m1, multiplied by twiddle[k2 * m1] and stored as an fp16
-//           pair at G[(m1 * batch + b) * Q + k2].
-//   mode 3 (stage 2): row = (m1, b); column pair (2 m2, 2 m2 + 1) = z[j],
-//           j = m1 + P m2, scaled; Re/Im go to output rows 4j, 4j+2
-//           (j < H/2) or 4(H-1-j)+3, 4(H-1-j)+1, at column b.
-// Stage 1 (mode 2), one 32-column chunk = complex outputs m1 in
-// [m1_0, m1_0 + 16) of row (b, k2).  `g` points at G[(0 * batch + b) * Q + k2]
-// (fp16 pairs as u32); consecutive m1 are `stride` = batch * Q apart.
-// The twiddles e^{2 pi i k2 m1 / H} run by recurrence from the table entry
-// at m1_0 (16 steps of an fp32 complex product).
-__device__ __forceinline__ void stage1_chunk(const uint32_t (&r)[32], uint32_t *g, uint64_t stride,
-                                             uint32_t m1_0, uint32_t P, float2 t, float2 w) {
-#pragma unroll
-    for (int j = 0; j < 16; j++) {
-        const uint32_t m1 = m1_0 + j;
-        if (m1 < P) {
-            const float re = __uint_as_float(r[2 * j]), im = __uint_as_float(r[2 * j + 1]);
-            const float yr = re * t.x - im * t.y, yi = re * t.y + im * t.x;
-            g[(uint64_t)m1 * stride] = (uint32_t)f2h(yr) | ((uint32_t)f2h(yi) << 16);
-        }
-        const float tx = t.x * w.x - t.y * w.y;
-        t.y = t.x * w.y + t.y * w.x;
-        t.x = tx;
-    }
-}
-
-// Stage 2 (mode 3), one chunk = z[j] for m2 in [m2_0, m2_0 + 16) of row
-// (m1, b), j = m1 + P m2; output rows per the Makhoul quartet map, column b.
-template <int DT>
-__device__ __forceinline__ void stage2_chunk(const uint32_t (&r)[32], void *out, uint64_t ldo,
-                                             uint32_t b, uint32_t m1, uint32_t m2_0,
-                                             const StageParams &sp) {
-    const uint32_t half = sp.H / 2;
-#pragma unroll
-    for (int j = 0; j < 16; j++) {
-        const uint32_t m2 = m2_0 + j;
-        if (m2 < sp.Q) {
-            const uint32_t jj = m1 + sp.P * m2;
-            const uint32_t n_re = jj < half ? 4 * jj : 4 * (sp.H - 1 - jj) + 3;
-            const uint32_t n_im = jj < half ? n_re + 2 : n_re - 2;
-            const float zr = __uint_as_float(r[2 * j]) * sp.scale;
-            const float zi = __uint_as_float(r[2 * j + 1]) * sp.scale;
-            const uint64_t ore = (uint64_t)n_re * ldo + b, oim = (uint64_t)n_im * ldo + b;
-            if (DT == HCT_B200_F32) {
-                reinterpret_cast<float *>(out)[ore] = zr;
-                reinterpret_cast<float *>(out)[oim] = zi;
-            } else if (DT == HCT_B200_BF16) {
-                reinterpret_cast<uint16_t *>(out)[ore] = f2bf(zr);
-                reinterpret_cast<uint16_t *>(out)[oim] = f2bf(zi);
-            } else {
-                reinterpret_cast<uint16_t *>(out)[ore] = f2h(zr);
-                reinterpret_cast<uint16_t *>(out)[oim] = f2h(zi);
-            }
-        }
-    }
 }
 
 template <int BN>
@@ -422,17 +369,6 @@ __global__ void __launch_bounds__(THREADS, 1)
 // accumulators alternate so that the epilogue of one tile overlaps the TMA
 // loads and MMAs of the next.  One CTA per SM; same warp roles and bounded
 // waits as umma_gemm_kernel.
-template <int BN>
-struct StageCfg {
-    static constexpr int KB_MAX = BN / 64;           // K <= BN (K = N = 2 * DFT size)
-    static constexpr int W_KB_BYTES = BN * BK * 2;   // one 64-column k-block of W
-    // BN = 128: 32 KB of W + 4 x 16 KB ring -> two CTAs per SM
-    static constexpr int RING = BN == 256 ? 5 : 4;
-    static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr size_t SMEM_BYTES =
-        1024 + (size_t)KB_MAX * W_KB_BYTES + (size_t)RING * A_TILE_BYTES + 256;
-};
-
 struct StageCtl {
     uint64_t full[8];
     uint64_t empty[8];
@@ -453,20 +389,213 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 
 constexpr int STAGE_THREADS = 320;  // producer, MMA, 8 epilogue warps
 
-template <int BN>
-__global__ void __launch_bounds__(STAGE_THREADS, 1)
-    dft_stage_kernel(const __grid_constant__ CUtensorMap tmA,
-                     const __grid_constant__ CUtensorMap tmB, uint32_t M, uint32_t N, uint32_t K,
-                     uint32_t m_tiles, void *out, uint64_t ldo, int mode, int out_dtype, int *flag,
-                     const StageParams sp) {
-    using SC = StageCfg<BN>;
+// ---------------------------------------------------------------- output-major stages
+
+// DFT stage with the operands swapped: D^T = W . A^T, i.e. TMEM lane o holds
+// DFT output o (the realified row of W) and TMEM column c holds data row
+// r0 + c of the 128-row tile.  A lane's 32 columns are then 32 consecutive
+// data rows of one output, which both stages store as contiguous runs:
+//   stage 1: G[m1][b][k2] = G[m1 * batch * Q + r] for row r = (b, k2): the
+//            lane pair (2 m1, 2 m1 + 1) trades halves of its chunk so that
+//            each lane holds 16 complex values, twiddles them and writes
+//            64 contiguous bytes;
+//   stage 2: output row n(j, ri), j = m1 + P m2, columns b..b+31 of the
+//            chunk (one m1 when batch % 32 == 0): 32 scaled values, 64 or
+//            128 contiguous bytes.
+// MT 128-row halves of W (2S <= 128 MT outputs) are resident in shared
+// memory; the data tiles (128 rows x 64 K) stream through a TMA ring; per
+// k-step one elected thread issues MT tcgen05 MMAs of M = 128, N = 128
+// into a double-buffered TMEM accumulator.
+// Per-warp staging of one 32-column chunk for coalesced stores: 32 rows of
+// 64 bytes (+16 bytes of padding, so that the 16-byte accesses of 8
+// consecutive lanes hit distinct banks).
+constexpr int XROW = 80;
+constexpr int XWARP_BYTES = 32 * XROW;
+
+template <int MT>
+struct StageTCfg {
+    static constexpr int WROWS = 128 * MT;
+    static constexpr int KB_MAX = 2 * MT;              // K = 2S <= 128 MT
+    static constexpr int W_KB_BYTES = WROWS * BK * 2;  // one 64-column k-block of W
+    static constexpr int NT = 128;                     // data rows per tile (MMA N)
+    static constexpr int B_TILE_BYTES = NT * BK * 2;
+    static constexpr int RING = MT == 1 ? 3 : 4;
+    static constexpr int TMEM_COLS = 2 * MT * NT;      // double-buffered
+    static constexpr int X_BYTES = 8 * XWARP_BYTES;    // epilogue staging, 8 warps
+    // MT = 1: 32 KB of W + 48 KB ring + 20 KB staging -> two CTAs per SM;
+    // MT = 2: 128 KB of W + 64 KB ring + 20 KB staging -> one
+    static constexpr size_t SMEM_BYTES = 1024 + (size_t)KB_MAX * W_KB_BYTES +
+                                         (size_t)RING * B_TILE_BYTES + X_BYTES + 256;
+    static constexpr uint32_t IDESC =
+        (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+};
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+__device__ __forceinline__ uint32_t pack_bf2(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// Stage 1 chunk: lane o = 2 m1 + ri holds columns rT..rT+31 of output o.
+// After the pair exchange lane o owns 16 complex values of m1 (columns
+// 16 ri..16 ri+15), twiddled and packed as fp16 pairs; the warp's 16 values
+// of m1 (128 contiguous bytes of G) are then written by 8 lanes at a time.
+__device__ __forceinline__ void stage1_chunk_t(const uint32_t (&r)[32], uint32_t o, uint32_t rT,
+                                               uint32_t M, void *out, const StageParams &sp,
+                                               uint8_t *xs, int lane) {
+    const uint32_t m1 = o >> 1, ri = o & 1u;
+    // even lane keeps columns 0..15 (needs the odd lane's Im), odd lane 16..31
+    float re[16], im[16];
+#pragma unroll
+    for (int t = 0; t < 16; t++) {
+        const uint32_t send = ri ? r[t] : r[16 + t];
+        const float got = __uint_as_float(__shfl_xor_sync(0xffffffffu, send, 1));
+        re[t] = ri ? got : __uint_as_float(r[t]);
+        im[t] = ri ? __uint_as_float(r[16 + t]) : got;
+    }
+    const uint32_t Q = sp.Q;
+    const uint32_t r1 = rT + 16 * ri;  // first data row of my 16
+    uint32_t k2 = r1 % Q;
+    float2 tw = sp.twiddle[m1 < sp.P ? k2 * m1 : 0];  // e^{2 pi i k2 m1 / H}, k2 m1 < H
+    const float2 w = sp.twiddle[m1 < sp.P ? m1 : 0];  // step of k2 -> k2 + 1
+    uint32_t v[16];
+#pragma unroll
+    for (int t = 0; t < 16; t++) {
+        v[t] = pack_h2(re[t] * tw.x - im[t] * tw.y, re[t] * tw.y + im[t] * tw.x);
+        if (++k2 == Q) {
+            k2 = 0;
+            tw = make_float2(1.0f, 0.0f);
+        } else {
+            const float tx = tw.x * w.x - tw.y * w.y;
+            tw.y = tw.x * w.y + tw.y * w.x;
+            tw.x = tx;
+        }
+    }
+    // stage: row (lane >> 1) = the warp's m1 slot, 128 bytes = 32 complex
+    uint4 *xw = reinterpret_cast<uint4 *>(xs + (lane >> 1) * (2 * XROW) + 64 * ri);
+#pragma unroll
+    for (int t = 0; t < 4; t++) xw[t] = make_uint4(v[4 * t], v[4 * t + 1], v[4 * t + 2], v[4 * t + 3]);
+    __syncwarp();
+    // 16 m1 rows of 128 bytes: lane writes piece (lane & 7) of rows (lane >> 3) + 4 i
+    const uint32_t m1_base = (o - (uint32_t)lane) >> 1;
+    const uint32_t piece = lane & 7;
+    const uint32_t c0 = rT + 4 * piece;  // first data row of the piece (4 complex)
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const uint32_t slot = (uint32_t)(lane >> 3) + 4 * i;
+        const uint32_t mm = m1_base + slot;
+        const uint4 val = *reinterpret_cast<const uint4 *>(xs + slot * (2 * XROW) + 16 * piece);
+        if (mm < sp.P) {
+            uint32_t *g = reinterpret_cast<uint32_t *>(out) + (uint64_t)mm * sp.batch * Q + c0;
+            if (c0 + 4 <= M) {
+                *reinterpret_cast<uint4 *>(g) = val;  // 16-byte aligned (batch Q, c0 % 4 == 0)
+            } else {
+                const uint32_t e[4] = {val.x, val.y, val.z, val.w};
+                for (int t = 0; t < 4; t++)
+                    if (c0 + t < M) g[t] = e[t];
+            }
+        }
+    }
+    __syncwarp();
+}
+
+// Stage 2 chunk: lane o = 2 m2 + ri holds columns rT..rT+31 = rows (m1, b).
+// With batch % 32 == 0 the chunk is one m1 and b0..b0+31: each output row
+// n(j, ri) receives 32 contiguous values, staged as 64-byte rows (two
+// rounds for f32) and written 4 lanes per row.
+template <int DT>
+__device__ __forceinline__ void stage2_chunk_t(const uint32_t (&r)[32], uint32_t o, uint32_t rT,
+                                               uint32_t M, void *out, uint64_t ldo,
+                                               const StageParams &sp, uint8_t *xs, int lane) {
+    const uint32_t batch = (uint32_t)sp.batch, half = sp.H / 2;
+    if (batch % 32 == 0 && sp.vec_out) {
+        if (rT >= M) return;  // warp-uniform
+        const uint32_t m1 = rT / batch, b0 = rT - m1 * batch;
+        const float sc = sp.scale;
+        constexpr int PARTS = DT == HCT_B200_F32 ? 2 : 1;  // 64 bytes of a row per part
+        constexpr int PER = 32 / PARTS;                    // values per part
+        const uint32_t o_base = o - (uint32_t)lane, piece = lane & 3;
+        uint32_t nrow[4];
+        bool ok[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t oo = o_base + (uint32_t)(lane >> 2) + 8 * i, m2 = oo >> 1, ri = oo & 1u;
+            const uint32_t j = m1 + sp.P * m2;
+            ok[i] = m2 < sp.Q;
+            nrow[i] = j < half ? 4 * j + 2 * ri : 4 * (sp.H - 1 - j) + 3 - 2 * ri;
+        }
+#pragma unroll
+        for (int part = 0; part < PARTS; part++) {
+            uint4 *xw = reinterpret_cast<uint4 *>(xs + lane * XROW);
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                uint32_t p[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    if (DT == HCT_B200_F32) {
+                        p[u] = __float_as_uint(__uint_as_float(r[PER * part + 4 * t + u]) * sc);
+                    } else {
+                        const float a = __uint_as_float(r[8 * t + 2 * u]) * sc;
+                        const float b = __uint_as_float(r[8 * t + 2 * u + 1]) * sc;
+                        p[u] = DT == HCT_B200_BF16 ? pack_bf2(a, b) : pack_h2(a, b);
+                    }
+                }
+                xw[t] = make_uint4(p[0], p[1], p[2], p[3]);
+            }
+            __syncwarp();
+            // rows (lane >> 2) + 8 i of the staging, 16-byte piece (lane & 3)
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint32_t row = (uint32_t)(lane >> 2) + 8 * i;
+                const uint4 val = *reinterpret_cast<const uint4 *>(xs + row * XROW + 16 * piece);
+                if (ok[i]) {
+                    if (DT == HCT_B200_F32)
+                        *reinterpret_cast<uint4 *>(reinterpret_cast<float *>(out) +
+                                                   (uint64_t)nrow[i] * ldo + b0 + PER * part +
+                                                   4 * piece) = val;
+                    else
+                        *reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(out) +
+                                                   (uint64_t)nrow[i] * ldo + b0 + 8 * piece) = val;
+                }
+            }
+            __syncwarp();
+        }
+        return;
+    }
+    const uint32_t m2 = o >> 1, ri = o & 1u;
+    if (m2 >= sp.Q) return;
+    for (int t = 0; t < 32; t++) {
+        const uint32_t rr = rT + t;
+        if (rr >= M) break;
+        const uint32_t m1 = rr / batch, b = rr - m1 * batch;
+        const uint32_t j = m1 + sp.P * m2;
+        const uint32_t n = j < half ? 4 * j + 2 * ri : 4 * (sp.H - 1 - j) + 3 - 2 * ri;
+        const float v = __uint_as_float(r[t]) * sp.scale;
+        const uint64_t idx = (uint64_t)n * ldo + b;
+        if (DT == HCT_B200_F32) reinterpret_cast<float *>(out)[idx] = v;
+        else if (DT == HCT_B200_BF16) reinterpret_cast<uint16_t *>(out)[idx] = f2bf(v);
+        else reinterpret_cast<uint16_t *>(out)[idx] = f2h(v);
+    }
+}
+
+template <int MT>
+__global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
+    dft_stage_t_kernel(const __grid_constant__ CUtensorMap tmD,
+                       const __grid_constant__ CUtensorMap tmW, uint32_t M, uint32_t K,
+                       uint32_t m_tiles, void *out, uint64_t ldo, int mode, int out_dtype,
+                       int *flag, const StageParams sp) {
+    using SC = StageTCfg<MT>;
     constexpr int RING = SC::RING;
-    constexpr uint32_t IDESC = Cfg<BN>::IDESC;
+    constexpr int NT = SC::NT;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *w_smem = smem;
-    uint8_t *a_smem = smem + (size_t)SC::KB_MAX * SC::W_KB_BYTES;
-    StageCtl *ctl = reinterpret_cast<StageCtl *>(a_smem + (size_t)RING * A_TILE_BYTES);
+    uint8_t *d_smem = smem + (size_t)SC::KB_MAX * SC::W_KB_BYTES;
+    uint8_t *x_smem = d_smem + (size_t)RING * SC::B_TILE_BYTES;
+    StageCtl *ctl = reinterpret_cast<StageCtl *>(x_smem + SC::X_BYTES);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kbs = (int)((K + BK - 1) / BK);
     const uint32_t my_tiles =
@@ -504,15 +633,15 @@ __global__ void __launch_bounds__(STAGE_THREADS, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA))
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmD))
                          : "memory");
             const uint32_t wb = smem_u32(&ctl->wfull);
             mbar_expect_tx(wb, (uint32_t)(kbs * SC::W_KB_BYTES));
             for (int kb = 0; kb < kbs; kb++)
-                tma_load_2d(smem_u32(w_smem + (size_t)kb * SC::W_KB_BYTES), &tmB, wb, kb * BK, 0);
+                tma_load_2d(smem_u32(w_smem + (size_t)kb * SC::W_KB_BYTES), &tmW, wb, kb * BK, 0);
             int it = 0;
             for (uint32_t i = 0; i < my_tiles; i++) {
-                const int m0 = (int)((blockIdx.x + i * gridDim.x) * BM);
+                const int r0 = (int)((blockIdx.x + i * gridDim.x) * NT);
                 bool stop = false;
                 for (int kb = 0; kb < kbs; kb++, it++) {
                     const int s = it % RING;
@@ -525,8 +654,9 @@ __global__ void __launch_bounds__(STAGE_THREADS, 1)
                         break;
                     }
                     const uint32_t fb = smem_u32(&ctl->full[s]);
-                    mbar_expect_tx(fb, A_TILE_BYTES);
-                    tma_load_2d(smem_u32(a_smem + (size_t)s * A_TILE_BYTES), &tmA, fb, kb * BK, m0);
+                    mbar_expect_tx(fb, SC::B_TILE_BYTES);
+                    tma_load_2d(smem_u32(d_smem + (size_t)s * SC::B_TILE_BYTES), &tmD, fb, kb * BK,
+                                r0);
                     *(volatile int *)&ctl->issued = it + 1;
                 }
                 if (stop) break;
@@ -543,18 +673,24 @@ __global__ void __launch_bounds__(STAGE_THREADS, 1)
                 if (*(volatile int *)&ctl->abort) break;
                 if (!mbar_wait(smem_u32(&ctl->tempty[buf]), (use & 1u) ^ 1u)) { ok = false; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t d = tmem + (uint32_t)(buf * BN);
+                const uint32_t d = tmem + (uint32_t)(buf * MT * NT);
                 for (int kb = 0; kb < kbs; kb++, it++) {
                     const int s = it % RING;
                     const uint32_t ph = (uint32_t)(it / RING) & 1u;
                     if (!mbar_wait(smem_u32(&ctl->full[s]), ph)) { ok = false; break; }
                     *(volatile int *)&ctl->consumed = it + 1;
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint64_t da = umma_desc_sw128(smem_u32(a_smem + (size_t)s * A_TILE_BYTES));
-                    const uint64_t db = umma_desc_sw128(smem_u32(w_smem + (size_t)kb * SC::W_KB_BYTES));
+                    const uint64_t db = umma_desc_sw128(smem_u32(d_smem + (size_t)s * SC::B_TILE_BYTES));
 #pragma unroll
-                    for (int k = 0; k < BK / 16; k++)
-                        umma_f16(d, da + 2 * k, db + 2 * k, IDESC, (kb | k) != 0);
+                    for (int hh = 0; hh < MT; hh++) {
+                        // rows 128 hh.. of the k-block: 16 core groups of 1 KB further
+                        const uint64_t da = umma_desc_sw128(
+                            smem_u32(w_smem + (size_t)kb * SC::W_KB_BYTES + (size_t)hh * 128 * 128));
+#pragma unroll
+                        for (int k = 0; k < BK / 16; k++)
+                            umma_f16(d + (uint32_t)(hh * NT), da + 2 * k, db + 2 * k, SC::IDESC,
+                                     (kb | k) != 0);
+                    }
                     umma_commit(smem_u32(&ctl->empty[s]));
                 }
                 if (!ok) break;
@@ -567,9 +703,14 @@ __global__ void __launch_bounds__(STAGE_THREADS, 1)
             umma_commit(smem_u32(&ctl->drain));  // arrives once every MMA above retired
         }
     } else {
-        // 8 epilogue warps: TMEM lane quarter q = warp % 4, column-chunk parity h
+        // 8 epilogue warps: TMEM lane quarter q = warp % 4; h = column half
+        // (MT = 1) or W half (MT = 2)
         const int q = warp & 3;
         const int h = (warp - 2) >> 2;
+        const int hh = MT == 2 ? h : 0;
+        const int c_begin = MT == 2 ? 0 : 64 * h, c_end = MT == 2 ? NT : 64 * h + 64;
+        const uint32_t o = (uint32_t)(128 * hh + 32 * q + lane);  // my DFT output
+        uint8_t *xs = x_smem + (warp - 2) * XWARP_BYTES;
         for (uint32_t i = 0; i < my_tiles; i++) {
             const int buf = (int)(i & 1u);
             const uint32_t use = i >> 1;
@@ -579,34 +720,20 @@ __global__ void __launch_bounds__(STAGE_THREADS, 1)
                 break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t rowi = (blockIdx.x + i * gridDim.x) * BM + q * 32 + lane;
-            const bool valid = rowi < M;
-            const uint32_t taddr = tmem + (uint32_t)(buf * BN) + ((uint32_t)(q * 32) << 16);
-            if (mode == 2) {
-                const uint32_t b = rowi / sp.Q, k2 = rowi - b * sp.Q;
-                uint32_t *g = reinterpret_cast<uint32_t *>(out) + (uint64_t)b * sp.Q + k2;
-                const uint64_t stride = sp.batch * sp.Q;
-                const float2 w = valid ? sp.twiddle[k2] : make_float2(1.f, 0.f);
-                for (int c = 32 * h; c < (int)N; c += 64) {
-                    uint32_t r[32];
-                    tmem_ld32(taddr + (uint32_t)c, r);
-                    const uint32_t m1_0 = (uint32_t)c >> 1;
-                    if (valid && m1_0 < sp.P)
-                        stage1_chunk(r, g, stride, m1_0, sp.P, sp.twiddle[k2 * m1_0], w);
-                }
-            } else {
-                const uint32_t m1 = rowi / (uint32_t)sp.batch, b = rowi - m1 * (uint32_t)sp.batch;
-                for (int c = 32 * h; c < (int)N; c += 64) {
-                    uint32_t r[32];
-                    tmem_ld32(taddr + (uint32_t)c, r);
-                    if (!valid) continue;
-                    const uint32_t m2_0 = (uint32_t)c >> 1;
-                    if (out_dtype == HCT_B200_F16)
-                        stage2_chunk<HCT_B200_F16>(r, out, ldo, b, m1, m2_0, sp);
-                    else if (out_dtype == HCT_B200_BF16)
-                        stage2_chunk<HCT_B200_BF16>(r, out, ldo, b, m1, m2_0, sp);
-                    else
-                        stage2_chunk<HCT_B200_F32>(r, out, ldo, b, m1, m2_0, sp);
+            const uint32_t r0 = (blockIdx.x + i * gridDim.x) * NT;
+            const uint32_t taddr =
+                tmem + (uint32_t)(buf * MT * NT + hh * NT) + ((uint32_t)(q * 32) << 16);
+            for (int c = c_begin; c < c_end; c += 32) {
+                uint32_t r[32];
+                tmem_ld32(taddr + (uint32_t)c, r);
+                if (mode == 2) {
+                    stage1_chunk_t(r, o, r0 + c, M, out, sp, xs, lane);
+                } else if (out_dtype == HCT_B200_F16) {
+                    stage2_chunk_t<HCT_B200_F16>(r, o, r0 + c, M, out, ldo, sp, xs, lane);
+                } else if (out_dtype == HCT_B200_BF16) {
+                    stage2_chunk_t<HCT_B200_BF16>(r, o, r0 + c, M, out, ldo, sp, xs, lane);
+                } else {
+                    stage2_chunk_t<HCT_B200_F32>(r, o, r0 + c, M, out, ldo, sp, xs, lane);
                 }
             }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -740,25 +867,28 @@ int sm_count() {
     return n;
 }
 
-template <int BN>
-cudaError_t launch_stage(const GemmArgs &a, cudaStream_t s) {
-    using SC = StageCfg<BN>;
-    if (a.K > (uint64_t)SC::KB_MAX * BK || a.N > (uint64_t)BN) return cudaErrorInvalidValue;
-    alignas(64) CUtensorMap ta, tb;
-    if (!make_operand_map(&ta, a.A, a.M, a.K, a.lda, BM)) return cudaErrorInvalidValue;
-    if (!make_operand_map(&tb, a.B, a.N, a.K, a.ldb, BN)) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(dft_stage_kernel<BN>,
+template <int MT>
+cudaError_t launch_stage_t(const GemmArgs &a, cudaStream_t s) {
+    using SC = StageTCfg<MT>;
+    if (a.K > (uint64_t)SC::KB_MAX * BK || a.N > (uint64_t)SC::WROWS) return cudaErrorInvalidValue;
+    alignas(64) CUtensorMap td, tw;
+    if (!make_operand_map(&td, a.A, a.M, a.K, a.lda, SC::NT)) return cudaErrorInvalidValue;
+    if (!make_operand_map(&tw, a.B, a.N, a.K, a.ldb, SC::WROWS)) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(dft_stage_t_kernel<MT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)SC::SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    const uint64_t m_tiles = (a.M + BM - 1) / BM;
+    const uint64_t m_tiles = (a.M + SC::NT - 1) / SC::NT;
     if (m_tiles > 0x7fffffffull) return cudaErrorInvalidValue;
-    const uint64_t per_sm = BN == 128 ? 2 : 1;  // shared memory and TMEM allow two 128-wide CTAs
+    const uint64_t per_sm = MT == 1 ? 2 : 1;  // shared memory and TMEM
     const uint32_t grid = (uint32_t)std::min<uint64_t>(m_tiles, per_sm * (uint64_t)sm_count());
-    StageParams sp{a.P, a.Q, a.H, 0, a.batch, reinterpret_cast<const float2 *>(a.twiddle), a.scale};
-    dft_stage_kernel<BN><<<grid, STAGE_THREADS, SC::SMEM_BYTES, s>>>(
-        ta, tb, (uint32_t)a.M, (uint32_t)a.N, (uint32_t)a.K, (uint32_t)m_tiles, a.out, a.ldo,
-        a.mode, a.out_dtype, a.d_flag, sp);
+    // 16-byte output runs need an aligned base and row stride (stage 2)
+    const uint32_t vec = ((uintptr_t)a.out % 16 == 0) && (a.ldo % 8 == 0);
+    StageParams sp{a.P, a.Q, a.H, vec, a.batch, reinterpret_cast<const float2 *>(a.twiddle),
+                   a.scale};
+    dft_stage_t_kernel<MT><<<grid, STAGE_THREADS, SC::SMEM_BYTES, s>>>(
+        td, tw, (uint32_t)a.M, (uint32_t)a.K, (uint32_t)m_tiles, a.out, a.ldo, a.mode,
+        a.out_dtype, a.d_flag, sp);
     return cudaGetLastError();
 }
 
@@ -773,8 +903,8 @@ cudaError_t launch_umma_gemm(const GemmArgs &a, cudaStream_t s) {
                                          (a.mode == 2 && !a.twiddle)))
         return cudaErrorInvalidValue;
     if (a.mode == 2 || a.mode == 3) {
-        if (a.N <= 128 && a.K <= 128) return launch_stage<128>(a, s);
-        return launch_stage<256>(a, s);
+        if (a.N <= 128 && a.K <= 128) return launch_stage_t<1>(a, s);
+        return launch_stage_t<2>(a, s);
     }
     if (a.N <= 128) return launch_bn<128>(a, s);
     return launch_bn<256>(a, s);
