@@ -166,11 +166,11 @@ def set_profiling(ctx, on: bool):
 
 KERNEL_NAMES = {  # profile record -> kernel
     "lz4_decode_blocks": "hct::lz4_decode_blocks_kernel",
-    "spectral_rank": "hct::chunk_popcount_kernel + hct::chunk_scan_kernel",
+    "spectral_rank": "hct::chunk_rank_kernel + hct::chunk_scan_kernel",
     "spectral_pack": "hct::spectral_pack_kernel (bitmap/INT4 decode + Makhoul pack, row axis)",
     "makhoul_pack": "hct::makhoul_pack_kernel (Makhoul pack, column axis)",
-    "dft_stage1": "hct::dft_stage_kernel<256> mode 2 (tcgen05 DFT over k1, twiddled)",
-    "dft_stage2": "hct::dft_stage_kernel<128> mode 3 (tcgen05 DFT over k2, quartet store)",
+    "dft_stage1": "hct::dft_stage_t_kernel mode 2 (tcgen05 DFT over k1, twiddled)",
+    "dft_stage2": "hct::dft_stage_t_kernel mode 3 (tcgen05 DFT over k2, quartet store)",
     "umma_gemm": "hct::umma_gemm_kernel (dense-basis tcgen05 IDCT contraction)",
     "spectral_scatter": "hct::chunk_scan_kernel + hct::spectral_scatter_kernel",
     "dequant_int4": "hct::dequant_int4_kernel",
