@@ -65,6 +65,54 @@ __device__ __forceinline__ uint32_t pack_z(float re, float im) {
 // srow[pad_idx(L)] must hold zero: it is c[L] of the k = 0 term.  Along a
 // lane's k1 = l, l + 32, ... every index moves by a constant (32 Q is a
 // multiple of 64, so pad_idx(k + 32 Q) = pad_idx(k) + 33 Q).
+// The same pack for NR rows staged sstride halves apart (outputs ostride
+// words apart, the first nvalid of them written): the coefficient loads and
+// the index arithmetic are shared by the rows.
+template <int NR>
+__device__ __forceinline__ void pack_rows(const uint16_t *srow, uint32_t sstride,
+                                          const float4 *__restrict__ coefT, uint32_t L, uint32_t P,
+                                          uint32_t Q, uint32_t *__restrict__ orow, uint64_t ostride,
+                                          uint32_t nvalid) {
+    const uint32_t H = L / 2;
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    const uint32_t sstep = 33 * Q;
+    for (uint32_t k2 = warp; 2 * k2 <= Q; k2 += nwarps) {
+        const uint32_t k1_end = k2 == 0 ? P / 2 + 1 : (2 * k2 == Q ? P / 2 : P);
+        const uint32_t k = Q * lane + k2;
+        uint32_t ia = pad_idx(k), ib = pad_idx(L - k), ic = pad_idx(H + k), id = pad_idx(H - k);
+        uint32_t io = k2 * P + lane;
+        uint32_t jo = k2 == 0 ? P - lane : (Q - k2) * P + (P - 1 - lane);
+        for (uint32_t k1 = lane; k1 < k1_end; k1 += 32) {
+            const float4 t = coefT[io];  // (alpha.re, alpha.im, beta.re, beta.im)
+            const bool partner = k2 != 0 || (k1 != 0 && 2 * k1 != P);  // k != 0 and k != H/2
+            const float4 u = partner ? coefT[jo] : t;
+#pragma unroll
+            for (int q = 0; q < NR; q++) {
+                const uint16_t *sr = srow + q * sstride;
+                const float ck = h2f(sr[ia]);
+                const float cLk = h2f(sr[ib]);
+                const float cHk = h2f(sr[ic]);
+                const float cHmk = h2f(sr[id]);  // H - k >= 1 for k < H
+                const float zr = fmaf(t.x, ck, fmaf(t.y, cLk, fmaf(t.z, cHk, t.w * cHmk)));
+                const float zi = fmaf(t.y, ck, fmaf(-t.x, cLk, fmaf(t.w, cHk, -t.z * cHmk)));
+                if ((uint32_t)q < nvalid) orow[q * ostride + io] = pack_z(zr, zi);
+                if (partner && (uint32_t)q < nvalid) {
+                    // k' = H - k: c[k'] = c[H-k], c[L-k'] = c[H+k], c[H+k'] = c[L-k], c[H-k'] = c[k]
+                    const float yr = fmaf(u.x, cHmk, fmaf(u.y, cHk, fmaf(u.z, cLk, u.w * ck)));
+                    const float yi = fmaf(u.y, cHmk, fmaf(-u.x, cHk, fmaf(u.w, cLk, -u.z * ck)));
+                    orow[q * ostride + jo] = pack_z(yr, yi);
+                }
+            }
+            ia += sstep;
+            ib -= sstep;
+            ic += sstep;
+            id -= sstep;
+            io += 32;
+            jo -= 32;
+        }
+    }
+}
+
 __device__ __forceinline__ void pack_row(const uint16_t *srow, const float4 *__restrict__ coefT,
                                          uint32_t L, uint32_t P, uint32_t Q,
                                          uint32_t *__restrict__ orow) {
@@ -103,47 +151,55 @@ __device__ __forceinline__ void pack_row(const uint16_t *srow, const float4 *__r
     }
 }
 
-// Pack of dense fp16 rows (stride ld_in): one CTA per row, the row staged in
-// shared memory with up to 4 independent 16-byte loads in flight per thread.
-// THREADS = 256 with 5 CTAs per SM for rows up to 16384 elements, 512 with 2
-// beyond (the staged row then takes up to 57 KB).
-template <int THREADS, int MIN_CTAS>
+// Pack of dense fp16 rows (stride ld_in): one CTA per NR rows (sharing the
+// coefficient loads and index arithmetic), the rows staged in shared memory
+// with up to 4 independent 16-byte loads in flight per thread and row.
+// THREADS = 256, NR = 2 with 4 CTAs per SM for rows up to 16384 elements;
+// THREADS = 512, NR = 1 with 2 beyond (a staged row then takes up to 57 KB).
+template <int THREADS, int MIN_CTAS, int NR>
 __global__ void __launch_bounds__(THREADS, MIN_CTAS) makhoul_pack_kernel(
     const uint16_t *__restrict__ in, uint64_t ld_in, uint64_t B, uint32_t L, uint32_t P,
     uint32_t Q, const float4 *__restrict__ coefT, uint32_t *__restrict__ out) {
     extern __shared__ uint16_t srow[];
+    const uint32_t sstride = srow_halves(L);
     const bool vec = ((ld_in & 7) == 0) && (((uintptr_t)in & 15) == 0) && ((L & 7) == 0);
     const uint32_t nv = L / 8;
-    if (threadIdx.x == 0) srow[pad_idx(L)] = 0;  // c[L] = 0 (never overwritten)
-    for (uint64_t b = blockIdx.x; b < B; b += gridDim.x) {
-        const uint16_t *row = in + b * ld_in;
-        __syncthreads();  // previous row fully consumed
-        if (vec) {
-            const uint4 *r4 = reinterpret_cast<const uint4 *>(row);
-            for (uint32_t v0 = threadIdx.x; v0 < nv; v0 += 4 * THREADS) {
-                uint4 x[4];
+    if (threadIdx.x < NR) srow[threadIdx.x * sstride + pad_idx(L)] = 0;  // c[L] = 0
+    for (uint64_t b = (uint64_t)blockIdx.x * NR; b < B; b += (uint64_t)gridDim.x * NR) {
+        const uint32_t nvalid = (uint32_t)(B - b < (uint64_t)NR ? B - b : (uint64_t)NR);
+        __syncthreads();  // previous rows fully consumed
 #pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const uint32_t v = v0 + u * THREADS;
-                    if (v < nv) x[u] = __ldg(r4 + v);
-                }
+        for (int q = 0; q < NR; q++) {
+            if ((uint32_t)q >= nvalid) break;
+            const uint16_t *row = in + (b + q) * ld_in;
+            uint16_t *sr = srow + q * sstride;
+            if (vec) {
+                const uint4 *r4 = reinterpret_cast<const uint4 *>(row);
+                for (uint32_t v0 = threadIdx.x; v0 < nv; v0 += 4 * THREADS) {
+                    uint4 x[4];
 #pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const uint32_t v = v0 + u * THREADS;
-                    if (v < nv) {  // 8 elements never straddle a 64-element pad
-                        uint32_t *d = reinterpret_cast<uint32_t *>(srow + pad_idx(8 * v));
-                        d[0] = x[u].x;
-                        d[1] = x[u].y;
-                        d[2] = x[u].z;
-                        d[3] = x[u].w;
+                    for (int u = 0; u < 4; u++) {
+                        const uint32_t v = v0 + u * THREADS;
+                        if (v < nv) x[u] = __ldg(r4 + v);
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const uint32_t v = v0 + u * THREADS;
+                        if (v < nv) {  // 8 elements never straddle a 64-element pad
+                            uint32_t *d = reinterpret_cast<uint32_t *>(sr + pad_idx(8 * v));
+                            d[0] = x[u].x;
+                            d[1] = x[u].y;
+                            d[2] = x[u].z;
+                            d[3] = x[u].w;
+                        }
                     }
                 }
+            } else {
+                for (uint32_t k = threadIdx.x; k < L; k += THREADS) sr[pad_idx(k)] = row[k];
             }
-        } else {
-            for (uint32_t k = threadIdx.x; k < L; k += THREADS) srow[pad_idx(k)] = row[k];
         }
         __syncthreads();
-        pack_row(srow, coefT, L, P, Q, out + b * (uint64_t)(L / 2));
+        pack_rows<NR>(srow, sstride, coefT, L, P, Q, out + b * (uint64_t)(L / 2), L / 2, nvalid);
     }
 }
 
@@ -402,15 +458,16 @@ bool fdct_factor(uint64_t L, uint32_t *P, uint32_t *Q) {
 cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t B, uint32_t L,
                                 uint32_t P, uint32_t Q, const float *d_tables, half_bits *d_out,
                                 cudaStream_t s) {
-    const size_t smem = (size_t)srow_halves(L) * 2;
-    if (smem > 220 * 1024) return cudaErrorInvalidValue;
     const bool small = L <= 16384;
-    auto kern = small ? makhoul_pack_kernel<256, 5> : makhoul_pack_kernel<512, 2>;
+    const size_t smem = (size_t)srow_halves(L) * 2 * (small ? 2 : 1);
+    if (smem > 220 * 1024) return cudaErrorInvalidValue;
+    auto kern = small ? makhoul_pack_kernel<256, 4, 2> : makhoul_pack_kernel<512, 2, 1>;
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    const uint64_t per_sm = small ? 5 : 2;
-    uint64_t g = B < 148ull * per_sm ? B : 148ull * per_sm;
+    const uint64_t per_sm = small ? 4 : 2;
+    const uint64_t units = small ? (B + 1) / 2 : B;  // row pairs or rows
+    uint64_t g = units < 148ull * per_sm ? units : 148ull * per_sm;
     if (g < 1) g = 1;
     kern<<<(unsigned)g, small ? 256 : 512, smem, s>>>(d_in, ld_in, B, L, P, Q,
                                                       reinterpret_cast<const float4 *>(d_tables),
