@@ -7,7 +7,9 @@ CUDA library (libhct_b200.so) through its C ABI:
   surface (crates/haagenti-lz4/src/decompress.rs:28-73), decoded on the GPU,
   plus a batched ``decompress_blocks`` for many independent blocks.
 * ``dequantize_int4`` -- haagenti::testing::dequantize_int4
-  (crates/haagenti/src/testing/quantization.rs:82-131).
+  (crates/haagenti/src/testing/quantization.rs:82-131); ``dequantize_int4_mp``
+  -- the mixed-precision pair's zero-filling form (crates/haagenti/src/
+  mixed_precision.rs:489-539).
 * ``idct_2d`` -- haagenti_core::dct::idct_2d (crates/haagenti-core/src/dct.rs:311-337).
 * ``HctReader`` / ``HctReaderV2`` -- crates/haagenti-hct/src/tensor.rs:408-516,
   832-1021, with ``decompress_all`` on the GPU and ``decode`` for the full
@@ -30,7 +32,8 @@ IDCT_AUTO, IDCT_DENSE = 0, 1
 
 __all__ = [
     "HaagentiError", "CorruptedData", "BufferTooSmall", "UnexpectedEof", "ChecksumMismatch",
-    "Unsupported", "DeviceError", "Context", "Lz4Decompressor", "dequantize_int4", "idct_2d",
+    "Unsupported", "DeviceError", "Context", "Lz4Decompressor", "dequantize_int4",
+    "dequantize_int4_mp", "idct_2d",
     "spectral_q4_decode", "HctReader", "HctReaderV2", "F32", "F16", "BF16", "FLAG_SPECTRAL_Q4",
 ]
 
@@ -252,6 +255,22 @@ def dequantize_int4(data, num_elements: int, out_dtype: int = F32, device=None, 
     _check(L.load().hct_b200_dequantize_int4(data.data_ptr(), data.numel(), num_elements,
                                              out.data_ptr(), out_dtype, C.byref(written),
                                              _stream_ptr(stream)))
+    return out[: written.value]
+
+
+def dequantize_int4_mp(data, num_elements: int, out_dtype: int = F32, device=None, stream=None):
+    """mixed_precision.rs:489-539 on the GPU: ``num_elements`` values, zero where
+    the data runs short (an empty tensor for ``num_elements == 0`` or empty data)."""
+    torch = _torch()
+    if not (hasattr(data, "is_cuda") and data.is_cuda):
+        host = _as_host_u8(data)
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        data = torch.from_numpy(host.copy()).to(dev)
+    out = torch.empty(max(num_elements, 1), dtype=_torch_dtype(out_dtype), device=data.device)
+    written = C.c_size_t(0)
+    _check(L.load().hct_b200_dequantize_int4_mp(data.data_ptr(), data.numel(), num_elements,
+                                                out.data_ptr(), out_dtype, C.byref(written),
+                                                _stream_ptr(stream)))
     return out[: written.value]
 
 

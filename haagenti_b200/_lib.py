@@ -77,6 +77,7 @@ SIGNATURES = {
     "hct_b200_lz4_compress_chunks": (C.c_int, [_u8p, _sz, _sz, _u8p, _sz,
                                                C.POINTER(C.c_uint32)]),
     "hct_b200_quantize_int4": (C.c_int, [_vp, _sz, _u8p]),
+    "hct_b200_quantize_int4_mp": (C.c_int, [_vp, _sz, _u8p]),
     "hct_b200_spectral_select": (C.c_int, [_vp, _sz, _sz, _u8p, _vp, C.POINTER(C.c_size_t)]),
     "hct_b200_lz4_decompress_blocks": (C.c_int, [_vp, _vp, C.c_uint32, _vp, _vp, C.c_uint64,
                                                  _vp]),
@@ -86,6 +87,8 @@ SIGNATURES = {
                                              C.POINTER(C.c_size_t), C.POINTER(Error)]),
     "hct_b200_dequantize_int4": (C.c_int, [_vp, _sz, _sz, _vp, C.c_int,
                                            C.POINTER(C.c_size_t), _vp]),
+    "hct_b200_dequantize_int4_mp": (C.c_int, [_vp, _sz, _sz, _vp, C.c_int,
+                                              C.POINTER(C.c_size_t), _vp]),
     "hct_b200_idct_2d": (C.c_int, [_vp, _vp, _vp, C.c_int, _sz, _sz, _vp]),
     "hct_b200_spectral_q4_decode": (C.c_int, [_vp, _vp, _sz, _sz, _sz, _vp, C.c_int, _vp]),
     "hct_b200_spectral_q4_decode_noalloc": (C.c_int, [_vp, _sz, _sz, _sz, _vp, C.c_int, _vp]),

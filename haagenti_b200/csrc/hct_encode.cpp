@@ -8,10 +8,12 @@
 // HctWriter::compress_data does (crates/haagenti-hct/src/tensor.rs:556-562).
 // The reference clears its hash table per call; a generation tag per entry
 // gives identical lookups without re-zeroing 512 KiB per 16 KiB block.
-#include <cstdint>
-#include <cstring>
+#include <cuda_fp16.h>
+
 #include <algorithm>
 #include <cmath>
+#include <cstdint>
+#include <cstring>
 #include <vector>
 
 #include "../../include/hct_b200.h"
@@ -145,10 +147,12 @@ inline uint32_t mag_bits(float v) {
 
 }  // namespace
 
-extern "C" {
+namespace {
 
-// quantization.rs:30-70 (one OpenMP task per 32-element block).
-int hct_b200_quantize_int4(const float *w, size_t n, uint8_t *out) {
+// quantization.rs:30-70 (one OpenMP task per 32-element block), the scale
+// stored through ScaleBits.
+template <uint16_t (*ScaleBits)(float)>
+int quantize_int4_impl(const float *w, size_t n, uint8_t *out) {
     if (n == 0) return HCT_B200_OK;
     if (!w || !out) return HCT_B200_ERR_INVALID_ARGUMENT;
     const size_t nb = (n + 31) / 32;
@@ -159,7 +163,7 @@ int hct_b200_quantize_int4(const float *w, size_t n, uint8_t *out) {
         float max_abs = 0.0f;
         for (size_t i = s; i < e; i++) max_abs = std::fmax(max_abs, std::fabs(w[i]));
         const float scale = max_abs > 1e-10f ? max_abs / 7.0f : 1.0f;
-        const uint16_t h = f32_to_f16_trunc(scale);
+        const uint16_t h = ScaleBits(scale);
         out[2 * b] = (uint8_t)(h & 0xff);
         out[2 * b + 1] = (uint8_t)(h >> 8);
         // a 32-element block spans 16 whole nibble bytes, so threads never share a byte
@@ -172,6 +176,23 @@ int hct_b200_quantize_int4(const float *w, size_t n, uint8_t *out) {
         }
     }
     return HCT_B200_OK;
+}
+
+// half::f16::from_f32 (round-to-nearest-even), as mixed_precision.rs:463
+uint16_t f32_to_f16_rne(float v) { return __half_as_ushort(__float2half_rn(v)); }
+
+}  // namespace
+
+extern "C" {
+
+// quantization.rs:30-70: truncating, flush-to-zero f16 scales.
+int hct_b200_quantize_int4(const float *w, size_t n, uint8_t *out) {
+    return quantize_int4_impl<f32_to_f16_trunc>(w, n, out);
+}
+
+// mixed_precision.rs:448-486: the same blocks with round-to-nearest-even scales.
+int hct_b200_quantize_int4_mp(const float *w, size_t n, uint8_t *out) {
+    return quantize_int4_impl<f32_to_f16_rne>(w, n, out);
 }
 
 // compressive.rs:140-172: keep the k largest |c| (ties to the lower index),

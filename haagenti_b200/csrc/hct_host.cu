@@ -715,6 +715,31 @@ int hct_b200_dequantize_int4(const uint8_t *d_data, size_t data_len, size_t num_
     return HCT_B200_OK;
 }
 
+int hct_b200_dequantize_int4_mp(const uint8_t *d_data, size_t data_len, size_t num_elements,
+                                void *d_out, int out_dtype, size_t *written, void *stream) {
+    if (!written) return HCT_B200_ERR_INVALID_ARGUMENT;
+    *written = 0;
+    if (out_dtype < HCT_B200_F32 || out_dtype > HCT_B200_BF16) return HCT_B200_ERR_INVALID_ARGUMENT;
+    if (num_elements == 0 || data_len == 0) return HCT_B200_OK;  // mixed_precision.rs:490-492
+    if (!d_data || !d_out) return HCT_B200_ERR_INVALID_ARGUMENT;
+    const cudaStream_t s = (cudaStream_t)stream;
+    const size_t esz = out_dtype == HCT_B200_F32 ? 4 : 2;
+    const size_t nb = (num_elements + 31) / 32, sb = nb * 2;
+    // all zero when the scales do not fit (:497-499), zero past the nibbles (:510-514)
+    const size_t n = data_len < sb ? 0 : std::min<size_t>(num_elements, 2 * (data_len - sb));
+    if (n) {
+        cudaError_t e = launch_dequant_int4(d_data, data_len, n, num_elements, d_out, out_dtype, s);
+        if (e != cudaSuccess) return cuda_code(e);
+    }
+    if (n < num_elements) {
+        cudaError_t e = cudaMemsetAsync(static_cast<uint8_t *>(d_out) + n * esz, 0,
+                                        (num_elements - n) * esz, s);
+        if (e != cudaSuccess) return cuda_code(e);
+    }
+    *written = num_elements;
+    return HCT_B200_OK;
+}
+
 int hct_b200_idct_2d(hct_b200_ctx *ctx, const float *d_in, void *d_out, int out_dtype,
                      size_t width, size_t height, void *stream) {
     if (!ctx || !d_in || !d_out) return HCT_B200_ERR_INVALID_ARGUMENT;

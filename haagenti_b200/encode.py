@@ -71,6 +71,18 @@ def quantize_int4(weights) -> np.ndarray:
     return out[: int4_compressed_size(w.size)]
 
 
+def quantize_int4_mp(weights) -> np.ndarray:
+    """mixed_precision.rs:448-486 (round-to-nearest-even f16 scales) via
+    hct_b200_quantize_int4_mp."""
+    w = np.ascontiguousarray(weights, np.float32).reshape(-1)
+    out = np.zeros(max(int4_compressed_size(w.size), 1), np.uint8)
+    if w.size:
+        rc = L.load().hct_b200_quantize_int4_mp(w.ctypes.data, w.size, out.ctypes.data)
+        if rc:
+            raise RuntimeError(f"quantize_int4_mp failed: {rc}")
+    return out[: int4_compressed_size(w.size)]
+
+
 def retain_count(n: int, ratio: float) -> int:
     p = np.float32(n) * np.float32(ratio)
     return max(int(p) if p > 0 else 0, 1)

@@ -188,6 +188,9 @@ int hct_b200_lz4_compress_chunks(const uint8_t *in, size_t in_len, size_t block_
 /* quantize_int4 (crates/haagenti/src/testing/quantization.rs:30-70): `out`
  * holds ceil(n/32)*2 + ceil(n/2) bytes (scales first, low nibble first). */
 int hct_b200_quantize_int4(const float *w, size_t n, uint8_t *out);
+/* mixed_precision.rs:448-486: the same layout with each scale stored as the
+ * round-to-nearest-even f16 (half::f16::from_f32). */
+int hct_b200_quantize_int4_mp(const float *w, size_t n, uint8_t *out);
 /* Retention step of CompressiveSpectralEncoder::encode_2d (crates/haagenti/src/
  * compressive.rs:140-172): the k largest |c| (ties to the lower index) as an
  * LSB-first bitmap of ceil(n/8) bytes and their values in index order. */
@@ -203,6 +206,13 @@ int hct_b200_spectral_select(const float *coeffs, size_t n, size_t k, uint8_t *b
  * F16/BF16 outputs are the round-to-nearest-even of that f32 value. */
 int hct_b200_dequantize_int4(const uint8_t *d_data, size_t data_len, size_t num_elements,
                              void *d_out, int out_dtype, size_t *written, void *stream);
+/* The private INT4 pair of haagenti::mixed_precision (crates/haagenti/src/
+ * mixed_precision.rs:489-539): the same values, but always num_elements of
+ * them -- all zero when the scales do not fit, zero past the end of the
+ * nibbles -- and nothing for num_elements == 0 or empty data
+ * (*written = 0). */
+int hct_b200_dequantize_int4_mp(const uint8_t *d_data, size_t data_len, size_t num_elements,
+                                void *d_out, int out_dtype, size_t *written, void *stream);
 
 /* ---- IDCT ---------------------------------------------------------------
  * haagenti_core::dct::idct_2d (crates/haagenti-core/src/dct.rs:311-337) and

@@ -73,6 +73,12 @@ def _load() -> C.CDLL:
     lib.orc_quantize_int4.argtypes = [f32p, sz, u8p]
     lib.orc_dequantize_int4.restype = sz
     lib.orc_dequantize_int4.argtypes = [u8p, sz, sz, f32p]
+    lib.orc_f32_to_f16_rne.restype = C.c_uint16
+    lib.orc_f32_to_f16_rne.argtypes = [C.c_float]
+    lib.orc_quantize_int4_mp.restype = None
+    lib.orc_quantize_int4_mp.argtypes = [f32p, sz, u8p]
+    lib.orc_dequantize_int4_mp.restype = sz
+    lib.orc_dequantize_int4_mp.argtypes = [u8p, sz, sz, f32p]
     for name in ("orc_dct_1d", "orc_idct_1d"):
         getattr(lib, name).restype = None
         getattr(lib, name).argtypes = [f32p, f32p, sz]
@@ -238,6 +244,29 @@ def dequantize_int4(data, num_elements: int) -> np.ndarray:
     src = _as_u8(data)
     out = np.zeros(max(num_elements, 1), dtype=np.float32)
     n = lib().orc_dequantize_int4(_u8(src) if src.size else None, src.size, num_elements, _f32(out))
+    return out[:n]
+
+
+def f32_to_f16_rne(x: float) -> int:
+    """half::f16::from_f32 bits (IEEE round-to-nearest-even)."""
+    return int(lib().orc_f32_to_f16_rne(float(x)))
+
+
+def quantize_int4_mp(weights) -> bytes:
+    """mixed_precision.rs:448-486 (scales as round-to-nearest-even f16)."""
+    w = np.ascontiguousarray(weights, dtype=np.float32).reshape(-1)
+    out = np.zeros(max(int4_compressed_size(w.size), 1), dtype=np.uint8)
+    if w.size:
+        lib().orc_quantize_int4_mp(_f32(w), w.size, _u8(out))
+    return out[: int4_compressed_size(w.size)].tobytes()
+
+
+def dequantize_int4_mp(data, num_elements: int) -> np.ndarray:
+    """mixed_precision.rs:489-539 (n values, zero-filled when the data is short)."""
+    src = _as_u8(data)
+    out = np.zeros(max(num_elements, 1), dtype=np.float32)
+    n = lib().orc_dequantize_int4_mp(_u8(src) if src.size else None, src.size, num_elements,
+                                     _f32(out))
     return out[:n]
 
 

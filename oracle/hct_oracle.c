@@ -393,6 +393,85 @@ size_t orc_dequantize_int4(const uint8_t *data, size_t len, size_t n, float *out
     return w;
 }
 
+/* f32 -> f16 with IEEE round-to-nearest-even, subnormals and overflow to
+ * infinity: the conversion of half 2.7.1's f16::from_f32 that
+ * mixed_precision.rs:463 stores its scales with (infinity and NaN map to
+ * the f16 infinity / a quiet NaN). */
+uint16_t orc_f32_to_f16_rne(float val) {
+    uint32_t bits;
+    memcpy(&bits, &val, 4);
+    const uint32_t sign = (bits >> 16) & 0x8000u;
+    const int32_t exp = (int32_t)((bits >> 23) & 0xff);
+    const uint32_t mant = bits & 0x7fffffu;
+    if (exp == 0xff) return (uint16_t)(sign | 0x7c00u | (mant ? 0x200u : 0u));
+    const int32_t e = exp - 127;
+    if (e > 15) return (uint16_t)(sign | 0x7c00u);
+    if (e >= -14) {  /* normal half: keep 10 mantissa bits, round the other 13 */
+        uint32_t h = ((uint32_t)(e + 15) << 10) | (mant >> 13);
+        const uint32_t rest = mant & 0x1fffu;
+        if (rest > 0x1000u || (rest == 0x1000u && (h & 1u))) h++;  /* may carry to inf */
+        return (uint16_t)(sign | h);
+    }
+    if (exp == 0) return (uint16_t)sign;  /* f32 zero or subnormal: far below 2^-25 */
+    /* subnormal half: units of 2^-24; value = m * 2^(e-23), m with the implicit 1 */
+    const uint32_t m = mant | 0x800000u;
+    const int32_t sh = -(e + 1); /* >= 14 */
+    if (sh > 24) return (uint16_t)sign;
+    uint32_t h = m >> sh;
+    const uint32_t rest = m & ((1u << sh) - 1u), halfway = 1u << (sh - 1);
+    if (rest > halfway || (rest == halfway && (h & 1u))) h++;
+    return (uint16_t)(sign | h);
+}
+
+/* mixed_precision.rs:448-486: the quantize_int4 of quantization.rs:30-70
+ * with the scale stored as the round-to-nearest-even f16.  `out` must hold
+ * orc_int4_compressed_size(n). */
+void orc_quantize_int4_mp(const float *w, size_t n, uint8_t *out) {
+    if (n == 0) return;
+    size_t nb = (n + Q4_BLOCK - 1) / Q4_BLOCK;
+    uint8_t *nib = out + nb * 2;
+    for (size_t b = 0; b < nb; b++) {
+        size_t s = b * Q4_BLOCK, e = s + Q4_BLOCK < n ? s + Q4_BLOCK : n;
+        float max_abs = 0.0f;
+        for (size_t i = s; i < e; i++) max_abs = fmaxf(max_abs, fabsf(w[i]));
+        float scale = max_abs > 1e-10f ? max_abs / 7.0f : 1.0f;
+        uint16_t h = orc_f32_to_f16_rne(scale);
+        out[2 * b] = (uint8_t)(h & 0xff);
+        out[2 * b + 1] = (uint8_t)(h >> 8);
+        for (size_t i = s; i < e; i++) {
+            int q = rust_round_i8(w[i] / scale);
+            if (q < -8) q = -8;
+            if (q > 7) q = 7;
+            uint8_t v = (uint8_t)(q + 8);
+            if (i & 1) nib[i >> 1] |= (uint8_t)((v & 0x0f) << 4);
+            else nib[i >> 1] = (uint8_t)(v & 0x0f);
+        }
+    }
+}
+
+/* mixed_precision.rs:489-539.  Returns the number of values written: 0 for
+ * n == 0 or empty data, else n -- all zero when the scales do not fit,
+ * zero past the end of the nibbles. */
+size_t orc_dequantize_int4_mp(const uint8_t *data, size_t len, size_t n, float *out) {
+    if (n == 0 || len == 0) return 0;
+    size_t nb = (n + Q4_BLOCK - 1) / Q4_BLOCK;
+    size_t sb = nb * 2;
+    if (len < sb) {
+        for (size_t i = 0; i < n; i++) out[i] = 0.0f;
+        return n;
+    }
+    const uint8_t *packed = data + sb;
+    size_t plen = len - sb;
+    for (size_t i = 0; i < n; i++) {
+        size_t b = i / Q4_BLOCK, byte = i >> 1;
+        if (byte >= plen) { out[i] = 0.0f; continue; }
+        float scale = orc_f16_bits_to_f32((uint16_t)(data[2 * b] | (data[2 * b + 1] << 8)));
+        uint8_t nibble = (i & 1) ? (packed[byte] >> 4) & 0x0f : packed[byte] & 0x0f;
+        out[i] = (float)((int8_t)nibble - 8) * scale;
+    }
+    return n;
+}
+
 /* ======================================================================
  * Mixed-radix complex FFT (f32 data, twiddles rounded from f64)
  * ====================================================================== */

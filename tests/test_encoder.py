@@ -69,3 +69,13 @@ def test_written_files_decode_with_oracle(orc):
         assert np.array_equal(OH.decode_int4_hct_cpu(f4), orc.dequantize_int4(orc.quantize_int4(w), w.size))
     # same DCT as the oracle within f32 accuracy
     np.testing.assert_allclose(E.dct_2d(w), orc.dct_2d(w), atol=1e-5)
+
+
+def test_quantize_int4_mp_matches_oracle(orc):
+    from haagenti_b200 import encode as E
+
+    rng = np.random.default_rng(9)
+    for n in (1, 31, 32, 33, 1000, 65537):
+        w = (rng.standard_normal(n) * 10.0 ** rng.integers(-8, 3)).astype(np.float32)
+        w[::17] = 0.0
+        assert E.quantize_int4_mp(w).tobytes() == orc.quantize_int4_mp(w), n

@@ -79,3 +79,20 @@ def test_unaligned_device_buffers(hb, orc, dev):
         assert rc == 0 and written.value == n
         got = out[1:].cpu().numpy()
         assert np.array_equal(_bits(got), _bits(ref)), off
+
+
+def test_dequantize_int4_mp_vs_oracle(hb, orc):
+    """mixed_precision.rs:489-539: bit-exact values, zero fill for short data."""
+    import torch
+
+    rng = np.random.default_rng(10)
+    w = (rng.standard_normal(4099) * 0.02).astype(np.float32)
+    q = orc.quantize_int4_mp(w)
+    for cut in (len(q), len(q) - 1, 2 * 129 + 7, 2 * 129, 100, 1):
+        ref = orc.dequantize_int4_mp(q[:cut], w.size)
+        got = hb.dequantize_int4_mp(q[:cut], w.size).cpu().numpy()
+        assert got.shape == ref.shape and np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+        bf = hb.dequantize_int4_mp(q[:cut], w.size, hb.BF16).cpu()
+        assert torch.equal(bf, torch.from_numpy(ref).to(torch.bfloat16))
+    assert hb.dequantize_int4_mp(q, 0).numel() == 0
+    assert hb.dequantize_int4_mp(b"", 10).numel() == 0

@@ -181,3 +181,49 @@ def test_topk_tie_break_and_count(orc):
         order = sorted(range(len(c)), key=lambda j: (-abs(c[j]), j))[:k]
         got = np.nonzero(np.unpackbits(bm, bitorder="little")[: len(c)])[0]
         assert list(got) == sorted(order)
+
+
+# ---- mixed_precision.rs:448-539 (the private INT4 pair)
+
+def test_f16_rne_matches_ieee(orc):
+    """The RNE f32 -> f16 of half::f16::from_f32, against numpy's IEEE cast."""
+    rng = np.random.default_rng(7)
+    mags = np.float32(10.0) ** rng.integers(-9, 6, 100000).astype(np.float32)
+    vals = np.concatenate([rng.standard_normal(100000).astype(np.float32) * mags, np.array(
+        [0.0, -0.0, 65504.0, 65519.99, 65520.0, 1e6, -1e6, np.inf, -np.inf, 2.0 ** -24,
+         2.0 ** -25, 3 * 2.0 ** -26, 2.0 ** -14, 5.960464477539063e-08 * 1.5], np.float32)])
+    with np.errstate(over="ignore"):
+        ref = vals.astype(np.float16).view(np.uint16)
+    got = np.array([orc.f32_to_f16_rne(v) for v in vals], np.uint16)
+    assert np.array_equal(got, ref)
+
+
+def test_int4_mp_scales_and_values(orc):
+    rng = np.random.default_rng(8)
+    w = (rng.standard_normal(1000) * 0.02).astype(np.float32)
+    q = np.frombuffer(orc.quantize_int4_mp(w), np.uint8)
+    nb = (w.size + 31) // 32
+    scales = q[: 2 * nb].view(np.uint16)
+    for b in range(nb):
+        blk = w[32 * b: 32 * b + 32]
+        m = np.max(np.abs(blk))
+        s = np.float32(m) / np.float32(7.0) if m > 1e-10 else np.float32(1.0)
+        assert scales[b] == np.array([s], np.float32).astype(np.float16).view(np.uint16)[0]
+    # nibbles equal the testing quantizer's (same f32 scale); only the stored scale differs
+    q_t = np.frombuffer(orc.quantize_int4(w), np.uint8)
+    assert np.array_equal(q[2 * nb:], q_t[2 * nb:])
+    d = orc.dequantize_int4_mp(q.tobytes(), w.size)
+    s32 = scales.view(np.float16).astype(np.float32)
+    nib = np.stack([q[2 * nb:] & 15, q[2 * nb:] >> 4], 1).reshape(-1)[: w.size].astype(np.int32)
+    assert np.array_equal(d, (nib - 8).astype(np.float32) * np.repeat(s32, 32)[: w.size])
+
+
+def test_int4_mp_short_data_zero_fills(orc):
+    w = np.linspace(-1, 1, 100, dtype=np.float32)
+    q = orc.quantize_int4_mp(w)
+    assert orc.dequantize_int4_mp(q, 0).size == 0
+    assert orc.dequantize_int4_mp(b"", 100).size == 0
+    assert np.array_equal(orc.dequantize_int4_mp(q[:5], 100), np.zeros(100, np.float32))  # < scales
+    full = orc.dequantize_int4_mp(q, 100)
+    cut = orc.dequantize_int4_mp(q[: 8 + 20], 100)  # 8 scale bytes + 20 nibble bytes = 40 values
+    assert np.array_equal(cut[:40], full[:40]) and not cut[40:].any()
