@@ -235,7 +235,7 @@ __device__ __forceinline__ float deq_nibble(uint32_t byte, uint64_t r, float sca
     return __fmul_rn((float)((int)nib - 8), scale);
 }
 
-__global__ void __launch_bounds__(SPACK_THREADS, 3) spectral_pack_kernel(
+__global__ void __launch_bounds__(SPACK_THREADS, 4) spectral_pack_kernel(
     const uint8_t *__restrict__ payload, uint64_t bmb, const uint32_t *__restrict__ chunk_base,
     uint64_t group_off, const uint64_t *__restrict__ meta, uint64_t B, uint32_t L, uint32_t P,
     uint32_t Q, const float4 *__restrict__ coef, uint32_t *__restrict__ out) {

@@ -462,16 +462,26 @@ __device__ __forceinline__ void stage1_chunk_t(const uint32_t (&r)[32], uint32_t
     float2 tw = sp.twiddle[m1 < sp.P ? k2 * m1 : 0];  // e^{2 pi i k2 m1 / H}, k2 m1 < H
     const float2 w = sp.twiddle[m1 < sp.P ? m1 : 0];  // step of k2 -> k2 + 1
     uint32_t v[16];
+    if (Q % 16 == 0) {  // my 16 rows start at a multiple of 16: one b, no wrap of k2
 #pragma unroll
-    for (int t = 0; t < 16; t++) {
-        v[t] = pack_h2(re[t] * tw.x - im[t] * tw.y, re[t] * tw.y + im[t] * tw.x);
-        if (++k2 == Q) {
-            k2 = 0;
-            tw = make_float2(1.0f, 0.0f);
-        } else {
+        for (int t = 0; t < 16; t++) {
+            v[t] = pack_h2(re[t] * tw.x - im[t] * tw.y, re[t] * tw.y + im[t] * tw.x);
             const float tx = tw.x * w.x - tw.y * w.y;
             tw.y = tw.x * w.y + tw.y * w.x;
             tw.x = tx;
+        }
+    } else {
+#pragma unroll
+        for (int t = 0; t < 16; t++) {
+            v[t] = pack_h2(re[t] * tw.x - im[t] * tw.y, re[t] * tw.y + im[t] * tw.x);
+            if (++k2 == Q) {
+                k2 = 0;
+                tw = make_float2(1.0f, 0.0f);
+            } else {
+                const float tx = tw.x * w.x - tw.y * w.y;
+                tw.y = tw.x * w.y + tw.y * w.x;
+                tw.x = tx;
+            }
         }
     }
     // stage: row (lane >> 1) = the warp's m1 slot, 128 bytes = 32 complex
