@@ -121,32 +121,40 @@ __device__ __forceinline__ void pack_row(const uint16_t *srow, const float4 *__r
     const uint32_t sstep = 33 * Q;
     for (uint32_t k2 = warp; 2 * k2 <= Q; k2 += nwarps) {
         const uint32_t k1_end = k2 == 0 ? P / 2 + 1 : (2 * k2 == Q ? P / 2 : P);
+        if (lane >= k1_end) continue;
         const uint32_t k = Q * lane + k2;
-        uint32_t ia = pad_idx(k), ib = pad_idx(L - k), ic = pad_idx(H + k), id = pad_idx(H - k);
-        uint32_t io = k2 * P + lane;
-        uint32_t jo = k2 == 0 ? P - lane : (Q - k2) * P + (P - 1 - lane);
+        const uint16_t *pa = srow + pad_idx(k), *pb = srow + pad_idx(L - k);
+        const uint16_t *pc = srow + pad_idx(H + k), *pd = srow + pad_idx(H - k);
+        const uint32_t io = k2 * P + lane;
+        const uint32_t jo = k2 == 0 ? P - lane : (Q - k2) * P + (P - 1 - lane);
+        const float4 *ct = coefT + io, *cu = coefT + jo;
+        uint32_t *ot = orow + io, *ou = orow + jo;
+        // the partner H - k exists except for k = 0 and k = H/2 (both in row k2 = 0)
+        const bool edge = k2 == 0;
         for (uint32_t k1 = lane; k1 < k1_end; k1 += 32) {
-            const float ck = h2f(srow[ia]);
-            const float cLk = h2f(srow[ib]);
-            const float cHk = h2f(srow[ic]);
-            const float cHmk = h2f(srow[id]);  // H - k >= 1 for k < H
-            const float4 t = coefT[io];        // (alpha.re, alpha.im, beta.re, beta.im)
+            const float ck = h2f(*pa);
+            const float cLk = h2f(*pb);
+            const float cHk = h2f(*pc);
+            const float cHmk = h2f(*pd);  // H - k >= 1 for k < H
+            const float4 t = *ct;         // (alpha.re, alpha.im, beta.re, beta.im)
             const float zr = fmaf(t.x, ck, fmaf(t.y, cLk, fmaf(t.z, cHk, t.w * cHmk)));
             const float zi = fmaf(t.y, ck, fmaf(-t.x, cLk, fmaf(t.w, cHk, -t.z * cHmk)));
-            orow[io] = pack_z(zr, zi);
-            if (k2 != 0 || (k1 != 0 && 2 * k1 != P)) {  // k != 0 and k != H/2
+            *ot = pack_z(zr, zi);
+            if (!edge || (k1 != 0 && 2 * k1 != P)) {
                 // k' = H - k: c[k'] = c[H-k], c[L-k'] = c[H+k], c[H+k'] = c[L-k], c[H-k'] = c[k]
-                const float4 u = coefT[jo];
+                const float4 u = *cu;
                 const float yr = fmaf(u.x, cHmk, fmaf(u.y, cHk, fmaf(u.z, cLk, u.w * ck)));
                 const float yi = fmaf(u.y, cHmk, fmaf(-u.x, cHk, fmaf(u.w, cLk, -u.z * ck)));
-                orow[jo] = pack_z(yr, yi);
+                *ou = pack_z(yr, yi);
             }
-            ia += sstep;
-            ib -= sstep;
-            ic += sstep;
-            id -= sstep;
-            io += 32;
-            jo -= 32;
+            pa += sstep;
+            pb -= sstep;
+            pc += sstep;
+            pd -= sstep;
+            ct += 32;
+            cu -= 32;
+            ot += 32;
+            ou -= 32;
         }
     }
 }
