@@ -34,7 +34,8 @@ __all__ = [
     "HaagentiError", "CorruptedData", "BufferTooSmall", "UnexpectedEof", "ChecksumMismatch",
     "Unsupported", "DeviceError", "Context", "Lz4Decompressor", "dequantize_int4",
     "dequantize_int4_mp", "idct_2d",
-    "spectral_q4_decode", "HctReader", "HctReaderV2", "F32", "F16", "BF16", "FLAG_SPECTRAL_Q4",
+    "spectral_q4_decode", "HctReader", "HctReaderV2", "HctV3Decoder", "hct_v3_decode", "F32",
+    "F16", "BF16", "FLAG_SPECTRAL_Q4",
 ]
 
 
@@ -300,6 +301,61 @@ def spectral_q4_decode(payload, rows: int, cols: int, out_dtype: int = F32,
                                                 rows, cols, out.data_ptr(), out_dtype,
                                                 _stream_ptr(stream)))
     return out
+
+
+# ------------------------------------------------------------------ HCT V3 fragments
+
+class HctV3Decoder:
+    """GpuDecompressor::decompress for HCT V3 fragment data
+    (crates/haagenti-cuda/src/decompress.rs:322-438; ref/c/hct_decoder.h:322-394):
+    bitmap + fp16 coefficients per fragment, scattered and inverse-DCT'd on the GPU."""
+
+    def __init__(self, data, rows: int, cols: int, ctx: Context | None = None):
+        self.ctx = ctx or Context.default()
+        self._data = _as_host_u8(data)
+        self.rows, self.cols = int(rows), int(cols)
+        h = C.c_void_p()
+        err = L.Error()
+        _check(L.load().hct_b200_v3_open(self.ctx.handle,
+                                         self._data.ctypes.data if self._data.size else None,
+                                         self._data.size, self.rows, self.cols, C.byref(h),
+                                         C.byref(err)), err)
+        self._h = h
+
+    @property
+    def num_fragments(self) -> int:
+        return int(L.load().hct_b200_v3_num_fragments(self._h))
+
+    def decode(self, out_dtype: int = F32, out=None, stream=None):
+        torch = _torch()
+        if out is None:
+            out = torch.empty((self.rows, self.cols), dtype=_torch_dtype(out_dtype),
+                              device=torch.device("cuda", self.ctx.device))
+        err = L.Error()
+        _check(L.load().hct_b200_v3_decode(self._h, out.data_ptr(), out_dtype, _stream_ptr(stream),
+                                           C.byref(err)), err)
+        return out
+
+    def close(self):
+        if getattr(self, "_h", None):
+            L.load().hct_b200_v3_close(self._h)
+            self._h = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def hct_v3_decode(data, rows: int, cols: int, out_dtype: int = F32, ctx: Context | None = None,
+                  stream=None):
+    """One-shot form (the reference C decoder's hct_decode(data, len, rows, cols))."""
+    d = HctV3Decoder(data, rows, cols, ctx)
+    try:
+        return d.decode(out_dtype, stream=stream)
+    finally:
+        d.close()
 
 
 # ------------------------------------------------------------------ HCT reader

@@ -92,6 +92,13 @@ SIGNATURES = {
     "hct_b200_idct_2d": (C.c_int, [_vp, _vp, _vp, C.c_int, _sz, _sz, _vp]),
     "hct_b200_spectral_q4_decode": (C.c_int, [_vp, _vp, _sz, _sz, _sz, _vp, C.c_int, _vp]),
     "hct_b200_spectral_q4_decode_noalloc": (C.c_int, [_vp, _sz, _sz, _sz, _vp, C.c_int, _vp]),
+    "hct_b200_v3_open": (C.c_int, [_vp, _u8p, _sz, C.c_uint64, C.c_uint64,
+                                   C.POINTER(C.c_void_p), C.POINTER(Error)]),
+    "hct_b200_v3_num_fragments": (C.c_int, [_vp]),
+    "hct_b200_v3_decode": (C.c_int, [_vp, _vp, C.c_int, _vp, C.POINTER(Error)]),
+    "hct_b200_v3_close": (None, [_vp]),
+    "hct_b200_hct_v3_decode": (C.c_int, [_vp, _u8p, _sz, C.c_uint64, C.c_uint64, _vp, C.c_int,
+                                         _vp, C.POINTER(Error)]),
     "hct_b200_reader_open": (C.c_int, [_vp, _u8p, _sz, C.c_int, C.POINTER(C.c_void_p),
                                        C.POINTER(Error)]),
     "hct_b200_reader_upload": (C.c_int, [_vp, _u8p, _sz, _vp]),

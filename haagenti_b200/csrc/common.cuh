@@ -50,6 +50,15 @@ cudaError_t launch_spectral_scatter(const uint8_t *d_payload, size_t payload_len
                                     uint64_t cols, uint32_t *d_chunk, uint64_t *d_meta,
                                     half_bits *d_dense, uint64_t ld, int *d_flag, cudaStream_t s);
 
+// One V3 fragment (bitmap ++ fp16 values) scattered into the dense fp16
+// matrix: its values at its set bits in index order (set bits past nvals
+// keep their value).  first: the matrix is unwritten, so clear bits (and pad
+// columns) are written as zero.  d_bitmap 16-byte and d_vals 2-byte aligned.
+cudaError_t launch_v3_scatter(const uint8_t *d_bitmap, uint64_t total, uint64_t cols,
+                              const uint16_t *d_vals, uint64_t nvals, uint32_t *d_chunk,
+                              uint64_t *d_meta, int *d_flag, half_bits *d_dense, uint64_t ld,
+                              bool first, cudaStream_t s);
+
 // f32 row-major rows x cols -> fp16 with row stride ld (zero padded).
 cudaError_t launch_f32_to_f16_padded(const float *d_in, uint64_t rows, uint64_t cols,
                                      half_bits *d_out, uint64_t ld, cudaStream_t s);

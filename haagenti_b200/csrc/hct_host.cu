@@ -208,6 +208,19 @@ struct hct_b200_ctx {
     }
 };
 
+// A parsed V3 fragment container on the device: each fragment's bitmap and
+// fp16 values copied to 16-byte aligned places of d_data.
+struct hct_b200_v3 {
+    struct Frag {
+        size_t bm_off, vals_off;
+        uint64_t nvals;
+    };
+    hct_b200_ctx *ctx = nullptr;
+    uint64_t rows = 0, cols = 0;  // of the transform (a column vector is one row)
+    DevBuf d_data;
+    std::vector<Frag> frags;
+};
+
 struct hct_b200_reader {
     hct_b200_ctx *ctx = nullptr;
     hct_b200_header hdr{};
@@ -783,6 +796,140 @@ int hct_b200_spectral_q4_decode(hct_b200_ctx *ctx, const uint8_t *d_payload, siz
     rc = run_idct(ctx, rows, cols, d_out, out_dtype, s, err, d_payload, payload_len);
     if (rc) return rc;
     return read_flag(ctx, s, err);
+}
+
+// ---- V3 fragment container -----------------------------------------------
+// haagenti-cuda's GpuDecompressor::parse_hct_fragments + reconstruct_coefficients
+// (crates/haagenti-cuda/src/decompress.rs:322-438) and the reference's C
+// hct_decode (ref/c/hct_decoder.h:322-394).  Fragments are accepted as the C
+// decoder accepts them: parsing stops at a header or fragment that runs past
+// the data, and a fragment is skipped when its coefficient count, bitmap or
+// values do not fit (the Rust parser raises on a fragment past the end and
+// reads as many values as the bytes hold; on well-formed data both agree).
+
+int hct_b200_v3_open(hct_b200_ctx *ctx, const uint8_t *data, size_t len, uint64_t rows,
+                     uint64_t cols, hct_b200_v3 **out, hct_b200_error *err) {
+    clear_err(err);
+    if (!ctx || !out || (!data && len)) {
+        set_err(err, HCT_B200_ERR_INVALID_ARGUMENT, -1, 0, 0, 0, "null argument");
+        return HCT_B200_ERR_INVALID_ARGUMENT;
+    }
+    *out = nullptr;
+    if (len < 2) {  // decompress.rs:323-325
+        set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0, "HCT data too short");
+        return HCT_B200_ERR_CORRUPTED;
+    }
+    auto v = std::make_unique<hct_b200_v3>();
+    v->ctx = ctx;
+    v->rows = rows;
+    v->cols = cols;
+    if (v->cols == 1 && v->rows > 1) std::swap(v->rows, v->cols);
+    const uint64_t total = rows * cols;
+    const uint64_t bmb = (total + 7) / 8;
+    struct Src {
+        size_t bm, vals;
+        uint64_t n;
+    };
+    std::vector<Src> src;
+    if (total) {
+        const uint32_t nfrag = rd16(data);
+        size_t pos = 2;
+        for (uint32_t f = 0; f < nfrag && pos < len; f++) {
+            if (pos + 16 > len) break;
+            const uint64_t dlen = rd32(data + pos + 12);
+            pos += 16;
+            if (pos + dlen > len) break;
+            const size_t fd = pos;
+            pos += dlen;
+            if (dlen < 4) continue;
+            const uint64_t n = rd32(data + fd);
+            if (4 + bmb > dlen || 4 + bmb + 2 * n > dlen) continue;
+            src.push_back(Src{fd + 4, fd + 4 + bmb, n});
+        }
+    }
+    // device layout: per fragment its bitmap then its values, each 16-byte aligned
+    size_t bytes = 0;
+    for (const Src &f : src) {
+        hct_b200_v3::Frag g;
+        g.bm_off = bytes;
+        bytes += round_up(bmb, 16);
+        g.vals_off = bytes;
+        bytes += round_up(2 * f.n, 16);
+        g.nvals = f.n;
+        v->frags.push_back(g);
+    }
+    int rc = ensure_device(ctx);
+    if (rc) { set_err(err, rc, -1, 0, 0, 0, "no CUDA device"); return rc; }
+    cudaStream_t s = ctx->stream;
+    CK(v->d_data.reserve(bytes + 64));
+    for (size_t i = 0; i < src.size(); i++) {
+        CK(cudaMemcpyAsync(v->d_data.as<uint8_t>() + v->frags[i].bm_off, data + src[i].bm, bmb,
+                           cudaMemcpyHostToDevice, s));
+        if (src[i].n)
+            CK(cudaMemcpyAsync(v->d_data.as<uint8_t>() + v->frags[i].vals_off, data + src[i].vals,
+                               2 * src[i].n, cudaMemcpyHostToDevice, s));
+    }
+    if (total) {
+        rc = reserve_spectral(ctx, v->rows, v->cols, err);
+        if (rc) return rc;
+    }
+    CK(cudaStreamSynchronize(s));
+    *out = v.release();
+    return HCT_B200_OK;
+}
+
+int hct_b200_v3_num_fragments(const hct_b200_v3 *v) { return v ? (int)v->frags.size() : 0; }
+
+int hct_b200_v3_decode(hct_b200_v3 *v, void *d_out, int out_dtype, void *stream,
+                       hct_b200_error *err) {
+    clear_err(err);
+    if (!v || !d_out) {
+        set_err(err, HCT_B200_ERR_INVALID_ARGUMENT, -1, 0, 0, 0, "null argument");
+        return HCT_B200_ERR_INVALID_ARGUMENT;
+    }
+    if (out_dtype < HCT_B200_F32 || out_dtype > HCT_B200_BF16) {
+        set_err(err, HCT_B200_ERR_INVALID_ARGUMENT, -1, 0, 0, 0, "bad output dtype");
+        return HCT_B200_ERR_INVALID_ARGUMENT;
+    }
+    hct_b200_ctx *ctx = v->ctx;
+    const uint64_t rows = v->rows, cols = v->cols, total = rows * cols;
+    if (total == 0) return HCT_B200_OK;
+    int rc = ensure_device(ctx);
+    if (rc) return rc;
+    const cudaStream_t s = (cudaStream_t)stream;
+    const uint64_t ldw = round_up(cols, 8);
+    int *flag = ctx->flag.as<int>();
+    CK(cudaMemsetAsync(flag, 0, sizeof(int), s));
+    if (v->frags.empty()) CK(cudaMemsetAsync(ctx->dense.p, 0, rows * ldw * 2, s));
+    for (size_t i = 0; i < v->frags.size(); i++) {
+        const hct_b200_v3::Frag &f = v->frags[i];
+        int slot = ctx->prof_begin(s);
+        CK(launch_v3_scatter(v->d_data.as<uint8_t>() + f.bm_off, total, cols,
+                             reinterpret_cast<const uint16_t *>(v->d_data.as<uint8_t>() + f.vals_off),
+                             f.nvals, ctx->chunk.as<uint32_t>(), ctx->meta.as<uint64_t>(), flag,
+                             ctx->dense.as<half_bits>(), ldw, i == 0, s));
+        ctx->prof_end(slot, PK_SCATTER, (double)((total + 7) / 8) + 2.0 * f.nvals + 2.0 * total, s);
+    }
+    rc = run_idct(ctx, rows, cols, d_out, out_dtype, s, err);
+    if (rc) return rc;
+    return read_flag(ctx, s, err);
+}
+
+void hct_b200_v3_close(hct_b200_v3 *v) {
+    if (!v) return;
+    cudaSetDevice(v->ctx->device);
+    delete v;
+}
+
+int hct_b200_hct_v3_decode(hct_b200_ctx *ctx, const uint8_t *data, size_t len, uint64_t rows,
+                           uint64_t cols, void *d_out, int out_dtype, void *stream,
+                           hct_b200_error *err) {
+    hct_b200_v3 *v = nullptr;
+    int rc = hct_b200_v3_open(ctx, data, len, rows, cols, &v, err);
+    if (rc) return rc;
+    rc = hct_b200_v3_decode(v, d_out, out_dtype, stream, err);
+    hct_b200_v3_close(v);
+    return rc;
 }
 
 // ---- reader ----------------------------------------------------------------

@@ -315,6 +315,76 @@ __global__ void __launch_bounds__(256) spectral_scatter_kernel(
     }
 }
 
+// V3 fragment scatter (hct_decoder.h:360-371): the fp16 values vals[0, nvals)
+// go, in index order, to the set bits of the fragment's bitmap; set bits past
+// nvals are left alone.  overwrite: also write zero at the clear bits and
+// the set bits past nvals (the first fragment, onto an unwritten matrix);
+// else only the set bits below nvals are written (later fragments).  Same
+// warp-per-1024-bit-chunk walk as spectral_scatter_kernel; bm and vals are
+// 16- and 2-byte aligned.
+__global__ void __launch_bounds__(256) v3_scatter_kernel(
+    const uint8_t *__restrict__ bm, uint64_t bmb, uint64_t total, uint64_t cols, uint64_t nchunks,
+    const uint32_t *__restrict__ chunk_base, const uint32_t *__restrict__ group_base,
+    const uint16_t *__restrict__ vals, uint64_t nvals, uint16_t *__restrict__ dense, uint64_t ld,
+    bool vec_rows, bool overwrite) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t warps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+    for (uint64_t c = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; c < nchunks;
+         c += warps) {
+        const uint32_t word = bitmap_word(bm, bmb, total, 32 * c + lane);
+        const uint32_t pc = __popc(word);
+        uint32_t incl = pc;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
+        }
+        const uint64_t wrank =
+            (uint64_t)chunk_base[c] + group_base[c / RANK_GROUP] + (incl - pc);
+#pragma unroll
+        for (int pass = 0; pass < 4; pass++) {
+            const int src_lane = pass * 8 + (lane >> 2);  // word holding my 8 bits
+            const uint32_t wv = __shfl_sync(0xffffffffu, word, src_lane);
+            const uint64_t wr = __shfl_sync(0xffffffffu, wrank, src_lane);
+            const uint32_t shift = (lane & 3) * 8;
+            const uint32_t bits = (wv >> shift) & 0xffu;
+            uint64_t r = wr + __popc(wv & ((1u << shift) - 1u));
+            const uint64_t e0 = 1024 * c + 256 * pass + 8 * lane;
+            if (e0 >= total) continue;
+            uint16_t h[8];
+            uint32_t set = 0;  // elements this fragment writes
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                h[j] = 0;
+                if ((bits >> j) & 1u) {
+                    if (r < nvals) {
+                        h[j] = vals[r];
+                        set |= 1u << j;
+                    }
+                    r++;
+                }
+            }
+            if (overwrite) set = 0xffu;
+            if (!set) continue;
+            if (set == 0xffu && vec_rows && e0 + 8 <= total) {
+                const uint64_t row = e0 / cols, col = e0 - row * cols;
+                uint4 u;
+                u.x = h[0] | ((uint32_t)h[1] << 16);
+                u.y = h[2] | ((uint32_t)h[3] << 16);
+                u.z = h[4] | ((uint32_t)h[5] << 16);
+                u.w = h[6] | ((uint32_t)h[7] << 16);
+                *reinterpret_cast<uint4 *>(dense + row * ld + col) = u;
+            } else {
+                for (int j = 0; j < 8 && e0 + j < total; j++) {
+                    if (!((set >> j) & 1u)) continue;
+                    const uint64_t e = e0 + j, row = e / cols, col = e - row * cols;
+                    dense[row * ld + col] = h[j];
+                }
+            }
+        }
+    }
+}
+
 __global__ void f32_to_f16_padded_kernel(const float *__restrict__ in, uint64_t rows,
                                          uint64_t cols, uint16_t *__restrict__ out, uint64_t ld) {
     const uint64_t n = rows * ld;
@@ -373,6 +443,28 @@ cudaError_t launch_spectral_scatter(const uint8_t *d_payload, size_t payload_len
     spectral_scatter_kernel<<<grid_for(nchunks * 32, 256), 256, 0, s>>>(
         d_payload, bmb, total, cols, nchunks, d_chunk, d_chunk + rank_group_offset(total), d_meta,
         d_dense, ld, vec_rows);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_v3_scatter(const uint8_t *d_bitmap, uint64_t total, uint64_t cols,
+                              const uint16_t *d_vals, uint64_t nvals, uint32_t *d_chunk,
+                              uint64_t *d_meta, int *d_flag, half_bits *d_dense, uint64_t ld,
+                              bool first, cudaStream_t s) {
+    const uint64_t bmb = (total + 7) / 8;
+    const uint64_t nchunks = spectral_chunks(total);
+    if (first && ld != cols) {  // pad columns zero
+        cudaError_t e = cudaMemset2DAsync(d_dense + cols, ld * 2, 0, (ld - cols) * 2,
+                                          (total + cols - 1) / cols, s);
+        if (e != cudaSuccess) return e;
+    }
+    // the rank directory only (no INT4 section follows: no short-payload check)
+    cudaError_t e = launch_spectral_rank(d_bitmap, ~(size_t)0 >> 2, total, d_chunk, d_meta,
+                                         d_flag, s);
+    if (e != cudaSuccess) return e;
+    const bool vec_rows = (cols % 8 == 0) && (ld % 8 == 0) && (((uintptr_t)d_dense & 15u) == 0);
+    v3_scatter_kernel<<<grid_for(nchunks * 32, 256), 256, 0, s>>>(
+        d_bitmap, bmb, total, cols, nchunks, d_chunk, d_chunk + rank_group_offset(total), d_vals,
+        nvals, d_dense, ld, vec_rows, first);
     return cudaGetLastError();
 }
 

@@ -109,6 +109,7 @@ typedef struct {
 
 typedef struct hct_b200_ctx hct_b200_ctx;
 typedef struct hct_b200_reader hct_b200_reader;
+typedef struct hct_b200_v3 hct_b200_v3;
 
 /* ---- context ------------------------------------------------------------
  * One context per device owns the scratch memory, the cached DCT bases and
@@ -246,6 +247,31 @@ int hct_b200_spectral_q4_decode(hct_b200_ctx *ctx, const uint8_t *d_payload, siz
  * `stream` to report the device-side status. */
 int hct_b200_spectral_q4_decode_noalloc(const uint8_t *d_payload, size_t payload_len, size_t rows,
                                         size_t cols, void *d_out, int out_dtype, void *stream);
+
+/* ---- HCT V3 fragments (bitmap + fp16 coefficients) ----------------------
+ * GpuDecompressor::decompress for HCT V3 data (crates/haagenti-cuda/src/
+ * decompress.rs:322-438: parse_hct_fragments, reconstruct_coefficients, IDCT)
+ * and the reference's C hct_decode (ref/c/hct_decoder.h:322-394):
+ *   [num_fragments u16], per fragment [index u16][flags u16][checksum u64]
+ *   [data_len u32][num_coefficients u32][bitmap ceil(rows*cols/8)][f16 values]
+ * Each fragment writes its values, in index order, at its bitmap's set bits
+ * (later fragments over earlier ones, the rest zero), then the orthonormal
+ * 2-D DCT-III of rows x cols.  Fragments are accepted as hct_decode accepts
+ * them (a fragment whose bitmap or values do not fit is skipped; parsing
+ * stops at a fragment past the end).  open parses the headers on the host
+ * and uploads each fragment's bitmap and values once; decode is
+ * stream-ordered and synchronises once to read the device flag.
+ * hct_b200_hct_v3_decode is open + decode + close.  Fewer than 2 bytes of
+ * data is HCT_B200_ERR_CORRUPTED ("HCT data too short", decompress.rs:323). */
+int hct_b200_v3_open(hct_b200_ctx *ctx, const uint8_t *data, size_t len, uint64_t rows,
+                     uint64_t cols, hct_b200_v3 **out, hct_b200_error *err);
+int hct_b200_v3_num_fragments(const hct_b200_v3 *v);
+int hct_b200_v3_decode(hct_b200_v3 *v, void *d_out, int out_dtype, void *stream,
+                       hct_b200_error *err);
+void hct_b200_v3_close(hct_b200_v3 *v);
+int hct_b200_hct_v3_decode(hct_b200_ctx *ctx, const uint8_t *data, size_t len, uint64_t rows,
+                           uint64_t cols, void *d_out, int out_dtype, void *stream,
+                           hct_b200_error *err);
 
 /* ---- HCT reader ---------------------------------------------------------
  * HctReader::new / HctReaderV2::new (crates/haagenti-hct/src/tensor.rs:417-444,

@@ -268,6 +268,77 @@ def decode_int4_hct_cpu(file: bytes, threads: int = 0) -> np.ndarray:
 
 # ------------------------------------------------------------ seeded generators
 
+# ------------------------------------------------------------------ HCT V3 fragments
+#
+# The fragment container that haagenti-cuda's GpuDecompressor decodes
+# (crates/haagenti-cuda/src/decompress.rs:322-438) and the reference's own C
+# decoder reads (ref/c/hct_decoder.h:322-394):
+#   [num_fragments u16], then per fragment
+#   [index u16][flags u16][checksum u64][data_len u32][data: data_len bytes]
+#   data = [num_coefficients u32][bitmap ceil(rows*cols/8)][f16 x num_coefficients]
+# Fragments are applied in order: each writes its coefficients (in index
+# order) at its bitmap's set bits, the rest of the matrix stays zero; then the
+# 2-D IDCT of rows x cols.
+
+def encode_hct_v3(w: np.ndarray, retention: float = 0.30, num_fragments: int = 1,
+                  threads: int = 0) -> bytes:
+    """Writer (tests and bench): DCT -> top-k -> f16 values, the retained set split in
+    index order over ``num_fragments`` fragments with disjoint bitmaps."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    m, n = tensor_dims(w.shape)
+    coeffs = dct_2d(w.reshape(m, n), threads).reshape(-1)
+    total = m * n
+    k = retain_count(total, retention)
+    bm = topk_bitmap(coeffs, k, threads)
+    idx = np.nonzero(np.unpackbits(bm, bitorder="little")[:total])[0]
+    out = [struct.pack("<H", num_fragments)]
+    for f, part in enumerate(np.array_split(idx, num_fragments)):
+        fb = np.zeros((total + 7) // 8, np.uint8)
+        np.bitwise_or.at(fb, part // 8, (1 << (part % 8)).astype(np.uint8))
+        vals = coeffs[part].astype(np.float16)  # round to nearest even, as half::f16::from_f32
+        data = struct.pack("<I", part.size) + fb.tobytes() + vals.tobytes()
+        out.append(struct.pack("<HHQI", f, 0, xxh3_64(data), len(data)))
+        out.append(data)
+    return b"".join(out)
+
+
+def parse_hct_v3(data: bytes, total: int) -> list:
+    """Fragments as hct_decoder.h:330-373 accepts them: (bitmap, f16 values)."""
+    frags = []
+    if len(data) < 2 or total == 0:
+        return frags
+    nfrag = struct.unpack_from("<H", data, 0)[0]
+    pos = 2
+    bmb = (total + 7) // 8
+    for _ in range(nfrag):
+        if pos >= len(data) or pos + 16 > len(data):
+            break
+        dlen = struct.unpack_from("<I", data, pos + 12)[0]
+        pos += 16
+        if pos + dlen > len(data):
+            break
+        fd = data[pos:pos + dlen]
+        pos += dlen
+        if dlen < 4:
+            continue
+        ncoef = struct.unpack_from("<I", fd, 0)[0]
+        if 4 + bmb > dlen or 4 + bmb + 2 * ncoef > dlen:
+            continue
+        frags.append((np.frombuffer(fd, np.uint8, bmb, 4),
+                      np.frombuffer(fd, np.float16, ncoef, 4 + bmb)))
+    return frags
+
+
+def decode_hct_v3_cpu(data: bytes, rows: int, cols: int, threads: int = 0) -> np.ndarray:
+    """hct_decoder.h:322-394 restated: scatter every fragment, then the oracle IDCT."""
+    total = rows * cols
+    dense = np.zeros(total, np.float32)
+    for bm, vals in parse_hct_v3(data, total):
+        pos = np.nonzero(np.unpackbits(bm, bitorder="little")[:total])[0][: vals.size]
+        dense[pos] = vals[: pos.size].astype(np.float32)
+    return idct_2d(dense.reshape(rows, cols), threads)
+
+
 def gen_weight(shape, seed: int, outlier_frac: float = 0.01, std: float = 0.02) -> np.ndarray:
     """N(0, std) f32: 2^22-element chunks, chunk i from PCG64(SeedSequence(seed).spawn(n)[i]);
     the first 1% of a default_rng([seed, 1]) column permutation is scaled x10."""

@@ -16,6 +16,10 @@ Contents
   ref_c_idct      outputs of the reference's own C decoder
                   (ref/c/hct_decoder.h hct_idct_2d / hct_dct_2d, compiled into
                   oracle/_ref) on seeded inputs
+  ref_c_v3        V3 fragment containers (decompress.rs:322-438 layout) and the
+                  reference C decoder's hct_decode output for them: 1-3
+                  fragments, a truncated trailing fragment, a fragment whose
+                  coefficient count is below its bitmap's popcount
 """
 from __future__ import annotations
 
@@ -128,6 +132,45 @@ def ref_c(reference: str):
     return cases
 
 
+def ref_c_v3(reference: str):
+    from oracle import hct as OH
+
+    so = os.path.join(REPO, "oracle", "_ref", "libhct_ref.so")
+    if not os.path.exists(so):
+        oracle.build()
+    lib = C.CDLL(so)
+    lib.hct_decode.restype = C.POINTER(C.c_float)
+    lib.hct_decode.argtypes = [C.c_char_p, C.c_size_t, C.c_size_t, C.c_size_t]
+    libc = C.CDLL(None)
+    libc.free.argtypes = [C.c_void_p]
+    cases = []
+
+    def add(name, data, rows, cols):
+        p = lib.hct_decode(data, len(data), rows, cols)
+        out = np.ctypeslib.as_array(p, (rows * cols,)).astype(np.float32).copy()
+        libc.free(C.cast(p, C.c_void_p))
+        cases.append(dict(name=name, rows=rows, cols=cols, data=data.hex(), out=out.tolist()))
+
+    for name, (rows, cols), nf, seed in [("one_fragment", (16, 24), 1, 1),
+                                         ("two_fragments", (24, 40), 2, 2),
+                                         ("three_fragments_odd", (33, 17), 3, 3),
+                                         ("row_vector", (1, 64), 1, 4),
+                                         ("column_vector", (48, 1), 2, 5)]:
+        w = OH.gen_weight((rows, cols), 2000 + seed)
+        add(name, OH.encode_hct_v3(w, 0.3, nf), rows, cols)
+    # the last fragment cut short: hct_decode stops before it
+    w = OH.gen_weight((16, 32), 2010)
+    d = OH.encode_hct_v3(w, 0.4, 2)
+    add("truncated_fragment", d[:-7], 16, 32)
+    # fewer coefficients than set bits: the count fields say 5 fewer
+    d = bytearray(OH.encode_hct_v3(OH.gen_weight((16, 16), 2011), 0.5, 1))
+    n = int.from_bytes(d[18:22], "little")
+    d[18:22] = (n - 5).to_bytes(4, "little")
+    d[14:18] = (int.from_bytes(d[14:18], "little") - 10).to_bytes(4, "little")
+    add("short_coefficients", bytes(d[:len(d) - 10]), 16, 16)
+    return cases
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -142,6 +185,7 @@ def main():
                        for (n, b, o, c, code, p, pv, w) in LZ4_ERRORS],
         "spec_dct": spec_dct(args.reference),
         "ref_c_idct": ref_c(args.reference),
+        "ref_c_v3": ref_c_v3(args.reference),
     }
     with open(os.path.join(HERE, "golden.json"), "w") as f:
         json.dump(g, f, indent=1)

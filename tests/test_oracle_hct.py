@@ -83,3 +83,26 @@ def test_generator_shapes_and_outliers():
     assert w.dtype == np.float32 and w.shape == (128, 200)
     col_std = w.std(axis=0)
     assert (col_std > 0.1).sum() == 2  # 1% of 200 columns scaled x10
+
+
+# ---- HCT V3 fragment containers (decompress.rs:322-438, hct_decoder.h:322-394)
+
+def test_v3_oracle_matches_reference_c_decoder(golden):
+    """The oracle's restatement against hct_decode's own outputs (golden)."""
+    from oracle import hct as OH
+
+    for case in golden["ref_c_v3"]:
+        got = OH.decode_hct_v3_cpu(bytes.fromhex(case["data"]), case["rows"], case["cols"])
+        ref = np.array(case["out"], np.float32).reshape(case["rows"], case["cols"])
+        assert np.abs(got - ref).max() <= 1e-5 + 1e-4 * np.abs(ref).max(), case["name"]
+
+
+def test_v3_encoder_roundtrip_within_retention():
+    from oracle import hct as OH
+
+    w = OH.gen_weight((64, 96), 7)
+    for nf in (1, 2, 4):
+        d = OH.encode_hct_v3(w, 1.0, nf)
+        assert len(OH.parse_hct_v3(d, w.size)) == nf
+        back = OH.decode_hct_v3_cpu(d, 64, 96)
+        assert np.abs(back - w).max() < 2e-3  # f16 coefficients, full retention
