@@ -65,24 +65,28 @@ def layer_files(rank_local: int, world: int, barrier) -> dict:
     """HCT-Q4 files of the layer, encoded once per node and cached under /tmp."""
     from haagenti_b200 import encode as E
 
-    cache = os.path.join(tempfile.gettempdir(), f"hct_b200_bench_l70b_s{SEED}_r{int(RETENTION*100)}")
+    cache = os.path.join(tempfile.gettempdir(),
+                         f"hct_b200_bench_l70b_s{SEED}_r{int(RETENTION*100)}_q4v3")
     done = os.path.join(cache, "DONE")
     if rank_local == 0 and not os.path.exists(done):
         os.makedirs(cache, exist_ok=True)
         t0 = time.time()
         for i, (name, m, n) in enumerate(LAYER_70B):
             w = E.synthetic_weight((m, n), SEED * 100 + i)
-            data = E.encode_spectral_q4(w, RETENTION, version=1)
+            c = E.dct_2d(w)  # one DCT for both formats
             with open(os.path.join(cache, name + ".hct"), "wb") as f:
-                f.write(data)
-            del w
+                f.write(E.encode_spectral_q4(w, RETENTION, version=1, coeffs=c))
+            with open(os.path.join(cache, name + ".v3"), "wb") as f:
+                f.write(E.encode_hct_v3(w, RETENTION, 1, coeffs=c))
+            del w, c
         with open(done, "w") as f:
             f.write(f"{time.time() - t0:.1f}\n")
     barrier()
     out = {}
     for name, m, n in LAYER_70B:
-        with open(os.path.join(cache, name + ".hct"), "rb") as f:
-            out[name] = f.read()
+        for ext in ("hct", "v3"):
+            with open(os.path.join(cache, f"{name}.{ext}"), "rb") as f:
+                out[name if ext == "hct" else name + ".v3"] = f.read()
     return out
 
 
@@ -272,6 +276,7 @@ def run_b200(args):
 
     files = layer_files(local, world, barrier)
     ctx = H.Context(local)
+    ctx.set_idct({"auto": H.IDCT_AUTO, "scatter": H.IDCT_SCATTER, "dense": H.IDCT_DENSE}[args.idct])
     readers = {n: H.HctReader(files[n], ctx) for n, _, _ in TENS}
     outs = {n: torch.empty((m, c), dtype=torch.bfloat16, device=dev) for n, m, c in TENS}
     stream = torch.cuda.current_stream(dev)
@@ -340,7 +345,7 @@ def run_b200(args):
     # pinned host memory inside the timed region (step k+1's copies overlap
     # step k's decode) and every step's statuses read back
     pinned = {}
-    for n in files:
+    for n, _, _ in TENS:
         a = torch.empty(len(files[n]), dtype=torch.uint8, pin_memory=True)
         a.numpy()[:] = np.frombuffer(files[n], np.uint8)
         pinned[n] = a.numpy()
@@ -365,6 +370,8 @@ def run_b200(args):
     # ---- secondary: LZ4 (config 2) and INT4 (config 1) ------------------
     lz4 = bench_lz4(H, torch, dev, stream, args) if rank == 0 and not args.no_secondary else None
     int4 = bench_int4(H, torch, dev, stream, args) if rank == 0 and not args.no_secondary else None
+    v3 = (bench_v3(H, torch, dev, stream, files, TENS, ctx)
+          if rank == 0 and not args.no_secondary else None)
 
     # ---- roofline of the dominant kernel --------------------------------
     pk = peaks()
@@ -430,7 +437,7 @@ def run_b200(args):
             "kernels": kern,
             # the dense-path scatter is two kernels (chunk scan + scatter) under one record
             "gpu_launches": launches_total + ks.get("spectral_scatter", {}).get("launches", 0),
-            "lz4": lz4, "int4": int4,
+            "lz4": lz4, "int4": int4, "hct_v3": v3,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
         }
@@ -452,6 +459,37 @@ def _data_len(f: bytes) -> int:
     ent = 16 if (ver >= 2 and flags & 2) else 8
     q = 8 if (ver >= 2 and flags & 4) else 0
     return len(f) - 64 - q - nb * ent
+
+
+def bench_v3(H, torch, dev, stream, files, tens, ctx):
+    """the same layer as HCT V3 fragment containers (bitmap + fp16
+    coefficients, one fragment per tensor) decoded to bf16, inputs resident in HBM."""
+    decs = {n: H.HctV3Decoder(files[n + ".v3"], m, c, ctx) for n, m, c in tens}
+    outs = {n: torch.empty((m, c), dtype=torch.bfloat16, device=dev) for n, m, c in tens}
+
+    def step():
+        for n, _, _ in tens:
+            decs[n].decode(H.BF16, out=outs[n], stream=stream)
+
+    for _ in range(2):
+        step()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(reps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / reps
+    out_bytes = sum(2 * m * c for _, m, c in tens)
+    in_bytes = sum(len(files[n + ".v3"]) for n, _, _ in tens)
+    for d in decs.values():
+        d.close()
+    return {"config": "BASELINE config 3 layer as HCT V3 fragments (bitmap + fp16, 1 per tensor)",
+            "value": round(out_bytes / (ms / 1e3) / 1e9, 2), "unit": "GB/s bf16 out",
+            "ms": round(ms, 3), "compressed_bytes": in_bytes,
+            "path": "HctV3Decoder.decode per tensor (scatter -> factored IDCT), synchronous"}
 
 
 def bench_lz4(H, torch, dev, stream, args):
@@ -552,6 +590,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true", help="skip the LZ4 / INT4 lines")
     ap.add_argument("--tensors", default="", help="comma list of layer tensors (default: all)")
+    ap.add_argument("--idct", choices=["auto", "scatter", "dense"], default="auto",
+                    help="IDCT mode of the decode context (hct_b200_ctx_set_idct)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

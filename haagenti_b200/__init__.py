@@ -28,7 +28,7 @@ import numpy as np
 from . import _lib as L
 from ._lib import BF16, F16, F32, FLAG_SPECTRAL_Q4
 
-IDCT_AUTO, IDCT_DENSE = 0, 1
+IDCT_AUTO, IDCT_DENSE, IDCT_SCATTER = 0, 1, 2
 
 __all__ = [
     "HaagentiError", "CorruptedData", "BufferTooSmall", "UnexpectedEof", "ChecksumMismatch",

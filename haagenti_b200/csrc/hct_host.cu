@@ -361,12 +361,13 @@ RankDir ctx_rank_dir(hct_b200_ctx *ctx) {
 // whether it then decodes a spectral payload straight into the row pack.
 bool idct_factored(const hct_b200_ctx *ctx, uint64_t rows, uint64_t cols, uint32_t *pn,
                    uint32_t *qn, uint32_t *pm, uint32_t *qm) {
-    return ctx->idct_mode == HCT_B200_IDCT_AUTO && fdct_factor(cols, pn, qn) &&
+    return ctx->idct_mode != HCT_B200_IDCT_DENSE && fdct_factor(cols, pn, qn) &&
            (rows == 1 || fdct_factor(rows, pm, qm));
 }
 bool spectral_fused(const hct_b200_ctx *ctx, uint64_t rows, uint64_t cols) {
     uint32_t a, b, c, d;
-    return idct_factored(ctx, rows, cols, &a, &b, &c, &d) && spectral_pack_supported(cols);
+    return ctx->idct_mode == HCT_B200_IDCT_AUTO && idct_factored(ctx, rows, cols, &a, &b, &c, &d) &&
+           spectral_pack_supported(cols);
 }
 
 // One axis of the factored IDCT: rows of length L (fp16, stride ld_in) in
@@ -445,7 +446,7 @@ int run_idct(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols, void *d_out, int o
     const uint8_t *src = nullptr;
     if (payload) {
         const uint64_t total = rows * cols;
-        if (factored && spectral_pack_supported(cols)) {
+        if (spectral_fused(ctx, rows, cols)) {
             if (!dir.ranked) {
                 int slot = ctx->prof_begin(s);
                 CK(launch_spectral_rank(payload, payload_len, total, dir.chunk, dir.meta, flag, s));
@@ -651,7 +652,8 @@ int hct_b200_ctx_reserve(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols) {
 }
 
 int hct_b200_ctx_set_idct(hct_b200_ctx *ctx, int mode) {
-    if (!ctx || (mode != HCT_B200_IDCT_AUTO && mode != HCT_B200_IDCT_DENSE))
+    if (!ctx || (mode != HCT_B200_IDCT_AUTO && mode != HCT_B200_IDCT_DENSE &&
+                 mode != HCT_B200_IDCT_SCATTER))
         return HCT_B200_ERR_INVALID_ARGUMENT;
     ctx->idct_mode = mode;
     return HCT_B200_OK;

@@ -185,6 +185,28 @@ def encode_spectral_q4(w: np.ndarray, retention: float = 0.30, version: int = 1,
     return write_hct(payload, list(w.shape), DTYPE_I4, FLAG_SPECTRAL_Q4, version, block_size)
 
 
+def encode_hct_v3(w: np.ndarray, retention: float = 0.30, num_fragments: int = 1,
+                  coeffs: np.ndarray | None = None) -> bytes:
+    """HCT V3 fragment container (the layout crates/haagenti-cuda/src/decompress.rs:322-438
+    parses): DCT-II -> top-k -> fp16 values (round to nearest even), the retained set
+    split in index order over ``num_fragments`` fragments with disjoint bitmaps."""
+    m, n = tensor_dims(w.shape)
+    if coeffs is None:
+        coeffs = dct_2d(np.asarray(w, np.float32).reshape(m, n))
+    bitmap, vals = spectral_select(coeffs, retention)
+    total = m * n
+    idx = np.nonzero(np.unpackbits(bitmap, bitorder="little")[:total])[0]
+    out = [struct.pack("<H", num_fragments)]
+    for f, (part, pv) in enumerate(zip(np.array_split(idx, num_fragments),
+                                       np.array_split(vals, num_fragments))):
+        fb = np.zeros((total + 7) // 8, np.uint8)
+        np.bitwise_or.at(fb, part // 8, (1 << (part % 8)).astype(np.uint8))
+        data = struct.pack("<I", part.size) + fb.tobytes() + pv.astype(np.float16).tobytes()
+        out.append(struct.pack("<HHQI", f, 0, _xxh3(data), len(data)))
+        out.append(data)
+    return b"".join(out)
+
+
 def encode_int4(w: np.ndarray, version: int = 1, block_size: int = DEFAULT_BLOCK_SIZE) -> bytes:
     """INT4 + LZ4 on raw weights (examples/safetensors_to_int4_hct.rs:241-284)."""
     return write_hct(quantize_int4(w), list(w.shape), DTYPE_I4, 0, version, block_size)

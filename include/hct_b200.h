@@ -130,7 +130,9 @@ int hct_b200_abi_version(void);
  * contraction against the full DCT basis otherwise; DENSE always uses the
  * dense contraction.  Both compute haagenti_core::dct::idct_2d
  * (crates/haagenti-core/src/dct.rs:311-337). */
-enum { HCT_B200_IDCT_AUTO = 0, HCT_B200_IDCT_DENSE = 1 };
+/* SCATTER: the factored transform, but a spectral payload is first scattered
+ * into a dense fp16 matrix instead of being decoded inside the row pack. */
+enum { HCT_B200_IDCT_AUTO = 0, HCT_B200_IDCT_DENSE = 1, HCT_B200_IDCT_SCATTER = 2 };
 int hct_b200_ctx_set_idct(hct_b200_ctx *ctx, int mode);
 
 /* Per-kernel timing of the context's own launches, for roofline reports.

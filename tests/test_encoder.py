@@ -79,3 +79,13 @@ def test_quantize_int4_mp_matches_oracle(orc):
         w = (rng.standard_normal(n) * 10.0 ** rng.integers(-8, 3)).astype(np.float32)
         w[::17] = 0.0
         assert E.quantize_int4_mp(w).tobytes() == orc.quantize_int4_mp(w), n
+
+
+def test_hct_v3_writer_matches_oracle(orc):
+    from haagenti_b200 import encode as E
+    from oracle import hct as OH
+
+    w = OH.gen_weight((96, 160), 12)
+    c = OH.dct_2d(w)  # the same coefficients (the writers' DCTs differ in the last ulp)
+    for nf in (1, 3):
+        assert E.encode_hct_v3(w, 0.3, nf, coeffs=c) == OH.encode_hct_v3(w, 0.3, nf)
