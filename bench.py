@@ -46,6 +46,7 @@ LAYER_70B = [  # (name, rows, cols)
 ]
 SEED = 2
 RETENTION = 0.30
+HOLO_FRAGMENTS = 8  # HoloTensorEncoder's default fragment count
 
 
 def peaks():
@@ -66,7 +67,7 @@ def layer_files(rank_local: int, world: int, barrier) -> dict:
     from haagenti_b200 import encode as E
 
     cache = os.path.join(tempfile.gettempdir(),
-                         f"hct_b200_bench_l70b_s{SEED}_r{int(RETENTION*100)}_q4v3")
+                         f"hct_b200_bench_l70b_s{SEED}_r{int(RETENTION*100)}_q4v3holo")
     done = os.path.join(cache, "DONE")
     if rank_local == 0 and not os.path.exists(done):
         os.makedirs(cache, exist_ok=True)
@@ -78,15 +79,17 @@ def layer_files(rank_local: int, world: int, barrier) -> dict:
                 f.write(E.encode_spectral_q4(w, RETENTION, version=1, coeffs=c))
             with open(os.path.join(cache, name + ".v3"), "wb") as f:
                 f.write(E.encode_hct_v3(w, RETENTION, 1, coeffs=c))
+            with open(os.path.join(cache, name + ".holo"), "wb") as f:
+                f.write(E.encode_holotensor(w, HOLO_FRAGMENTS, coeffs=c))
             del w, c
         with open(done, "w") as f:
             f.write(f"{time.time() - t0:.1f}\n")
     barrier()
     out = {}
     for name, m, n in LAYER_70B:
-        for ext in ("hct", "v3"):
+        for ext in ("hct", "v3", "holo"):
             with open(os.path.join(cache, f"{name}.{ext}"), "rb") as f:
-                out[name if ext == "hct" else name + ".v3"] = f.read()
+                out[name if ext == "hct" else name + "." + ext] = f.read()
     return out
 
 
@@ -372,6 +375,8 @@ def run_b200(args):
     int4 = bench_int4(H, torch, dev, stream, args) if rank == 0 and not args.no_secondary else None
     v3 = (bench_v3(H, torch, dev, stream, files, TENS, ctx)
           if rank == 0 and not args.no_secondary else None)
+    holo = (bench_holo(H, torch, dev, stream, files, TENS, ctx)
+            if rank == 0 and not args.no_secondary else None)
 
     # ---- roofline of the dominant kernel --------------------------------
     pk = peaks()
@@ -437,7 +442,7 @@ def run_b200(args):
             "kernels": kern,
             # the dense-path scatter is two kernels (chunk scan + scatter) under one record
             "gpu_launches": launches_total + ks.get("spectral_scatter", {}).get("launches", 0),
-            "lz4": lz4, "int4": int4, "hct_v3": v3,
+            "lz4": lz4, "int4": int4, "hct_v3": v3, "holotensor": holo,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
         }
@@ -490,6 +495,40 @@ def bench_v3(H, torch, dev, stream, files, tens, ctx):
             "value": round(out_bytes / (ms / 1e3) / 1e9, 2), "unit": "GB/s bf16 out",
             "ms": round(ms, 3), "compressed_bytes": in_bytes,
             "path": "HctV3Decoder.decode per tensor (scatter -> factored IDCT), synchronous"}
+
+
+def bench_holo(H, torch, dev, stream, files, tens, ctx):
+    """The same layer as spectral HoloTensor files (HOLO_FRAGMENTS "SV03" raster slices of
+    the f32 DCT coefficients per tensor), all fragments decoded to bf16, inputs resident
+    in HBM."""
+    readers = {n: H.HoloTensorReader(files[n + ".holo"], ctx) for n, _, _ in tens}
+    outs = {n: torch.empty((m, c), dtype=torch.bfloat16, device=dev) for n, m, c in tens}
+
+    def step():
+        for n, _, _ in tens:
+            readers[n].decode(out_dtype=H.BF16, out=outs[n], stream=stream)
+
+    for _ in range(2):
+        step()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(reps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / reps
+    out_bytes = sum(2 * m * c for _, m, c in tens)
+    in_bytes = sum(len(files[n + ".holo"]) for n, _, _ in tens)
+    for r in readers.values():
+        r.close()
+    return {"config": f"BASELINE config 3 layer as spectral HoloTensor files "
+                      f"({HOLO_FRAGMENTS} SV03 fragments of f32 coefficients per tensor)",
+            "value": round(out_bytes / (ms / 1e3) / 1e9, 2), "unit": "GB/s bf16 out",
+            "ms": round(ms, 3), "file_bytes": in_bytes,
+            "path": "HoloTensorReader.decode per tensor (SV03 interleave -> factored IDCT), "
+                    "synchronous"}
 
 
 def bench_lz4(H, torch, dev, stream, args):

@@ -34,7 +34,8 @@ __all__ = [
     "HaagentiError", "CorruptedData", "BufferTooSmall", "UnexpectedEof", "ChecksumMismatch",
     "Unsupported", "DeviceError", "Context", "Lz4Decompressor", "dequantize_int4",
     "dequantize_int4_mp", "idct_2d",
-    "spectral_q4_decode", "HctReader", "HctReaderV2", "HctV3Decoder", "hct_v3_decode", "F32",
+    "spectral_q4_decode", "HctReader", "HctReaderV2", "HctV3Decoder", "hct_v3_decode",
+    "HoloTensorReader", "F32",
     "F16", "BF16", "FLAG_SPECTRAL_Q4",
 ]
 
@@ -356,6 +357,84 @@ def hct_v3_decode(data, rows: int, cols: int, out_dtype: int = F32, ctx: Context
         return d.decode(out_dtype, stream=stream)
     finally:
         d.close()
+
+
+# ------------------------------------------------------------------ HoloTensor
+
+class HoloTensorReader:
+    """HoloTensorReader + HoloTensorDecoder for spectral HoloTensor files
+    (crates/haagenti-hct/src/holotensor.rs:1935-2192, 1719-1810) held in
+    memory: the header and fragment index parsed on the host, the SV03
+    fragments' values uploaded once, and each decode (scatter of the first k
+    fragments + 2-D DCT-III) run on the GPU."""
+
+    def __init__(self, file, ctx: Context | None = None):
+        self.ctx = ctx or Context.default()
+        self._data = _as_host_u8(file)
+        h = C.c_void_p()
+        err = L.Error()
+        _check(L.load().hct_b200_holo_open(self.ctx.handle,
+                                           self._data.ctypes.data if self._data.size else None,
+                                           self._data.size, C.byref(h), C.byref(err)), err)
+        self._h = h
+        info = L.HoloInfo()
+        _check(L.load().hct_b200_holo_header(self._h, C.byref(info)))
+        self.info = info
+        self.shape = tuple(int(info.shape[i]) for i in range(info.ndim))
+        self.rows, self.cols = int(info.rows), int(info.cols)
+        self.quality = None  # SpectralDecoder::quality of the last decode
+
+    @property
+    def total_fragments(self) -> int:
+        """HoloTensorReader::total_fragments (holotensor.rs:2025-2031)."""
+        return int(L.load().hct_b200_holo_total_fragments(self._h))
+
+    @property
+    def is_inline_format(self) -> bool:
+        return bool(self.info.inline_format)
+
+    def predict_quality(self, k: int) -> float:
+        """QualityCurve::predict(k, total) of the header's curve."""
+        return float(L.load().hct_b200_holo_predict_quality(self._h, int(k)))
+
+    def fragments_for_quality(self, target: float) -> int:
+        """The number of fragments read_to_quality(target) reads."""
+        return int(L.load().hct_b200_holo_fragments_for_quality(self._h, float(target)))
+
+    def decode(self, num_fragments: int | None = None, out_dtype: int = F32, out=None,
+               stream=None):
+        """Reconstruction from fragments 0..k-1 (all by default) as a
+        rows x cols tensor; self.quality is the decoder's coverage."""
+        torch = _torch()
+        k = self.total_fragments if num_fragments is None else int(num_fragments)
+        if out is None:
+            out = torch.empty((self.rows, self.cols), dtype=_torch_dtype(out_dtype),
+                              device=torch.device("cuda", self.ctx.device))
+        q = C.c_float(0.0)
+        err = L.Error()
+        _check(L.load().hct_b200_holo_decode(self._h, k, out.data_ptr(), out_dtype,
+                                             _stream_ptr(stream), C.byref(q), C.byref(err)), err)
+        self.quality = float(q.value)
+        return out
+
+    def decode_to_quality(self, target: float, out_dtype: int = F32, stream=None):
+        """decode_from_file_progressive (holotensor.rs:2332-2348): the
+        fragments read_to_quality(target) reads, and its predicted quality."""
+        k = self.fragments_for_quality(target)
+        out = self.decode(k, out_dtype, stream=stream)
+        q = 1.0 if self.is_inline_format else self.predict_quality(k)
+        return out, q
+
+    def close(self):
+        if getattr(self, "_h", None):
+            L.load().hct_b200_holo_close(self._h)
+            self._h = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 # ------------------------------------------------------------------ HCT reader

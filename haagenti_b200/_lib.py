@@ -54,6 +54,15 @@ class Header(C.Structure):
                 ("has_quant_meta", C.c_uint32), ("reserved2", C.c_uint32)]
 
 
+class HoloInfo(C.Structure):
+    _fields_ = [("encoding", C.c_uint8), ("compression", C.c_uint8), ("flags", C.c_uint16),
+                ("total_fragments", C.c_uint16), ("min_fragments", C.c_uint16),
+                ("original_size", C.c_uint64), ("seed", C.c_uint64), ("dtype", C.c_uint8),
+                ("ndim", C.c_uint8), ("inline_format", C.c_uint16), ("reserved", C.c_uint32),
+                ("shape", C.c_uint64 * 7), ("quality_curve", C.c_float * 4),
+                ("rows", C.c_uint64), ("cols", C.c_uint64)]
+
+
 class KernelStats(C.Structure):
     _fields_ = [("name", C.c_char * 32), ("launches", C.c_uint64), ("total_ms", C.c_double),
                 ("work", C.c_double)]
@@ -99,6 +108,14 @@ SIGNATURES = {
     "hct_b200_v3_close": (None, [_vp]),
     "hct_b200_hct_v3_decode": (C.c_int, [_vp, _u8p, _sz, C.c_uint64, C.c_uint64, _vp, C.c_int,
                                          _vp, C.POINTER(Error)]),
+    "hct_b200_holo_open": (C.c_int, [_vp, _u8p, _sz, C.POINTER(C.c_void_p), C.POINTER(Error)]),
+    "hct_b200_holo_header": (C.c_int, [_vp, C.POINTER(HoloInfo)]),
+    "hct_b200_holo_total_fragments": (C.c_int, [_vp]),
+    "hct_b200_holo_predict_quality": (C.c_float, [_vp, C.c_uint32]),
+    "hct_b200_holo_fragments_for_quality": (C.c_uint32, [_vp, C.c_float]),
+    "hct_b200_holo_decode": (C.c_int, [_vp, C.c_uint32, _vp, C.c_int, _vp,
+                                       C.POINTER(C.c_float), C.POINTER(Error)]),
+    "hct_b200_holo_close": (None, [_vp]),
     "hct_b200_reader_open": (C.c_int, [_vp, _u8p, _sz, C.c_int, C.POINTER(C.c_void_p),
                                        C.POINTER(Error)]),
     "hct_b200_reader_upload": (C.c_int, [_vp, _u8p, _sz, _vp]),

@@ -93,6 +93,10 @@ struct GemmArgs {
     uint64_t batch = 0;
     const float *twiddle = nullptr;  // e^{2 pi i j / H}, complex fp32 (mode 2)
     float scale = 1.0f;              // mode 3
+    // modes 2 and 3: a device word for dynamic tile scheduling (CTAs take the
+    // next tile from it, so CTAs that start late do fewer tiles); cleared by
+    // the launch.  nullptr: tiles are dealt out statically.
+    uint32_t *tile_counter = nullptr;
 };
 cudaError_t launch_umma_gemm(const GemmArgs &args, cudaStream_t s);
 
@@ -100,11 +104,12 @@ cudaError_t launch_umma_gemm(const GemmArgs &args, cudaStream_t s);
 // L even, H = L/2 = P*Q with P, Q multiples of 4 and <= 128.
 bool fdct_factor(uint64_t L, uint32_t *P, uint32_t *Q);
 // rows of length L (fp16, stride ld_in) -> Z[b][k2][k1] complex fp16 pairs.
-// d_tables: the per-k pack coefficients written by launch_pack_tables(L, P, Q).
+// d_tables: the per-k pack coefficients (natural k order) written by
+// launch_pack_tables(L, P, Q).
 cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t batch, uint32_t L,
                                 uint32_t P, uint32_t Q, const float *d_tables, half_bits *d_out,
                                 cudaStream_t s);
-// L/2 float4 (alpha_k, beta_k) in (k2, k1) order, k = Q k1 + k2 (P Q = L/2).
+// L/2 float4 (alpha_k, beta_k) in natural k order (P Q = L/2).
 cudaError_t launch_pack_tables(uint32_t L, uint32_t P, uint32_t Q, float *d_tables,
                                cudaStream_t s);
 // Rank directory of a spectral payload (layout at spectral_chunks above) in
@@ -118,6 +123,23 @@ cudaError_t launch_spectral_pack(const uint8_t *d_payload, uint64_t bmb, const u
                                  const uint64_t *d_meta, uint64_t batch, uint32_t L, uint32_t P,
                                  uint32_t Q, const float *d_tables, half_bits *d_out,
                                  cudaStream_t s);
+// ---- HoloTensor SV03 fragments (holo.cu) ---------------------------------
+// One residue class r of the raster positions p = r + F i: fragment values
+// vals[src + i - q0] for q0 <= i < q0 + count, no fragment when count == 0.
+struct Sv03Residue {
+    uint64_t src, q0, count;
+};
+// dense[b][k] (fp16, row stride ldw) = value of raster position b cols + k
+// from its residue (zero where none), for all rows x cols; F > 0.
+cudaError_t launch_sv03_interleave(const float *d_vals, const Sv03Residue *d_res, uint32_t F,
+                                   uint64_t rows, uint64_t cols, half_bits *d_dense, uint64_t ldw,
+                                   cudaStream_t s);
+// One fragment's values at positions start + j F (< n), j < count; F == 0
+// writes the last value at start.  The matrix must be cleared beforehand.
+cudaError_t launch_sv03_scatter(const float *d_vals, uint64_t count, uint64_t start, uint64_t F,
+                                uint64_t n, uint64_t cols, half_bits *d_dense, uint64_t ldw,
+                                cudaStream_t s);
+
 // realified n-point inverse-DFT matrix, 2n x 2n fp16 (rows_pad x ld).
 cudaError_t launch_dft_matrix(uint32_t n, uint32_t rows_pad, uint32_t ld, half_bits *d_out,
                               cudaStream_t s);

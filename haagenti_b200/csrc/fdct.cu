@@ -38,16 +38,25 @@
 namespace hct {
 namespace {
 
-__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 __device__ __forceinline__ uint16_t f2h(float v) { return __half_as_ushort(__float2half_rn(v)); }
 
-// Shared-memory index of row element k: two fp16 of padding every 64
-// elements, so the pack's reads at stride Q (lanes = consecutive k1) spread
-// over the banks.
-__device__ __forceinline__ uint32_t pad_idx(uint32_t k) { return k + 2 * (k >> 6); }
+// Shared-memory index of row element k: 8 fp16 (16 bytes) of padding after
+// every 64 elements and SPAD2 more after every 512.  Every group of 8
+// elements stays 16-byte aligned (the row is staged and expanded with
+// 16-byte stores), and the pack's reads are free of bank conflicts: a warp
+// reads 8 consecutive elements (5 words at most) at 4 places 8 Q elements
+// apart, which are 8 banks apart with SPAD2 = 16 for Q = 64 (296 words) and
+// SPAD2 = 8 for Q = 128 (584 words).
+__host__ __device__ __forceinline__ constexpr uint32_t spad2_of(int qc) { return qc == 64 ? 16 : 8; }
 
-__host__ __device__ __forceinline__ uint32_t srow_halves(uint32_t L) {
-    return (L + 2 * (L >> 6) + 8) & ~7u;
+template <int QC>
+__host__ __device__ __forceinline__ uint32_t spad(uint32_t k) {
+    return k + 8 * (k >> 6) + spad2_of(QC) * (k >> 9);
+}
+
+// staged row: L elements, padding, and the zero c[L] at spad(L)
+__host__ __device__ __forceinline__ uint32_t srow_halves(uint32_t L, int qc) {
+    return L + 8 * (L >> 6) + spad2_of(qc) * (L >> 9) + 8;
 }
 
 __device__ __forceinline__ uint32_t pack_z(float re, float im) {
@@ -55,211 +64,232 @@ __device__ __forceinline__ uint32_t pack_z(float re, float im) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-// Pack of one staged row, written straight to the output row in (k2, k1)
-// order, k = Q k1 + k2: warp w takes the k2 rows w, w + nwarps, ... <= Q/2 and
-// lane l the k1 = l, l + 32, ...; each item also produces its partner H - k,
-// which reads the same four inputs c[k], c[L-k], c[H+k], c[H-k] with the
-// roles permuted and lies at k2' = Q - k2, k1' = P - 1 - k1 (k2 > 0) or
-// k2' = 0, k1' = P - k1 (k2 = 0).  coefT holds (alpha_k, beta_k) in the same
-// (k2, k1) order, so every global access of a warp is contiguous.
-// srow[pad_idx(L)] must hold zero: it is c[L] of the k = 0 term.  Along a
-// lane's k1 = l, l + 32, ... every index moves by a constant (32 Q is a
-// multiple of 64, so pad_idx(k + 32 Q) = pad_idx(k) + 33 Q).
-// The same pack for NR rows staged sstride halves apart (outputs ostride
-// words apart, the first nvalid of them written): the coefficient loads and
-// the index arithmetic are shared by the rows.
-template <int NR>
-__device__ __forceinline__ void pack_rows(const uint16_t *srow, uint32_t sstride,
-                                          const float4 *__restrict__ coefT, uint32_t L, uint32_t P,
-                                          uint32_t Q, uint32_t *__restrict__ orow, uint64_t ostride,
-                                          uint32_t nvalid) {
-    const uint32_t H = L / 2;
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    const uint32_t sstep = 33 * Q;
-    for (uint32_t k2 = warp; 2 * k2 <= Q; k2 += nwarps) {
-        const uint32_t k1_end = k2 == 0 ? P / 2 + 1 : (2 * k2 == Q ? P / 2 : P);
-        const uint32_t k = Q * lane + k2;
-        uint32_t ia = pad_idx(k), ib = pad_idx(L - k), ic = pad_idx(H + k), id = pad_idx(H - k);
-        uint32_t io = k2 * P + lane;
-        uint32_t jo = k2 == 0 ? P - lane : (Q - k2) * P + (P - 1 - lane);
-        for (uint32_t k1 = lane; k1 < k1_end; k1 += 32) {
-            const float4 t = coefT[io];  // (alpha.re, alpha.im, beta.re, beta.im)
-            const bool partner = k2 != 0 || (k1 != 0 && 2 * k1 != P);  // k != 0 and k != H/2
-            const float4 u = partner ? coefT[jo] : t;
-#pragma unroll
-            for (int q = 0; q < NR; q++) {
-                const uint16_t *sr = srow + q * sstride;
-                const float ck = h2f(sr[ia]);
-                const float cLk = h2f(sr[ib]);
-                const float cHk = h2f(sr[ic]);
-                const float cHmk = h2f(sr[id]);  // H - k >= 1 for k < H
-                const float zr = fmaf(t.x, ck, fmaf(t.y, cLk, fmaf(t.z, cHk, t.w * cHmk)));
-                const float zi = fmaf(t.y, ck, fmaf(-t.x, cLk, fmaf(t.w, cHk, -t.z * cHmk)));
-                if ((uint32_t)q < nvalid) orow[q * ostride + io] = pack_z(zr, zi);
-                if (partner && (uint32_t)q < nvalid) {
-                    // k' = H - k: c[k'] = c[H-k], c[L-k'] = c[H+k], c[H+k'] = c[L-k], c[H-k'] = c[k]
-                    const float yr = fmaf(u.x, cHmk, fmaf(u.y, cHk, fmaf(u.z, cLk, u.w * ck)));
-                    const float yi = fmaf(u.y, cHmk, fmaf(-u.x, cHk, fmaf(u.w, cLk, -u.z * ck)));
-                    orow[q * ostride + jo] = pack_z(yr, yi);
-                }
-            }
-            ia += sstep;
-            ib -= sstep;
-            ic += sstep;
-            id -= sstep;
-            io += 32;
-            jo -= 32;
-        }
-    }
+// spad<QC>(Q (K + j) + x) - spad<QC>(Q K + x) for a compile-time Q = QC in {64, 128}:
+// Q K a multiple of 512 and 0 <= x < Q (no 512-boundary inside a run other
+// than the one at Q j = 512), and likewise spad(M - x - Q j) =
+// spad(M - x) - koff(j) below a multiple M of 512 with 1 <= x <= Q / 2.
+template <int QC>
+__device__ __forceinline__ constexpr uint32_t koff(int j) {
+    return (uint32_t)(QC * j + 8 * ((QC * j) / 64) + spad2_of(QC) * ((QC * j) / 512));
 }
 
-__device__ __forceinline__ void pack_row(const uint16_t *srow, const float4 *__restrict__ coefT,
-                                         uint32_t L, uint32_t P, uint32_t Q,
-                                         uint32_t *__restrict__ orow) {
-    const uint32_t H = L / 2;
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    const uint32_t sstep = 33 * Q;
-    for (uint32_t k2 = warp; 2 * k2 <= Q; k2 += nwarps) {
-        const uint32_t k1_end = k2 == 0 ? P / 2 + 1 : (2 * k2 == Q ? P / 2 : P);
-        if (lane >= k1_end) continue;
-        const uint32_t k = Q * lane + k2;
-        const uint16_t *pa = srow + pad_idx(k), *pb = srow + pad_idx(L - k);
-        const uint16_t *pc = srow + pad_idx(H + k), *pd = srow + pad_idx(H - k);
-        const uint32_t io = k2 * P + lane;
-        const uint32_t jo = k2 == 0 ? P - lane : (Q - k2) * P + (P - 1 - lane);
-        const float4 *ct = coefT + io, *cu = coefT + jo;
-        uint32_t *ot = orow + io, *ou = orow + jo;
-        // the partner H - k exists except for k = 0 and k = H/2 (both in row k2 = 0)
-        const bool edge = k2 == 0;
-        for (uint32_t k1 = lane; k1 < k1_end; k1 += 32) {
-            const float ck = h2f(*pa);
-            const float cLk = h2f(*pb);
-            const float cHk = h2f(*pc);
-            const float cHmk = h2f(*pd);  // H - k >= 1 for k < H
-            const float4 t = *ct;         // (alpha.re, alpha.im, beta.re, beta.im)
-            const float zr = fmaf(t.x, ck, fmaf(t.y, cLk, fmaf(t.z, cHk, t.w * cHmk)));
-            const float zi = fmaf(t.y, ck, fmaf(-t.x, cLk, fmaf(t.w, cHk, -t.z * cHmk)));
-            *ot = pack_z(zr, zi);
-            if (!edge || (k1 != 0 && 2 * k1 != P)) {
-                // k' = H - k: c[k'] = c[H-k], c[L-k'] = c[H+k], c[H+k'] = c[L-k], c[H-k'] = c[k]
-                const float4 u = *cu;
-                const float yr = fmaf(u.x, cHmk, fmaf(u.y, cHk, fmaf(u.z, cLk, u.w * ck)));
-                const float yi = fmaf(u.y, cHmk, fmaf(-u.x, cHk, fmaf(u.w, cLk, -u.z * ck)));
-                *ou = pack_z(yr, yi);
-            }
-            pa += sstep;
-            pb -= sstep;
-            pc += sstep;
-            pd -= sstep;
-            ct += 32;
-            cu -= 32;
-            ot += 32;
-            ou -= 32;
-        }
-    }
+__device__ __forceinline__ float ld_h(const uint16_t *s, uint32_t i) {
+    return __half2float(__ushort_as_half(s[i]));
 }
 
-// Pack of dense fp16 rows (stride ld_in): one CTA per NR rows (sharing the
-// coefficient loads and index arithmetic), the rows staged in shared memory
-// with up to 4 independent 16-byte loads in flight per thread and row.
-// THREADS = 256, NR = 2 with 4 CTAs per SM for rows up to 16384 elements;
-// THREADS = 512, NR = 1 with 2 beyond (a staged row then takes up to 57 KB).
-template <int THREADS, int MIN_CTAS, int NR>
-__global__ void __launch_bounds__(THREADS, MIN_CTAS) makhoul_pack_kernel(
-    const uint16_t *__restrict__ in, uint64_t ld_in, uint64_t B, uint32_t L, uint32_t P,
-    uint32_t Q, const float4 *__restrict__ coefT, uint32_t *__restrict__ out) {
-    extern __shared__ uint16_t srow[];
-    const uint32_t sstride = srow_halves(L);
-    const bool vec = ((ld_in & 7) == 0) && (((uintptr_t)in & 15) == 0) && ((L & 7) == 0);
-    const uint32_t nv = L / 8;
-    if (threadIdx.x < NR) srow[threadIdx.x * sstride + pad_idx(L)] = 0;  // c[L] = 0
-    for (uint64_t b = (uint64_t)blockIdx.x * NR; b < B; b += (uint64_t)gridDim.x * NR) {
-        const uint32_t nvalid = (uint32_t)(B - b < (uint64_t)NR ? B - b : (uint64_t)NR);
-        __syncthreads();  // previous rows fully consumed
+// One lane's share of the pack: row k2 in [1, Q/2] and the run of J
+// consecutive k1 = J g .. J g + J - 1.  For each k = Q k1 + k2 of the run it
+// reads a = c[k], b = c[L-k], c = c[H+k], d = c[H-k] and writes
+//   Z[k]   = alpha_k (a - i b) + beta_k (c - i d)
+//   Z[H-k] = w [conj(alpha_k) (d - i c) + conj(beta_k) (a + i b)],
+//            w = e^{i pi / 4}
+// (alpha_{H-k} = w conj(alpha_k) and beta_{H-k} = w^3 conj(beta_k) for
+// k != 0, so the table is read once per pair).  Z[H-k] lies in row Q - k2
+// at k1' = P - 1 - k1: two runs of J contiguous outputs.  The row k2 = Q/2 is
+// its own partner row; its runs write only Z[k], which covers it.
+template <int QC, int J>
+__device__ __forceinline__ void pack_run(const uint16_t *s, const float4 *__restrict__ coef,
+                                         uint32_t L, uint32_t P, uint32_t Q, uint32_t g,
+                                         uint32_t k2, uint32_t *__restrict__ orow) {
+    constexpr float RS2 = 0.70710678118654752440f;
+    const uint32_t H = L / 2, k1a = J * g;
+    const uint32_t ka = Q * k1a + k2;  // k of the run's first element
+    const float4 *ct = coef + ka;
+    uint4 *zd = reinterpret_cast<uint4 *>(orow + k2 * P + k1a);
+    uint4 *yd = reinterpret_cast<uint4 *>(orow + (Q - k2) * P + (P - J - k1a));
+    const bool partner = 2 * k2 != Q;
+    const uint32_t pa = spad<QC>(ka), pb = spad<QC>(L - ka), pc = spad<QC>(H + ka), pd = spad<QC>(H - ka);
 #pragma unroll
-        for (int q = 0; q < NR; q++) {
-            if ((uint32_t)q >= nvalid) break;
-            const uint16_t *row = in + (b + q) * ld_in;
-            uint16_t *sr = srow + q * sstride;
-            if (vec) {
-                const uint4 *r4 = reinterpret_cast<const uint4 *>(row);
-                for (uint32_t v0 = threadIdx.x; v0 < nv; v0 += 4 * THREADS) {
-                    uint4 x[4];
+    for (int h = 0; h < J / 4; h++) {
+        uint32_t zo[4], yo[4];
 #pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const uint32_t v = v0 + u * THREADS;
-                        if (v < nv) x[u] = __ldg(r4 + v);
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const uint32_t v = v0 + u * THREADS;
-                        if (v < nv) {  // 8 elements never straddle a 64-element pad
-                            uint32_t *d = reinterpret_cast<uint32_t *>(sr + pad_idx(8 * v));
-                            d[0] = x[u].x;
-                            d[1] = x[u].y;
-                            d[2] = x[u].z;
-                            d[3] = x[u].w;
-                        }
-                    }
-                }
+        for (int t = 0; t < 4; t++) {
+            const int j = 4 * h + t;
+            uint32_t ia, ib, ic, id;
+            if (QC) {
+                ia = pa + koff<QC>(j);
+                ib = pb - koff<QC>(j);
+                ic = pc + koff<QC>(j);
+                id = pd - koff<QC>(j);
             } else {
-                for (uint32_t k = threadIdx.x; k < L; k += THREADS) sr[pad_idx(k)] = row[k];
+                const uint32_t k = ka + Q * (uint32_t)j;
+                ia = spad<QC>(k);
+                ib = spad<QC>(L - k);
+                ic = spad<QC>(H + k);
+                id = spad<QC>(H - k);
             }
+            const float a = ld_h(s, ia), b = ld_h(s, ib), c = ld_h(s, ic), d = ld_h(s, id);
+            const float4 tt = ct[Q * j];  // (alpha.re, alpha.im, beta.re, beta.im) of k
+            zo[t] = pack_z(fmaf(tt.x, a, fmaf(tt.y, b, fmaf(tt.z, c, tt.w * d))),
+                           fmaf(tt.y, a, fmaf(-tt.x, b, fmaf(tt.w, c, -tt.z * d))));
+            const float s1 = d + c, s2 = d - c, s3 = a - b, s4 = a + b;
+            yo[t] = pack_z(RS2 * fmaf(tt.x, s1, fmaf(tt.y, s2, fmaf(tt.z, s3, tt.w * s4))),
+                           RS2 * fmaf(tt.x, s2, fmaf(-tt.y, s1, fmaf(tt.z, s4, -tt.w * s3))));
+        }
+        zd[h] = make_uint4(zo[0], zo[1], zo[2], zo[3]);
+        if (partner) yd[J / 4 - 1 - h] = make_uint4(yo[3], yo[2], yo[1], yo[0]);
+    }
+}
+
+// Row k2 = 0 pairs with itself at k1' = P - k1: its outputs are computed
+// directly, one k1 per lane (k = 0 reads c[L], the zero at spad<QC>(L)).
+template <int QC>
+__device__ __forceinline__ void pack_k2_zero(const uint16_t *s, const float4 *__restrict__ coef,
+                                             uint32_t L, uint32_t Q, uint32_t k1,
+                                             uint32_t *__restrict__ orow) {
+    const uint32_t H = L / 2, k = Q * k1;
+    const float a = ld_h(s, spad<QC>(k)), b = ld_h(s, spad<QC>(L - k));
+    const float c = ld_h(s, spad<QC>(H + k)), d = ld_h(s, spad<QC>(H - k));
+    const float4 tt = coef[k];
+    orow[k1] = pack_z(fmaf(tt.x, a, fmaf(tt.y, b, fmaf(tt.z, c, tt.w * d))),
+                      fmaf(tt.y, a, fmaf(-tt.x, b, fmaf(tt.w, c, -tt.z * d))));
+}
+
+// Pack of one staged row s (spad layout) into its output row, in (k2, k1)
+// order, by the warps warp, warp + nwarps, ...
+//   QC in {64, 128} (runs of 8): warp task (kg, og) takes rows
+//     k2 = 8 kg + 1 .. 8 kg + 8 and runs g = 4 og .. 4 og + 3, lane
+//     8 o + r taking row 8 kg + 1 + r and run 4 og + o: the 4 runs of a row
+//     are 128 contiguous output bytes, so a 16-byte store of the warp
+//     touches 8 rows;
+//   QC = 0 (any Q, runs of 4): lane items (run g, row k2), k2 fastest;
+// the remaining tasks cover row k2 = 0.
+template <int QC, int J>
+__device__ __forceinline__ void pack_row(const uint16_t *s, const float4 *__restrict__ coef,
+                                         uint32_t L, uint32_t P, uint32_t Q,
+                                         uint32_t *__restrict__ orow, uint32_t warp,
+                                         uint32_t nwarps, uint32_t lane) {
+    const uint32_t half = QC ? (uint32_t)QC / 2 : Q / 2;
+    const uint32_t runs = P / J;
+    uint32_t ntask;
+    if (QC) ntask = (half / 8) * ((runs + 3) / 4);
+    else ntask = (runs * half + 31) / 32;
+    const uint32_t nall = ntask + (P + 31) / 32;
+    for (uint32_t tau = warp; tau < nall; tau += nwarps) {
+        if (tau < ntask) {
+            if (QC) {
+                const uint32_t kg = tau % (half / 8), og = tau / (half / 8);
+                const uint32_t g = 4 * og + (lane >> 3);
+                if (g < runs) pack_run<QC, J>(s, coef, L, P, QC, g, 8 * kg + 1 + (lane & 7), orow);
+            } else {
+                const uint32_t i = 32 * tau + lane;
+                if (i < runs * half) {
+                    const uint32_t g = i / half;
+                    pack_run<0, J>(s, coef, L, P, Q, g, 1 + i - g * half, orow);
+                }
+            }
+        } else {
+            const uint32_t k1 = 32 * (tau - ntask) + lane;
+            if (k1 < P) pack_k2_zero<QC>(s, coef, L, QC ? (uint32_t)QC : Q, k1, orow);
+        }
+    }
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+    asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// Pack of dense fp16 rows (stride ld_in): one CTA per row at a time, several
+// CTAs per SM; the row is staged with 16-byte cp.async copies.
+template <int THREADS, int QC, int J>
+__global__ void __launch_bounds__(THREADS, THREADS == 128 ? 7 : 3) makhoul_pack_kernel(
+    const uint16_t *__restrict__ in, uint64_t ld_in, uint64_t B, uint32_t L, uint32_t P,
+    uint32_t Q, const float4 *__restrict__ coef, uint32_t *__restrict__ out) {
+    extern __shared__ uint4 smem_v[];
+    uint16_t *srow = reinterpret_cast<uint16_t *>(smem_v);
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool vec = ((ld_in & 7) == 0) && (((uintptr_t)in & 15) == 0);
+    const uint32_t nv = L / 8;  // L % 32 == 0 for every factored length
+    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(srow);
+    if (threadIdx.x == 0) srow[spad<QC>(L)] = 0;  // c[L] = 0 (never overwritten)
+    for (uint64_t b = blockIdx.x; b < B; b += gridDim.x) {
+        __syncthreads();  // previous row fully consumed
+        const uint16_t *row = in + b * ld_in;
+        if (vec) {
+            for (uint32_t v = threadIdx.x; v < nv; v += THREADS)
+                cp_async16(sbase + 2 * spad<QC>(8 * v), row + 8 * v);
+            cp_async_wait_all();
+        } else {
+            for (uint32_t k = threadIdx.x; k < L; k += THREADS) srow[spad<QC>(k)] = row[k];
         }
         __syncthreads();
-        pack_rows<NR>(srow, sstride, coefT, L, P, Q, out + b * (uint64_t)(L / 2), L / 2, nvalid);
+        pack_row<QC, J>(srow, coef, L, P, Q, out + b * (uint64_t)(L / 2), warp, THREADS / 32,
+                        lane);
     }
 }
 
-// Row pack straight from the spectral payload (bitmap ++ INT4).  Each CTA
-// decodes the coefficients of its row into shared memory and then runs the
-// pack:
-//   A. warp w takes a run of the row's 64-bit bitmap words (a multiple of 4,
-//      one per lane) and a warp scan of their popcounts; warp 0 adds up the
-//      row's rank (the rank directory of launch_spectral_rank for its
-//      1024-bit chunk plus a partial popcount);
-//   B. the row's coefficients in rank order are staged in shared memory:
-//      fp16((nibble - 8) * scale) per set bit, four ranks per thread and
-//      step (one 16-bit nibble load, one scale) when the row has at most L/2
-//      of them; else the raw nibble bytes and the f32 scales;
-//   C. each warp expands its words 256 elements per step: lane l takes bitmap
-//      byte l of four consecutive words and writes its 8 elements (zero where
-//      the bit is clear) as four 32-bit words, which the one-word pad per 64
-//      elements spreads over all 32 banks.
-// Requires L % 64 == 0 (rows start on a 64-bit bitmap boundary) and
-// L / 64 <= 32 * SPACK_WARPS.
-constexpr int SPACK_THREADS = 512;
-constexpr int SPACK_WARPS = SPACK_THREADS / 32;
+// Row pack straight from the spectral payload (bitmap ++ INT4): one CTA per
+// row at a time, several CTAs per SM.
+//   A. the row's 64-bit bitmap words into shared memory and their
+//      popcounts scanned over the CTA (each word's rank within the row);
+//      warp 0 reads the row's first rank from the rank directory of
+//      launch_spectral_rank plus a partial popcount;
+//   B. the row's coefficients in rank order are staged: when the row has at
+//      most L/2 of them as fp16 (nibble - 8) * scale, 8 ranks per thread and
+//      step (a nibble placed in the mantissa of 1024.0 gives 1024 + nibble;
+//      HSUB2 of 1032 is exact and HMUL2 rounds the exact product once, as
+//      the f32 product rounded to fp16 does); else the raw nibble bytes and
+//      the f32 scales;
+//   C. lane l of a warp step takes byte (l & 7) of word 4 s + (l >> 3) and
+//      writes its 8 elements (zero where the bit is clear) as one 16-byte
+//      store into the staged row;
+//   D. pack_row.
+// Requires L % 64 == 0 (rows start on a 64-bit bitmap boundary).
+__host__ __device__ __forceinline__ uint32_t spack_raw_nib_bytes(uint32_t L) {
+    return (L / 2 + 16 + 15) & ~15u;
+}
 
-// bytes of the staging area behind the row: L/2 + 8 fp16 values, or L/2
-// nibble bytes (+ 16 slack) and L/32 + 4 f32 scales
+// bytes of the staging area: L/2 + 16 fp16 values, or L/2 nibble bytes
+// (+ slack) and L/32 + 4 f32 scales
 __host__ __device__ __forceinline__ uint32_t spack_stage_bytes(uint32_t L) {
-    const uint32_t vals = L + 16, raw = ((L / 2 + 16 + 15) & ~15u) + (L / 32 + 4) * 4;
+    const uint32_t vals = L + 32, raw = spack_raw_nib_bytes(L) + (L / 32 + 4) * 4;
     return vals > raw ? vals : raw;
 }
 
-__device__ __forceinline__ float deq_nibble(uint32_t byte, uint64_t r, float scale) {
-    const uint32_t nib = (r & 1) ? byte >> 4 : byte & 0xfu;
-    return __fmul_rn((float)((int)nib - 8), scale);
+__host__ __device__ __forceinline__ uint32_t spack_words_pad(uint32_t L) {
+    return (L / 64 + 3) & ~3u;
 }
 
-__global__ void __launch_bounds__(SPACK_THREADS, 4) spectral_pack_kernel(
+__host__ __device__ __forceinline__ size_t spack_smem_bytes(uint32_t L, int qc) {
+    return (size_t)srow_halves(L, qc) * 2 + (size_t)spack_words_pad(L) * 12 +
+           spack_stage_bytes(L);
+}
+
+// 16 bits of the nibble section at byte nb (even); bytes at or past nib_len
+// read as zero
+__device__ __forceinline__ uint32_t ld_nib16(const uint8_t *nibbles, uint32_t nb,
+                                             uint64_t nib_len) {
+    if ((uint64_t)nb + 1 < nib_len) return *reinterpret_cast<const uint16_t *>(nibbles + nb);
+    return (uint64_t)nb < nib_len ? (uint32_t)nibbles[nb] : 0u;
+}
+
+__device__ __forceinline__ uint16_t deq_nibble_h(uint32_t byte, uint32_t r, float scale) {
+    const uint32_t nib = (r & 1) ? byte >> 4 : byte & 0xfu;
+    return __half_as_ushort(__float2half_rn(__fmul_rn((float)((int)nib - 8), scale)));
+}
+
+template <int THREADS, int QC, int J>
+__global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack_kernel(
     const uint8_t *__restrict__ payload, uint64_t bmb, const uint32_t *__restrict__ chunk_base,
     uint64_t group_off, const uint64_t *__restrict__ meta, uint64_t B, uint32_t L, uint32_t P,
     uint32_t Q, const float4 *__restrict__ coef, uint32_t *__restrict__ out) {
-    extern __shared__ uint16_t srow[];
-    __shared__ uint32_t warp_tot[SPACK_WARPS];
-    __shared__ uint32_t s_rank_start;
-    uint8_t *stage = reinterpret_cast<uint8_t *>(srow + srow_halves(L));
+    constexpr uint32_t NW = THREADS / 32;
+    extern __shared__ uint4 smem_v[];
+    __shared__ uint32_t warp_tot[NW];
+    __shared__ uint32_t s_rank0;
+    const uint32_t W = L / 64;
+    uint16_t *srow = reinterpret_cast<uint16_t *>(smem_v);
+    uint64_t *sw = reinterpret_cast<uint64_t *>(srow + srow_halves(L, QC));
+    uint32_t *swr = reinterpret_cast<uint32_t *>(sw + spack_words_pad(L));
+    uint8_t *stage = reinterpret_cast<uint8_t *>(swr + spack_words_pad(L));
     uint16_t *vals_s = reinterpret_cast<uint16_t *>(stage);
     uint8_t *nib_s = stage;
-    float *sc_s = reinterpret_cast<float *>(stage + ((L / 2 + 16 + 15) & ~15u));
-    uint32_t *srow32 = reinterpret_cast<uint32_t *>(srow);
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t segs = L / 64;
-    const uint32_t spw = ((segs + SPACK_WARPS - 1) / SPACK_WARPS + 3) & ~3u;  // <= 32
-    const uint32_t seg0 = warp * spw;
-    const uint32_t nseg = seg0 < segs ? min(spw, segs - seg0) : 0u;
+    float *sc_s = reinterpret_cast<float *>(stage + spack_raw_nib_bytes(L));
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint64_t k_total = meta[0];
     const uint64_t nib_len = (k_total + 1) >> 1;  // bytes of the nibble section
     const uint8_t *scales = payload + bmb;
@@ -267,24 +297,29 @@ __global__ void __launch_bounds__(SPACK_THREADS, 4) spectral_pack_kernel(
     const bool bad = meta[2] != 0;
     const uint64_t *bm64 = reinterpret_cast<const uint64_t *>(payload);
     const uint32_t *bm32 = reinterpret_cast<const uint32_t *>(payload);
+    const uint32_t wpt = (W + THREADS - 1) / THREADS, w0 = tid * wpt;
     // expand geometry of this lane: byte (lane & 7) of word (lane >> 3) of a span
-    const uint32_t sub = lane >> 3, bshift = 8 * (lane & 7);
-    const uint64_t below8 = (1ull << bshift) - 1ull;
-    // raw-nibble expand (rows over half full): elements (2l, 2l + 1) of a word
-    const uint32_t pair_shift = 2 * lane;
-    const uint64_t below2 = (1ull << pair_shift) - 1ull;
-    if (threadIdx.x == 0) srow[pad_idx(L)] = 0;  // c[L] = 0 (never overwritten)
+    const uint32_t sub = lane >> 3, bsh = 8 * (lane & 7);
+    const uint64_t below8 = (1ull << bsh) - 1ull;
+    if (tid == 0) srow[spad<QC>(L)] = 0;  // c[L] = 0 (never overwritten)
 
     for (uint64_t b = blockIdx.x; b < B; b += gridDim.x) {
         __syncthreads();  // previous row fully consumed
         // A. bitmap words and their ranks
-        const uint64_t mw = lane < nseg ? bm64[b * segs + seg0 + lane] : 0ull;
-        const uint32_t cnt = __popcll(mw);
+        uint32_t cnt = 0;
+        for (uint32_t i = 0; i < wpt; i++) {
+            const uint32_t w = w0 + i;
+            if (w < W) {
+                const uint64_t x = bm64[b * W + w];
+                sw[w] = x;
+                cnt += __popcll(x);
+            }
+        }
         uint32_t incl = cnt;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += t;
+            if (lane >= (uint32_t)o) incl += t;
         }
         if (lane == 31) warp_tot[warp] = incl;
         if (warp == 0) {
@@ -295,105 +330,104 @@ __global__ void __launch_bounds__(SPACK_THREADS, 4) spectral_pack_kernel(
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
             if (lane == 0)
-                s_rank_start = chunk_base[c0] + chunk_base[group_off + c0 / RANK_GROUP] + part;
+                s_rank0 = chunk_base[c0] + chunk_base[group_off + c0 / RANK_GROUP] + part;
         }
         __syncthreads();
-        // rank of this warp's first bit within the row, and the row's count
-        const uint32_t wt = lane < SPACK_WARPS ? warp_tot[lane] : 0u;
-        uint32_t wincl = wt;
+        uint32_t run = incl - cnt, row_count = 0;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t t = __shfl_up_sync(0xffffffffu, wincl, o);
-            if (lane >= o) wincl += t;
+        for (uint32_t v = 0; v < NW; v++) {
+            const uint32_t t = warp_tot[v];
+            run += v < warp ? t : 0u;
+            row_count += t;
         }
-        const uint32_t before = __shfl_sync(0xffffffffu, wincl - wt, warp);
-        const uint32_t row_count = __shfl_sync(0xffffffffu, wincl, SPACK_WARPS - 1);
-        const uint64_t rank0 = s_rank_start;
-        const bool packed_vals = 2 * row_count <= L;
-        const uint64_t a4 = rank0 & ~3ull;  // vals_s[i] holds rank a4 + i
-        const uint64_t nb0 = rank0 >> 1, sb0 = rank0 >> 5;
+        for (uint32_t i = 0; i < wpt; i++) {
+            const uint32_t w = w0 + i;
+            if (w < W) {
+                swr[w] = run;
+                run += __popcll(sw[w]);
+            }
+        }
+        const uint32_t rank0 = s_rank0;
+        const bool packed = 2 * row_count <= L;
+        const uint32_t a8 = rank0 & ~7u;  // vals_s[i] holds rank a8 + i
+        const uint32_t nb0 = rank0 >> 1, sb0 = rank0 >> 5;
         // B. stage the row's coefficients (rank order); a short payload
         // (meta[2]) decodes to zeros and never reads past its end
         if (!bad) {
-            if (packed_vals) {
-                const uint32_t ngroups = (uint32_t)((rank0 + row_count + 3 - a4) >> 2);
-                for (uint32_t g = threadIdx.x; g < ngroups; g += SPACK_THREADS) {
-                    const uint64_t r = a4 + 4ull * g;  // a multiple of 4, below k_total
-                    const uint64_t nb = r >> 1;        // even: a 16-bit aligned pair
-                    uint32_t nib4;
-                    if (nb + 1 < nib_len) nib4 = *reinterpret_cast<const uint16_t *>(nibbles + nb);
-                    else nib4 = nb < nib_len ? (uint32_t)nibbles[nb] : 0u;
-                    const float sc = __half2float(__ushort_as_half(
-                        *reinterpret_cast<const uint16_t *>(scales + 2 * (r >> 5))));
-                    float v[4];
+            if (packed) {
+                const uint32_t n8 = (rank0 + row_count - a8 + 7) >> 3;
+                const __half2 off = __float2half2_rn(1032.0f);
+                for (uint32_t gi = tid; gi < n8; gi += THREADS) {
+                    const uint32_t r = a8 + 8 * gi;  // below k_total
+                    const uint32_t nb = r >> 1;      // a multiple of 4
+                    const uint32_t x =
+                        ld_nib16(nibbles, nb, nib_len) | (ld_nib16(nibbles, nb + 2, nib_len) << 16);
+                    const uint32_t e = x & 0x0F0F0F0Fu, o = (x >> 4) & 0x0F0F0F0Fu;
+                    const __half sh = __ushort_as_half(
+                        *reinterpret_cast<const uint16_t *>(scales + 2 * (r >> 5)));
+                    const __half2 s2 = __halves2half2(sh, sh);
+                    uint32_t wv[4];
 #pragma unroll
-                    for (int t = 0; t < 4; t++)
-                        v[t] = __fmul_rn((float)((int)((nib4 >> (4 * t)) & 0xfu) - 8), sc);
-                    *reinterpret_cast<uint2 *>(vals_s + 4 * g) =
-                        make_uint2(pack_z(v[0], v[1]), pack_z(v[2], v[3]));
+                    for (uint32_t i = 0; i < 4; i++) {
+                        // (nibble 2i, nibble 2i + 1) as (1024 + n0, 1024 + n1)
+                        const uint32_t p = (__byte_perm(e, o, i | ((4 + i) << 8)) & 0x00FF00FFu) |
+                                           0x64006400u;
+                        const __half2 h = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&p), off), s2);
+                        wv[i] = *reinterpret_cast<const uint32_t *>(&h);
+                    }
+                    *reinterpret_cast<uint4 *>(vals_s + 8 * gi) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
                 }
             } else {
-                const uint64_t nb1 = (rank0 + row_count + 1) >> 1;
-                const uint64_t sb1 = row_count ? ((rank0 + row_count - 1) >> 5) + 1 : sb0;
-                for (uint64_t i = nb0 + threadIdx.x; i < nb1; i += SPACK_THREADS)
-                    nib_s[i - nb0] = nibbles[i];
-                for (uint64_t i = sb0 + threadIdx.x; i < sb1; i += SPACK_THREADS)
+                const uint32_t nb1 = (rank0 + row_count + 1) >> 1;
+                const uint32_t sb1 = row_count ? ((rank0 + row_count - 1) >> 5) + 1 : sb0;
+                for (uint32_t i = nb0 + tid; i < nb1; i += THREADS) nib_s[i - nb0] = nibbles[i];
+                for (uint32_t i = sb0 + tid; i < sb1; i += THREADS)
                     sc_s[i - sb0] = __half2float(__ushort_as_half(
-                        (uint16_t)((uint32_t)scales[2 * i] | ((uint32_t)scales[2 * i + 1] << 8))));
+                        (uint16_t)((uint32_t)scales[2 * (uint64_t)i] |
+                                   ((uint32_t)scales[2 * (uint64_t)i + 1] << 8))));
             }
         }
         __syncthreads();
-        // C. expand this warp's words into the staged row
-        const uint32_t wrank = before + incl - cnt;  // rank of my word within the row
-        if (packed_vals) {
-            const uint32_t roff = (uint32_t)(rank0 - a4);
-            uint32_t *dst = srow32 + 33 * (seg0 + sub) + 4 * (lane & 7);
-            const uint32_t nspan = (nseg + 3) >> 2;  // nseg <= 32: s stays below 32
-            for (uint32_t i = 0; i < nspan; i++, dst += 132) {  // 4 x (64 elements + pad)
-                const uint32_t s = 4 * i + sub;
-                const uint64_t w = __shfl_sync(0xffffffffu, mw, s);
-                const uint32_t wr = __shfl_sync(0xffffffffu, wrank, s);
-                if (s < nseg) {
-                    const uint32_t byte = bad ? 0u : (uint32_t)(w >> bshift) & 0xffu;
-                    uint32_t r = wr + roff + __popcll(w & below8);
-                    uint32_t h[8];
+        // C. expand the words into the staged row, 4 words per warp step
+        const uint32_t roff = rank0 - a8;
+        for (uint32_t sp = warp; 4 * sp < W; sp += NW) {
+            const uint32_t w = 4 * sp + sub;
+            if (w < W) {
+                const uint64_t x = sw[w];
+                const uint32_t byte = bad ? 0u : (uint32_t)(x >> bsh) & 0xffu;
+                const uint32_t q = swr[w] + __popcll(x & below8);  // rank within the row
+                uint32_t h[8];
+                if (packed) {
+                    uint32_t r = q + roff;
 #pragma unroll
-                    for (int j = 0; j < 8; j++) {
-                        const uint32_t bit = (byte >> j) & 1u;
-                        h[j] = bit ? (uint32_t)vals_s[r] : 0u;
+                    for (int t = 0; t < 8; t++) {
+                        const uint32_t bit = (byte >> t) & 1u;
+                        h[t] = bit ? (uint32_t)vals_s[r] : 0u;
                         r += bit;
                     }
-                    dst[0] = h[0] | (h[1] << 16);
-                    dst[1] = h[2] | (h[3] << 16);
-                    dst[2] = h[4] | (h[5] << 16);
-                    dst[3] = h[6] | (h[7] << 16);
+                } else {
+                    uint32_t gr = rank0 + q;
+#pragma unroll
+                    for (int t = 0; t < 8; t++) {
+                        const uint32_t bit = (byte >> t) & 1u;
+                        h[t] = bit ? (uint32_t)deq_nibble_h(nib_s[(gr >> 1) - nb0], gr,
+                                                            sc_s[(gr >> 5) - sb0])
+                                   : 0u;
+                        gr += bit;
+                    }
                 }
-            }
-        } else {
-            uint32_t *dst = srow32 + 33 * seg0 + lane;  // 64 elements + 2 pad halves per word
-            for (uint32_t i = 0; i < nseg; i++, dst += 33) {
-                const uint64_t w = __shfl_sync(0xffffffffu, mw, i);
-                const uint32_t r = __shfl_sync(0xffffffffu, wrank, i) + __popcll(w & below2);
-                const uint32_t m2 = (uint32_t)(w >> pair_shift) & 3u;
-                uint32_t pair = 0;
-                if (!bad && m2) {
-                    const uint64_t g0 = rank0 + r, g1 = g0 + (m2 & 1u);
-                    float v0 = 0.0f, v1 = 0.0f;
-                    if (m2 & 1u) v0 = deq_nibble(nib_s[(g0 >> 1) - nb0], g0, sc_s[(g0 >> 5) - sb0]);
-                    if (m2 & 2u) v1 = deq_nibble(nib_s[(g1 >> 1) - nb0], g1, sc_s[(g1 >> 5) - sb0]);
-                    pair = pack_z(v0, v1);
-                }
-                *dst = pair;
+                *reinterpret_cast<uint4 *>(srow + spad<QC>(64 * w + 8 * (lane & 7))) =
+                    make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16),
+                               h[6] | (h[7] << 16));
             }
         }
         __syncthreads();
-        pack_row(srow, coef, L, P, Q, out + b * (uint64_t)(L / 2));
+        pack_row<QC, J>(srow, coef, L, P, Q, out + b * (uint64_t)(L / 2), warp, NW, lane);
     }
 }
 
-// coefT[k2 * P + k1] = (alpha_k, beta_k), k = Q k1 + k2 < L/2 (see the file
-// comment), in f64.
-__global__ void pack_tables_kernel(uint32_t L, uint32_t P, uint32_t Q, float4 *coefT) {
+// coef[k] = (alpha_k, beta_k) for k < L/2 (see the file comment), in f64.
+__global__ void pack_tables_kernel(uint32_t L, float4 *coef) {
     const uint32_t H = L / 2;
     for (uint32_t k = blockIdx.x * blockDim.x + threadIdx.x; k < H; k += gridDim.x * blockDim.x) {
         double sa, ca, sb, cb, st, ct;
@@ -407,7 +441,7 @@ __global__ void pack_tables_kernel(uint32_t L, uint32_t P, uint32_t Q, float4 *c
         // beta = 1/2 b (1 - i t) = 1/2 b (1 + st - i ct)
         const double qr = 1.0 + st, qi = -ct;
         const double br = 0.5 * (cb * qr - sb * qi), bi = 0.5 * (cb * qi + sb * qr);
-        coefT[(k % Q) * P + k / Q] = make_float4((float)ar, (float)ai, (float)br, (float)bi);
+        coef[k] = make_float4((float)ar, (float)ai, (float)br, (float)bi);
     }
 }
 
@@ -448,14 +482,19 @@ bool fdct_factor(uint64_t L, uint32_t *P, uint32_t *Q) {
     if (L < 16 || (L & 1)) return false;
     const uint64_t H = L / 2;
     uint32_t best_p = 0, best_q = 0;
+    auto fast_q = [](uint64_t q) { return q == 16 || q == 32 || q == 64 || q == 128; };
     for (uint32_t p = 4; p <= 128; p += 4) {
         if (H % p) continue;
         const uint64_t q = H / p;
         if (q > 128 || q % 4) continue;
-        // most balanced split
+        // most balanced split; among equally balanced ones, a Q that the
+        // pack kernels specialise (16, 32, 64, 128)
         const uint64_t cur = best_p ? (best_p > best_q ? best_p - best_q : best_q - best_p) : ~0ull;
         const uint64_t d = p > q ? p - q : q - p;
-        if (d < cur) { best_p = p; best_q = (uint32_t)q; }
+        if (d < cur || (d == cur && fast_q(q) && !fast_q(best_q))) {
+            best_p = p;
+            best_q = (uint32_t)q;
+        }
     }
     if (!best_p) return false;
     *P = best_p;
@@ -463,54 +502,116 @@ bool fdct_factor(uint64_t L, uint32_t *P, uint32_t *Q) {
     return true;
 }
 
-cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t B, uint32_t L,
-                                uint32_t P, uint32_t Q, const float *d_tables, half_bits *d_out,
-                                cudaStream_t s) {
-    const bool small = L <= 16384;
-    const size_t smem = (size_t)srow_halves(L) * 2 * (small ? 2 : 1);
-    if (smem > 220 * 1024) return cudaErrorInvalidValue;
-    auto kern = small ? makhoul_pack_kernel<256, 4, 2> : makhoul_pack_kernel<512, 2, 1>;
+namespace {
+
+int sm_count() {
+    static int n = 0;
+    if (n <= 0) {
+        int dev = 0, v = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess &&
+            cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
+            n = v;
+        else
+            return 148;
+    }
+    return n;
+}
+
+// Specialisation of the pack for (P, Q): runs of 8 with compile-time read
+// offsets for Q in {64, 128} and P % 8 == 0; else 0 (runs of 4, any Q).
+int pack_qc(uint32_t P, uint32_t Q) {
+    if (P % 8 == 0 && (Q == 64 || Q == 128)) return (int)Q;
+    return 0;
+}
+
+using MakhoulFn = void (*)(const uint16_t *, uint64_t, uint64_t, uint32_t, uint32_t, uint32_t,
+                           const float4 *, uint32_t *);
+using SpectralFn = void (*)(const uint8_t *, uint64_t, const uint32_t *, uint64_t,
+                            const uint64_t *, uint64_t, uint32_t, uint32_t, uint32_t,
+                            const float4 *, uint32_t *);
+
+template <int T>
+MakhoulFn makhoul_fn(int qc) {
+    switch (qc) {
+        case 64: return makhoul_pack_kernel<T, 64, 8>;
+        case 128: return makhoul_pack_kernel<T, 128, 8>;
+        default: return makhoul_pack_kernel<T, 0, 4>;
+    }
+}
+
+template <int T>
+SpectralFn spectral_fn(int qc) {
+    switch (qc) {
+        case 64: return spectral_pack_kernel<T, 64, 8>;
+        case 128: return spectral_pack_kernel<T, 128, 8>;
+        default: return spectral_pack_kernel<T, 0, 4>;
+    }
+}
+
+// grid of a persistent row kernel: resident CTAs x SMs, at most one per row
+template <typename F>
+cudaError_t row_grid(F kern, int threads, size_t smem, uint64_t B, unsigned *grid) {
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    const uint64_t per_sm = small ? 4 : 2;
-    const uint64_t units = small ? (B + 1) / 2 : B;  // row pairs or rows
-    uint64_t g = units < 148ull * per_sm ? units : 148ull * per_sm;
-    if (g < 1) g = 1;
-    kern<<<(unsigned)g, small ? 256 : 512, smem, s>>>(d_in, ld_in, B, L, P, Q,
-                                                      reinterpret_cast<const float4 *>(d_tables),
-                                                      reinterpret_cast<uint32_t *>(d_out));
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    const uint64_t cap = (uint64_t)per_sm * (uint64_t)sm_count();
+    *grid = (unsigned)(B < cap ? (B < 1 ? 1 : B) : cap);
+    return cudaSuccess;
+}
+
+}  // namespace
+
+cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t B, uint32_t L,
+                                uint32_t P, uint32_t Q, const float *d_tables, half_bits *d_out,
+                                cudaStream_t s) {
+    if (L % 32 || (uint64_t)P * Q != L / 2 || P % 4 || Q % 4) return cudaErrorInvalidValue;
+    const int qc = pack_qc(P, Q);
+    const size_t smem = (size_t)srow_halves(L, qc) * 2;
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    const bool small = L <= 16384;
+    const int threads = small ? 128 : 256;
+    MakhoulFn kern = small ? makhoul_fn<128>(qc) : makhoul_fn<256>(qc);
+    unsigned g = 0;
+    cudaError_t e = row_grid(kern, threads, smem, B, &g);
+    if (e != cudaSuccess) return e;
+    kern<<<g, threads, smem, s>>>(d_in, ld_in, B, L, P, Q,
+                                  reinterpret_cast<const float4 *>(d_tables),
+                                  reinterpret_cast<uint32_t *>(d_out));
     return cudaGetLastError();
 }
 
 bool spectral_pack_supported(uint64_t L) {
-    return L % 64 == 0 && L / 64 <= 32ull * SPACK_WARPS;
+    return L % 64 == 0 && L <= (1u << 20) && spack_smem_bytes((uint32_t)L, 64) <= 200 * 1024;
 }
 
 cudaError_t launch_spectral_pack(const uint8_t *d_payload, uint64_t bmb, const uint32_t *d_chunk,
                                  const uint64_t *d_meta, uint64_t B, uint32_t L, uint32_t P,
                                  uint32_t Q, const float *d_tables, half_bits *d_out,
                                  cudaStream_t s) {
-    if (!spectral_pack_supported(L)) return cudaErrorInvalidValue;
-    // dynamic shared memory: the row and its staged coefficients
-    const size_t smem = (size_t)srow_halves(L) * 2 + spack_stage_bytes(L);
-    if (smem > 220 * 1024) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(spectral_pack_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (!spectral_pack_supported(L) || (uint64_t)P * Q != L / 2 || P % 4 || Q % 4)
+        return cudaErrorInvalidValue;
+    const int qc = pack_qc(P, Q);
+    const size_t smem = spack_smem_bytes(L, qc);
+    const bool small = L <= 16384;
+    const int threads = small ? 128 : 256;
+    SpectralFn kern = small ? spectral_fn<128>(qc) : spectral_fn<256>(qc);
+    unsigned g = 0;
+    cudaError_t e = row_grid(kern, threads, smem, B, &g);
     if (e != cudaSuccess) return e;
-    uint64_t g = B < 148ull * 4 ? B : 148ull * 4;
-    if (g < 1) g = 1;
-    spectral_pack_kernel<<<(unsigned)g, SPACK_THREADS, smem, s>>>(
-        d_payload, bmb, d_chunk, rank_group_offset(B * (uint64_t)L), d_meta, B, L, P, Q,
-        reinterpret_cast<const float4 *>(d_tables), reinterpret_cast<uint32_t *>(d_out));
+    kern<<<g, threads, smem, s>>>(d_payload, bmb, d_chunk, rank_group_offset(B * (uint64_t)L),
+                                  d_meta, B, L, P, Q, reinterpret_cast<const float4 *>(d_tables),
+                                  reinterpret_cast<uint32_t *>(d_out));
     return cudaGetLastError();
 }
 
 cudaError_t launch_pack_tables(uint32_t L, uint32_t P, uint32_t Q, float *d_tables,
                                cudaStream_t s) {
     if ((uint64_t)P * Q != L / 2) return cudaErrorInvalidValue;
-    pack_tables_kernel<<<(L / 2 + 255) / 256, 256, 0, s>>>(L, P, Q,
-                                                            reinterpret_cast<float4 *>(d_tables));
+    pack_tables_kernel<<<(L / 2 + 255) / 256, 256, 0, s>>>(L, reinterpret_cast<float4 *>(d_tables));
     return cudaGetLastError();
 }
 

@@ -171,6 +171,7 @@ struct hct_b200_ctx {
     cudaStream_t side = nullptr;
     DevBuf dense, tt, chunk, meta, flag;
     DevBuf za, zb;  // factored-IDCT intermediates (rows*cols fp16 each)
+    DevBuf sched;   // tile counters of the DFT stage kernels
     DevBuf io_in, io_out, io_blk, io_status;
     std::map<uint64_t, std::unique_ptr<Basis>> bases;
     std::map<uint32_t, std::unique_ptr<DevBuf>> dft_mats;  // realified n-point DFT, fp16
@@ -219,6 +220,33 @@ struct hct_b200_v3 {
     uint64_t rows = 0, cols = 0;  // of the transform (a column vector is one row)
     DevBuf d_data;
     std::vector<Frag> frags;
+};
+
+// A parsed HoloTensor file: the header, one record per fragment index entry
+// (what read_fragment + add_fragment would make of it), and the f32 values
+// of its SV03 fragments on the device.
+struct hct_b200_holo {
+    enum Kind {
+        SV03 = 0,
+        PAST_END,    // the stored bytes run past the file ("failed to read fragment data")
+        COMPRESSED,  // entry flag bit 0: zstd
+        SHORT,       // fewer than 8 bytes ("fragment too short")
+        V3_SHORT,    // SV03 magic, fewer than 20 bytes ("V3 fragment too short")
+        LEGACY,      // the V1 or V2 spectral layouts
+    };
+    struct Frag {
+        uint16_t index = 0;
+        Kind kind = SV03;
+        bool checksum_ok = true;
+        uint32_t num_coeffs = 0, F = 0, start = 0;
+        uint64_t count = 0;  // values add_fragment_v3 writes (before its position < n check)
+        uint64_t dev_off = 0;  // f32 elements into d_vals
+    };
+    hct_b200_ctx *ctx = nullptr;
+    hct_b200_holo_info hdr{};
+    std::vector<Frag> frags;  // index-table order; the inline form has one
+    uint64_t rows = 0, cols = 0;  // of the transform (a column vector is one row)
+    DevBuf d_vals, d_res;
 };
 
 struct hct_b200_reader {
@@ -408,8 +436,10 @@ int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint
                                ctx->za.as<half_bits>(), s));
         ctx->prof_end(slot, PK_PACK, 4.0 * elems, s);
     }
+    CK(ctx->sched.reserve(64));
     GemmArgs g1{ctx->za.as<half_bits>(), wp, batch * Q, 2ull * P, 2ull * P, 2ull * P, 2ull * P,
                 ctx->zb.p, 0, 2, HCT_B200_F16, flag};
+    g1.tile_counter = ctx->sched.as<uint32_t>();
     g1.P = P;
     g1.Q = Q;
     g1.H = H;
@@ -420,6 +450,7 @@ int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint
     ctx->prof_end(slot, PK_DFT1, 4.0 * elems, s);
     GemmArgs g2{ctx->zb.as<half_bits>(), wq, (uint64_t)P * batch, 2ull * Q, 2ull * Q, 2ull * Q,
                 2ull * Q, out, ldo, 3, out_dtype, flag};
+    g2.tile_counter = ctx->sched.as<uint32_t>() + 1;
     g2.P = P;
     g2.Q = Q;
     g2.H = H;
@@ -932,6 +963,361 @@ int hct_b200_hct_v3_decode(hct_b200_ctx *ctx, const uint8_t *data, size_t len, u
     rc = hct_b200_v3_decode(v, d_out, out_dtype, stream, err);
     hct_b200_v3_close(v);
     return rc;
+}
+
+// ---- HoloTensor -------------------------------------------------------------
+// HoloTensorReader (crates/haagenti-hct/src/holotensor.rs:1935-2192) and the
+// SV03 part of SpectralDecoder (:840-1051).  The container is parsed on the
+// host; every fragment's values are uploaded once; a decode scatters the
+// first k fragments into the dense fp16 coefficient matrix (holo.cu) and runs
+// the IDCT of idct_gemm.cu / fdct.cu on it.
+
+namespace {
+
+constexpr uint32_t HOLO_VERSION = 1;                  // holotensor.rs:50
+constexpr uint16_t HOLO_FLAG_HEADER_CHECKSUM = 0x0001;  // :53
+constexpr uint16_t HOLO_FLAG_FRAGMENT_CHECKSUMS = 0x0002;  // :56
+constexpr size_t HOLO_HEADER_SIZE = 96;               // HoloTensorHeader::BASE_SIZE, :442
+constexpr size_t HOLO_ENTRY_SIZE = 24;                // FragmentIndexEntry::SIZE, :349
+constexpr uint32_t SV03_MAGIC = 0x33305653;           // :794
+
+// QualityCurve::predict (holotensor.rs:199-220) in f32, one rounding per
+// operation as the Rust code has.
+float holo_predict(const hct_b200_holo_info &h, uint32_t k, uint32_t n) {
+    if (n == 0) return 0.0f;
+    if (k >= n) return 1.0f;
+    if (k < h.min_fragments) return 0.0f;
+    const float x = (float)k / (float)n;
+    float result = 0.0f, xp = 1.0f;
+    for (int i = 0; i < 4; i++) {
+        volatile float t = h.quality_curve[i] * xp;
+        result = result + t;
+        volatile float nx = xp * x;
+        xp = nx;
+    }
+    return result < 0.0f ? 0.0f : (result > 1.0f ? 1.0f : result);
+}
+
+uint32_t holo_total(const hct_b200_holo *h) {
+    return h->hdr.inline_format ? 1u : (uint32_t)h->hdr.total_fragments;
+}
+
+}  // namespace
+
+int hct_b200_holo_open(hct_b200_ctx *ctx, const uint8_t *file, size_t len, hct_b200_holo **out,
+                       hct_b200_error *err) {
+    clear_err(err);
+    if (!ctx || !out || (!file && len)) {
+        set_err(err, HCT_B200_ERR_INVALID_ARGUMENT, -1, 0, 0, 0, "null argument");
+        return HCT_B200_ERR_INVALID_ARGUMENT;
+    }
+    *out = nullptr;
+    // HoloTensorHeader::from_bytes (holotensor.rs:571-656)
+    if (len < HOLO_HEADER_SIZE) {
+        set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0, "failed to read header");
+        return HCT_B200_ERR_CORRUPTED;
+    }
+    if (memcmp(file, "HTNS", 4) != 0) {
+        set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0, "invalid magic bytes");
+        return HCT_B200_ERR_CORRUPTED;
+    }
+    const uint32_t version = rd32(file + 4);
+    if (version != HOLO_VERSION) {
+        set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0, "unsupported version: %u", version);
+        return HCT_B200_ERR_CORRUPTED;
+    }
+    const uint16_t flags = rd16(file + 10);
+    Xxh3Fn xxh = xxh3_fn();
+    if ((flags & (HOLO_FLAG_HEADER_CHECKSUM | HOLO_FLAG_FRAGMENT_CHECKSUMS)) && !xxh) {
+        set_err(err, HCT_B200_ERR_UNSUPPORTED, -1, 0, 0, 0, "XXH3 (libxxhash) unavailable");
+        return HCT_B200_ERR_UNSUPPORTED;
+    }
+    if ((flags & HOLO_FLAG_HEADER_CHECKSUM) && rd64(file + 88) != xxh(file, 88)) {
+        set_err(err, HCT_B200_ERR_CHECKSUM, -1, 0, 0, 0, "header checksum mismatch");
+        return HCT_B200_ERR_CHECKSUM;
+    }
+    if (file[8] > 2 || file[9] > 1 || file[32] > 4) {
+        set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0, "unknown %s: %u",
+                file[8] > 2 ? "encoding" : (file[9] > 1 ? "algorithm" : "dtype"),
+                file[8] > 2 ? file[8] : (file[9] > 1 ? file[9] : file[32]));
+        return HCT_B200_ERR_CORRUPTED;
+    }
+    auto h = std::make_unique<hct_b200_holo>();
+    h->ctx = ctx;
+    hct_b200_holo_info &hd = h->hdr;
+    hd.encoding = file[8];
+    hd.compression = file[9];
+    hd.flags = flags;
+    hd.total_fragments = rd16(file + 12);
+    hd.min_fragments = rd16(file + 14);
+    hd.original_size = rd64(file + 16);
+    hd.seed = rd64(file + 24);
+    hd.dtype = file[32];
+    hd.ndim = file[33];
+    if (34 + 8 * (size_t)hd.ndim > HOLO_HEADER_SIZE) {  // the shape would run past the header
+        set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0, "shape of %u dimensions", hd.ndim);
+        return HCT_B200_ERR_CORRUPTED;
+    }
+    for (int i = 0; i < hd.ndim; i++) hd.shape[i] = rd64(file + 34 + 8 * i);
+    for (int i = 0; i < 4; i++) {
+        const uint32_t bits = rd32(file + 66 + 4 * i);
+        memcpy(&hd.quality_curve[i], &bits, 4);
+    }
+    // HoloTensorDecoder::new's 2-D view (holotensor.rs:1732-1744)
+    uint64_t rows = 1, cols = 1;
+    if (hd.ndim == 1) {
+        cols = hd.shape[0];
+    } else if (hd.ndim == 2) {
+        rows = hd.shape[0];
+        cols = hd.shape[1];
+    } else if (hd.ndim > 2) {
+        rows = hd.shape[0];
+        for (int i = 1; i < hd.ndim; i++) {
+            if (hd.shape[i] && cols > UINT64_MAX / hd.shape[i]) {
+                set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0, "shape overflows");
+                return HCT_B200_ERR_CORRUPTED;
+            }
+            cols *= hd.shape[i];
+        }
+    }
+    if (cols && rows > UINT64_MAX / cols) {
+        set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0, "shape overflows");
+        return HCT_B200_ERR_CORRUPTED;
+    }
+    hd.rows = rows;
+    hd.cols = cols;
+    h->rows = rows;
+    h->cols = cols;
+    if (h->cols == 1 && h->rows > 1) std::swap(h->rows, h->cols);
+    // fragment index (HoloTensorReader::new, holotensor.rs:1955-2003)
+    const size_t nidx = hd.total_fragments;
+    size_t data_offset = HOLO_HEADER_SIZE + nidx * HOLO_ENTRY_SIZE;
+    if (len < data_offset) {
+        set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0, "failed to read fragment index");
+        return HCT_B200_ERR_CORRUPTED;
+    }
+    struct Entry {
+        uint16_t index, flags;
+        uint32_t offset, csize;
+        uint64_t checksum;
+        size_t base;  // file offset the entry's offset is relative to
+    };
+    std::vector<Entry> entries;
+    for (size_t i = 0; i < nidx; i++) {
+        const uint8_t *e = file + HOLO_HEADER_SIZE + i * HOLO_ENTRY_SIZE;
+        entries.push_back(Entry{rd16(e), rd16(e + 2), rd32(e + 4), rd32(e + 8), rd64(e + 16),
+                                data_offset});
+    }
+    if (nidx == 0 && len >= data_offset + HOLO_ENTRY_SIZE) {
+        const uint8_t *e = file + data_offset;
+        const uint32_t csize = rd32(e + 8);
+        if (rd16(e) == 0 && csize > 0 && csize < 1000000000u) {
+            entries.push_back(Entry{0, rd16(e + 2), rd32(e + 4), csize, rd64(e + 16),
+                                    data_offset + HOLO_ENTRY_SIZE});
+            hd.inline_format = 1;
+        }
+    }
+    // each fragment as read_fragment + add_fragment would see it
+    struct Src {
+        size_t at;
+        uint64_t n;
+    };
+    std::vector<Src> src;
+    uint64_t total_vals = 0;
+    for (const Entry &e : entries) {
+        hct_b200_holo::Frag f;
+        f.index = e.index;
+        const size_t at = e.base + e.offset;
+        if (at > len || e.csize > len - at) {
+            f.kind = hct_b200_holo::PAST_END;
+        } else {
+            const uint8_t *d = file + at;
+            if (flags & HOLO_FLAG_FRAGMENT_CHECKSUMS) f.checksum_ok = xxh(d, e.csize) == e.checksum;
+            if (e.flags & 1) {
+                f.kind = hct_b200_holo::COMPRESSED;
+            } else if (e.csize < 8) {
+                f.kind = hct_b200_holo::SHORT;
+            } else if (rd32(d) != SV03_MAGIC) {
+                f.kind = hct_b200_holo::LEGACY;
+            } else if (e.csize < 20) {
+                f.kind = hct_b200_holo::V3_SHORT;
+            } else {
+                // add_fragment_v3 (holotensor.rs:979-1015)
+                f.num_coeffs = rd32(d + 4);
+                f.F = rd32(d + 8);
+                f.start = rd32(d + 12);
+                const uint64_t nv = (e.csize - 20) / 4;
+                if (f.start >= f.num_coeffs) f.count = 0;
+                else if (f.F == 0) f.count = nv;
+                else f.count = std::min<uint64_t>(nv, (f.num_coeffs - f.start + (uint64_t)f.F - 1) / f.F);
+                f.dev_off = total_vals;
+                total_vals += round_up(f.count, 4);
+                src.push_back(Src{at + 20, f.count});
+            }
+        }
+        h->frags.push_back(f);
+    }
+    int rc = ensure_device(ctx);
+    if (rc) { set_err(err, rc, -1, 0, 0, 0, "no CUDA device"); return rc; }
+    cudaStream_t s = ctx->stream;
+    CK(h->d_vals.reserve(total_vals * 4 + 64));
+    {
+        size_t j = 0;
+        for (const hct_b200_holo::Frag &f : h->frags) {
+            if (f.kind != hct_b200_holo::SV03) continue;
+            if (f.count)
+                CK(cudaMemcpyAsync(h->d_vals.as<float>() + f.dev_off, file + src[j].at,
+                                   4 * src[j].n, cudaMemcpyHostToDevice, s));
+            j++;
+        }
+    }
+    if (h->rows && h->cols) {
+        rc = reserve_spectral(ctx, h->rows, h->cols, err);
+        if (rc) return rc;
+    }
+    CK(cudaStreamSynchronize(s));
+    *out = h.release();
+    return HCT_B200_OK;
+}
+
+int hct_b200_holo_header(const hct_b200_holo *h, hct_b200_holo_info *out) {
+    if (!h || !out) return HCT_B200_ERR_INVALID_ARGUMENT;
+    *out = h->hdr;
+    return HCT_B200_OK;
+}
+
+int hct_b200_holo_total_fragments(const hct_b200_holo *h) { return h ? (int)holo_total(h) : 0; }
+
+float hct_b200_holo_predict_quality(const hct_b200_holo *h, uint32_t k) {
+    if (!h) return 0.0f;
+    const uint32_t n = holo_total(h);
+    return holo_predict(h->hdr, k, n ? n : 1);
+}
+
+uint32_t hct_b200_holo_fragments_for_quality(const hct_b200_holo *h, float target) {
+    if (!h) return 0;
+    const uint32_t total = holo_total(h);
+    for (uint32_t i = 0; i < total; i++)
+        if (holo_predict(h->hdr, i + 1, total ? total : 1) >= target) return i + 1;
+    return total;
+}
+
+int hct_b200_holo_decode(hct_b200_holo *h, uint32_t num_fragments, void *d_out, int out_dtype,
+                         void *stream, float *quality, hct_b200_error *err) {
+    clear_err(err);
+    if (!h || !d_out) {
+        set_err(err, HCT_B200_ERR_INVALID_ARGUMENT, -1, 0, 0, 0, "null argument");
+        return HCT_B200_ERR_INVALID_ARGUMENT;
+    }
+    if (out_dtype < HCT_B200_F32 || out_dtype > HCT_B200_BF16) {
+        set_err(err, HCT_B200_ERR_INVALID_ARGUMENT, -1, 0, 0, 0, "bad output dtype");
+        return HCT_B200_ERR_INVALID_ARGUMENT;
+    }
+    if (h->hdr.encoding != 0) {
+        set_err(err, HCT_B200_ERR_UNSUPPORTED, -1, 0, 0, 0,
+                "HoloTensor encoding %u (only the spectral encoding is decoded)", h->hdr.encoding);
+        return HCT_B200_ERR_UNSUPPORTED;
+    }
+    // read_fragment(i) for i < k, then add_fragment (holotensor.rs:2039-2098, 840-858)
+    std::vector<const hct_b200_holo::Frag *> used;
+    for (uint32_t i = 0; i < num_fragments; i++) {
+        const hct_b200_holo::Frag *f = nullptr;
+        if (h->hdr.inline_format) {
+            if (i != 0) {
+                set_err(err, HCT_B200_ERR_CORRUPTED, (int)i, 0, 0, 0,
+                        "inline format only has fragment 0, requested %u", i);
+                return HCT_B200_ERR_CORRUPTED;
+            }
+            f = &h->frags[0];
+        } else {
+            for (const auto &g : h->frags)
+                if (g.index == i) { f = &g; break; }
+            if (!f) {
+                set_err(err, HCT_B200_ERR_CORRUPTED, (int)i, 0, 0, 0, "fragment %u not found", i);
+                return HCT_B200_ERR_CORRUPTED;
+            }
+        }
+        const char *why = nullptr;
+        int code = HCT_B200_ERR_CORRUPTED;
+        if (f->kind == hct_b200_holo::PAST_END) why = "failed to read fragment data";
+        else if (!f->checksum_ok) { why = "fragment checksum mismatch"; code = HCT_B200_ERR_CHECKSUM; }
+        else if (f->kind == hct_b200_holo::COMPRESSED) { why = "zstd-compressed fragment"; code = HCT_B200_ERR_UNSUPPORTED; }
+        else if (f->kind == hct_b200_holo::SHORT) why = "fragment too short";
+        else if (f->kind == hct_b200_holo::V3_SHORT) why = "V3 fragment too short";
+        else if (f->kind == hct_b200_holo::LEGACY) { why = "V1/V2 spectral fragment layout"; code = HCT_B200_ERR_UNSUPPORTED; }
+        if (why) {
+            set_err(err, code, (int)i, 0, 0, 0, "fragment %u: %s", i, why);
+            return code;
+        }
+        used.push_back(f);
+    }
+    if (used.empty()) {
+        set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0, "no fragments loaded");
+        return HCT_B200_ERR_CORRUPTED;
+    }
+    hct_b200_ctx *ctx = h->ctx;
+    const uint64_t rows = h->rows, cols = h->cols, n = rows * cols;
+    if (n == 0) {
+        if (quality) *quality = NAN;  // 0 / 0, as the reference's f32 division
+        return HCT_B200_OK;
+    }
+    int rc = ensure_device(ctx);
+    if (rc) return rc;
+    const cudaStream_t s = (cudaStream_t)stream;
+    const uint64_t ldw = round_up(cols, 8);
+    half_bits *dense = ctx->dense.as<half_bits>();
+    // One stride and distinct residues: the output-major interleave.
+    const uint32_t F = used[0]->F;
+    bool interleave = F > 0 && F <= (1u << 22) && n < (1ull << 40);
+    std::vector<Sv03Residue> res;
+    if (interleave) {
+        res.assign(F, Sv03Residue{0, 0, 0});
+        std::vector<uint8_t> seen(F, 0);
+        for (const auto *f : used) {
+            if (f->F != F || seen[f->start % F]) { interleave = false; break; }
+            seen[f->start % F] = 1;
+            res[f->start % F] = Sv03Residue{f->dev_off, f->start / F, f->count};
+        }
+    }
+    uint64_t covered = 0;
+    int *flag = ctx->flag.as<int>();
+    CK(cudaMemsetAsync(flag, 0, sizeof(int), s));
+    int slot = ctx->prof_begin(s);
+    if (interleave) {
+        for (const auto *f : used)
+            if (f->start < n) covered += std::min<uint64_t>(f->count, (n - f->start + F - 1) / F);
+        CK(h->d_res.reserve(sizeof(Sv03Residue) * F));
+        CK(cudaMemcpyAsync(h->d_res.p, res.data(), sizeof(Sv03Residue) * F,
+                           cudaMemcpyHostToDevice, s));
+        CK(launch_sv03_interleave(h->d_vals.as<float>(), h->d_res.as<Sv03Residue>(), F, rows, cols,
+                                  dense, ldw, s));
+    } else {
+        // positions in load order, later fragments over earlier ones
+        std::vector<bool> set(n, false);
+        CK(cudaMemsetAsync(dense, 0, rows * ldw * 2, s));
+        for (const auto *f : used) {
+            CK(launch_sv03_scatter(h->d_vals.as<float>() + f->dev_off, f->count, f->start, f->F,
+                                   n, cols, dense, ldw, s));
+            for (uint64_t j = 0; j < f->count; j++) {
+                if (f->F == 0 && j + 1 != f->count) continue;
+                const uint64_t p = f->start + (uint64_t)f->F * j;
+                if (p < n && !set[p]) { set[p] = true; covered++; }
+            }
+        }
+    }
+    uint64_t vals_read = 0;
+    for (const auto *f : used) vals_read += f->count;
+    ctx->prof_end(slot, PK_SCATTER, 4.0 * (double)vals_read + 2.0 * (double)n, s);
+    if (quality) *quality = (float)covered / (float)n;
+    rc = run_idct(ctx, rows, cols, d_out, out_dtype, s, err);
+    if (rc) return rc;
+    return read_flag(ctx, s, err);
+}
+
+void hct_b200_holo_close(hct_b200_holo *h) {
+    if (!h) return;
+    cudaSetDevice(h->ctx->device);
+    delete h;
 }
 
 // ---- reader ----------------------------------------------------------------

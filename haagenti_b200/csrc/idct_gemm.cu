@@ -369,6 +369,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 // accumulators alternate so that the epilogue of one tile overlaps the TMA
 // loads and MMAs of the next.  One CTA per SM; same warp roles and bounded
 // waits as umma_gemm_kernel.
+constexpr int TILE_SLOTS = 4;  // tiles announced ahead by the producer
+
 struct StageCtl {
     uint64_t full[8];
     uint64_t empty[8];
@@ -376,6 +378,9 @@ struct StageCtl {
     uint64_t tfull[2];
     uint64_t tempty[2];
     uint64_t drain;
+    uint64_t tid_full[TILE_SLOTS];   // tile index published (producer arrives)
+    uint64_t tid_empty[TILE_SLOTS];  // tile index read (MMA thread + 8 epilogue warps)
+    int tiles[TILE_SLOTS];           // tile index, -1 = no more tiles
     uint32_t tmem_base;
     int abort;
     int issued;    // ring slots the producer filled
@@ -596,7 +601,7 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
     dft_stage_t_kernel(const __grid_constant__ CUtensorMap tmD,
                        const __grid_constant__ CUtensorMap tmW, uint32_t M, uint32_t K,
                        uint32_t m_tiles, void *out, uint64_t ldo, int mode, int out_dtype,
-                       int *flag, const StageParams sp) {
+                       int *flag, const StageParams sp, uint32_t *tile_counter) {
     using SC = StageTCfg<MT>;
     constexpr int RING = SC::RING;
     constexpr int NT = SC::NT;
@@ -608,8 +613,6 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
     StageCtl *ctl = reinterpret_cast<StageCtl *>(x_smem + SC::X_BYTES);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kbs = (int)((K + BK - 1) / BK);
-    const uint32_t my_tiles =
-        blockIdx.x < m_tiles ? (m_tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < RING; s++) {
@@ -622,6 +625,10 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
             mbar_init(smem_u32(&ctl->tempty[b]), 8);  // one arrive per epilogue warp
         }
         mbar_init(smem_u32(&ctl->drain), 1);
+        for (int t = 0; t < TILE_SLOTS; t++) {
+            mbar_init(smem_u32(&ctl->tid_full[t]), 1);
+            mbar_init(smem_u32(&ctl->tid_empty[t]), 9);  // MMA thread + 8 epilogue warps
+        }
         ctl->abort = 0;
         ctl->issued = 0;
         ctl->consumed = 0;
@@ -650,8 +657,21 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
             for (int kb = 0; kb < kbs; kb++)
                 tma_load_2d(smem_u32(w_smem + (size_t)kb * SC::W_KB_BYTES), &tmW, wb, kb * BK, 0);
             int it = 0;
-            for (uint32_t i = 0; i < my_tiles; i++) {
-                const int r0 = (int)((blockIdx.x + i * gridDim.x) * NT);
+            for (uint32_t i = 0;; i++) {
+                // the next tile: from the counter, or every gridDim.x-th
+                const uint32_t t = tile_counter ? atomicAdd(tile_counter, 1u)
+                                                : blockIdx.x + i * gridDim.x;
+                const int slot = (int)(i % TILE_SLOTS);
+                if (*(volatile int *)&ctl->abort) break;
+                if (!mbar_wait(smem_u32(&ctl->tid_empty[slot]), ((i / TILE_SLOTS) & 1u) ^ 1u)) {
+                    atomicExch(flag, HCT_B200_ERR_TIMEOUT);
+                    atomicExch(&ctl->abort, 1);
+                    break;
+                }
+                *(volatile int *)&ctl->tiles[slot] = t < m_tiles ? (int)t : -1;
+                mbar_arrive(smem_u32(&ctl->tid_full[slot]));
+                if (t >= m_tiles) break;
+                const int r0 = (int)(t * NT);
                 bool stop = false;
                 for (int kb = 0; kb < kbs; kb++, it++) {
                     const int s = it % RING;
@@ -677,10 +697,18 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
             bool ok = mbar_wait(smem_u32(&ctl->wfull), 0);
             if (ok) *(volatile int *)&ctl->w_waited = 1;
             int it = 0;
-            for (uint32_t i = 0; ok && i < my_tiles; i++) {
+            for (uint32_t i = 0; ok; i++) {
                 const int buf = (int)(i & 1u);
                 const uint32_t use = i >> 1;
                 if (*(volatile int *)&ctl->abort) break;
+                const int slot = (int)(i % TILE_SLOTS);
+                if (!mbar_wait(smem_u32(&ctl->tid_full[slot]), (i / TILE_SLOTS) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                const int tile = *(volatile int *)&ctl->tiles[slot];
+                mbar_arrive(smem_u32(&ctl->tid_empty[slot]));
+                if (tile < 0) break;
                 if (!mbar_wait(smem_u32(&ctl->tempty[buf]), (use & 1u) ^ 1u)) { ok = false; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t d = tmem + (uint32_t)(buf * MT * NT);
@@ -721,16 +749,26 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
         const int c_begin = MT == 2 ? 0 : 64 * h, c_end = MT == 2 ? NT : 64 * h + 64;
         const uint32_t o = (uint32_t)(128 * hh + 32 * q + lane);  // my DFT output
         uint8_t *xs = x_smem + (warp - 2) * XWARP_BYTES;
-        for (uint32_t i = 0; i < my_tiles; i++) {
+        for (uint32_t i = 0;; i++) {
             const int buf = (int)(i & 1u);
             const uint32_t use = i >> 1;
+            const int slot = (int)(i % TILE_SLOTS);
+            if (!mbar_wait(smem_u32(&ctl->tid_full[slot]), (i / TILE_SLOTS) & 1u)) {
+                atomicExch(flag, HCT_B200_ERR_TIMEOUT);
+                atomicExch(&ctl->abort, 1);
+                break;
+            }
+            const int tile = *(volatile int *)&ctl->tiles[slot];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&ctl->tid_empty[slot]));
+            if (tile < 0) break;
             if (!mbar_wait(smem_u32(&ctl->tfull[buf]), use & 1u)) {
                 atomicExch(flag, HCT_B200_ERR_TIMEOUT);
                 atomicExch(&ctl->abort, 1);
                 break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t r0 = (blockIdx.x + i * gridDim.x) * NT;
+            const uint32_t r0 = (uint32_t)tile * NT;
             const uint32_t taddr =
                 tmem + (uint32_t)(buf * MT * NT + hh * NT) + ((uint32_t)(q * 32) << 16);
             for (int c = c_begin; c < c_end; c += 32) {
@@ -896,9 +934,13 @@ cudaError_t launch_stage_t(const GemmArgs &a, cudaStream_t s) {
     const uint32_t vec = ((uintptr_t)a.out % 16 == 0) && (a.ldo % 8 == 0);
     StageParams sp{a.P, a.Q, a.H, vec, a.batch, reinterpret_cast<const float2 *>(a.twiddle),
                    a.scale};
+    if (a.tile_counter) {
+        e = cudaMemsetAsync(a.tile_counter, 0, sizeof(uint32_t), s);
+        if (e != cudaSuccess) return e;
+    }
     dft_stage_t_kernel<MT><<<grid, STAGE_THREADS, SC::SMEM_BYTES, s>>>(
         td, tw, (uint32_t)a.M, (uint32_t)a.K, (uint32_t)m_tiles, a.out, a.ldo, a.mode,
-        a.out_dtype, a.d_flag, sp);
+        a.out_dtype, a.d_flag, sp, a.tile_counter);
     return cudaGetLastError();
 }
 

@@ -207,6 +207,48 @@ def encode_hct_v3(w: np.ndarray, retention: float = 0.30, num_fragments: int = 1
     return b"".join(out)
 
 
+HOLO_SPECTRAL_CURVE = (0.6, 0.3, 0.08, 0.02)  # holotensor.rs:114-118
+
+
+def holo_dims(shape) -> tuple[int, int]:
+    """HoloTensorEncoder::flatten_shape (holotensor.rs:1626-1638)."""
+    shape = [int(s) for s in shape]
+    if len(shape) == 0:
+        return 1, 1
+    if len(shape) == 1:
+        return 1, shape[0]
+    return shape[0], int(np.prod(shape[1:]))
+
+
+def encode_holotensor(w: np.ndarray, num_fragments: int = 8, shape=None, seed: int = 0,
+                      coeffs: np.ndarray | None = None) -> bytes:
+    """Spectral HoloTensor file (HoloTensorEncoder::encode_nd + HoloTensorWriter::write,
+    crates/haagenti-hct/src/holotensor.rs:1656-1688, 1859-1902): the DCT-II
+    coefficients dealt out in raster order to ``num_fragments`` "SV03" fragments
+    (fragment f holds positions f, f + F, ...), header and fragment checksums on."""
+    shape = list(w.shape) if shape is None else [int(d) for d in shape]
+    rows, cols = holo_dims(shape)
+    if coeffs is None:
+        coeffs = dct_2d(np.asarray(w, np.float32).reshape(rows, cols))
+    c = np.ascontiguousarray(coeffs, np.float32).reshape(-1)
+    n, F = c.size, max(int(num_fragments), 1)
+    hdr = bytearray(b"HTNS")
+    hdr += struct.pack("<IBBHHHQQBB", 1, 0, 0, 0x0003, F, 1, n * 4, seed, 0, len(shape))
+    for i in range(4):
+        hdr += struct.pack("<Q", shape[i] if i < len(shape) else 0)
+    hdr += struct.pack("<4f", *HOLO_SPECTRAL_CURVE) + bytes(6)
+    hdr += struct.pack("<Q", _xxh3(bytes(hdr)))
+    frags = []
+    for f in range(F):
+        count = (max(n - f, 0) + F - 1) // F
+        frags.append(struct.pack("<5I", 0x33305653, n, F, f, count) + c[f::F].tobytes())
+    index, off = [], 0
+    for f, d in enumerate(frags):
+        index.append(struct.pack("<HHIIIQ", f, 0, off, len(d), len(d), _xxh3(d)))
+        off += len(d)
+    return b"".join([bytes(hdr)] + index + frags)
+
+
 def encode_int4(w: np.ndarray, version: int = 1, block_size: int = DEFAULT_BLOCK_SIZE) -> bytes:
     """INT4 + LZ4 on raw weights (examples/safetensors_to_int4_hct.rs:241-284)."""
     return write_hct(quantize_int4(w), list(w.shape), DTYPE_I4, 0, version, block_size)

@@ -110,6 +110,7 @@ typedef struct {
 typedef struct hct_b200_ctx hct_b200_ctx;
 typedef struct hct_b200_reader hct_b200_reader;
 typedef struct hct_b200_v3 hct_b200_v3;
+typedef struct hct_b200_holo hct_b200_holo;
 
 /* ---- context ------------------------------------------------------------
  * One context per device owns the scratch memory, the cached DCT bases and
@@ -274,6 +275,58 @@ void hct_b200_v3_close(hct_b200_v3 *v);
 int hct_b200_hct_v3_decode(hct_b200_ctx *ctx, const uint8_t *data, size_t len, uint64_t rows,
                            uint64_t cols, void *d_out, int out_dtype, void *stream,
                            hct_b200_error *err);
+
+/* ---- HoloTensor (spectral fragments) -----------------------------------
+ * HoloTensorReader + HoloTensorDecoder for the spectral encoding
+ * (crates/haagenti-hct/src/holotensor.rs).  open parses the 96-byte header
+ * (HoloTensorHeader::from_bytes, :571-656: magic "HTNS", version 1, XXH3-64
+ * of bytes [0, 88) at 88 when flag 0x0001, encoding / compression / dtype
+ * codes, shape), the fragment index (24-byte FragmentIndexEntry, :332-380)
+ * and the inline one-fragment form of files with total_fragments == 0
+ * (:1978-2003); it uploads every SV03 fragment's f32 values once.
+ * decode(k) reads fragments 0..k-1 as HoloTensorReader::read_fragment does
+ * (:2039-2098: the entry whose index is i, XXH3 of the stored bytes when flag
+ * 0x0002) into a SpectralDecoder (:840-1051: "SV03" raster slices, later
+ * fragments over earlier ones, the rest zero) and writes its
+ * reconstruction, the orthonormal 2-D DCT-III of the rows x cols view of the
+ * shape (HoloTensorDecoder::new, :1732-1759), to d_out (rows x cols of
+ * out_dtype).  *quality (may be NULL) receives SpectralDecoder::quality, the
+ * fraction of positions the k fragments cover.  k == 0 is
+ * HCT_B200_ERR_CORRUPTED ("no fragments loaded").  Not decoded, with
+ * HCT_B200_ERR_UNSUPPORTED: the random-projection and low-rank encodings,
+ * zstd-compressed fragments (entry flag bit 0) and the legacy V1/V2 spectral
+ * fragment layouts.  decode is stream-ordered and synchronises once to read
+ * the device flag. */
+typedef struct {
+    uint8_t encoding;    /* 0 spectral, 1 random projection, 2 low-rank */
+    uint8_t compression; /* 0 LZ4, 1 Zstd */
+    uint16_t flags;
+    uint16_t total_fragments; /* as in the header */
+    uint16_t min_fragments;
+    uint64_t original_size;
+    uint64_t seed;
+    uint8_t dtype;
+    uint8_t ndim;
+    uint16_t inline_format; /* 1: the inline one-fragment form */
+    uint32_t reserved;
+    uint64_t shape[7];
+    float quality_curve[4];
+    uint64_t rows, cols; /* the decoder's 2-D view of the shape */
+} hct_b200_holo_info;
+
+int hct_b200_holo_open(hct_b200_ctx *ctx, const uint8_t *file, size_t len, hct_b200_holo **out,
+                       hct_b200_error *err);
+int hct_b200_holo_header(const hct_b200_holo *h, hct_b200_holo_info *out);
+/* HoloTensorReader::total_fragments (:2025-2031): 1 for the inline form. */
+int hct_b200_holo_total_fragments(const hct_b200_holo *h);
+/* QualityCurve::predict(k, total) of the header's curve (:199-220). */
+float hct_b200_holo_predict_quality(const hct_b200_holo *h, uint32_t k);
+/* How many fragments HoloTensorReader::read_to_quality(target) reads
+ * (:2164-2187): the first k whose predicted quality reaches target, else all. */
+uint32_t hct_b200_holo_fragments_for_quality(const hct_b200_holo *h, float target);
+int hct_b200_holo_decode(hct_b200_holo *h, uint32_t num_fragments, void *d_out, int out_dtype,
+                         void *stream, float *quality, hct_b200_error *err);
+void hct_b200_holo_close(hct_b200_holo *h);
 
 /* ---- HCT reader ---------------------------------------------------------
  * HctReader::new / HctReaderV2::new (crates/haagenti-hct/src/tensor.rs:417-444,

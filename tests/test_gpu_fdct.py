@@ -36,8 +36,9 @@ def ctxs(hb):
     return auto, dense
 
 
-@pytest.mark.parametrize("shape", [(32, 32), (64, 128), (128, 96), (1024, 1024), (1, 8192),
-                                   (8192, 1), (1024, 8192), (8192, 8192)])
+@pytest.mark.parametrize("shape", [(32, 32), (64, 128), (128, 96), (512, 256), (768, 4608),
+                                   (1024, 1024), (1, 8192), (8192, 1), (1024, 8192),
+                                   (8192, 8192)])
 def test_factored_vs_oracle_truth_and_dense(hb, orc, dev, ctxs, shape):
     import torch
 
@@ -69,7 +70,8 @@ def test_factored_full_gate_shape(hb, dev, ctxs):
     assert cos.item() >= MIN_COS
 
 
-@pytest.mark.parametrize("shape", [(1024, 8192), (8192, 1024), (4096, 14336)])
+@pytest.mark.parametrize("shape", [(1024, 8192), (8192, 1024), (4096, 14336), (256, 512),
+                                   (320, 4608), (64, 28672)])
 def test_factored_hct_decode(hb, orc, shape):
     from oracle import hct as OH
 
