@@ -73,6 +73,13 @@ __device__ __forceinline__ constexpr uint32_t koff(int j) {
     return (uint32_t)(QC * j + 8 * ((QC * j) / 64) + spad2_of(QC) * ((QC * j) / 512));
 }
 
+// 32 bytes at a 32-byte aligned global address in one access (sm_100)
+__device__ __forceinline__ void st_global_v8(uint32_t *p, const uint32_t (&v)[8]) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+
 __device__ __forceinline__ float ld_h(const uint16_t *s, uint32_t i) {
     return __half2float(__ushort_as_half(s[i]));
 }
@@ -95,13 +102,13 @@ __device__ __forceinline__ void pack_run(const uint16_t *s, const float4 *__rest
     const uint32_t H = L / 2, k1a = J * g;
     const uint32_t ka = Q * k1a + k2;  // k of the run's first element
     const float4 *ct = coef + ka;
-    uint4 *zd = reinterpret_cast<uint4 *>(orow + k2 * P + k1a);
-    uint4 *yd = reinterpret_cast<uint4 *>(orow + (Q - k2) * P + (P - J - k1a));
+    uint32_t *zd = orow + k2 * P + k1a;
+    uint32_t *yd = orow + (Q - k2) * P + (P - J - k1a);
     const bool partner = 2 * k2 != Q;
     const uint32_t pa = spad<QC>(ka), pb = spad<QC>(L - ka), pc = spad<QC>(H + ka), pd = spad<QC>(H - ka);
+    uint32_t zo[J], yo[J];
 #pragma unroll
     for (int h = 0; h < J / 4; h++) {
-        uint32_t zo[4], yo[4];
 #pragma unroll
         for (int t = 0; t < 4; t++) {
             const int j = 4 * h + t;
@@ -120,14 +127,27 @@ __device__ __forceinline__ void pack_run(const uint16_t *s, const float4 *__rest
             }
             const float a = ld_h(s, ia), b = ld_h(s, ib), c = ld_h(s, ic), d = ld_h(s, id);
             const float4 tt = ct[Q * j];  // (alpha.re, alpha.im, beta.re, beta.im) of k
-            zo[t] = pack_z(fmaf(tt.x, a, fmaf(tt.y, b, fmaf(tt.z, c, tt.w * d))),
+            zo[j] = pack_z(fmaf(tt.x, a, fmaf(tt.y, b, fmaf(tt.z, c, tt.w * d))),
                            fmaf(tt.y, a, fmaf(-tt.x, b, fmaf(tt.w, c, -tt.z * d))));
             const float s1 = d + c, s2 = d - c, s3 = a - b, s4 = a + b;
-            yo[t] = pack_z(RS2 * fmaf(tt.x, s1, fmaf(tt.y, s2, fmaf(tt.z, s3, tt.w * s4))),
-                           RS2 * fmaf(tt.x, s2, fmaf(-tt.y, s1, fmaf(tt.z, s4, -tt.w * s3))));
+            // Z[H - k] goes to position J - 1 - j of the partner run
+            yo[J - 1 - j] = pack_z(RS2 * fmaf(tt.x, s1, fmaf(tt.y, s2, fmaf(tt.z, s3, tt.w * s4))),
+                                   RS2 * fmaf(tt.x, s2, fmaf(-tt.y, s1, fmaf(tt.z, s4, -tt.w * s3))));
         }
-        zd[h] = make_uint4(zo[0], zo[1], zo[2], zo[3]);
-        if (partner) yd[J / 4 - 1 - h] = make_uint4(yo[3], yo[2], yo[1], yo[0]);
+    }
+    if (J == 8) {
+        // runs of 8 start at multiples of 8 words (P % 8 == 0): 32-byte aligned
+        st_global_v8(zd, reinterpret_cast<const uint32_t(&)[8]>(zo));
+        if (partner) st_global_v8(yd, reinterpret_cast<const uint32_t(&)[8]>(yo));
+    } else {
+#pragma unroll
+        for (int v = 0; v < J / 4; v++) {
+            reinterpret_cast<uint4 *>(zd)[v] =
+                make_uint4(zo[4 * v], zo[4 * v + 1], zo[4 * v + 2], zo[4 * v + 3]);
+            if (partner)
+                reinterpret_cast<uint4 *>(yd)[v] =
+                    make_uint4(yo[4 * v], yo[4 * v + 1], yo[4 * v + 2], yo[4 * v + 3]);
+        }
     }
 }
 
@@ -569,7 +589,8 @@ cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t 
                                 uint32_t P, uint32_t Q, const float *d_tables, half_bits *d_out,
                                 cudaStream_t s) {
     if (L % 32 || (uint64_t)P * Q != L / 2 || P % 4 || Q % 4) return cudaErrorInvalidValue;
-    const int qc = pack_qc(P, Q);
+    // the specialised pack writes 32-byte runs: it needs a 32-byte aligned output
+    const int qc = ((uintptr_t)d_out & 31) ? 0 : pack_qc(P, Q);
     const size_t smem = (size_t)srow_halves(L, qc) * 2;
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     const bool small = L <= 16384;
@@ -594,7 +615,7 @@ cudaError_t launch_spectral_pack(const uint8_t *d_payload, uint64_t bmb, const u
                                  cudaStream_t s) {
     if (!spectral_pack_supported(L) || (uint64_t)P * Q != L / 2 || P % 4 || Q % 4)
         return cudaErrorInvalidValue;
-    const int qc = pack_qc(P, Q);
+    const int qc = ((uintptr_t)d_out & 31) ? 0 : pack_qc(P, Q);
     const size_t smem = spack_smem_bytes(L, qc);
     const bool small = L <= 16384;
     const int threads = small ? 128 : 256;
