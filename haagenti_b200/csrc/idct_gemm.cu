@@ -411,11 +411,13 @@ constexpr int STAGE_THREADS = 320;  // producer, MMA, 8 epilogue warps
 // memory; the data tiles (128 rows x 64 K) stream through a TMA ring; per
 // k-step one elected thread issues MT tcgen05 MMAs of M = 128, N = 128
 // into a double-buffered TMEM accumulator.
-// Per-warp staging of one 32-column chunk for coalesced stores: 32 rows of
-// 64 bytes (+16 bytes of padding, so that the 16-byte accesses of 8
-// consecutive lanes hit distinct banks).
-constexpr int XROW = 80;
-constexpr int XWARP_BYTES = 32 * XROW;
+// Per-warp staging of one 32-column chunk for coalesced stores: 2 KB per
+// warp, its 16-byte pieces XOR-swizzled so that the 16-byte accesses of
+// every quarter warp (on both the write and the read side) hit 8 distinct
+// 4-bank groups:
+//   stage 1: 16 slots of 128 bytes, piece p of slot s at (p ^ (s & 3));
+//   stage 2: 32 rows of 64 bytes, piece p of row r at (p ^ ((r >> 1) & 3)).
+constexpr int XWARP_BYTES = 2048;
 
 template <int MT>
 struct StageTCfg {
@@ -427,8 +429,8 @@ struct StageTCfg {
     static constexpr int RING = MT == 1 ? 3 : 4;
     static constexpr int TMEM_COLS = 2 * MT * NT;      // double-buffered
     static constexpr int X_BYTES = 8 * XWARP_BYTES;    // epilogue staging, 8 warps
-    // MT = 1: 32 KB of W + 48 KB ring + 20 KB staging -> two CTAs per SM;
-    // MT = 2: 128 KB of W + 64 KB ring + 20 KB staging -> one
+    // MT = 1: 32 KB of W + 48 KB ring + 16 KB staging -> two CTAs per SM;
+    // MT = 2: 128 KB of W + 64 KB ring + 16 KB staging -> one
     static constexpr size_t SMEM_BYTES = 1024 + (size_t)KB_MAX * W_KB_BYTES +
                                          (size_t)RING * B_TILE_BYTES + X_BYTES + 256;
     static constexpr uint32_t IDESC =
@@ -489,10 +491,12 @@ __device__ __forceinline__ void stage1_chunk_t(const uint32_t (&r)[32], uint32_t
             }
         }
     }
-    // stage: row (lane >> 1) = the warp's m1 slot, 128 bytes = 32 complex
-    uint4 *xw = reinterpret_cast<uint4 *>(xs + (lane >> 1) * (2 * XROW) + 64 * ri);
+    // stage: slot (lane >> 1) = the warp's m1 slot, 128 bytes = 32 complex
+    const uint32_t wslot = (uint32_t)lane >> 1;
 #pragma unroll
-    for (int t = 0; t < 4; t++) xw[t] = make_uint4(v[4 * t], v[4 * t + 1], v[4 * t + 2], v[4 * t + 3]);
+    for (int t = 0; t < 4; t++)
+        *reinterpret_cast<uint4 *>(xs + wslot * 128 + (((4 * ri + t) ^ (wslot & 3)) * 16)) =
+            make_uint4(v[4 * t], v[4 * t + 1], v[4 * t + 2], v[4 * t + 3]);
     __syncwarp();
     // 16 m1 rows of 128 bytes: lane writes piece (lane & 7) of rows (lane >> 3) + 4 i
     const uint32_t m1_base = (o - (uint32_t)lane) >> 1;
@@ -502,7 +506,8 @@ __device__ __forceinline__ void stage1_chunk_t(const uint32_t (&r)[32], uint32_t
     for (int i = 0; i < 4; i++) {
         const uint32_t slot = (uint32_t)(lane >> 3) + 4 * i;
         const uint32_t mm = m1_base + slot;
-        const uint4 val = *reinterpret_cast<const uint4 *>(xs + slot * (2 * XROW) + 16 * piece);
+        const uint4 val =
+            *reinterpret_cast<const uint4 *>(xs + slot * 128 + ((piece ^ (slot & 3)) * 16));
         if (mm < sp.P) {
             uint32_t *g = reinterpret_cast<uint32_t *>(out) + (uint64_t)mm * sp.batch * Q + c0;
             if (c0 + 4 <= M) {
@@ -544,7 +549,8 @@ __device__ __forceinline__ void stage2_chunk_t(const uint32_t (&r)[32], uint32_t
         }
 #pragma unroll
         for (int part = 0; part < PARTS; part++) {
-            uint4 *xw = reinterpret_cast<uint4 *>(xs + lane * XROW);
+            uint8_t *xw = xs + lane * 64;
+            const uint32_t wsw = ((uint32_t)lane >> 1) & 3;
 #pragma unroll
             for (int t = 0; t < 4; t++) {
                 uint32_t p[4];
@@ -558,14 +564,15 @@ __device__ __forceinline__ void stage2_chunk_t(const uint32_t (&r)[32], uint32_t
                         p[u] = DT == HCT_B200_BF16 ? pack_bf2(a, b) : pack_h2(a, b);
                     }
                 }
-                xw[t] = make_uint4(p[0], p[1], p[2], p[3]);
+                *reinterpret_cast<uint4 *>(xw + ((t ^ wsw) * 16)) = make_uint4(p[0], p[1], p[2], p[3]);
             }
             __syncwarp();
             // rows (lane >> 2) + 8 i of the staging, 16-byte piece (lane & 3)
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 const uint32_t row = (uint32_t)(lane >> 2) + 8 * i;
-                const uint4 val = *reinterpret_cast<const uint4 *>(xs + row * XROW + 16 * piece);
+                const uint4 val = *reinterpret_cast<const uint4 *>(
+                    xs + row * 64 + ((piece ^ ((row >> 1) & 3)) * 16));
                 if (ok[i]) {
                     if (DT == HCT_B200_F32)
                         *reinterpret_cast<uint4 *>(reinterpret_cast<float *>(out) +
