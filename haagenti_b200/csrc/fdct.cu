@@ -524,19 +524,6 @@ bool fdct_factor(uint64_t L, uint32_t *P, uint32_t *Q) {
 
 namespace {
 
-int sm_count() {
-    static int n = 0;
-    if (n <= 0) {
-        int dev = 0, v = 0;
-        if (cudaGetDevice(&dev) == cudaSuccess &&
-            cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0)
-            n = v;
-        else
-            return 148;
-    }
-    return n;
-}
-
 // Specialisation of the pack for (P, Q): runs of 8 with compile-time read
 // offsets for Q in {64, 128} and P % 8 == 0; else 0 (runs of 4, any Q).
 int pack_qc(uint32_t P, uint32_t Q) {
@@ -568,7 +555,9 @@ SpectralFn spectral_fn(int qc) {
     }
 }
 
-// grid of a persistent row kernel: resident CTAs x SMs, at most one per row
+// grid of a row kernel: one CTA per row, so that the block scheduler keeps
+// the SMs balanced when other streams' kernels hold some of them (the
+// kernels also loop over rows, for grids capped below the row count)
 template <typename F>
 cudaError_t row_grid(F kern, int threads, size_t smem, uint64_t B, unsigned *grid) {
     cudaError_t e =
@@ -578,7 +567,7 @@ cudaError_t row_grid(F kern, int threads, size_t smem, uint64_t B, unsigned *gri
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
     if (e != cudaSuccess) return e;
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
-    const uint64_t cap = (uint64_t)per_sm * (uint64_t)sm_count();
+    const uint64_t cap = 0x7fffffffull;
     *grid = (unsigned)(B < cap ? (B < 1 ? 1 : B) : cap);
     return cudaSuccess;
 }
