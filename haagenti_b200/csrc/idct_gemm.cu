@@ -450,9 +450,12 @@ __device__ __forceinline__ uint32_t pack_bf2(float a, float b) {
 // After the pair exchange lane o owns 16 complex values of m1 (columns
 // 16 ri..16 ri+15), twiddled and packed as fp16 pairs; the warp's 16 values
 // of m1 (128 contiguous bytes of G) are then written by 8 lanes at a time.
+// tw0: e^{2 pi i k2 m1 / H} of the chunk's first row (k2 = r1 mod Q), w: its
+// step e^{2 pi i m1 / H}; both read from the table when have_tw is false.
 __device__ __forceinline__ void stage1_chunk_t(const uint32_t (&r)[32], uint32_t o, uint32_t rT,
                                                uint32_t M, void *out, const StageParams &sp,
-                                               uint8_t *xs, int lane) {
+                                               uint8_t *xs, int lane, float2 tw0, float2 w0,
+                                               bool have_tw) {
     const uint32_t m1 = o >> 1, ri = o & 1u;
     // even lane keeps columns 0..15 (needs the odd lane's Im), odd lane 16..31
     float re[16], im[16];
@@ -466,8 +469,9 @@ __device__ __forceinline__ void stage1_chunk_t(const uint32_t (&r)[32], uint32_t
     const uint32_t Q = sp.Q;
     const uint32_t r1 = rT + 16 * ri;  // first data row of my 16
     uint32_t k2 = r1 % Q;
-    float2 tw = sp.twiddle[m1 < sp.P ? k2 * m1 : 0];  // e^{2 pi i k2 m1 / H}, k2 m1 < H
-    const float2 w = sp.twiddle[m1 < sp.P ? m1 : 0];  // step of k2 -> k2 + 1
+    // e^{2 pi i k2 m1 / H} (k2 m1 < H) and the step of k2 -> k2 + 1
+    float2 tw = have_tw ? tw0 : sp.twiddle[m1 < sp.P ? k2 * m1 : 0];
+    const float2 w = have_tw ? w0 : sp.twiddle[m1 < sp.P ? m1 : 0];
     uint32_t v[16];
     if (Q % 16 == 0) {  // my 16 rows start at a multiple of 16: one b, no wrap of k2
 #pragma unroll
@@ -753,9 +757,25 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
         const int q = warp & 3;
         const int h = (warp - 2) >> 2;
         const int hh = MT == 2 ? h : 0;
-        const int c_begin = MT == 2 ? 0 : 64 * h, c_end = MT == 2 ? NT : 64 * h + 64;
+        const int c_begin = MT == 2 ? 0 : 64 * h;  // my columns: c_begin .. c_begin + 32 NCH
         const uint32_t o = (uint32_t)(128 * hh + 32 * q + lane);  // my DFT output
         uint8_t *xs = x_smem + (warp - 2) * XWARP_BYTES;
+        // stage 1: the twiddle step of my output, and, when Q divides the tile
+        // height (k2 of a chunk's first row is then the same in every tile),
+        // the first twiddle of each of my chunks
+        constexpr int NCH = MT == 2 ? NT / 32 : 2;
+        float2 tw_first[NCH], tw_step = make_float2(1.0f, 0.0f);
+        const bool tw_fixed = mode == 2 && NT % sp.Q == 0;
+        if (mode == 2) {
+            const uint32_t m1 = o >> 1, ri = o & 1u;
+            const bool live = m1 < sp.P;
+            tw_step = sp.twiddle[live ? m1 : 0];
+#pragma unroll
+            for (int ci = 0; ci < NCH; ci++) {
+                const uint32_t k2 = ((uint32_t)c_begin + 32 * ci + 16 * ri) % sp.Q;
+                tw_first[ci] = tw_fixed && live ? sp.twiddle[k2 * m1] : make_float2(1.0f, 0.0f);
+            }
+        }
         for (uint32_t i = 0;; i++) {
             const int buf = (int)(i & 1u);
             const uint32_t use = i >> 1;
@@ -778,11 +798,14 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
             const uint32_t r0 = (uint32_t)tile * NT;
             const uint32_t taddr =
                 tmem + (uint32_t)(buf * MT * NT + hh * NT) + ((uint32_t)(q * 32) << 16);
-            for (int c = c_begin; c < c_end; c += 32) {
+#pragma unroll
+            for (int ci = 0; ci < NCH; ci++) {
+                const int c = c_begin + 32 * ci;
                 uint32_t r[32];
                 tmem_ld32(taddr + (uint32_t)c, r);
                 if (mode == 2) {
-                    stage1_chunk_t(r, o, r0 + c, M, out, sp, xs, lane);
+                    stage1_chunk_t(r, o, r0 + c, M, out, sp, xs, lane, tw_first[ci], tw_step,
+                                   tw_fixed);
                 } else if (out_dtype == HCT_B200_F16) {
                     stage2_chunk_t<HCT_B200_F16>(r, o, r0 + c, M, out, ldo, sp, xs, lane);
                 } else if (out_dtype == HCT_B200_BF16) {
