@@ -377,6 +377,7 @@ def run_b200(args):
           if rank == 0 and not args.no_secondary else None)
     holo = (bench_holo(H, torch, dev, stream, files, TENS, ctx)
             if rank == 0 and not args.no_secondary else None)
+    zstd = bench_zstd(H, torch, dev, stream, args) if rank == 0 and not args.no_secondary else None
 
     # ---- roofline of the dominant kernel --------------------------------
     pk = peaks()
@@ -442,7 +443,7 @@ def run_b200(args):
             "kernels": kern,
             # the dense-path scatter is two kernels (chunk scan + scatter) under one record
             "gpu_launches": launches_total + ks.get("spectral_scatter", {}).get("launches", 0),
-            "lz4": lz4, "int4": int4, "hct_v3": v3, "holotensor": holo,
+            "lz4": lz4, "int4": int4, "hct_v3": v3, "holotensor": holo, "zstd": zstd,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
         }
@@ -529,6 +530,60 @@ def bench_holo(H, torch, dev, stream, files, tens, ctx):
             "ms": round(ms, 3), "file_bytes": in_bytes,
             "path": "HoloTensorReader.decode per tensor (SV03 interleave -> factored IDCT), "
                     "synchronous"}
+
+
+def bench_zstd(H, torch, dev, stream, args):
+    """The LZ4 config-2 data (256 MiB of N(0,0.02) fp16, seed 1) as 4096 independent
+    64 KiB zstd frames (level 3), decoded in one batched launch (a warp per frame)."""
+    from haagenti_b200 import encode as E
+
+    rng = np.random.default_rng(1)
+    raw = (rng.standard_normal(128 * 1024 * 1024, dtype=np.float32) * np.float32(0.02)).astype(
+        np.float16).view(np.uint8)
+    chunk = 65536
+    nb = raw.size // chunk
+    frames = [E.zstd_compress(raw[i * chunk:(i + 1) * chunk], 3) for i in range(nb)]
+    jobs = np.zeros(nb, dtype=H.ZSTD_JOB)
+    offs = np.zeros(nb + 1, np.uint64)
+    offs[1:] = np.cumsum([(len(f) + 15) // 16 * 16 for f in frames])
+    jobs["src_off"] = offs[:-1]
+    jobs["src_len"] = [len(f) for f in frames]
+    jobs["dst_off"] = np.arange(nb, dtype=np.uint64) * chunk
+    jobs["dst_cap"] = chunk
+    packed = np.zeros(int(offs[-1]), np.uint8)
+    for i, f in enumerate(frames):
+        packed[int(offs[i]): int(offs[i]) + len(f)] = np.frombuffer(f, np.uint8)
+    d_src = torch.from_numpy(packed).to(dev)
+    d_dst = torch.empty(raw.size, dtype=torch.uint8, device=dev)
+    z = H.ZstdDecompressor()
+    st = z.decompress_jobs(d_src, jobs, d_dst, stream)
+    ok = bool((st["code"] == 0).all()) and bool(
+        torch.equal(d_dst, torch.from_numpy(raw).to(dev)))
+    from haagenti_b200 import _lib as L
+    lib = L.load()
+    d_jobs = torch.from_numpy(jobs.view(np.uint8).copy()).to(dev)
+    d_status = torch.zeros(nb * 32, dtype=torch.uint8, device=dev)
+
+    def launch():
+        lib.hct_b200_zstd_decompress_jobs(z.ctx.handle, d_src.data_ptr(), d_jobs.data_ptr(), nb,
+                                          d_dst.data_ptr(), d_status.data_ptr(), stream.cuda_stream)
+
+    for _ in range(3):
+        launch()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    torch.cuda.synchronize(dev)
+    e0.record(stream)
+    for _ in range(reps):
+        launch()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / reps
+    return {"config": "BASELINE config 2 data (256 MiB fp16 N(0,0.02) seed 1) as 4096 x 64 KiB "
+                      "zstd frames (libzstd level 3)",
+            "value": round(raw.size / (ms / 1e3) / 1e9, 2), "unit": "GB/s decompressed",
+            "ms": round(ms, 3), "ratio": round(raw.size / sum(len(f) for f in frames), 4),
+            "bytes_checked_ok": ok}
 
 
 def bench_lz4(H, torch, dev, stream, args):

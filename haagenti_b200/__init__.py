@@ -35,7 +35,7 @@ __all__ = [
     "Unsupported", "DeviceError", "Context", "Lz4Decompressor", "dequantize_int4",
     "dequantize_int4_mp", "idct_2d",
     "spectral_q4_decode", "HctReader", "HctReaderV2", "HctV3Decoder", "hct_v3_decode",
-    "HoloTensorReader", "F32",
+    "HoloTensorReader", "ZstdDecompressor", "zstd_decompress", "F32",
     "F16", "BF16", "FLAG_SPECTRAL_Q4",
 ]
 
@@ -357,6 +357,87 @@ def hct_v3_decode(data, rows: int, cols: int, out_dtype: int = F32, ctx: Context
         return d.decode(out_dtype, stream=stream)
     finally:
         d.close()
+
+
+# ------------------------------------------------------------------ Zstandard
+
+class ZstdDecompressor:
+    """GPU Zstandard decode with the semantics of ``zstd::decode_all``, which the
+    reference calls for zstd-compressed HoloTensor fragments
+    (crates/haagenti-hct/src/holotensor.rs:2081-2091) and zstd-wrapped HCT data
+    (crates/haagenti-cuda/src/decompress.rs:296-319)."""
+
+    def __init__(self, ctx: Context | None = None):
+        self.ctx = ctx or Context.default()
+
+    @staticmethod
+    def algorithm() -> str:
+        return "zstd"
+
+    @staticmethod
+    def content_size(data) -> int | None:
+        """Sum of the frames' recorded content sizes, None if a frame lacks one."""
+        src = _as_host_u8(data)
+        size = C.c_uint64(0)
+        rc = L.load().hct_b200_zstd_content_size(src.ctypes.data if src.size else None, src.size,
+                                                 C.byref(size))
+        if rc == L.UNSUPPORTED:
+            return None
+        _check(rc)
+        return int(size.value)
+
+    def decompress_with_size(self, data, capacity: int) -> bytes:
+        """Decode every frame into at most ``capacity`` bytes (BufferTooSmall beyond)."""
+        src = _as_host_u8(data)
+        out = np.zeros(max(capacity, 1), dtype=np.uint8)
+        written = C.c_size_t(0)
+        err = L.Error()
+        _check(L.load().hct_b200_zstd_decompress(self.ctx.handle,
+                                                 src.ctypes.data if src.size else None, src.size,
+                                                 out.ctypes.data, capacity, C.byref(written),
+                                                 C.byref(err)), err)
+        return out[: written.value].tobytes()
+
+    def decompress(self, data) -> bytes:
+        """decode_all: the recorded content size, else 4x the input doubled on
+        BufferTooSmall."""
+        src = _as_host_u8(data)
+        known = self.content_size(src) if src.size else 0
+        size = known if known is not None else max(4 * src.size, 4096)
+        while True:
+            try:
+                return self.decompress_with_size(src, size)
+            except BufferTooSmall:
+                if known is not None or size >= 1 << 32:
+                    raise
+                size *= 2
+
+    def decompress_jobs(self, d_src, jobs: np.ndarray, d_dst, stream=None):
+        """Batched decode on device buffers: ``jobs`` is a structured array of
+        (src_off, src_len, dst_off, dst_cap) rows; returns the per-job status
+        array (code, position, provided, written), synchronising the stream."""
+        torch = _torch()
+        jobs = np.ascontiguousarray(jobs)
+        n = len(jobs)
+        dev = torch.device("cuda", self.ctx.device)
+        d_jobs = torch.from_numpy(jobs.view(np.uint8).copy()).to(dev)
+        d_status = torch.zeros(max(n, 1) * 32, dtype=torch.uint8, device=dev)
+        _check(L.load().hct_b200_zstd_decompress_jobs(self.ctx.handle, d_src.data_ptr(),
+                                                      d_jobs.data_ptr(), n, d_dst.data_ptr(),
+                                                      d_status.data_ptr(), _stream_ptr(stream)))
+        st = d_status.cpu().numpy()[: n * 32].view(
+            [("code", "<i4"), ("reserved", "<i4"), ("position", "<u8"), ("provided", "<u8"),
+             ("written", "<u8")])
+        return st
+
+
+def zstd_decompress(data, ctx: Context | None = None) -> bytes:
+    """``zstd::decode_all(data)`` on the GPU."""
+    return ZstdDecompressor(ctx).decompress(data)
+
+
+ZSTD_JOB = np.dtype([("src_off", "<u8"), ("src_len", "<u8"), ("dst_off", "<u8"),
+                     ("dst_cap", "<u8")])
 
 
 # ------------------------------------------------------------------ HoloTensor

@@ -108,6 +108,10 @@ SIGNATURES = {
     "hct_b200_v3_close": (None, [_vp]),
     "hct_b200_hct_v3_decode": (C.c_int, [_vp, _u8p, _sz, C.c_uint64, C.c_uint64, _vp, C.c_int,
                                          _vp, C.POINTER(Error)]),
+    "hct_b200_zstd_decompress_jobs": (C.c_int, [_vp, _vp, _vp, C.c_uint32, _vp, _vp, _vp]),
+    "hct_b200_zstd_decompress": (C.c_int, [_vp, _u8p, _sz, _u8p, _sz, C.POINTER(C.c_size_t),
+                                           C.POINTER(Error)]),
+    "hct_b200_zstd_content_size": (C.c_int, [_u8p, _sz, C.POINTER(C.c_uint64)]),
     "hct_b200_holo_open": (C.c_int, [_vp, _u8p, _sz, C.POINTER(C.c_void_p), C.POINTER(Error)]),
     "hct_b200_holo_header": (C.c_int, [_vp, C.POINTER(HoloInfo)]),
     "hct_b200_holo_total_fragments": (C.c_int, [_vp]),

@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libhct_b200.so")
 SOURCES = ["lz4_decode.cu", "int4_dequant.cu", "idct_gemm.cu", "fdct.cu", "hct_host.cu", "hct_encode.cpp",
-           "hct_noalloc.cu", "holo.cu"]
+           "hct_noalloc.cu", "holo.cu", "zstd_decode.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

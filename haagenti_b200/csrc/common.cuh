@@ -140,6 +140,14 @@ cudaError_t launch_sv03_scatter(const float *d_vals, uint64_t count, uint64_t st
                                 uint64_t n, uint64_t cols, half_bits *d_dense, uint64_t ldw,
                                 cudaStream_t s);
 
+// ---- Zstandard (zstd_decode.cu) --------------------------------------------
+// Device scratch for launch_zstd_decode over n jobs (128 KiB of literals per
+// warp in flight).
+size_t zstd_scratch_bytes(uint32_t n);
+cudaError_t launch_zstd_decode(const uint8_t *d_src, const hct_b200_zstd_job *d_jobs, uint32_t n,
+                               uint8_t *d_dst, hct_b200_status *d_status, uint8_t *d_scratch,
+                               cudaStream_t s);
+
 // realified n-point inverse-DFT matrix, 2n x 2n fp16 (rows_pad x ld).
 cudaError_t launch_dft_matrix(uint32_t n, uint32_t rows_pad, uint32_t ld, half_bits *d_out,
                               cudaStream_t s);

@@ -172,6 +172,7 @@ struct hct_b200_ctx {
     DevBuf dense, tt, chunk, meta, flag;
     DevBuf za, zb;  // factored-IDCT intermediates (rows*cols fp16 each)
     DevBuf sched;   // tile counters of the DFT stage kernels
+    DevBuf zscratch, zsrc, zdst, zjob, zstatus;  // Zstandard decode
     DevBuf io_in, io_out, io_blk, io_status;
     std::map<uint64_t, std::unique_ptr<Basis>> bases;
     std::map<uint32_t, std::unique_ptr<DevBuf>> dft_mats;  // realified n-point DFT, fp16
@@ -229,7 +230,7 @@ struct hct_b200_holo {
     enum Kind {
         SV03 = 0,
         PAST_END,    // the stored bytes run past the file ("failed to read fragment data")
-        COMPRESSED,  // entry flag bit 0: zstd
+        ZSTD_BAD,    // entry flag bit 0 and the zstd frames did not decode
         SHORT,       // fewer than 8 bytes ("fragment too short")
         V3_SHORT,    // SV03 magic, fewer than 20 bytes ("V3 fragment too short")
         LEGACY,      // the V1 or V2 spectral layouts
@@ -831,6 +832,164 @@ int hct_b200_spectral_q4_decode(hct_b200_ctx *ctx, const uint8_t *d_payload, siz
     return read_flag(ctx, s, err);
 }
 
+// ---- Zstandard --------------------------------------------------------------
+// zstd::decode_all on the GPU (zstd_decode.cu): the host only moves bytes and
+// reads statuses.
+
+namespace {
+
+// Skips one zstd frame's blocks and checksum (header already read); false
+// when they run past the end.
+bool zstd_skip_blocks(const uint8_t *src, size_t len, size_t *p, bool cksum) {
+    for (;;) {
+        if (len - *p < 3) return false;
+        const uint32_t bh = (uint32_t)src[*p] | ((uint32_t)src[*p + 1] << 8) |
+                            ((uint32_t)src[*p + 2] << 16);
+        *p += 3;
+        const uint32_t type = (bh >> 1) & 3, bsize = bh >> 3;
+        if (type == 3) return false;
+        const size_t body = type == 1 ? 1 : bsize;
+        if (len - *p < body) return false;
+        *p += body;
+        if (bh & 1) break;
+    }
+    if (cksum) {
+        if (len - *p < 4) return false;
+        *p += 4;
+    }
+    return true;
+}
+
+// Content size of every frame (RFC 8878 3.1.1.1.4): HCT_B200_OK with the sum,
+// HCT_B200_ERR_UNSUPPORTED if a frame does not record it.
+int zstd_sizes(const uint8_t *src, size_t len, uint64_t *total) {
+    size_t ip = 0;
+    uint64_t sum = 0;
+    bool known = true;
+    while (ip < len) {
+        if (len - ip < 4) return HCT_B200_ERR_CORRUPTED;
+        const uint32_t magic = rd32(src + ip);
+        if ((magic & 0xFFFFFFF0u) == 0x184D2A50u) {
+            if (len - ip < 8) return HCT_B200_ERR_CORRUPTED;
+            const uint64_t sz = rd32(src + ip + 4);
+            if (len - ip - 8 < sz) return HCT_B200_ERR_CORRUPTED;
+            ip += 8 + sz;
+            continue;
+        }
+        if (magic != 0xFD2FB528u || len - ip < 5) return HCT_B200_ERR_CORRUPTED;
+        size_t p = ip + 4;
+        const int fhd = src[p++];
+        const int fcs_flag = fhd >> 6, single = (fhd >> 5) & 1, dflag = fhd & 3;
+        const int dbytes = dflag == 0 ? 0 : (dflag == 1 ? 1 : (dflag == 2 ? 2 : 4));
+        const int fbytes = fcs_flag == 0 ? (single ? 1 : 0) : (fcs_flag == 1 ? 2 : (fcs_flag == 2 ? 4 : 8));
+        const size_t hl = (size_t)(single ? 0 : 1) + dbytes + fbytes;
+        if (len - p < hl) return HCT_B200_ERR_CORRUPTED;
+        p += (single ? 0 : 1) + dbytes;
+        uint64_t fcs = 0;
+        for (int i = 0; i < fbytes; i++) fcs |= (uint64_t)src[p + i] << (8 * i);
+        if (fbytes == 2) fcs += 256;
+        p += fbytes;
+        if (fbytes == 0) known = false;
+        sum += fcs;
+        if (!zstd_skip_blocks(src, len, &p, (fhd >> 2) & 1)) return HCT_B200_ERR_CORRUPTED;
+        ip = p;
+    }
+    *total = sum;
+    return known ? HCT_B200_OK : HCT_B200_ERR_UNSUPPORTED;
+}
+
+// Host bytes in -> host bytes out on the context's stream; capacity cap.
+// Returns the decode status code (the error filled for non-OK codes).
+int zstd_host_call(hct_b200_ctx *ctx, const uint8_t *in, size_t in_len, size_t cap,
+                   std::vector<uint8_t> *out, hct_b200_error *err) {
+    int rc = ensure_device(ctx);
+    if (rc) { set_err(err, rc, -1, 0, 0, 0, "no CUDA device"); return rc; }
+    const cudaStream_t s = ctx->stream;
+    CK(ctx->zsrc.reserve(in_len + 16));
+    CK(ctx->zdst.reserve(cap + 16));
+    CK(ctx->zjob.reserve(sizeof(hct_b200_zstd_job)));
+    CK(ctx->zstatus.reserve(sizeof(hct_b200_status)));
+    CK(ctx->zscratch.reserve(zstd_scratch_bytes(1)));
+    if (in_len) CK(cudaMemcpyAsync(ctx->zsrc.p, in, in_len, cudaMemcpyHostToDevice, s));
+    const hct_b200_zstd_job job{0, in_len, 0, cap};
+    CK(cudaMemcpyAsync(ctx->zjob.p, &job, sizeof(job), cudaMemcpyHostToDevice, s));
+    CK(launch_zstd_decode(ctx->zsrc.as<uint8_t>(), ctx->zjob.as<hct_b200_zstd_job>(), 1,
+                          ctx->zdst.as<uint8_t>(), ctx->zstatus.as<hct_b200_status>(),
+                          ctx->zscratch.as<uint8_t>(), s));
+    hct_b200_status st{};
+    CK(cudaMemcpyAsync(&st, ctx->zstatus.p, sizeof(st), cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    if (st.code != HCT_B200_OK) {
+        set_err(err, st.code, -1, st.position, st.code == HCT_B200_ERR_BUFFER_TOO_SMALL ? cap + 1 : 0,
+                cap, "zstd: %s at input offset %llu",
+                st.code == HCT_B200_ERR_BUFFER_TOO_SMALL
+                    ? "output larger than the buffer"
+                    : (st.code == HCT_B200_ERR_CHECKSUM
+                           ? "content checksum mismatch"
+                           : (st.code == HCT_B200_ERR_UNSUPPORTED ? "frame needs a dictionary"
+                                                                  : "corrupted frame")),
+                (unsigned long long)st.position);
+        return st.code;
+    }
+    out->resize(st.written);
+    if (st.written)
+        CK(cudaMemcpy(out->data(), ctx->zdst.p, st.written, cudaMemcpyDeviceToHost));
+    return HCT_B200_OK;
+}
+
+// zstd::decode_all: the content size when every frame records it, else
+// growing capacities (the 4x guess and doubling of the reference's
+// Decompressor::decompress, up to 4 GiB).
+int zstd_decode_all(hct_b200_ctx *ctx, const uint8_t *in, size_t in_len,
+                    std::vector<uint8_t> *out, hct_b200_error *err) {
+    uint64_t known = 0;
+    size_t cap = zstd_sizes(in, in_len, &known) == HCT_B200_OK ? (size_t)known
+                                                               : std::max<size_t>(in_len * 4, 4096);
+    for (;;) {
+        const int rc = zstd_host_call(ctx, in, in_len, cap, out, err);
+        if (rc != HCT_B200_ERR_BUFFER_TOO_SMALL || cap >= (4ull << 30)) return rc;
+        cap *= 2;
+    }
+}
+
+}  // namespace
+
+int hct_b200_zstd_content_size(const uint8_t *in, size_t in_len, uint64_t *size) {
+    if (!size || (!in && in_len)) return HCT_B200_ERR_INVALID_ARGUMENT;
+    *size = 0;
+    return zstd_sizes(in, in_len, size);
+}
+
+int hct_b200_zstd_decompress_jobs(hct_b200_ctx *ctx, const uint8_t *d_src,
+                                  const hct_b200_zstd_job *d_jobs, uint32_t n, uint8_t *d_dst,
+                                  hct_b200_status *d_status, void *stream) {
+    if (!ctx || (n && (!d_src || !d_jobs || !d_dst || !d_status))) return HCT_B200_ERR_INVALID_ARGUMENT;
+    if (n == 0) return HCT_B200_OK;
+    int rc = ensure_device(ctx);
+    if (rc) return rc;
+    cudaError_t e = ctx->zscratch.reserve(zstd_scratch_bytes(n));
+    if (e != cudaSuccess) return cuda_code(e);
+    e = launch_zstd_decode(d_src, d_jobs, n, d_dst, d_status, ctx->zscratch.as<uint8_t>(),
+                           (cudaStream_t)stream);
+    return cuda_code(e);
+}
+
+int hct_b200_zstd_decompress(hct_b200_ctx *ctx, const uint8_t *in, size_t in_len, uint8_t *out,
+                             size_t out_cap, size_t *written, hct_b200_error *err) {
+    clear_err(err);
+    if (!ctx || !written || (!in && in_len) || (!out && out_cap)) {
+        set_err(err, HCT_B200_ERR_INVALID_ARGUMENT, -1, 0, 0, 0, "null argument");
+        return HCT_B200_ERR_INVALID_ARGUMENT;
+    }
+    *written = 0;
+    std::vector<uint8_t> res;
+    const int rc = zstd_host_call(ctx, in, in_len, out_cap, &res, err);
+    if (rc) return rc;
+    if (!res.empty()) memcpy(out, res.data(), res.size());
+    *written = res.size();
+    return HCT_B200_OK;
+}
+
 // ---- V3 fragment container -----------------------------------------------
 // haagenti-cuda's GpuDecompressor::parse_hct_fragments + reconstruct_coefficients
 // (crates/haagenti-cuda/src/decompress.rs:322-438) and the reference's C
@@ -848,6 +1007,17 @@ int hct_b200_v3_open(hct_b200_ctx *ctx, const uint8_t *data, size_t len, uint64_
         return HCT_B200_ERR_INVALID_ARGUMENT;
     }
     *out = nullptr;
+    // zstd wrapper (decompress.rs:296-319): decoded on the GPU; data that
+    // does not decode is parsed as it is
+    std::vector<uint8_t> unwrapped;
+    if (len >= 4 && rd32(data) == 0xFD2FB528u) {
+        hct_b200_error zerr;
+        if (zstd_decode_all(ctx, data, len, &unwrapped, &zerr) == HCT_B200_OK) {
+            data = unwrapped.data();
+            len = unwrapped.size();
+        }
+        clear_err(err);
+    }
     if (len < 2) {  // decompress.rs:323-325
         set_err(err, HCT_B200_ERR_CORRUPTED, -1, 0, 0, 0, "HCT data too short");
         return HCT_B200_ERR_CORRUPTED;
@@ -1098,32 +1268,52 @@ int hct_b200_holo_open(hct_b200_ctx *ctx, const uint8_t *file, size_t len, hct_b
     }
     struct Entry {
         uint16_t index, flags;
-        uint32_t offset, csize;
+        uint32_t offset, csize, usize;
         uint64_t checksum;
         size_t base;  // file offset the entry's offset is relative to
     };
     std::vector<Entry> entries;
     for (size_t i = 0; i < nidx; i++) {
         const uint8_t *e = file + HOLO_HEADER_SIZE + i * HOLO_ENTRY_SIZE;
-        entries.push_back(Entry{rd16(e), rd16(e + 2), rd32(e + 4), rd32(e + 8), rd64(e + 16),
-                                data_offset});
+        entries.push_back(Entry{rd16(e), rd16(e + 2), rd32(e + 4), rd32(e + 8), rd32(e + 12),
+                                rd64(e + 16), data_offset});
     }
     if (nidx == 0 && len >= data_offset + HOLO_ENTRY_SIZE) {
         const uint8_t *e = file + data_offset;
         const uint32_t csize = rd32(e + 8);
         if (rd16(e) == 0 && csize > 0 && csize < 1000000000u) {
-            entries.push_back(Entry{0, rd16(e + 2), rd32(e + 4), csize, rd64(e + 16),
+            entries.push_back(Entry{0, rd16(e + 2), rd32(e + 4), csize, rd32(e + 12), rd64(e + 16),
                                     data_offset + HOLO_ENTRY_SIZE});
             hd.inline_format = 1;
         }
     }
     // each fragment as read_fragment + add_fragment would see it
     struct Src {
-        size_t at;
-        uint64_t n;
+        size_t frag;  // index into h->frags
+        size_t at;    // file offset of its values (SV03) or of its zstd frames
+        uint64_t n;   // values, or compressed bytes
+        uint64_t cap; // zstd: output capacity
     };
-    std::vector<Src> src;
-    uint64_t total_vals = 0;
+    std::vector<Src> plain, packed;
+    // SV03 header of fragment bytes d (n of them) into f
+    auto classify = [](hct_b200_holo::Frag &f, const uint8_t *d, uint64_t n) {
+        if (n < 8) {
+            f.kind = hct_b200_holo::SHORT;
+        } else if (rd32(d) != SV03_MAGIC) {
+            f.kind = hct_b200_holo::LEGACY;
+        } else if (n < 20) {
+            f.kind = hct_b200_holo::V3_SHORT;
+        } else {  // add_fragment_v3 (holotensor.rs:979-1015)
+            f.kind = hct_b200_holo::SV03;
+            f.num_coeffs = rd32(d + 4);
+            f.F = rd32(d + 8);
+            f.start = rd32(d + 12);
+            const uint64_t nv = (n - 20) / 4;
+            if (f.start >= f.num_coeffs) f.count = 0;
+            else if (f.F == 0) f.count = nv;
+            else f.count = std::min<uint64_t>(nv, (f.num_coeffs - f.start + (uint64_t)f.F - 1) / f.F);
+        }
+    };
     for (const Entry &e : entries) {
         hct_b200_holo::Frag f;
         f.index = e.index;
@@ -1133,26 +1323,15 @@ int hct_b200_holo_open(hct_b200_ctx *ctx, const uint8_t *file, size_t len, hct_b
         } else {
             const uint8_t *d = file + at;
             if (flags & HOLO_FLAG_FRAGMENT_CHECKSUMS) f.checksum_ok = xxh(d, e.csize) == e.checksum;
-            if (e.flags & 1) {
-                f.kind = hct_b200_holo::COMPRESSED;
-            } else if (e.csize < 8) {
-                f.kind = hct_b200_holo::SHORT;
-            } else if (rd32(d) != SV03_MAGIC) {
-                f.kind = hct_b200_holo::LEGACY;
-            } else if (e.csize < 20) {
-                f.kind = hct_b200_holo::V3_SHORT;
+            if (e.flags & 1) {  // zstd (holotensor.rs:2081-2091), decoded on the GPU below
+                uint64_t fcs = 0;
+                uint64_t cap = zstd_sizes(d, e.csize, &fcs) == HCT_B200_OK ? fcs : 0;
+                cap = std::max<uint64_t>(cap, e.usize);
+                if (cap == 0) cap = 4ull * e.csize + 4096;
+                packed.push_back(Src{h->frags.size(), at, e.csize, cap});
             } else {
-                // add_fragment_v3 (holotensor.rs:979-1015)
-                f.num_coeffs = rd32(d + 4);
-                f.F = rd32(d + 8);
-                f.start = rd32(d + 12);
-                const uint64_t nv = (e.csize - 20) / 4;
-                if (f.start >= f.num_coeffs) f.count = 0;
-                else if (f.F == 0) f.count = nv;
-                else f.count = std::min<uint64_t>(nv, (f.num_coeffs - f.start + (uint64_t)f.F - 1) / f.F);
-                f.dev_off = total_vals;
-                total_vals += round_up(f.count, 4);
-                src.push_back(Src{at + 20, f.count});
+                classify(f, d, e.csize);
+                if (f.kind == hct_b200_holo::SV03) plain.push_back(Src{h->frags.size(), at + 20, f.count, 0});
             }
         }
         h->frags.push_back(f);
@@ -1160,16 +1339,70 @@ int hct_b200_holo_open(hct_b200_ctx *ctx, const uint8_t *file, size_t len, hct_b
     int rc = ensure_device(ctx);
     if (rc) { set_err(err, rc, -1, 0, 0, 0, "no CUDA device"); return rc; }
     cudaStream_t s = ctx->stream;
-    CK(h->d_vals.reserve(total_vals * 4 + 64));
-    {
-        size_t j = 0;
-        for (const hct_b200_holo::Frag &f : h->frags) {
-            if (f.kind != hct_b200_holo::SV03) continue;
-            if (f.count)
-                CK(cudaMemcpyAsync(h->d_vals.as<float>() + f.dev_off, file + src[j].at,
-                                   4 * src[j].n, cudaMemcpyHostToDevice, s));
-            j++;
+    // device layout: the plain fragments' values, then one 16-byte aligned
+    // region per zstd fragment for its decoded bytes (values at +20 bytes)
+    for (int attempt = 0;; attempt++) {
+        uint64_t total_vals = 0;
+        for (const Src &p : plain) {
+            h->frags[p.frag].dev_off = total_vals;
+            total_vals += round_up(p.n, 4);
         }
+        std::vector<uint64_t> region(packed.size());
+        uint64_t zbytes = 0, zin = 0;
+        for (size_t i = 0; i < packed.size(); i++) {
+            region[i] = 4 * total_vals + zbytes;
+            zbytes += round_up(packed[i].cap, 16);
+            zin += round_up(packed[i].n, 16);
+        }
+        CK(h->d_vals.reserve(total_vals * 4 + zbytes + 64));
+        for (const Src &p : plain)
+            if (p.n)
+                CK(cudaMemcpyAsync(h->d_vals.as<float>() + h->frags[p.frag].dev_off, file + p.at,
+                                   4 * p.n, cudaMemcpyHostToDevice, s));
+        if (packed.empty()) break;
+        std::vector<hct_b200_zstd_job> jobs(packed.size());
+        CK(ctx->zsrc.reserve(zin + 16));
+        uint64_t off = 0;
+        for (size_t i = 0; i < packed.size(); i++) {
+            CK(cudaMemcpyAsync(ctx->zsrc.as<uint8_t>() + off, file + packed[i].at, packed[i].n,
+                               cudaMemcpyHostToDevice, s));
+            jobs[i] = hct_b200_zstd_job{off, packed[i].n, region[i], packed[i].cap};
+            off += round_up(packed[i].n, 16);
+        }
+        CK(ctx->zjob.reserve(jobs.size() * sizeof(hct_b200_zstd_job)));
+        CK(ctx->zstatus.reserve(jobs.size() * sizeof(hct_b200_status)));
+        CK(ctx->zscratch.reserve(zstd_scratch_bytes((uint32_t)jobs.size())));
+        CK(cudaMemcpyAsync(ctx->zjob.p, jobs.data(), jobs.size() * sizeof(hct_b200_zstd_job),
+                           cudaMemcpyHostToDevice, s));
+        CK(launch_zstd_decode(ctx->zsrc.as<uint8_t>(), ctx->zjob.as<hct_b200_zstd_job>(),
+                              (uint32_t)jobs.size(), h->d_vals.as<uint8_t>(),
+                              ctx->zstatus.as<hct_b200_status>(), ctx->zscratch.as<uint8_t>(), s));
+        std::vector<hct_b200_status> st(jobs.size());
+        CK(cudaMemcpyAsync(st.data(), ctx->zstatus.p, st.size() * sizeof(hct_b200_status),
+                           cudaMemcpyDeviceToHost, s));
+        CK(cudaStreamSynchronize(s));
+        bool grow = false;
+        for (size_t i = 0; i < packed.size(); i++)
+            if (st[i].code == HCT_B200_ERR_BUFFER_TOO_SMALL && packed[i].cap < (4ull << 30)) {
+                packed[i].cap *= 2;  // decode_all grows its output until the frames fit
+                grow = true;
+            }
+        if (grow && attempt < 40) continue;
+        // the decoded fragments' SV03 headers
+        for (size_t i = 0; i < packed.size(); i++) {
+            hct_b200_holo::Frag &f = h->frags[packed[i].frag];
+            if (st[i].code != HCT_B200_OK) {
+                f.kind = hct_b200_holo::ZSTD_BAD;
+                continue;
+            }
+            uint8_t head[20] = {0};
+            const uint64_t w = st[i].written;
+            if (w) CK(cudaMemcpy(head, h->d_vals.as<uint8_t>() + region[i], std::min<uint64_t>(w, 20),
+                                 cudaMemcpyDeviceToHost));
+            classify(f, head, w);
+            f.dev_off = (region[i] + 20) / 4;
+        }
+        break;
     }
     if (h->rows && h->cols) {
         rc = reserve_spectral(ctx, h->rows, h->cols, err);
@@ -1241,7 +1474,7 @@ int hct_b200_holo_decode(hct_b200_holo *h, uint32_t num_fragments, void *d_out, 
         int code = HCT_B200_ERR_CORRUPTED;
         if (f->kind == hct_b200_holo::PAST_END) why = "failed to read fragment data";
         else if (!f->checksum_ok) { why = "fragment checksum mismatch"; code = HCT_B200_ERR_CHECKSUM; }
-        else if (f->kind == hct_b200_holo::COMPRESSED) { why = "zstd-compressed fragment"; code = HCT_B200_ERR_UNSUPPORTED; }
+        else if (f->kind == hct_b200_holo::ZSTD_BAD) why = "failed to decompress fragment";
         else if (f->kind == hct_b200_holo::SHORT) why = "fragment too short";
         else if (f->kind == hct_b200_holo::V3_SHORT) why = "V3 fragment too short";
         else if (f->kind == hct_b200_holo::LEGACY) { why = "V1/V2 spectral fragment layout"; code = HCT_B200_ERR_UNSUPPORTED; }

@@ -1,0 +1,883 @@
+// Zstandard frame decoder (RFC 8878), written for one warp per job.
+//
+// The reference decodes zstd data through the `zstd` crate (libzstd):
+// HoloTensorReader::read_fragment for fragments whose index entry has flag
+// bit 0 (crates/haagenti-hct/src/holotensor.rs:2081-2091) and
+// GpuDecompressor::try_zstd_decompress for zstd-wrapped HCT data
+// (crates/haagenti-cuda/src/decompress.rs:296-319), both `zstd::decode_all`:
+// every frame of the input in turn (skippable frames skipped), the frames'
+// contents concatenated.  This decoder follows the format as RFC 8878
+// specifies it and reports an error wherever libzstd's decoder does for the
+// checks listed at the functions below.
+//
+// Work split inside a warp (nl lanes; the same code runs with nl = 1 on the
+// host):
+//   * frame, block and section headers: every lane parses them (the same
+//     bytes, so the lanes agree without communication);
+//   * FSE and Huffman table construction, Huffman weights and the sequence
+//     bitstream: lane 0, results in the warp's workspace;
+//   * the 4 Huffman literal streams: one lane each;
+//   * raw / RLE blocks, literal copies and match copies: all lanes (a match
+//     with offset < length repeats the period-`offset` pattern, so each output
+//     byte is read from the bytes before the match and no lane waits on
+//     another within a copy);
+//   * XXH64 content checksum: lanes 0-3 run the 4 accumulators.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#if defined(__CUDACC__)
+#define ZHD __host__ __device__ __forceinline__
+#else
+#define ZHD inline
+#endif
+
+namespace hct {
+namespace zs {
+
+#if defined(__CUDA_ARCH__)
+__device__ __forceinline__ void warp_sync() { __syncwarp(); }
+#else
+inline void warp_sync() {}
+#endif
+
+enum : int { OK = 0, E_DST = 2, E_CORRUPT = 17, E_CHECKSUM = 18, E_UNSUPPORTED = 19 };
+
+constexpr uint32_t MAGIC = 0xFD2FB528u;
+constexpr uint32_t SKIP_MAGIC = 0x184D2A50u;  // low 4 bits: any
+constexpr uint32_t BLOCK_MAX = 128 * 1024;
+constexpr int LL_MAX_LOG = 9, OF_MAX_LOG = 8, ML_MAX_LOG = 9, HUF_MAX_LOG = 12;
+constexpr int LL_MAX_SYM = 35, OF_MAX_SYM = 31, ML_MAX_SYM = 52;
+constexpr int SEQ_BATCH = 64;
+constexpr size_t LIT_SCRATCH = BLOCK_MAX + 64;  // bytes of literal scratch per warp
+
+struct FseEntry {
+    uint16_t base;  // next state base
+    uint8_t sym;
+    uint8_t nb;  // bits to read for the next state
+};
+struct HufEntry {
+    uint8_t sym;
+    uint8_t nb;
+};
+
+// Per-warp state that lives across the blocks of a frame (shared memory on
+// the device).
+struct Workspace {
+    FseEntry ll[1 << LL_MAX_LOG];
+    FseEntry ml[1 << ML_MAX_LOG];
+    FseEntry of[1 << OF_MAX_LOG];
+    HufEntry huf[1 << HUF_MAX_LOG];
+    FseEntry wt[64];  // FSE table of the Huffman weights
+    int16_t norm[256];
+    uint16_t next[256];  // FSE table construction scratch
+    uint8_t weights[256];
+    uint32_t seq_ll[SEQ_BATCH], seq_ml[SEQ_BATCH], seq_of[SEQ_BATCH];
+    uint32_t rep[3];
+    int8_t ll_log, ml_log, of_log, huf_log;  // -1: no table yet
+    int err;
+    uint32_t nseq;      // sequences of the current batch
+    uint32_t seq_done;  // the bitstream was consumed completely
+};
+
+// ---- small helpers -------------------------------------------------------
+
+ZHD uint32_t rd16(const uint8_t *p) { return (uint32_t)p[0] | ((uint32_t)p[1] << 8); }
+ZHD uint32_t rd24(const uint8_t *p) { return rd16(p) | ((uint32_t)p[2] << 16); }
+ZHD uint32_t rd32(const uint8_t *p) { return rd16(p) | (rd16(p + 2) << 16); }
+ZHD uint64_t rd64(const uint8_t *p) { return (uint64_t)rd32(p) | ((uint64_t)rd32(p + 4) << 32); }
+
+ZHD int highbit(uint32_t v) {  // index of the highest set bit, v > 0
+#if defined(__CUDA_ARCH__)
+    return 31 - __clz(v);
+#else
+    return 31 - __builtin_clz(v);
+#endif
+}
+
+// 8 bytes at p (little endian); bytes at or past end read as zero
+ZHD uint64_t rd64_bounded(const uint8_t *p, const uint8_t *end) {
+    if (p + 8 <= end) return rd64(p);
+    uint64_t v = 0;
+    for (int i = 0; i < 8 && p + i < end; i++) v |= (uint64_t)p[i] << (8 * i);
+    return v;
+}
+
+// Backward bit reader over [start, end): bits are taken from the top, bit
+// pos - 1 first.  Reading below bit 0 yields zeros (pos goes negative),
+// which callers treat as the reference's "overflow".
+struct BitRev {
+    const uint8_t *base, *end;
+    int64_t pos;   // bits not yet consumed
+    int64_t cbit;  // first bit held in cont
+    uint64_t cont;
+
+    ZHD bool init(const uint8_t *s, const uint8_t *e) {
+        base = s;
+        end = e;
+        if (e <= s) return false;
+        const uint8_t last = e[-1];
+        if (last == 0) return false;  // no end mark
+        pos = (int64_t)(e - s) * 8 - (8 - highbit(last));
+        cbit = 1;  // forces a load
+        cont = 0;
+        reload();
+        return true;
+    }
+    ZHD void reload() {
+        int64_t b = pos >= 64 ? ((pos - 64 + 7) & ~(int64_t)7) : 0;
+        cbit = b;
+        cont = rd64_bounded(base + (b >> 3), end);
+    }
+    // n <= 56 bits
+    ZHD uint64_t peek(int n) {
+        if (n == 0) return 0;
+        if (pos - n < cbit && cbit > 0) reload();  // after it, pos - n >= cbit or cbit == 0
+        if (pos - n >= cbit) return (cont >> (pos - n - cbit)) & ((1ull << n) - 1);
+        // below the first bit (cbit == 0): the bits left, shifted up, zeros below
+        if (pos <= 0) return 0;
+        return (cont & ((1ull << pos) - 1)) << (n - pos);
+    }
+    ZHD uint64_t read(int n) {
+        const uint64_t v = peek(n);
+        pos -= n;
+        return v;
+    }
+    ZHD void skip(int n) { pos -= n; }
+};
+
+// Forward bit reader (FSE table descriptions): bit 0 of byte 0 first.
+struct BitFwd {
+    const uint8_t *base, *end;
+    int64_t pos;
+    ZHD uint64_t peek(int n) const {
+        const int64_t byte = pos >> 3;
+        const uint64_t v = rd64_bounded(base + byte, end) >> (pos & 7);
+        return v & ((1ull << n) - 1);
+    }
+    ZHD void skip(int n) { pos += n; }
+};
+
+// ---- FSE -----------------------------------------------------------------
+
+// FSE table description (RFC 8878 4.1.1; libzstd FSE_readNCount): the
+// normalized counts of symbols 0..max_sym into norm, *log the accuracy log.
+// Returns the bytes used, or -1 when the description is invalid.
+ZHD int fse_read_ncount(const uint8_t *src, size_t len, int16_t *norm, int max_sym, int max_log,
+                        int *log, int *nsym) {
+    if (len < 1) return -1;
+    BitFwd br{src, src + len, 0};
+    const int al = (int)br.peek(4) + 5;
+    br.skip(4);
+    if (al > max_log) return -1;
+    int remaining = (1 << al) + 1, threshold = 1 << al, nb = al + 1, sym = 0;
+    bool prev0 = false;
+    while (remaining > 1 && sym <= max_sym) {
+        if (prev0) {
+            int n0 = sym;
+            for (;;) {
+                const int r = (int)br.peek(2);
+                br.skip(2);
+                n0 += r;
+                if (r != 3) break;
+                if (br.pos > (int64_t)len * 8) return -1;
+            }
+            if (n0 > max_sym) return -1;
+            while (sym < n0) norm[sym++] = 0;
+            if (br.pos > (int64_t)len * 8) return -1;
+            if (sym > max_sym) break;
+        }
+        const int mx = (2 * threshold - 1) - remaining;
+        int count;
+        const uint32_t bits = (uint32_t)br.peek(nb);
+        if ((int)(bits & (threshold - 1)) < mx) {
+            count = (int)(bits & (threshold - 1));
+            br.skip(nb - 1);
+        } else {
+            count = (int)(bits & (2 * threshold - 1));
+            if (count >= threshold) count -= mx;
+            br.skip(nb);
+        }
+        count--;
+        remaining -= count < 0 ? -count : count;
+        norm[sym++] = (int16_t)count;
+        prev0 = count == 0;
+        while (remaining < threshold) {
+            nb--;
+            threshold >>= 1;
+        }
+        if (br.pos > (int64_t)len * 8) return -1;
+    }
+    if (remaining != 1 || sym > max_sym + 1) return -1;
+    *log = al;
+    *nsym = sym;
+    const int64_t used = (br.pos + 7) >> 3;
+    if (used > (int64_t)len) return -1;
+    return (int)used;
+}
+
+// Decoding table from normalized counts (RFC 8878 4.1.1; libzstd
+// FSE_buildDTable): low-probability symbols at the top, the others spread
+// with step (size/2 + size/8 + 3), then each state's bits and base.
+ZHD bool fse_build(FseEntry *t, const int16_t *norm, int nsym, int log, uint16_t *next) {
+    const int size = 1 << log;
+    int high = size - 1;
+    for (int s = 0; s < nsym; s++) {
+        if (norm[s] == -1) {
+            t[high--].sym = (uint8_t)s;
+            next[s] = 1;
+        } else {
+            next[s] = (uint16_t)norm[s];
+        }
+    }
+    const int step = (size >> 1) + (size >> 3) + 3, mask = size - 1;
+    int p = 0;
+    for (int s = 0; s < nsym; s++) {
+        for (int i = 0; i < norm[s]; i++) {
+            t[p].sym = (uint8_t)s;
+            do {
+                p = (p + step) & mask;
+            } while (p > high);
+        }
+    }
+    if (p != 0) return false;
+    for (int u = 0; u < size; u++) {
+        const int s = t[u].sym;
+        const uint32_t n = next[s]++;
+        const int nb = log - highbit(n);
+        t[u].nb = (uint8_t)nb;
+        t[u].base = (uint16_t)((n << nb) - (uint32_t)size);
+    }
+    return true;
+}
+
+// One-symbol table (RLE mode)
+ZHD void fse_rle(FseEntry *t, int sym) {
+    t[0].sym = (uint8_t)sym;
+    t[0].nb = 0;
+    t[0].base = 0;
+}
+
+// Predefined distributions (RFC 8878 3.1.1.3.2.2).
+ZHD int16_t ll_default(int s) {
+    constexpr int16_t v[36] = {4, 3, 2, 2, 2, 2, 2, 2, 2, 2, 2, 2, 2, 1, 1, 1, 2, 2,
+                               2, 2, 2, 2, 2, 2, 2, 3, 2, 1, 1, 1, 1, 1, -1, -1, -1, -1};
+    return v[s];
+}
+ZHD int16_t ml_default(int s) {
+    constexpr int16_t v[53] = {1, 4, 3, 2, 2, 2, 2, 2, 2, 1, 1, 1, 1, 1, 1, 1, 1, 1,
+                               1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1,
+                               1, 1, 1, 1, 1, 1, 1, 1, 1, 1, -1, -1, -1, -1, -1, -1, -1};
+    return v[s];
+}
+ZHD int16_t of_default(int s) {
+    constexpr int16_t v[29] = {1, 1, 1, 1, 1, 1, 2, 2, 2, 1, 1, 1, 1, 1, 1,
+                               1, 1, 1, 1, 1, 1, 1, 1, 1, -1, -1, -1, -1, -1};
+    return v[s];
+}
+
+// Literal and match length codes (RFC 8878 3.1.1.3.2.1.1).
+ZHD uint32_t ll_base(int c) {
+    constexpr uint32_t b[36] = {0,  1,  2,  3,  4,   5,   6,   7,   8,    9,    10,   11,
+                                12, 13, 14, 15, 16,  18,  20,  22,  24,   28,   32,   40,
+                                48, 64, 128, 256, 512, 1024, 2048, 4096, 8192, 16384, 32768, 65536};
+    return b[c];
+}
+ZHD int ll_bits(int c) {
+    constexpr uint8_t b[36] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 1, 1,
+                               1, 1, 2, 2, 3, 3, 4, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16};
+    return b[c];
+}
+ZHD uint32_t ml_base(int c) {
+    constexpr uint32_t b[53] = {3,  4,  5,  6,  7,  8,  9,  10,  11,  12,  13,   14,   15,   16,
+                                17, 18, 19, 20, 21, 22, 23, 24,  25,  26,  27,   28,   29,   30,
+                                31, 32, 33, 34, 35, 37, 39, 41,  43,  47,  51,   59,   67,   83,
+                                99, 131, 259, 515, 1027, 2051, 4099, 8195, 16387, 32771, 65539};
+    return b[c];
+}
+ZHD int ml_bits(int c) {
+    constexpr uint8_t b[53] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0,
+                               0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 1, 1, 1, 1,
+                               2, 2, 3, 3, 4, 4, 5, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16};
+    return b[c];
+}
+
+// ---- Huffman -------------------------------------------------------------
+
+// Huffman tree description (RFC 8878 4.2.1; libzstd HUF_readStats +
+// HUF_readDTableX1): weights (direct 4-bit, or FSE-compressed with two
+// interleaved states), the implied last weight, then the single-symbol
+// decoding table of 2^log entries.  Returns the bytes used, -1 if invalid.
+// Lane 0 only.
+ZHD int huf_read_table(Workspace *ws, const uint8_t *src, size_t len) {
+    if (len < 1) return -1;
+    const int isz = src[0];
+    int nw = 0;
+    size_t used;
+    if (isz >= 128) {
+        nw = isz - 127;
+        const size_t bytes = (size_t)(nw + 1) / 2;
+        if (bytes + 1 > len) return -1;
+        for (int n = 0; n < nw; n += 2) {
+            const uint8_t b = src[1 + n / 2];
+            ws->weights[n] = b >> 4;
+            if (n + 1 < nw) ws->weights[n + 1] = b & 15;
+        }
+        used = bytes + 1;
+    } else {
+        if ((size_t)isz + 1 > len) return -1;
+        int log = 0, nsym = 0;
+        const int h = fse_read_ncount(src + 1, (size_t)isz, ws->norm, 255, 6, &log, &nsym);
+        if (h < 0) return -1;
+        if (!fse_build(ws->wt, ws->norm, nsym, log, ws->next)) return -1;
+        BitRev br;
+        if (!br.init(src + 1 + h, src + 1 + isz)) return -1;
+        uint32_t s1 = (uint32_t)br.read(log), s2 = (uint32_t)br.read(log);
+        // libzstd FSE_decompress (two states): a symbol per state in turn
+        // until a state update reads past the start of the stream, then the
+        // other state's symbol ends the list.
+        for (;;) {
+            if (nw > 253) return -1;
+            ws->weights[nw++] = ws->wt[s1].sym;
+            s1 = ws->wt[s1].base + (uint32_t)br.read(ws->wt[s1].nb);
+            if (br.pos < 0) {
+                ws->weights[nw++] = ws->wt[s2].sym;
+                break;
+            }
+            if (nw > 253) return -1;
+            ws->weights[nw++] = ws->wt[s2].sym;
+            s2 = ws->wt[s2].base + (uint32_t)br.read(ws->wt[s2].nb);
+            if (br.pos < 0) {
+                ws->weights[nw++] = ws->wt[s1].sym;
+                break;
+            }
+        }
+        used = (size_t)isz + 1;
+    }
+    // weight statistics and the implied last weight
+    uint32_t rank[HUF_MAX_LOG + 2] = {0};
+    uint32_t total = 0;
+    for (int n = 0; n < nw; n++) {
+        const int w = ws->weights[n];
+        if (w > HUF_MAX_LOG) return -1;
+        rank[w]++;
+        total += (1u << w) >> 1;
+    }
+    if (total == 0) return -1;
+    const int log = highbit(total) + 1;
+    if (log > HUF_MAX_LOG) return -1;
+    const uint32_t rest = (1u << log) - total;
+    const int lastw = highbit(rest) + 1;
+    if ((1u << highbit(rest)) != rest) return -1;
+    if (nw > 255) return -1;
+    ws->weights[nw] = (uint8_t)lastw;
+    rank[lastw]++;
+    if (rank[1] < 2 || (rank[1] & 1)) return -1;
+    const int nsym = nw + 1;
+    // single-symbol decoding table: symbols of weight w fill 2^(w-1) entries
+    uint32_t start[HUF_MAX_LOG + 2];
+    uint32_t next = 0;
+    for (int w = 1; w <= log; w++) {
+        start[w] = next;
+        next += rank[w] << (w - 1);
+    }
+    for (int n = 0; n < nsym; n++) {
+        const int w = ws->weights[n];
+        if (!w) continue;
+        const uint32_t cnt = (1u << w) >> 1;
+        const uint8_t nb = (uint8_t)(log + 1 - w);
+        for (uint32_t u = start[w]; u < start[w] + cnt; u++) {
+            ws->huf[u].sym = (uint8_t)n;
+            ws->huf[u].nb = nb;
+        }
+        start[w] += cnt;
+    }
+    ws->huf_log = (int8_t)log;
+    return (int)used;
+}
+
+// One Huffman stream of n symbols into out; false unless the stream is
+// consumed exactly (libzstd HUF_decompress1X1: BIT_endOfDStream).
+ZHD bool huf_stream(const Workspace *ws, const uint8_t *s, const uint8_t *e, uint8_t *out,
+                    uint32_t n) {
+    BitRev br;
+    if (!br.init(s, e)) return false;
+    const int log = ws->huf_log;
+    for (uint32_t i = 0; i < n; i++) {
+        const HufEntry d = ws->huf[br.peek(log)];
+        out[i] = d.sym;
+        br.skip(d.nb);
+    }
+    return br.pos == 0;
+}
+
+// ---- XXH64 (content checksum) --------------------------------------------
+
+constexpr uint64_t P64_1 = 11400714785074694791ull, P64_2 = 14029467366897019727ull,
+                   P64_3 = 1609587929392839161ull, P64_4 = 9650029242287828579ull,
+                   P64_5 = 2870177450012600261ull;
+ZHD uint64_t rotl64(uint64_t x, int r) { return (x << r) | (x >> (64 - r)); }
+ZHD uint64_t xxh_round(uint64_t acc, uint64_t in) {
+    acc += in * P64_2;
+    return rotl64(acc, 31) * P64_1;
+}
+ZHD uint64_t xxh_merge(uint64_t acc, uint64_t v) {
+    acc ^= xxh_round(0, v);
+    return acc * P64_1 + P64_4;
+}
+
+// XXH64 with seed 0 of [p, p + n); the stripe accumulators run on lanes
+// 0..3 (nl >= 4) or all on lane 0.  Result valid on lane 0; acc is a
+// 4-entry scratch shared by the warp.
+ZHD uint64_t xxh64(const uint8_t *p, uint64_t n, int lane, int nl, uint64_t *acc) {
+    const uint64_t stripes = n / 32;
+    if (n >= 32) {
+        for (int a = lane; a < 4; a += nl) {
+            uint64_t v = a == 0 ? P64_1 + P64_2 : (a == 1 ? P64_2 : (a == 2 ? 0 : 0 - P64_1));
+            for (uint64_t s = 0; s < stripes; s++) v = xxh_round(v, rd64(p + 32 * s + 8 * a));
+            acc[a] = v;
+        }
+    }
+    warp_sync();
+    uint64_t h = 0;
+    if (lane == 0) {
+        if (n >= 32) {
+            h = rotl64(acc[0], 1) + rotl64(acc[1], 7) + rotl64(acc[2], 12) + rotl64(acc[3], 18);
+            for (int a = 0; a < 4; a++) h = xxh_merge(h, acc[a]);
+        } else {
+            h = P64_5;
+        }
+        h += n;
+        const uint8_t *q = p + 32 * stripes;
+        uint64_t r = n - 32 * stripes;
+        while (r >= 8) {
+            h ^= xxh_round(0, rd64(q));
+            h = rotl64(h, 27) * P64_1 + P64_4;
+            q += 8;
+            r -= 8;
+        }
+        if (r >= 4) {
+            h ^= (uint64_t)rd32(q) * P64_1;
+            h = rotl64(h, 23) * P64_2 + P64_3;
+            q += 4;
+            r -= 4;
+        }
+        while (r) {
+            h ^= (uint64_t)(*q) * P64_5;
+            h = rotl64(h, 11) * P64_1;
+            q++;
+            r--;
+        }
+        h ^= h >> 33;
+        h *= P64_2;
+        h ^= h >> 29;
+        h *= P64_3;
+        h ^= h >> 32;
+    }
+    return h;
+}
+
+// ---- sequences -----------------------------------------------------------
+
+// Table of one sequence field for its compression mode (RFC 8878
+// 3.1.1.3.2.1): 0 predefined, 1 RLE (one symbol byte), 2 FSE-compressed
+// (a table description), 3 repeat the previous table.  Returns bytes used
+// or -1.  Lane 0 only.
+ZHD int seq_table(Workspace *ws, int field, int mode, const uint8_t *src, size_t len) {
+    FseEntry *t = field == 0 ? ws->ll : (field == 1 ? ws->of : ws->ml);
+    int8_t *lg = field == 0 ? &ws->ll_log : (field == 1 ? &ws->of_log : &ws->ml_log);
+    const int max_sym = field == 0 ? LL_MAX_SYM : (field == 1 ? OF_MAX_SYM : ML_MAX_SYM);
+    const int max_log = field == 0 ? LL_MAX_LOG : (field == 1 ? OF_MAX_LOG : ML_MAX_LOG);
+    if (mode == 0) {
+        const int n = field == 0 ? 36 : (field == 1 ? 29 : 53);
+        for (int s = 0; s < n; s++)
+            ws->norm[s] = field == 0 ? ll_default(s) : (field == 1 ? of_default(s) : ml_default(s));
+        const int log = field == 1 ? 5 : 6;
+        if (!fse_build(t, ws->norm, n, log, ws->next)) return -1;
+        *lg = (int8_t)log;
+        return 0;
+    }
+    if (mode == 1) {
+        if (len < 1 || src[0] > max_sym) return -1;
+        fse_rle(t, src[0]);
+        *lg = 0;
+        return 1;
+    }
+    if (mode == 2) {
+        int log = 0, nsym = 0;
+        const int h = fse_read_ncount(src, len, ws->norm, max_sym, max_log, &log, &nsym);
+        if (h < 0) return -1;
+        if (!fse_build(t, ws->norm, nsym, log, ws->next)) return -1;
+        *lg = (int8_t)log;
+        return h;
+    }
+    return *lg < 0 ? -1 : 0;  // repeat: needs an earlier table
+}
+
+// ---- the decoder ---------------------------------------------------------
+
+struct Job {
+    const uint8_t *src;
+    uint64_t len;
+    uint8_t *dst;
+    uint64_t cap;
+    uint8_t *lit;  // LIT_SCRATCH bytes of the warp
+};
+
+struct Result {
+    int code;
+    uint64_t pos;      // input offset of the failing frame or block
+    uint64_t written;  // output bytes
+};
+
+// Cooperative copies (all lanes): n bytes from s to d (no overlap).
+ZHD void coop_copy(uint8_t *d, const uint8_t *s, uint64_t n, int lane, int nl) {
+    for (uint64_t i = (uint64_t)lane; i < n; i += (uint64_t)nl) d[i] = s[i];
+}
+
+// Match: ml bytes at d from d - off (off >= 1); with off < ml the bytes
+// repeat the period-off pattern, read from before d.
+ZHD void coop_match(uint8_t *d, uint64_t off, uint64_t ml, int lane, int nl) {
+    const uint8_t *s = d - off;
+    if (off >= ml) {
+        for (uint64_t i = (uint64_t)lane; i < ml; i += (uint64_t)nl) d[i] = s[i];
+        return;
+    }
+    uint64_t j = (uint64_t)lane % off;
+    const uint64_t stepm = (uint64_t)nl % off;
+    for (uint64_t i = (uint64_t)lane; i < ml; i += (uint64_t)nl) {
+        d[i] = s[j];
+        j += stepm;
+        if (j >= off) j -= off;
+    }
+}
+
+// A compressed block (RFC 8878 3.1.1.3) of bsize bytes at b, its output
+// appended at out (frame output starts at fstart).  Returns an error code.
+ZHD int decode_compressed_block(Workspace *ws, const Job &job, const uint8_t *b, uint32_t bsize,
+                                uint64_t fstart, uint64_t *out, int lane, int nl) {
+    // ---- literals section header (3.1.1.3.1.1)
+    if (bsize < 1) return E_CORRUPT;
+    const int ltype = b[0] & 3, sfmt = (b[0] >> 2) & 3;
+    uint32_t regen = 0, csize = 0, hs = 0;
+    int nstreams = 1;
+    if (ltype < 2) {  // raw / RLE
+        if (sfmt == 0 || sfmt == 2) {
+            hs = 1;
+            regen = b[0] >> 3;
+        } else if (sfmt == 1) {
+            hs = 2;
+            if (bsize < 2) return E_CORRUPT;
+            regen = (b[0] >> 4) | ((uint32_t)b[1] << 4);
+        } else {
+            hs = 3;
+            if (bsize < 3) return E_CORRUPT;
+            regen = (b[0] >> 4) | ((uint32_t)b[1] << 4) | ((uint32_t)b[2] << 12);
+        }
+    } else {  // compressed / treeless
+        if (sfmt < 2) {
+            hs = 3;
+            if (bsize < 3) return E_CORRUPT;
+            const uint32_t v = rd24(b);
+            regen = (v >> 4) & 0x3FF;
+            csize = (v >> 14) & 0x3FF;
+            nstreams = sfmt == 0 ? 1 : 4;
+        } else if (sfmt == 2) {
+            hs = 4;
+            if (bsize < 4) return E_CORRUPT;
+            const uint32_t v = rd32(b);
+            regen = (v >> 4) & 0x3FFF;
+            csize = (v >> 18) & 0x3FFF;
+            nstreams = 4;
+        } else {
+            hs = 5;
+            if (bsize < 5) return E_CORRUPT;
+            const uint64_t v = (uint64_t)rd32(b) | ((uint64_t)b[4] << 32);
+            regen = (uint32_t)((v >> 4) & 0x3FFFF);
+            csize = (uint32_t)((v >> 22) & 0x3FFFF);
+            nstreams = 4;
+        }
+    }
+    if (regen > BLOCK_MAX) return E_CORRUPT;
+    const uint8_t *lit = nullptr;  // the literals, or null for RLE
+    uint8_t rle_byte = 0;
+    uint32_t lsec;  // bytes of the literals section
+    if (ltype == 0) {
+        lsec = hs + regen;
+        if (lsec > bsize) return E_CORRUPT;
+        lit = b + hs;
+    } else if (ltype == 1) {
+        lsec = hs + 1;
+        if (lsec > bsize) return E_CORRUPT;
+        rle_byte = b[hs];
+    } else {
+        lsec = hs + csize;
+        if (lsec > bsize || csize == 0) return E_CORRUPT;
+        const uint8_t *p = b + hs, *pe = b + hs + csize;
+        if (lane == 0) {
+            ws->err = OK;
+            if (ltype == 2) {
+                const int h = huf_read_table(ws, p, (size_t)(pe - p));
+                if (h < 0) ws->err = E_CORRUPT;
+                else p += h;
+            } else if (ws->huf_log < 0) {
+                ws->err = E_CORRUPT;  // treeless without an earlier table
+            }
+            ws->seq_ll[0] = (uint32_t)(p - b);  // where the streams start
+        }
+        warp_sync();
+        if (ws->err) return ws->err;
+        p = b + ws->seq_ll[0];
+        warp_sync();
+        if (nstreams == 1) {
+            if (lane == 0) ws->err = huf_stream(ws, p, pe, job.lit, regen) ? OK : E_CORRUPT;
+        } else {
+            if (pe - p < 6) return E_CORRUPT;
+            const uint32_t s1 = rd16(p), s2 = rd16(p + 2), s3 = rd16(p + 4);
+            const uint8_t *q = p + 6;
+            const uint64_t total = (uint64_t)(pe - q);
+            if ((uint64_t)s1 + s2 + s3 > total) return E_CORRUPT;
+            const uint32_t seg = (regen + 3) / 4;
+            if (regen < 6 || 3 * seg > regen) return E_CORRUPT;  // libzstd: >= 6 for 4 streams
+            const uint8_t *st[5] = {q, q + s1, q + s1 + s2, q + s1 + s2 + s3, pe};
+            if (lane == 0) ws->err = OK;
+            warp_sync();
+            for (int k = lane; k < 4; k += nl) {
+                const uint32_t n = k < 3 ? seg : regen - 3 * seg;
+                if (!huf_stream(ws, st[k], st[k + 1], job.lit + (uint64_t)k * seg, n))
+                    ws->err = E_CORRUPT;
+            }
+        }
+        warp_sync();
+        if (ws->err) return ws->err;
+        lit = job.lit;
+    }
+    // ---- sequences section (3.1.1.3.2)
+    const uint8_t *s = b + lsec, *se = b + bsize;
+    if (s >= se) return E_CORRUPT;
+    uint32_t nseq;
+    if (s[0] < 128) {
+        nseq = s[0];
+        s += 1;
+    } else if (s[0] < 255) {
+        if (se - s < 2) return E_CORRUPT;
+        nseq = ((uint32_t)(s[0] - 128) << 8) | s[1];
+        s += 2;
+    } else {
+        if (se - s < 3) return E_CORRUPT;
+        nseq = (uint32_t)s[1] + ((uint32_t)s[2] << 8) + 0x7F00;
+        s += 3;
+    }
+    uint64_t o = *out;
+    uint32_t lused = 0;
+    if (nseq == 0) {
+        if (s != se) return E_CORRUPT;
+    } else {
+        if (s >= se) return E_CORRUPT;
+        const int modes = s[0];
+        if (modes & 3) return E_CORRUPT;
+        s++;
+        if (lane == 0) {
+            ws->err = OK;
+            const int m[3] = {modes >> 6, (modes >> 4) & 3, (modes >> 2) & 3};  // LL, OF, ML
+            for (int f = 0; f < 3 && !ws->err; f++) {
+                const int h = seq_table(ws, f, m[f], s, (size_t)(se - s));
+                if (h < 0) ws->err = E_CORRUPT;
+                else s += h;
+            }
+            ws->seq_ll[0] = (uint32_t)(s - b);
+        }
+        warp_sync();
+        if (ws->err) return ws->err;
+        s = b + ws->seq_ll[0];
+        warp_sync();
+        // lane 0 decodes batches of sequences; the warp executes them
+        BitRev br;
+        uint32_t sll = 0, sof = 0, sml = 0;
+        if (lane == 0) {
+            ws->err = br.init(s, se) ? OK : E_CORRUPT;
+            if (!ws->err) {
+                sll = (uint32_t)br.read(ws->ll_log);
+                sof = (uint32_t)br.read(ws->of_log);
+                sml = (uint32_t)br.read(ws->ml_log);
+            }
+        }
+        warp_sync();
+        if (ws->err) return ws->err;
+        for (uint32_t done = 0; done < nseq;) {
+            const uint32_t nb = nseq - done < (uint32_t)SEQ_BATCH ? nseq - done : (uint32_t)SEQ_BATCH;
+            if (lane == 0) {
+                for (uint32_t i = 0; i < nb; i++) {
+                    const FseEntry eo = ws->of[sof], em = ws->ml[sml], el = ws->ll[sll];
+                    const int oc = eo.sym, mc = em.sym, lc = el.sym;
+                    if (oc > OF_MAX_SYM) { ws->err = E_CORRUPT; break; }
+                    const uint64_t ofv = (1ull << oc) + br.read(oc);
+                    const uint32_t ml = ml_base(mc) + (uint32_t)br.read(ml_bits(mc));
+                    const uint32_t ll = ll_base(lc) + (uint32_t)br.read(ll_bits(lc));
+                    uint64_t off;
+                    if (ofv > 3) {
+                        off = ofv - 3;
+                        ws->rep[2] = ws->rep[1];
+                        ws->rep[1] = ws->rep[0];
+                        ws->rep[0] = (uint32_t)off;
+                    } else {
+                        const uint32_t idx = (uint32_t)ofv - 1 + (ll == 0 ? 1u : 0u);
+                        if (idx == 0) {
+                            off = ws->rep[0];
+                        } else {
+                            uint64_t t = idx == 3 ? (uint64_t)ws->rep[0] - 1 : ws->rep[idx];
+                            if (t == 0) t = ~0ull;  // invalid, caught below
+                            if (idx != 1) ws->rep[2] = ws->rep[1];
+                            ws->rep[1] = ws->rep[0];
+                            ws->rep[0] = (uint32_t)t;
+                            off = t;
+                        }
+                    }
+                    ws->seq_ll[i] = ll;
+                    ws->seq_ml[i] = ml;
+                    ws->seq_of[i] = off > 0xFFFFFFFFull ? 0xFFFFFFFFu : (uint32_t)off;
+                    if (done + i + 1 < nseq) {  // state updates: LL, ML, OF
+                        sll = el.base + (uint32_t)br.read(el.nb);
+                        sml = em.base + (uint32_t)br.read(em.nb);
+                        sof = eo.base + (uint32_t)br.read(eo.nb);
+                    }
+                }
+                if (!ws->err && done + nb == nseq && br.pos > 0) ws->err = E_CORRUPT;
+            }
+            warp_sync();
+            if (ws->err) return ws->err;
+            for (uint32_t i = 0; i < nb; i++) {
+                const uint32_t ll = ws->seq_ll[i], ml = ws->seq_ml[i], off = ws->seq_of[i];
+                if ((uint64_t)lused + ll > regen) return E_CORRUPT;
+                if (o + ll + ml > job.cap) return E_DST;
+                if (lit) coop_copy(job.dst + o, lit + lused, ll, lane, nl);
+                else for (uint64_t k = (uint64_t)lane; k < ll; k += (uint64_t)nl) job.dst[o + k] = rle_byte;
+                o += ll;
+                lused += ll;
+                if (off == 0 || (uint64_t)off > o - fstart) return E_CORRUPT;
+                warp_sync();
+                coop_match(job.dst + o, off, ml, lane, nl);
+                o += ml;
+                warp_sync();
+            }
+            done += nb;
+            warp_sync();
+        }
+    }
+    // the rest of the literals
+    const uint32_t rest = regen - lused;
+    if (o + rest > job.cap) return E_DST;
+    if (lit) coop_copy(job.dst + o, lit + lused, rest, lane, nl);
+    else for (uint64_t k = (uint64_t)lane; k < rest; k += (uint64_t)nl) job.dst[o + k] = rle_byte;
+    o += rest;
+    if (o - *out > BLOCK_MAX) return E_CORRUPT;
+    *out = o;
+    warp_sync();
+    return OK;
+}
+
+// Every frame of [src, src + len) (RFC 8878 3.1): skippable frames skipped,
+// zstd frames decoded in turn into dst.  ws must be private to the warp.
+ZHD Result decode(Workspace *ws, const Job &job, int lane, int nl, uint64_t *acc) {
+    Result r{OK, 0, 0};
+    const uint8_t *src = job.src;
+    uint64_t ip = 0, o = 0;
+    // an empty input decodes to nothing (libzstd ZSTD_decompress)
+    while (ip < job.len) {
+        r.pos = ip;
+        if (job.len - ip < 4) { r.code = E_CORRUPT; return r; }
+        const uint32_t magic = rd32(src + ip);
+        if ((magic & 0xFFFFFFF0u) == SKIP_MAGIC) {
+            if (job.len - ip < 8) { r.code = E_CORRUPT; return r; }
+            const uint64_t sz = rd32(src + ip + 4);
+            if (job.len - ip - 8 < sz) { r.code = E_CORRUPT; return r; }
+            ip += 8 + sz;
+            continue;
+        }
+        if (magic != MAGIC) { r.code = E_CORRUPT; return r; }
+        // ---- frame header (3.1.1.1)
+        uint64_t p = ip + 4;
+        if (p >= job.len) { r.code = E_CORRUPT; return r; }
+        const int fhd = src[p++];
+        const int fcs_flag = fhd >> 6, single = (fhd >> 5) & 1, cksum = (fhd >> 2) & 1;
+        const int dict_flag = fhd & 3;
+        if (fhd & 0x08) { r.code = E_CORRUPT; return r; }  // reserved bit
+        const int dict_bytes = dict_flag == 0 ? 0 : (dict_flag == 1 ? 1 : (dict_flag == 2 ? 2 : 4));
+        const int fcs_bytes = fcs_flag == 0 ? (single ? 1 : 0) : (fcs_flag == 1 ? 2 : (fcs_flag == 2 ? 4 : 8));
+        const uint64_t hlen = (uint64_t)(single ? 0 : 1) + dict_bytes + fcs_bytes;
+        if (job.len - p < hlen) { r.code = E_CORRUPT; return r; }
+        if (!single) {  // window descriptor: only its exponent is checked
+            const int wlog = 10 + (src[p++] >> 3);
+            if (wlog > 31) { r.code = E_UNSUPPORTED; return r; }
+        }
+        uint64_t dict = 0;
+        for (int i = 0; i < dict_bytes; i++) dict |= (uint64_t)src[p + i] << (8 * i);
+        p += dict_bytes;
+        if (dict) { r.code = E_UNSUPPORTED; return r; }  // no dictionaries here
+        uint64_t fcs = 0;
+        bool has_fcs = fcs_bytes > 0;
+        for (int i = 0; i < fcs_bytes; i++) fcs |= (uint64_t)src[p + i] << (8 * i);
+        if (fcs_bytes == 2) fcs += 256;
+        p += fcs_bytes;
+        // fresh per frame: repeat offsets and tables
+        if (lane == 0) {
+            ws->rep[0] = 1;
+            ws->rep[1] = 4;
+            ws->rep[2] = 8;
+            ws->ll_log = ws->ml_log = ws->of_log = ws->huf_log = -1;
+        }
+        warp_sync();
+        const uint64_t fstart = o;
+        // ---- blocks (3.1.1.2)
+        for (;;) {
+            r.pos = p;
+            if (job.len - p < 3) { r.code = E_CORRUPT; return r; }
+            const uint32_t bh = rd24(src + p);
+            p += 3;
+            const int last = bh & 1, type = (bh >> 1) & 3;
+            const uint32_t bsize = bh >> 3;
+            // libzstd: a compressed block is smaller than 128 KiB
+            if (type == 3 || bsize > BLOCK_MAX || (type == 2 && bsize == BLOCK_MAX)) {
+                r.code = E_CORRUPT;
+                return r;
+            }
+            if (type == 0) {
+                if (job.len - p < bsize) { r.code = E_CORRUPT; return r; }
+                if (o + bsize > job.cap) { r.code = E_DST; return r; }
+                coop_copy(job.dst + o, src + p, bsize, lane, nl);
+                o += bsize;
+                p += bsize;
+            } else if (type == 1) {
+                if (job.len - p < 1) { r.code = E_CORRUPT; return r; }
+                if (o + bsize > job.cap) { r.code = E_DST; return r; }
+                const uint8_t v = src[p];
+                for (uint64_t k = (uint64_t)lane; k < bsize; k += (uint64_t)nl) job.dst[o + k] = v;
+                o += bsize;
+                p += 1;
+            } else {
+                if (job.len - p < bsize) { r.code = E_CORRUPT; return r; }
+                const int e = decode_compressed_block(ws, job, src + p, bsize, fstart, &o, lane, nl);
+                if (e) { r.code = e; r.written = o; return r; }
+                p += bsize;
+            }
+            warp_sync();
+            if (last) break;
+        }
+        if (has_fcs && o - fstart != fcs) { r.code = E_CORRUPT; r.pos = ip; return r; }
+        if (cksum) {
+            if (job.len - p < 4) { r.code = E_CORRUPT; return r; }
+            const uint64_t h = xxh64(job.dst + fstart, o - fstart, lane, nl, acc);
+            if (lane == 0) ws->err = (uint32_t)h == rd32(src + p) ? OK : E_CHECKSUM;
+            warp_sync();
+            if (ws->err) { r.code = ws->err; r.pos = p; return r; }
+            p += 4;
+        }
+        ip = p;
+    }
+    r.written = o;
+    return r;
+}
+
+}  // namespace zs
+}  // namespace hct

@@ -207,6 +207,45 @@ def encode_hct_v3(w: np.ndarray, retention: float = 0.30, num_fragments: int = 1
     return b"".join(out)
 
 
+_ZSTD = None
+
+
+def zstd_compress(data, level: int = 3, checksum: bool = False) -> bytes:
+    """One zstd frame of ``data`` from the system libzstd (the writer side of
+    the zstd-compressed fragments and containers the GPU decoder reads; the
+    reference writes them with the `zstd` crate, i.e. libzstd)."""
+    global _ZSTD
+    if _ZSTD is None:
+        lib = C.CDLL("libzstd.so.1")
+        lib.ZSTD_createCCtx.restype = C.c_void_p
+        lib.ZSTD_freeCCtx.argtypes = [C.c_void_p]
+        lib.ZSTD_CCtx_setParameter.restype = C.c_size_t
+        lib.ZSTD_CCtx_setParameter.argtypes = [C.c_void_p, C.c_int, C.c_int]
+        lib.ZSTD_compressBound.restype = C.c_size_t
+        lib.ZSTD_compressBound.argtypes = [C.c_size_t]
+        lib.ZSTD_compress2.restype = C.c_size_t
+        lib.ZSTD_compress2.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t]
+        lib.ZSTD_isError.restype = C.c_uint
+        lib.ZSTD_isError.argtypes = [C.c_size_t]
+        _ZSTD = lib
+    lib = _ZSTD
+    src = np.ascontiguousarray(np.frombuffer(bytes(data), np.uint8) if not isinstance(data, np.ndarray)
+                               else data.view(np.uint8).reshape(-1))
+    cctx = lib.ZSTD_createCCtx()
+    try:
+        lib.ZSTD_CCtx_setParameter(cctx, 100, int(level))      # ZSTD_c_compressionLevel
+        lib.ZSTD_CCtx_setParameter(cctx, 201, int(checksum))   # ZSTD_c_checksumFlag
+        cap = lib.ZSTD_compressBound(src.size) + 64
+        out = np.empty(cap, np.uint8)
+        n = lib.ZSTD_compress2(cctx, out.ctypes.data, cap, src.ctypes.data if src.size else None,
+                               src.size)
+        if lib.ZSTD_isError(n):
+            raise ValueError("zstd compression failed")
+        return out[:n].tobytes()
+    finally:
+        lib.ZSTD_freeCCtx(cctx)
+
+
 HOLO_SPECTRAL_CURVE = (0.6, 0.3, 0.08, 0.02)  # holotensor.rs:114-118
 
 

@@ -264,8 +264,11 @@ int hct_b200_spectral_q4_decode_noalloc(const uint8_t *d_payload, size_t payload
  * stops at a fragment past the end).  open parses the headers on the host
  * and uploads each fragment's bitmap and values once; decode is
  * stream-ordered and synchronises once to read the device flag.
- * hct_b200_hct_v3_decode is open + decode + close.  Fewer than 2 bytes of
- * data is HCT_B200_ERR_CORRUPTED ("HCT data too short", decompress.rs:323). */
+ * hct_b200_hct_v3_decode is open + decode + close.  Data that starts with
+ * the zstd magic is zstd-decoded first (on the GPU; decompress.rs:296-319,
+ * where data that does not decode is parsed as it is).  Fewer than 2 bytes
+ * of data is HCT_B200_ERR_CORRUPTED ("HCT data too short",
+ * decompress.rs:323). */
 int hct_b200_v3_open(hct_b200_ctx *ctx, const uint8_t *data, size_t len, uint64_t rows,
                      uint64_t cols, hct_b200_v3 **out, hct_b200_error *err);
 int hct_b200_v3_num_fragments(const hct_b200_v3 *v);
@@ -275,6 +278,37 @@ void hct_b200_v3_close(hct_b200_v3 *v);
 int hct_b200_hct_v3_decode(hct_b200_ctx *ctx, const uint8_t *data, size_t len, uint64_t rows,
                            uint64_t cols, void *d_out, int out_dtype, void *stream,
                            hct_b200_error *err);
+
+/* ---- Zstandard ------------------------------------------------------------
+ * zstd::decode_all as the reference calls it (crates/haagenti-hct/src/
+ * holotensor.rs:2081-2091 for fragments with entry flag bit 0,
+ * crates/haagenti-cuda/src/decompress.rs:296-319 for zstd-wrapped HCT
+ * data): every frame of a job's input in turn (RFC 8878; skippable frames
+ * skipped, content checksums and frame content sizes verified), their
+ * contents concatenated.  Frames that need a dictionary are
+ * HCT_B200_ERR_UNSUPPORTED.  Valid frames decode to the same bytes as
+ * libzstd; on corrupted input this decoder reports an error wherever libzstd
+ * does and in some cases where libzstd's fast Huffman path returns data
+ * (every literal stream must be consumed exactly).
+ * jobs: one warp per job on the GPU, several jobs per launch; per-job status
+ * {code, position = input offset of the failing frame or block, provided =
+ * dst_cap, written}; codes HCT_B200_ERR_CORRUPTED, _BUFFER_TOO_SMALL,
+ * _CHECKSUM, _UNSUPPORTED.  d_src is read only inside each job's range. */
+typedef struct {
+    uint64_t src_off, src_len; /* input range in d_src */
+    uint64_t dst_off, dst_cap; /* output range in d_dst */
+} hct_b200_zstd_job;
+int hct_b200_zstd_decompress_jobs(hct_b200_ctx *ctx, const uint8_t *d_src,
+                                  const hct_b200_zstd_job *d_jobs, uint32_t n, uint8_t *d_dst,
+                                  hct_b200_status *d_status, void *stream);
+/* Host buffers: in -> out (capacity out_cap), *written = bytes; one job on
+ * the GPU, synchronous. */
+int hct_b200_zstd_decompress(hct_b200_ctx *ctx, const uint8_t *in, size_t in_len, uint8_t *out,
+                             size_t out_cap, size_t *written, hct_b200_error *err);
+/* Sum of the frames' content sizes read from their headers (host only);
+ * HCT_B200_ERR_UNSUPPORTED when a frame does not record it,
+ * HCT_B200_ERR_CORRUPTED when the headers do not parse. */
+int hct_b200_zstd_content_size(const uint8_t *in, size_t in_len, uint64_t *size);
 
 /* ---- HoloTensor (spectral fragments) -----------------------------------
  * HoloTensorReader + HoloTensorDecoder for the spectral encoding
@@ -292,11 +326,13 @@ int hct_b200_hct_v3_decode(hct_b200_ctx *ctx, const uint8_t *data, size_t len, u
  * shape (HoloTensorDecoder::new, :1732-1759), to d_out (rows x cols of
  * out_dtype).  *quality (may be NULL) receives SpectralDecoder::quality, the
  * fraction of positions the k fragments cover.  k == 0 is
- * HCT_B200_ERR_CORRUPTED ("no fragments loaded").  Not decoded, with
- * HCT_B200_ERR_UNSUPPORTED: the random-projection and low-rank encodings,
- * zstd-compressed fragments (entry flag bit 0) and the legacy V1/V2 spectral
- * fragment layouts.  decode is stream-ordered and synchronises once to read
- * the device flag. */
+ * HCT_B200_ERR_CORRUPTED ("no fragments loaded").  Fragments whose index
+ * entry has flag bit 0 are zstd frames (decoded at open on the GPU, as
+ * hct_b200_zstd_decompress_jobs; one that does not decode fails the decode
+ * that reads it with HCT_B200_ERR_CORRUPTED).  Not decoded, with
+ * HCT_B200_ERR_UNSUPPORTED: the random-projection and low-rank encodings and
+ * the legacy V1/V2 spectral fragment layouts.  decode is stream-ordered and
+ * synchronises once to read the device flag. */
 typedef struct {
     uint8_t encoding;    /* 0 spectral, 1 random projection, 2 low-rank */
     uint8_t compression; /* 0 LZ4, 1 Zstd */

@@ -248,8 +248,13 @@ def read_fragment(p: ParsedHolo, i: int):
         raise HoloError("failed to read fragment data")
     if p.header.flags & HOLO_FLAG_FRAGMENT_CHECKSUMS and xxh3_64(data) != e[5]:
         raise HoloError(f"fragment {i} checksum mismatch")
-    if e[1] & 1:
-        raise NotImplementedError("zstd-compressed fragment")
+    if e[1] & 1:  # zstd::decode_all, i.e. libzstd (oracle/zstd_ref.py)
+        from . import zstd_ref
+
+        ok, dec = zstd_ref.decompress(data, max(e[4], 1 << 26))
+        if not ok:
+            raise HoloError(f"failed to decompress fragment {i}: {dec}")
+        data = dec
     return e[0], data
 
 

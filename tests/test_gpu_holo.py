@@ -180,10 +180,12 @@ def test_errors(hb):
         r.decode(5)
     with pytest.raises(hb.CorruptedData, match="no fragments"):
         r.decode(0)
-    # zstd-flagged fragment, other encodings, legacy layouts: not decoded
+    # a fragment flagged as zstd that holds no zstd frame fails to decompress
+    # (read_fragment, holotensor.rs:2081-2091); other encodings and the legacy
+    # layouts are not decoded
     ents = [list(e) for e in p.entries]
     ents[1][1] = 1
-    with pytest.raises(hb.Unsupported):
+    with pytest.raises(hb.CorruptedData, match="decompress"):
         hb.HoloTensorReader(_rewrite(f, entries=ents)).decode()
     h = OHo.header_from_bytes(f[:96])
     h.encoding = OHo.ENC_LRDF
@@ -198,3 +200,33 @@ def test_errors(hb):
         hb.HoloTensorReader(legacy).decode()
     # fragments beyond the bad one are never read
     hb.HoloTensorReader(legacy).decode(1)
+
+
+def test_zstd_compressed_fragments(hb):
+    """Fragments stored as zstd frames (index entry flag bit 0) decode like the
+    uncompressed file; a fragment whose frames do not decode fails the decode
+    that reads it."""
+    from oracle import holo as OHo
+    from oracle import zstd_ref as Z
+
+    f = _file((384, 1024), 6, 76)
+    p = OHo.parse_holotensor(f)
+    bodies = [f[p.data_offset + e[2]: p.data_offset + e[2] + e[3]] for e in p.entries]
+    packed = [(i, 1, Z.compress(b, 3 + i % 3, checksum=bool(i % 2),
+                               content_size=bool(i % 3))) for i, b in enumerate(bodies)]
+    zf = OHo.write_holotensor(p.header, packed)
+    ref, q = OHo.decode_cpu(zf)
+    r = hb.HoloTensorReader(zf)
+    _check(r.decode().cpu().numpy(), ref, "zstd fragments")
+    assert r.quality == q == 1.0
+    _check(r.decode(3).cpu().numpy(), OHo.decode_cpu(zf, 3)[0], "zstd fragments, k=3")
+    bad = list(packed)
+    frame = bytearray(bad[4][2])
+    frame[len(frame) // 2] ^= 0xFF
+    frame[-5] ^= 0x5A
+    bad[4] = (4, 1, bytes(frame))
+    bf = OHo.write_holotensor(p.header, bad)
+    r = hb.HoloTensorReader(bf)
+    r.decode(4)
+    with pytest.raises(hb.CorruptedData):
+        r.decode(5)

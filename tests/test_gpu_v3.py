@@ -75,3 +75,24 @@ def test_v3_edge_cases(hb):
     ref = OH.decode_hct_v3_cpu(cut, 32, 64)
     got = hb.hct_v3_decode(cut, 32, 64).cpu().numpy()
     assert np.abs(got - ref).max() <= MAX_ABS
+
+
+def test_v3_zstd_wrapped(hb):
+    """decompress.rs:296-319: data that starts with the zstd magic is decoded
+    first (here on the GPU); data that does not decode is parsed as it is."""
+    from oracle import hct as OH
+    from oracle import zstd_ref as Z
+
+    shape = (256, 512)
+    w = OH.gen_weight(shape, 90)
+    data = OH.encode_hct_v3(w, 0.3, 3)
+    plain = hb.hct_v3_decode(data, *shape).cpu().numpy()
+    for lv, ck in ((1, False), (9, True)):
+        got = hb.hct_v3_decode(Z.compress(data, lv, checksum=ck), *shape).cpu().numpy()
+        assert np.array_equal(got, plain)
+    # a zstd magic in front of data that is no zstd frame: parsed raw, as the
+    # reference does (here a V3 container whose first bytes read as the magic)
+    fake = struct.pack("<I", 0xFD2FB528) + bytes(8)
+    ref = OH.decode_hct_v3_cpu(fake, *shape)
+    got = hb.hct_v3_decode(fake, *shape).cpu().numpy()
+    assert np.array_equal(got, ref)
