@@ -38,8 +38,10 @@ namespace zs {
 
 #if defined(__CUDA_ARCH__)
 __device__ __forceinline__ void warp_sync() { __syncwarp(); }
+__device__ __forceinline__ uint32_t warp_min(uint32_t v) { return __reduce_min_sync(0xffffffffu, v); }
 #else
 inline void warp_sync() {}
+inline uint32_t warp_min(uint32_t v) { return v; }
 #endif
 
 enum : int { OK = 0, E_DST = 2, E_CORRUPT = 17, E_CHECKSUM = 18, E_UNSUPPORTED = 19 };
@@ -74,6 +76,9 @@ struct Workspace {
     uint16_t next[256];  // FSE table construction scratch
     uint8_t weights[256];
     uint32_t seq_ll[SEQ_BATCH], seq_ml[SEQ_BATCH], seq_of[SEQ_BATCH];
+    uint64_t seq_pos[SEQ_BATCH];  // output position of each sequence's match
+    uint32_t seq_lit[SEQ_BATCH];  // its literals' offset in the literal buffer
+    uint8_t seq_state[SEQ_BATCH]; // match: 0 pending, 1 done, 2 ready for the whole warp
     uint32_t rep[3];
     int8_t ll_log, ml_log, of_log, huf_log;  // -1: no table yet
     int err;
@@ -96,8 +101,18 @@ ZHD int highbit(uint32_t v) {  // index of the highest set bit, v > 0
 #endif
 }
 
-// 8 bytes at p (little endian); bytes at or past end read as zero
+// 8 bytes at p (little endian); bytes at or past end read as zero.  On the
+// device, two aligned 8-byte loads when both lie before end (an 8-byte
+// aligned word never starts below an 8-byte aligned allocation).
 ZHD uint64_t rd64_bounded(const uint8_t *p, const uint8_t *end) {
+#if defined(__CUDA_ARCH__)
+    const uintptr_t a = (uintptr_t)p & 7;
+    const uint64_t *w = reinterpret_cast<const uint64_t *>(p - a);
+    if ((const uint8_t *)(w + 2) <= end) {
+        const uint64_t lo = w[0];
+        return a ? (lo >> (8 * a)) | (w[1] << (64 - 8 * a)) : lo;
+    }
+#endif
     if (p + 8 <= end) return rd64(p);
     uint64_t v = 0;
     for (int i = 0; i < 8 && p + i < end; i++) v |= (uint64_t)p[i] << (8 * i);
@@ -531,9 +546,25 @@ struct Result {
     uint64_t written;  // output bytes
 };
 
-// Cooperative copies (all lanes): n bytes from s to d (no overlap).
+// Cooperative copies (all lanes): n bytes from s to d (no overlap).  Each
+// lane moves 16 consecutive bytes per step, all loads before the stores, so
+// a step costs one memory latency for 16 * nl bytes.
+constexpr int CCH = 16;
 ZHD void coop_copy(uint8_t *d, const uint8_t *s, uint64_t n, int lane, int nl) {
-    for (uint64_t i = (uint64_t)lane; i < n; i += (uint64_t)nl) d[i] = s[i];
+    for (uint64_t i = (uint64_t)lane * CCH; i < n; i += (uint64_t)nl * CCH) {
+        uint8_t t[CCH];
+        const uint64_t m = n - i < (uint64_t)CCH ? n - i : (uint64_t)CCH;
+#pragma unroll
+        for (int k = 0; k < CCH; k++)
+            if ((uint64_t)k < m) t[k] = s[i + k];
+#pragma unroll
+        for (int k = 0; k < CCH; k++)
+            if ((uint64_t)k < m) d[i + k] = t[k];
+    }
+}
+
+ZHD void coop_fill(uint8_t *d, uint8_t v, uint64_t n, int lane, int nl) {
+    for (uint64_t i = (uint64_t)lane; i < n; i += (uint64_t)nl) d[i] = v;
 }
 
 // Match: ml bytes at d from d - off (off >= 1); with off < ml the bytes
@@ -541,15 +572,21 @@ ZHD void coop_copy(uint8_t *d, const uint8_t *s, uint64_t n, int lane, int nl) {
 ZHD void coop_match(uint8_t *d, uint64_t off, uint64_t ml, int lane, int nl) {
     const uint8_t *s = d - off;
     if (off >= ml) {
-        for (uint64_t i = (uint64_t)lane; i < ml; i += (uint64_t)nl) d[i] = s[i];
+        coop_copy(d, s, ml, lane, nl);
         return;
     }
-    uint64_t j = (uint64_t)lane % off;
-    const uint64_t stepm = (uint64_t)nl % off;
-    for (uint64_t i = (uint64_t)lane; i < ml; i += (uint64_t)nl) {
-        d[i] = s[j];
-        j += stepm;
-        if (j >= off) j -= off;
+    for (uint64_t i = (uint64_t)lane * CCH; i < ml; i += (uint64_t)nl * CCH) {
+        uint8_t t[CCH];
+        const uint64_t m = ml - i < (uint64_t)CCH ? ml - i : (uint64_t)CCH;
+        uint64_t j = i % off;
+#pragma unroll
+        for (int k = 0; k < CCH; k++) {
+            if ((uint64_t)k < m) t[k] = s[j];
+            if (++j == off) j = 0;
+        }
+#pragma unroll
+        for (int k = 0; k < CCH; k++)
+            if ((uint64_t)k < m) d[i + k] = t[k];
     }
 }
 
@@ -747,18 +784,61 @@ ZHD int decode_compressed_block(Workspace *ws, const Job &job, const uint8_t *b,
             }
             warp_sync();
             if (ws->err) return ws->err;
+            // the batch's positions, checked in sequence order (every lane the
+            // same); the first failing sequence decides the error
             for (uint32_t i = 0; i < nb; i++) {
                 const uint32_t ll = ws->seq_ll[i], ml = ws->seq_ml[i], off = ws->seq_of[i];
                 if ((uint64_t)lused + ll > regen) return E_CORRUPT;
                 if (o + ll + ml > job.cap) return E_DST;
-                if (lit) coop_copy(job.dst + o, lit + lused, ll, lane, nl);
-                else for (uint64_t k = (uint64_t)lane; k < ll; k += (uint64_t)nl) job.dst[o + k] = rle_byte;
+                if (lane == 0) {
+                    ws->seq_lit[i] = lused;
+                    ws->seq_pos[i] = o + ll;
+                    ws->seq_state[i] = 0;
+                }
                 o += ll;
                 lused += ll;
                 if (off == 0 || (uint64_t)off > o - fstart) return E_CORRUPT;
-                warp_sync();
-                coop_match(job.dst + o, off, ml, lane, nl);
                 o += ml;
+            }
+            warp_sync();
+            // literals: a lane per sequence (they never overlap)
+            for (uint32_t i = (uint32_t)lane; i < nb; i += (uint32_t)nl) {
+                const uint32_t ll = ws->seq_ll[i];
+                uint8_t *d = job.dst + ws->seq_pos[i] - ll;
+                if (lit) coop_copy(d, lit + ws->seq_lit[i], ll, 0, 1);
+                else coop_fill(d, rle_byte, ll, 0, 1);
+            }
+            warp_sync();
+            // matches in waves: a match whose source bytes all lie below the
+            // first pending match's output is final-sourced and runs now (on
+            // its lane, or on the whole warp when long); the first pending
+            // match itself always qualifies
+            for (;;) {
+                uint32_t mine = 0xFFFFFFFFu;
+                for (uint32_t i = (uint32_t)lane; i < nb; i += (uint32_t)nl)
+                    if (ws->seq_state[i] == 0 && i < mine) mine = i;
+                const uint32_t fp = warp_min(mine);
+                if (fp == 0xFFFFFFFFu) break;
+                const uint64_t limit = ws->seq_pos[fp];
+                for (uint32_t i = (uint32_t)lane; i < nb; i += (uint32_t)nl) {
+                    if (ws->seq_state[i] != 0) continue;
+                    const uint64_t mp = ws->seq_pos[i], off = ws->seq_of[i], ml = ws->seq_ml[i];
+                    const uint64_t hi = off >= ml ? mp - off + ml : mp;  // source bytes needed
+                    if (hi > limit) continue;
+                    if (ml > 64) {
+                        ws->seq_state[i] = 2;
+                    } else {
+                        coop_match(job.dst + mp, off, ml, 0, 1);
+                        ws->seq_state[i] = 1;
+                    }
+                }
+                warp_sync();
+                for (uint32_t i = fp; i < nb; i++) {
+                    if (ws->seq_state[i] != 2) continue;
+                    coop_match(job.dst + ws->seq_pos[i], ws->seq_of[i], ws->seq_ml[i], lane, nl);
+                    warp_sync();
+                    if (lane == 0) ws->seq_state[i] = 1;
+                }
                 warp_sync();
             }
             done += nb;
@@ -769,7 +849,7 @@ ZHD int decode_compressed_block(Workspace *ws, const Job &job, const uint8_t *b,
     const uint32_t rest = regen - lused;
     if (o + rest > job.cap) return E_DST;
     if (lit) coop_copy(job.dst + o, lit + lused, rest, lane, nl);
-    else for (uint64_t k = (uint64_t)lane; k < rest; k += (uint64_t)nl) job.dst[o + k] = rle_byte;
+    else coop_fill(job.dst + o, rle_byte, rest, lane, nl);
     o += rest;
     if (o - *out > BLOCK_MAX) return E_CORRUPT;
     *out = o;
@@ -851,8 +931,7 @@ ZHD Result decode(Workspace *ws, const Job &job, int lane, int nl, uint64_t *acc
             } else if (type == 1) {
                 if (job.len - p < 1) { r.code = E_CORRUPT; return r; }
                 if (o + bsize > job.cap) { r.code = E_DST; return r; }
-                const uint8_t v = src[p];
-                for (uint64_t k = (uint64_t)lane; k < bsize; k += (uint64_t)nl) job.dst[o + k] = v;
+                coop_fill(job.dst + o, src[p], bsize, lane, nl);
                 o += bsize;
                 p += 1;
             } else {
