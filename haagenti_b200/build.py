@@ -7,6 +7,7 @@ tcgen05 IDCT contraction) plus the C++ host code behind include/hct_b200.h.
 """
 from __future__ import annotations
 
+import glob
 import os
 import shutil
 import subprocess
@@ -29,8 +30,8 @@ def nvcc() -> str:
 
 def build(verbose: bool = False, force: bool = False) -> str:
     srcs = [os.path.join(CSRC, s) for s in SOURCES]
-    deps = srcs + [os.path.join(CSRC, "common.cuh"),
-                   os.path.join(os.path.dirname(HERE), "include", "hct_b200.h")]
+    deps = srcs + sorted(glob.glob(os.path.join(CSRC, "*.cuh"))) + [
+        os.path.join(os.path.dirname(HERE), "include", "hct_b200.h")]
     if (not force and os.path.exists(OUT)
             and all(os.path.getmtime(OUT) >= os.path.getmtime(d) for d in deps)):
         return OUT

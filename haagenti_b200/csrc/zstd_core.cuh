@@ -29,8 +29,18 @@
 
 #if defined(__CUDACC__)
 #define ZHD __host__ __device__ __forceinline__
+// rarely run parts (table construction, block headers) stay out of line so
+// their registers are not live across the hot loops
+#define ZCOLD __host__ __device__ __noinline__
 #else
 #define ZHD inline
+#define ZCOLD inline
+#endif
+
+#if defined(__CUDA_ARCH__)
+#define ZUNROLL _Pragma("unroll")
+#else
+#define ZUNROLL
 #endif
 
 namespace hct {
@@ -39,7 +49,9 @@ namespace zs {
 #if defined(__CUDA_ARCH__)
 __device__ __forceinline__ void warp_sync() { __syncwarp(); }
 __device__ __forceinline__ uint32_t warp_min(uint32_t v) { return __reduce_min_sync(0xffffffffu, v); }
+__device__ __forceinline__ uint64_t bcast0(uint64_t v) { return __shfl_sync(0xffffffffu, v, 0); }
 #else
+inline uint64_t bcast0(uint64_t v) { return v; }
 inline void warp_sync() {}
 inline uint32_t warp_min(uint32_t v) { return v; }
 #endif
@@ -59,10 +71,8 @@ struct FseEntry {
     uint8_t sym;
     uint8_t nb;  // bits to read for the next state
 };
-struct HufEntry {
-    uint8_t sym;
-    uint8_t nb;
-};
+// Huffman decoding table entry: symbol in bits 0-7, code length in 8-15.
+typedef uint16_t HufEntry;
 
 // Per-warp state that lives across the blocks of a frame (shared memory on
 // the device).
@@ -81,6 +91,7 @@ struct Workspace {
     uint8_t seq_state[SEQ_BATCH]; // match: 0 pending, 1 done, 2 ready for the whole warp
     uint32_t rep[3];
     int8_t ll_log, ml_log, of_log, huf_log;  // -1: no table yet
+    uint16_t huf_nsym;  // symbols of the Huffman description
     int err;
     uint32_t nseq;      // sequences of the current batch
     uint32_t seq_done;  // the bitstream was consumed completely
@@ -92,6 +103,15 @@ ZHD uint32_t rd16(const uint8_t *p) { return (uint32_t)p[0] | ((uint32_t)p[1] <<
 ZHD uint32_t rd24(const uint8_t *p) { return rd16(p) | ((uint32_t)p[2] << 16); }
 ZHD uint32_t rd32(const uint8_t *p) { return rd16(p) | (rd16(p + 2) << 16); }
 ZHD uint64_t rd64(const uint8_t *p) { return (uint64_t)rd32(p) | ((uint64_t)rd32(p + 4) << 32); }
+
+// 8 bytes to an 8-byte aligned address
+ZHD void st_u64(uint8_t *p, uint64_t v) {
+#if defined(__CUDA_ARCH__)
+    *reinterpret_cast<uint64_t *>(p) = v;
+#else
+    for (int k = 0; k < 8; k++) p[k] = (uint8_t)(v >> (8 * k));
+#endif
+}
 
 ZHD int highbit(uint32_t v) {  // index of the highest set bit, v > 0
 #if defined(__CUDA_ARCH__)
@@ -179,7 +199,7 @@ struct BitFwd {
 // FSE table description (RFC 8878 4.1.1; libzstd FSE_readNCount): the
 // normalized counts of symbols 0..max_sym into norm, *log the accuracy log.
 // Returns the bytes used, or -1 when the description is invalid.
-ZHD int fse_read_ncount(const uint8_t *src, size_t len, int16_t *norm, int max_sym, int max_log,
+ZCOLD int fse_read_ncount(const uint8_t *src, size_t len, int16_t *norm, int max_sym, int max_log,
                         int *log, int *nsym) {
     if (len < 1) return -1;
     BitFwd br{src, src + len, 0};
@@ -235,7 +255,7 @@ ZHD int fse_read_ncount(const uint8_t *src, size_t len, int16_t *norm, int max_s
 // Decoding table from normalized counts (RFC 8878 4.1.1; libzstd
 // FSE_buildDTable): low-probability symbols at the top, the others spread
 // with step (size/2 + size/8 + 3), then each state's bits and base.
-ZHD bool fse_build(FseEntry *t, const int16_t *norm, int nsym, int log, uint16_t *next) {
+ZCOLD bool fse_build(FseEntry *t, const int16_t *norm, int nsym, int log, uint16_t *next) {
     const int size = 1 << log;
     int high = size - 1;
     for (int s = 0; s < nsym; s++) {
@@ -275,48 +295,51 @@ ZHD void fse_rle(FseEntry *t, int sym) {
 }
 
 // Predefined distributions (RFC 8878 3.1.1.3.2.2).
-ZHD int16_t ll_default(int s) {
-    constexpr int16_t v[36] = {4, 3, 2, 2, 2, 2, 2, 2, 2, 2, 2, 2, 2, 1, 1, 1, 2, 2,
-                               2, 2, 2, 2, 2, 2, 2, 3, 2, 1, 1, 1, 1, 1, -1, -1, -1, -1};
-    return v[s];
-}
-ZHD int16_t ml_default(int s) {
-    constexpr int16_t v[53] = {1, 4, 3, 2, 2, 2, 2, 2, 2, 1, 1, 1, 1, 1, 1, 1, 1, 1,
-                               1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1,
-                               1, 1, 1, 1, 1, 1, 1, 1, 1, 1, -1, -1, -1, -1, -1, -1, -1};
-    return v[s];
-}
-ZHD int16_t of_default(int s) {
-    constexpr int16_t v[29] = {1, 1, 1, 1, 1, 1, 2, 2, 2, 1, 1, 1, 1, 1, 1,
-                               1, 1, 1, 1, 1, 1, 1, 1, 1, -1, -1, -1, -1, -1};
-    return v[s];
-}
+// Constant tables: __constant__ memory on the device (a function-local
+// array indexed at run time would be rebuilt on the stack at every call),
+// plain constants on the host.
+#if defined(__CUDACC__)
+#define ZTAB(type, name, n, ...)                                \
+    static __constant__ const type name##_dev[n] = __VA_ARGS__; \
+    static constexpr type name##_host[n] = __VA_ARGS__;
+#else
+#define ZTAB(type, name, n, ...) static constexpr type name##_host[n] = __VA_ARGS__;
+#endif
+#if defined(__CUDA_ARCH__)
+#define ZLOOK(name, i) name##_dev[i]
+#else
+#define ZLOOK(name, i) name##_host[i]
+#endif
 
+// Predefined distributions (RFC 8878 3.1.1.3.2.2).
+ZTAB(int16_t, LL_DEFAULT, 36, {4, 3, 2, 2, 2, 2, 2, 2, 2, 2, 2, 2, 2, 1, 1, 1, 2, 2,
+                               2, 2, 2, 2, 2, 2, 2, 3, 2, 1, 1, 1, 1, 1, -1, -1, -1, -1})
+ZTAB(int16_t, ML_DEFAULT, 53, {1, 4, 3, 2, 2, 2, 2, 2, 2, 1, 1, 1, 1, 1, 1, 1, 1, 1,
+                               1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1,
+                               1, 1, 1, 1, 1, 1, 1, 1, 1, 1, -1, -1, -1, -1, -1, -1, -1})
+ZTAB(int16_t, OF_DEFAULT, 29, {1, 1, 1, 1, 1, 1, 2, 2, 2, 1, 1, 1, 1, 1, 1,
+                               1, 1, 1, 1, 1, 1, 1, 1, 1, -1, -1, -1, -1, -1})
 // Literal and match length codes (RFC 8878 3.1.1.3.2.1.1).
-ZHD uint32_t ll_base(int c) {
-    constexpr uint32_t b[36] = {0,  1,  2,  3,  4,   5,   6,   7,   8,    9,    10,   11,
-                                12, 13, 14, 15, 16,  18,  20,  22,  24,   28,   32,   40,
-                                48, 64, 128, 256, 512, 1024, 2048, 4096, 8192, 16384, 32768, 65536};
-    return b[c];
-}
-ZHD int ll_bits(int c) {
-    constexpr uint8_t b[36] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 1, 1,
-                               1, 1, 2, 2, 3, 3, 4, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16};
-    return b[c];
-}
-ZHD uint32_t ml_base(int c) {
-    constexpr uint32_t b[53] = {3,  4,  5,  6,  7,  8,  9,  10,  11,  12,  13,   14,   15,   16,
-                                17, 18, 19, 20, 21, 22, 23, 24,  25,  26,  27,   28,   29,   30,
-                                31, 32, 33, 34, 35, 37, 39, 41,  43,  47,  51,   59,   67,   83,
-                                99, 131, 259, 515, 1027, 2051, 4099, 8195, 16387, 32771, 65539};
-    return b[c];
-}
-ZHD int ml_bits(int c) {
-    constexpr uint8_t b[53] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0,
-                               0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 1, 1, 1, 1,
-                               2, 2, 3, 3, 4, 4, 5, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16};
-    return b[c];
-}
+ZTAB(uint32_t, LL_BASE, 36, {0,  1,  2,  3,  4,   5,   6,   7,   8,    9,    10,   11,
+                             12, 13, 14, 15, 16,  18,  20,  22,  24,   28,   32,   40,
+                             48, 64, 128, 256, 512, 1024, 2048, 4096, 8192, 16384, 32768, 65536})
+ZTAB(uint8_t, LL_BITS, 36, {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 1, 1,
+                            1, 1, 2, 2, 3, 3, 4, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16})
+ZTAB(uint32_t, ML_BASE, 53, {3,  4,  5,  6,  7,  8,  9,  10,  11,  12,  13,   14,   15,   16,
+                             17, 18, 19, 20, 21, 22, 23, 24,  25,  26,  27,   28,   29,   30,
+                             31, 32, 33, 34, 35, 37, 39, 41,  43,  47,  51,   59,   67,   83,
+                             99, 131, 259, 515, 1027, 2051, 4099, 8195, 16387, 32771, 65539})
+ZTAB(uint8_t, ML_BITS, 53, {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0,
+                            0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 1, 1, 1, 1,
+                            2, 2, 3, 3, 4, 4, 5, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16})
+
+ZHD int16_t ll_default(int s) { return ZLOOK(LL_DEFAULT, s); }
+ZHD int16_t ml_default(int s) { return ZLOOK(ML_DEFAULT, s); }
+ZHD int16_t of_default(int s) { return ZLOOK(OF_DEFAULT, s); }
+ZHD uint32_t ll_base(int c) { return ZLOOK(LL_BASE, c); }
+ZHD int ll_bits(int c) { return ZLOOK(LL_BITS, c); }
+ZHD uint32_t ml_base(int c) { return ZLOOK(ML_BASE, c); }
+ZHD int ml_bits(int c) { return ZLOOK(ML_BITS, c); }
 
 // ---- Huffman -------------------------------------------------------------
 
@@ -325,7 +348,7 @@ ZHD int ml_bits(int c) {
 // interleaved states), the implied last weight, then the single-symbol
 // decoding table of 2^log entries.  Returns the bytes used, -1 if invalid.
 // Lane 0 only.
-ZHD int huf_read_table(Workspace *ws, const uint8_t *src, size_t len) {
+ZCOLD int huf_read_table(Workspace *ws, const uint8_t *src, size_t len) {
     if (len < 1) return -1;
     const int isz = src[0];
     int nw = 0;
@@ -346,7 +369,7 @@ ZHD int huf_read_table(Workspace *ws, const uint8_t *src, size_t len) {
         const int h = fse_read_ncount(src + 1, (size_t)isz, ws->norm, 255, 6, &log, &nsym);
         if (h < 0) return -1;
         if (!fse_build(ws->wt, ws->norm, nsym, log, ws->next)) return -1;
-        BitRev br;
+        BitRev br{};
         if (!br.init(src + 1 + h, src + 1 + isz)) return -1;
         uint32_t s1 = (uint32_t)br.read(log), s2 = (uint32_t)br.read(log);
         // libzstd FSE_decompress (two states): a symbol per state in turn
@@ -397,34 +420,137 @@ ZHD int huf_read_table(Workspace *ws, const uint8_t *src, size_t len) {
         start[w] = next;
         next += rank[w] << (w - 1);
     }
+    // each symbol's first entry (the warp fills the table: huf_fill)
     for (int n = 0; n < nsym; n++) {
         const int w = ws->weights[n];
-        if (!w) continue;
-        const uint32_t cnt = (1u << w) >> 1;
-        const uint8_t nb = (uint8_t)(log + 1 - w);
-        for (uint32_t u = start[w]; u < start[w] + cnt; u++) {
-            ws->huf[u].sym = (uint8_t)n;
-            ws->huf[u].nb = nb;
-        }
-        start[w] += cnt;
+        ws->next[n] = (uint16_t)start[w];
+        if (w) start[w] += (1u << w) >> 1;
     }
+    ws->huf_nsym = (uint16_t)nsym;
     ws->huf_log = (int8_t)log;
     return (int)used;
 }
+
+// Decoding table of the description huf_read_table just read, filled by
+// the warp: symbols of weight w take 2^(w-1) consecutive entries from their
+// first entry on, each entry {symbol, code length log + 1 - w}.
+ZHD void huf_fill(Workspace *ws, int lane, int nl) {
+    const int log = ws->huf_log, nsym = ws->huf_nsym;
+    for (int n = 0; n < nsym; n++) {
+        const int w = ws->weights[n];
+        if (!w) continue;
+        const uint32_t st = ws->next[n], cnt = (1u << w) >> 1;
+        const HufEntry e = (HufEntry)(n | ((uint32_t)(log + 1 - w) << 8));
+        for (uint32_t u = (uint32_t)lane; u < cnt; u += (uint32_t)nl) ws->huf[st + u] = e;
+    }
+}
+
+// Backward reader over aligned 32-bit words (Huffman streams, sequence
+// bitstreams).  Bits are numbered from base = s rounded down to 4 bytes; the
+// stream holds bits [lo, top) and pos counts the bits not yet consumed.
+// Words hi (index w, holding bit pos - 1) and lo_w (index w - 1) form a
+// window of at least 33 unconsumed bits: a read of up to 31 bits, or two
+// Huffman symbols of <= 12 bits, fit between window checks.  Bits below the
+// stream read as zero (libzstd's reader zero-fills below its start) and pos
+// then drops below lo; bits above pos are masked off.
+struct BitWin {
+    const uint8_t *s, *e;
+    const uint32_t *base;
+    int32_t lo, pos, w;
+    uint32_t hi, lo_w, nx;  // words w, w - 1 and (prefetched) w - 2
+
+    ZHD uint32_t word(int32_t i) const {
+#if defined(__CUDA_ARCH__)
+        // the aligned word holding a stream byte lies inside the allocation;
+        // selects instead of branches (the lanes of a warp run 4 streams)
+        uint32_t v = base[i < 0 ? 0 : i];
+        v = i < 0 ? 0u : v;
+#else
+        if (i < 0) return 0;
+        uint32_t v = 0;
+        const uint8_t *wb = reinterpret_cast<const uint8_t *>(base) + 4 * (int64_t)i;
+        for (int k = 0; k < 4; k++)
+            if (wb + k >= s && wb + k < e) v |= (uint32_t)wb[k] << (8 * k);
+#endif
+        return v & (i == 0 ? ~0u << lo : ~0u);  // lo < 32: bits of the bytes before s
+    }
+    ZHD bool init(const uint8_t *start, const uint8_t *end) {
+        if (end <= start) return false;
+        const uint8_t last = end[-1];
+        if (last == 0) return false;  // no end mark
+        s = start;
+        e = end;
+        base = reinterpret_cast<const uint32_t *>((uintptr_t)start & ~(uintptr_t)3);
+        lo = (int32_t)((uintptr_t)start & 3) * 8;
+        pos = lo + (int32_t)(end - start) * 8 - (8 - highbit(last));
+        w = (pos - 1) >> 5;
+        hi = word(w);
+        lo_w = word(w - 1);
+        nx = word(w - 2);
+        return true;
+    }
+    // the next n <= 31 bits (sh reaches 64 only for n == 0, masked to 0)
+    ZHD uint32_t peek(int n) const {
+        const uint32_t sh = (uint32_t)(pos - n - (w - 1) * 32) & 63;
+        return (uint32_t)((((uint64_t)hi << 32) | lo_w) >> sh) & ((1u << n) - 1);
+    }
+    ZHD void slide() {
+        const bool c = pos <= w * 32;
+        w -= c ? 1 : 0;
+        hi = c ? lo_w : hi;
+        lo_w = c ? nx : lo_w;
+        nx = word(w - 2);
+    }
+    ZHD uint32_t read(int n) {
+        const uint32_t v = peek(n);
+        pos -= n;
+        slide();
+        return v;
+    }
+};
 
 // One Huffman stream of n symbols into out; false unless the stream is
 // consumed exactly (libzstd HUF_decompress1X1: BIT_endOfDStream).
 ZHD bool huf_stream(const Workspace *ws, const uint8_t *s, const uint8_t *e, uint8_t *out,
                     uint32_t n) {
-    BitRev br;
+    BitWin br;
     if (!br.init(s, e)) return false;
     const int log = ws->huf_log;
-    for (uint32_t i = 0; i < n; i++) {
-        const HufEntry d = ws->huf[br.peek(log)];
-        out[i] = d.sym;
-        br.skip(d.nb);
+    auto sym = [&]() -> uint32_t {
+        const uint32_t d = ws->huf[br.peek(log)];
+        br.pos -= (int32_t)(d >> 8);
+        return d & 0xFF;
+    };
+    uint32_t i = 0;
+    // single symbols up to an 8-byte aligned output address
+    const uint32_t head = (uint32_t)((8 - ((uintptr_t)out & 7)) & 7);
+    for (; i < n && i < head; i++) {
+        out[i] = (uint8_t)sym();
+        br.slide();
     }
-    return br.pos == 0;
+    for (; i + 8 <= n; i += 8) {
+        uint32_t v0 = 0, v1 = 0;
+ZUNROLL
+        for (int k = 0; k < 4; k += 2) {
+            const uint32_t a = sym();
+            const uint32_t b = sym();
+            br.slide();
+            v0 |= (a | (b << 8)) << (8 * k);
+        }
+ZUNROLL
+        for (int k = 0; k < 4; k += 2) {
+            const uint32_t a = sym();
+            const uint32_t b = sym();
+            br.slide();
+            v1 |= (a | (b << 8)) << (8 * k);
+        }
+        st_u64(out + i, (uint64_t)v0 | ((uint64_t)v1 << 32));
+    }
+    for (; i < n; i++) {
+        out[i] = (uint8_t)sym();
+        br.slide();
+    }
+    return br.pos == br.lo;
 }
 
 // ---- XXH64 (content checksum) --------------------------------------------
@@ -445,12 +571,44 @@ ZHD uint64_t xxh_merge(uint64_t acc, uint64_t v) {
 // XXH64 with seed 0 of [p, p + n); the stripe accumulators run on lanes
 // 0..3 (nl >= 4) or all on lane 0.  Result valid on lane 0; acc is a
 // 4-entry scratch shared by the warp.
-ZHD uint64_t xxh64(const uint8_t *p, uint64_t n, int lane, int nl, uint64_t *acc) {
+ZHD uint64_t xxh64(const uint8_t *p, uint64_t n, int lane, int nl, uint64_t *acc, uint64_t *stage) {
     const uint64_t stripes = n / 32;
+    const uint8_t *pe = p + n;
+    auto init = [](int a) -> uint64_t {
+        return a == 0 ? P64_1 + P64_2 : (a == 1 ? P64_2 : (a == 2 ? 0 : 0 - P64_1));
+    };
+#if defined(__CUDA_ARCH__)
+    if (n >= 32 && nl == 32) {
+        // 1 KiB chunks (32 stripes) staged in shared memory: every lane
+        // loads 32 bytes of chunk c + 1 while lanes 0-3 run chunk c, so the
+        // rounds never wait on a global load
+        const uint64_t nch = stripes / 32;
+        uint64_t v = init(lane & 3), r[4];
+        ZUNROLL
+        for (int k = 0; k < 4; k++) r[k] = nch ? rd64_bounded(p + 32 * lane + 8 * k, pe) : 0;
+        for (uint64_t c = 0; c < nch; c++) {
+            warp_sync();
+            ZUNROLL
+            for (int k = 0; k < 4; k++) stage[4 * lane + k] = r[k];
+            warp_sync();
+            if (c + 1 < nch) {
+                const uint8_t *q = p + 1024 * (c + 1) + 32 * lane;
+                ZUNROLL
+                for (int k = 0; k < 4; k++) r[k] = rd64_bounded(q + 8 * k, pe);
+            }
+            if (lane < 4)
+                for (int t = 0; t < 32; t++) v = xxh_round(v, stage[4 * t + lane]);
+        }
+        if (lane < 4) {
+            for (uint64_t t = 32 * nch; t < stripes; t++) v = xxh_round(v, rd64_bounded(p + 32 * t + 8 * lane, pe));
+            acc[lane] = v;
+        }
+    } else
+#endif
     if (n >= 32) {
         for (int a = lane; a < 4; a += nl) {
-            uint64_t v = a == 0 ? P64_1 + P64_2 : (a == 1 ? P64_2 : (a == 2 ? 0 : 0 - P64_1));
-            for (uint64_t s = 0; s < stripes; s++) v = xxh_round(v, rd64(p + 32 * s + 8 * a));
+            uint64_t v = init(a);
+            for (uint64_t s = 0; s < stripes; s++) v = xxh_round(v, rd64_bounded(p + 32 * s + 8 * a, pe));
             acc[a] = v;
         }
     }
@@ -499,7 +657,7 @@ ZHD uint64_t xxh64(const uint8_t *p, uint64_t n, int lane, int nl, uint64_t *acc
 // 3.1.1.3.2.1): 0 predefined, 1 RLE (one symbol byte), 2 FSE-compressed
 // (a table description), 3 repeat the previous table.  Returns bytes used
 // or -1.  Lane 0 only.
-ZHD int seq_table(Workspace *ws, int field, int mode, const uint8_t *src, size_t len) {
+ZCOLD int seq_table(Workspace *ws, int field, int mode, const uint8_t *src, size_t len) {
     FseEntry *t = field == 0 ? ws->ll : (field == 1 ? ws->of : ws->ml);
     int8_t *lg = field == 0 ? &ws->ll_log : (field == 1 ? &ws->of_log : &ws->ml_log);
     const int max_sym = field == 0 ? LL_MAX_SYM : (field == 1 ? OF_MAX_SYM : ML_MAX_SYM);
@@ -554,10 +712,10 @@ ZHD void coop_copy(uint8_t *d, const uint8_t *s, uint64_t n, int lane, int nl) {
     for (uint64_t i = (uint64_t)lane * CCH; i < n; i += (uint64_t)nl * CCH) {
         uint8_t t[CCH];
         const uint64_t m = n - i < (uint64_t)CCH ? n - i : (uint64_t)CCH;
-#pragma unroll
+ZUNROLL
         for (int k = 0; k < CCH; k++)
             if ((uint64_t)k < m) t[k] = s[i + k];
-#pragma unroll
+ZUNROLL
         for (int k = 0; k < CCH; k++)
             if ((uint64_t)k < m) d[i + k] = t[k];
     }
@@ -579,12 +737,12 @@ ZHD void coop_match(uint8_t *d, uint64_t off, uint64_t ml, int lane, int nl) {
         uint8_t t[CCH];
         const uint64_t m = ml - i < (uint64_t)CCH ? ml - i : (uint64_t)CCH;
         uint64_t j = i % off;
-#pragma unroll
+ZUNROLL
         for (int k = 0; k < CCH; k++) {
             if ((uint64_t)k < m) t[k] = s[j];
             if (++j == off) j = 0;
         }
-#pragma unroll
+ZUNROLL
         for (int k = 0; k < CCH; k++)
             if ((uint64_t)k < m) d[i + k] = t[k];
     }
@@ -667,8 +825,16 @@ ZHD int decode_compressed_block(Workspace *ws, const Job &job, const uint8_t *b,
         if (ws->err) return ws->err;
         p = b + ws->seq_ll[0];
         warp_sync();
+        if (ltype == 2) {
+            huf_fill(ws, lane, nl);
+            warp_sync();
+        }
+        // a block whose sequence section is a lone zero byte (no sequences)
+        // is its literals: they are decoded straight into the output
+        const bool direct = lsec + 1 == bsize && b[lsec] == 0 && *out + regen <= job.cap;
+        uint8_t *ld = direct ? job.dst + *out : job.lit;
         if (nstreams == 1) {
-            if (lane == 0) ws->err = huf_stream(ws, p, pe, job.lit, regen) ? OK : E_CORRUPT;
+            if (lane == 0) ws->err = huf_stream(ws, p, pe, ld, regen) ? OK : E_CORRUPT;
         } else {
             if (pe - p < 6) return E_CORRUPT;
             const uint32_t s1 = rd16(p), s2 = rd16(p + 2), s3 = rd16(p + 4);
@@ -682,12 +848,16 @@ ZHD int decode_compressed_block(Workspace *ws, const Job &job, const uint8_t *b,
             warp_sync();
             for (int k = lane; k < 4; k += nl) {
                 const uint32_t n = k < 3 ? seg : regen - 3 * seg;
-                if (!huf_stream(ws, st[k], st[k + 1], job.lit + (uint64_t)k * seg, n))
+                if (!huf_stream(ws, st[k], st[k + 1], ld + (uint64_t)k * seg, n))
                     ws->err = E_CORRUPT;
             }
         }
         warp_sync();
         if (ws->err) return ws->err;
+        if (direct) {
+            *out += regen;
+            return OK;
+        }
         lit = job.lit;
     }
     // ---- sequences section (3.1.1.3.2)
@@ -730,7 +900,7 @@ ZHD int decode_compressed_block(Workspace *ws, const Job &job, const uint8_t *b,
         s = b + ws->seq_ll[0];
         warp_sync();
         // lane 0 decodes batches of sequences; the warp executes them
-        BitRev br;
+        BitWin br{};
         uint32_t sll = 0, sof = 0, sml = 0;
         if (lane == 0) {
             ws->err = br.init(s, se) ? OK : E_CORRUPT;
@@ -744,7 +914,10 @@ ZHD int decode_compressed_block(Workspace *ws, const Job &job, const uint8_t *b,
         if (ws->err) return ws->err;
         for (uint32_t done = 0; done < nseq;) {
             const uint32_t nb = nseq - done < (uint32_t)SEQ_BATCH ? nseq - done : (uint32_t)SEQ_BATCH;
+            // lane 0 decodes the batch and places each sequence, checking
+            // in sequence order (the first failing sequence decides the error)
             if (lane == 0) {
+                uint32_t r0 = ws->rep[0], r1 = ws->rep[1], r2 = ws->rep[2];
                 for (uint32_t i = 0; i < nb; i++) {
                     const FseEntry eo = ws->of[sof], em = ws->ml[sml], el = ws->ll[sll];
                     const int oc = eo.sym, mc = em.sym, lc = el.sym;
@@ -755,51 +928,50 @@ ZHD int decode_compressed_block(Workspace *ws, const Job &job, const uint8_t *b,
                     uint64_t off;
                     if (ofv > 3) {
                         off = ofv - 3;
-                        ws->rep[2] = ws->rep[1];
-                        ws->rep[1] = ws->rep[0];
-                        ws->rep[0] = (uint32_t)off;
+                        r2 = r1;
+                        r1 = r0;
+                        r0 = (uint32_t)off;
                     } else {
                         const uint32_t idx = (uint32_t)ofv - 1 + (ll == 0 ? 1u : 0u);
                         if (idx == 0) {
-                            off = ws->rep[0];
+                            off = r0;
                         } else {
-                            uint64_t t = idx == 3 ? (uint64_t)ws->rep[0] - 1 : ws->rep[idx];
+                            uint64_t t = idx == 3 ? (uint64_t)r0 - 1 : (idx == 1 ? r1 : r2);
                             if (t == 0) t = ~0ull;  // invalid, caught below
-                            if (idx != 1) ws->rep[2] = ws->rep[1];
-                            ws->rep[1] = ws->rep[0];
-                            ws->rep[0] = (uint32_t)t;
+                            if (idx != 1) r2 = r1;
+                            r1 = r0;
+                            r0 = (uint32_t)t;
                             off = t;
                         }
                     }
+                    const uint32_t of32 = off > 0xFFFFFFFFull ? 0xFFFFFFFFu : (uint32_t)off;
+                    if ((uint64_t)lused + ll > regen) { ws->err = E_CORRUPT; break; }
+                    if (o + ll + ml > job.cap) { ws->err = E_DST; break; }
                     ws->seq_ll[i] = ll;
                     ws->seq_ml[i] = ml;
-                    ws->seq_of[i] = off > 0xFFFFFFFFull ? 0xFFFFFFFFu : (uint32_t)off;
+                    ws->seq_of[i] = of32;
+                    ws->seq_lit[i] = lused;
+                    ws->seq_pos[i] = o + ll;
+                    ws->seq_state[i] = 0;
+                    o += ll;
+                    lused += ll;
+                    if (of32 == 0 || (uint64_t)of32 > o - fstart) { ws->err = E_CORRUPT; break; }
+                    o += ml;
                     if (done + i + 1 < nseq) {  // state updates: LL, ML, OF
                         sll = el.base + (uint32_t)br.read(el.nb);
                         sml = em.base + (uint32_t)br.read(em.nb);
                         sof = eo.base + (uint32_t)br.read(eo.nb);
                     }
                 }
-                if (!ws->err && done + nb == nseq && br.pos > 0) ws->err = E_CORRUPT;
+                ws->rep[0] = r0;
+                ws->rep[1] = r1;
+                ws->rep[2] = r2;
+                if (!ws->err && done + nb == nseq && br.pos > br.lo) ws->err = E_CORRUPT;
             }
+            o = bcast0(o);
+            lused = (uint32_t)bcast0(lused);
             warp_sync();
             if (ws->err) return ws->err;
-            // the batch's positions, checked in sequence order (every lane the
-            // same); the first failing sequence decides the error
-            for (uint32_t i = 0; i < nb; i++) {
-                const uint32_t ll = ws->seq_ll[i], ml = ws->seq_ml[i], off = ws->seq_of[i];
-                if ((uint64_t)lused + ll > regen) return E_CORRUPT;
-                if (o + ll + ml > job.cap) return E_DST;
-                if (lane == 0) {
-                    ws->seq_lit[i] = lused;
-                    ws->seq_pos[i] = o + ll;
-                    ws->seq_state[i] = 0;
-                }
-                o += ll;
-                lused += ll;
-                if (off == 0 || (uint64_t)off > o - fstart) return E_CORRUPT;
-                o += ml;
-            }
             warp_sync();
             // literals: a lane per sequence (they never overlap)
             for (uint32_t i = (uint32_t)lane; i < nb; i += (uint32_t)nl) {
@@ -946,7 +1118,9 @@ ZHD Result decode(Workspace *ws, const Job &job, int lane, int nl, uint64_t *acc
         if (has_fcs && o - fstart != fcs) { r.code = E_CORRUPT; r.pos = ip; return r; }
         if (cksum) {
             if (job.len - p < 4) { r.code = E_CORRUPT; return r; }
-            const uint64_t h = xxh64(job.dst + fstart, o - fstart, lane, nl, acc);
+            // the frame's tables are dead at its end: their space stages the hash input
+            const uint64_t h = xxh64(job.dst + fstart, o - fstart, lane, nl, acc,
+                                     reinterpret_cast<uint64_t *>(ws->huf));
             if (lane == 0) ws->err = (uint32_t)h == rd32(src + p) ? OK : E_CHECKSUM;
             warp_sync();
             if (ws->err) { r.code = ws->err; r.pos = p; return r; }

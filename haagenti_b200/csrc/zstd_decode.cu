@@ -11,8 +11,12 @@ namespace hct {
 namespace {
 
 constexpr int ZWARPS = 4;  // warps (jobs in flight) per CTA
+#ifndef ZSTD_MIN_CTAS
+#define ZSTD_MIN_CTAS 2  // resident CTAs per SM the register budget allows
+#endif
+constexpr uint64_t ZSTD_GRID_CAP = 148ull * ZSTD_MIN_CTAS;
 
-__global__ void __launch_bounds__(ZWARPS * 32) zstd_decode_kernel(
+__global__ void __launch_bounds__(ZWARPS * 32, ZSTD_MIN_CTAS) zstd_decode_kernel(
     const uint8_t *__restrict__ src, const hct_b200_zstd_job *__restrict__ jobs, uint32_t n,
     uint8_t *dst, hct_b200_status *__restrict__ status, uint8_t *scratch) {
     extern __shared__ uint8_t zsm[];
@@ -43,7 +47,7 @@ __global__ void __launch_bounds__(ZWARPS * 32) zstd_decode_kernel(
 
 size_t zstd_scratch_bytes(uint32_t n) {
     const uint64_t ctas = ((uint64_t)n + ZWARPS - 1) / ZWARPS;
-    const uint64_t cap = 148ull * 2;
+    const uint64_t cap = ZSTD_GRID_CAP;
     return (size_t)((ctas < cap ? (ctas ? ctas : 1) : cap) * ZWARPS * zs::LIT_SCRATCH);
 }
 
@@ -57,7 +61,7 @@ cudaError_t launch_zstd_decode(const uint8_t *d_src, const hct_b200_zstd_job *d_
     if (e != cudaSuccess) return e;
     // as many CTAs as zstd_scratch_bytes provides scratch for
     const uint64_t ctas = ((uint64_t)n + ZWARPS - 1) / ZWARPS;
-    const uint64_t grid = ctas < 148ull * 2 ? ctas : 148ull * 2;
+    const uint64_t grid = ctas < ZSTD_GRID_CAP ? ctas : ZSTD_GRID_CAP;
     zstd_decode_kernel<<<(unsigned)grid, ZWARPS * 32, smem, s>>>(d_src, d_jobs, n, d_dst, d_status,
                                                                  d_scratch);
     return cudaGetLastError();
