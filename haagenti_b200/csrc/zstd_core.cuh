@@ -97,6 +97,19 @@ struct Workspace {
     uint32_t seq_done;  // the bitstream was consumed completely
 };
 
+// Huffman state of the block-parallel decoder (one per warp, shared memory):
+// the members huf_read_table, huf_fill and huf_stream use.
+struct HufWs {
+    HufEntry huf[1 << HUF_MAX_LOG];
+    FseEntry wt[64];
+    int16_t norm[256];
+    uint16_t next[256];
+    uint8_t weights[256];
+    int8_t huf_log;
+    uint16_t huf_nsym;
+    int err;
+};
+
 // ---- small helpers -------------------------------------------------------
 
 ZHD uint32_t rd16(const uint8_t *p) { return (uint32_t)p[0] | ((uint32_t)p[1] << 8); }
@@ -345,10 +358,12 @@ ZHD int ml_bits(int c) { return ZLOOK(ML_BITS, c); }
 
 // Huffman tree description (RFC 8878 4.2.1; libzstd HUF_readStats +
 // HUF_readDTableX1): weights (direct 4-bit, or FSE-compressed with two
-// interleaved states), the implied last weight, then the single-symbol
-// decoding table of 2^log entries.  Returns the bytes used, -1 if invalid.
+// interleaved states), the implied last weight, then where each symbol's
+// entries start in the single-symbol decoding table of 2^log entries
+// (huf_fill writes the table).  Returns the bytes used, -1 if invalid.
 // Lane 0 only.
-ZCOLD int huf_read_table(Workspace *ws, const uint8_t *src, size_t len) {
+template <class W>
+ZCOLD int huf_read_table(W *ws, const uint8_t *src, size_t len) {
     if (len < 1) return -1;
     const int isz = src[0];
     int nw = 0;
@@ -434,7 +449,8 @@ ZCOLD int huf_read_table(Workspace *ws, const uint8_t *src, size_t len) {
 // Decoding table of the description huf_read_table just read, filled by
 // the warp: symbols of weight w take 2^(w-1) consecutive entries from their
 // first entry on, each entry {symbol, code length log + 1 - w}.
-ZHD void huf_fill(Workspace *ws, int lane, int nl) {
+template <class W>
+ZHD void huf_fill(W *ws, int lane, int nl) {
     const int log = ws->huf_log, nsym = ws->huf_nsym;
     for (int n = 0; n < nsym; n++) {
         const int w = ws->weights[n];
@@ -457,13 +473,15 @@ struct BitWin {
     const uint8_t *s, *e;
     const uint32_t *base;
     int32_t lo, pos, w;
-    uint32_t hi, lo_w, nx;  // words w, w - 1 and (prefetched) w - 2
+    uint32_t hi, lo_w;          // words w and w - 1
+    uint32_t q1, q2, q3, q4;    // words w - 2 .. w - 5, loaded ahead (an L2
+                                // round trip is ~17 symbols of decode)
 
     ZHD uint32_t word(int32_t i) const {
 #if defined(__CUDA_ARCH__)
         // the aligned word holding a stream byte lies inside the allocation;
         // selects instead of branches (the lanes of a warp run 4 streams)
-        uint32_t v = base[i < 0 ? 0 : i];
+        uint32_t v = __ldg(base + (i < 0 ? 0 : i));
         v = i < 0 ? 0u : v;
 #else
         if (i < 0) return 0;
@@ -486,7 +504,10 @@ struct BitWin {
         w = (pos - 1) >> 5;
         hi = word(w);
         lo_w = word(w - 1);
-        nx = word(w - 2);
+        q1 = word(w - 2);
+        q2 = word(w - 3);
+        q3 = word(w - 4);
+        q4 = word(w - 5);
         return true;
     }
     // the next n <= 31 bits (sh reaches 64 only for n == 0, masked to 0)
@@ -495,11 +516,15 @@ struct BitWin {
         return (uint32_t)((((uint64_t)hi << 32) | lo_w) >> sh) & ((1u << n) - 1);
     }
     ZHD void slide() {
-        const bool c = pos <= w * 32;
-        w -= c ? 1 : 0;
-        hi = c ? lo_w : hi;
-        lo_w = c ? nx : lo_w;
-        nx = word(w - 2);
+        if (pos <= w * 32) {  // predicated: the lanes of a warp run different streams
+            w--;
+            hi = lo_w;
+            lo_w = q1;
+            q1 = q2;
+            q2 = q3;
+            q3 = q4;
+            q4 = word(w - 5);
+        }
     }
     ZHD uint32_t read(int n) {
         const uint32_t v = peek(n);
@@ -511,7 +536,8 @@ struct BitWin {
 
 // One Huffman stream of n symbols into out; false unless the stream is
 // consumed exactly (libzstd HUF_decompress1X1: BIT_endOfDStream).
-ZHD bool huf_stream(const Workspace *ws, const uint8_t *s, const uint8_t *e, uint8_t *out,
+template <class W>
+ZHD bool huf_stream(const W *ws, const uint8_t *s, const uint8_t *e, uint8_t *out,
                     uint32_t n) {
     BitWin br;
     if (!br.init(s, e)) return false;
@@ -704,21 +730,49 @@ struct Result {
     uint64_t written;  // output bytes
 };
 
-// Cooperative copies (all lanes): n bytes from s to d (no overlap).  Each
-// lane moves 16 consecutive bytes per step, all loads before the stores, so
-// a step costs one memory latency for 16 * nl bytes.
-constexpr int CCH = 16;
+// Cooperative copies (lanes lane, lane + nl, ...): n bytes from s to d (no
+// overlap).
 ZHD void coop_copy(uint8_t *d, const uint8_t *s, uint64_t n, int lane, int nl) {
-    for (uint64_t i = (uint64_t)lane * CCH; i < n; i += (uint64_t)nl * CCH) {
-        uint8_t t[CCH];
-        const uint64_t m = n - i < (uint64_t)CCH ? n - i : (uint64_t)CCH;
+#if defined(__CUDA_ARCH__)
+    // bytes up to a 16-byte aligned destination, then 16-byte stores of
+    // source words realigned by funnel shifts (4 chunks in flight per lane),
+    // then the tail.  A source word read is an aligned word holding at least
+    // one byte of [s, s + n).
+    const uint64_t head = ((16 - ((uintptr_t)d & 15)) & 15) < n ? ((16 - ((uintptr_t)d & 15)) & 15) : n;
+    for (uint64_t i = (uint64_t)lane; i < head; i += (uint64_t)nl) d[i] = s[i];
+    const uint64_t nch = (n - head) / 16;
+    if (nch) {
+        const uint8_t *s1 = s + head;
+        uint4 *d1 = reinterpret_cast<uint4 *>(d + head);
+        const uint32_t sh = (uint32_t)((uintptr_t)s1 & 3) * 8;
+        const uint32_t *w = reinterpret_cast<const uint32_t *>(s1 - ((uintptr_t)s1 & 3));
+        auto chunk = [&](uint64_t c, uint32_t *v) {
+            const uint32_t *q = w + 4 * c;
+            const uint32_t a = q[0], b = q[1], e = q[2], f = q[3], g = sh ? q[4] : 0u;
+            v[0] = __funnelshift_r(a, b, sh);
+            v[1] = __funnelshift_r(b, e, sh);
+            v[2] = __funnelshift_r(e, f, sh);
+            v[3] = __funnelshift_r(f, g, sh);
+        };
+        const uint64_t step = (uint64_t)nl * 4;
+        uint64_t c = (uint64_t)lane;
+        for (; c + 3 * (uint64_t)nl < nch; c += step) {
+            uint32_t v[4][4];
 ZUNROLL
-        for (int k = 0; k < CCH; k++)
-            if ((uint64_t)k < m) t[k] = s[i + k];
+            for (int k = 0; k < 4; k++) chunk(c + (uint64_t)k * nl, v[k]);
 ZUNROLL
-        for (int k = 0; k < CCH; k++)
-            if ((uint64_t)k < m) d[i + k] = t[k];
+            for (int k = 0; k < 4; k++) d1[c + (uint64_t)k * nl] = make_uint4(v[k][0], v[k][1], v[k][2], v[k][3]);
+        }
+        for (; c < nch; c += (uint64_t)nl) {
+            uint32_t v[4];
+            chunk(c, v);
+            d1[c] = make_uint4(v[0], v[1], v[2], v[3]);
+        }
     }
+    for (uint64_t i = head + 16 * nch + (uint64_t)lane; i < n; i += (uint64_t)nl) d[i] = s[i];
+#else
+    for (uint64_t i = (uint64_t)lane; i < n; i += (uint64_t)nl) d[i] = s[i];
+#endif
 }
 
 ZHD void coop_fill(uint8_t *d, uint8_t v, uint64_t n, int lane, int nl) {
@@ -726,7 +780,9 @@ ZHD void coop_fill(uint8_t *d, uint8_t v, uint64_t n, int lane, int nl) {
 }
 
 // Match: ml bytes at d from d - off (off >= 1); with off < ml the bytes
-// repeat the period-off pattern, read from before d.
+// repeat the period-off pattern, read from before d, each lane 16
+// consecutive bytes per step with all loads before the stores.
+constexpr int CCH = 16;
 ZHD void coop_match(uint8_t *d, uint64_t off, uint64_t ml, int lane, int nl) {
     const uint8_t *s = d - off;
     if (off >= ml) {
@@ -748,12 +804,49 @@ ZUNROLL
     }
 }
 
-// A compressed block (RFC 8878 3.1.1.3) of bsize bytes at b, its output
-// appended at out (frame output starts at fstart).  Returns an error code.
-ZHD int decode_compressed_block(Workspace *ws, const Job &job, const uint8_t *b, uint32_t bsize,
-                                uint64_t fstart, uint64_t *out, int lane, int nl) {
-    // ---- literals section header (3.1.1.3.1.1)
-    if (bsize < 1) return E_CORRUPT;
+// The Huffman-coded literals (RFC 8878 3.1.1.3.1.6) of [p, pe): one stream,
+// or a 6-byte jump table and four streams of (regen + 3) / 4 symbols (the
+// last one the rest), into out.  False unless every stream decodes exactly.
+// All lanes call it; lanes 0-3 decode a stream each.
+template <class W>
+ZHD bool lit_streams(W *ws, const uint8_t *p, const uint8_t *pe, int nstreams, uint32_t regen,
+                     uint8_t *out, int lane, int nl) {
+    if (nstreams == 1) {
+        if (lane == 0) ws->err = huf_stream(ws, p, pe, out, regen) ? OK : E_CORRUPT;
+    } else {
+        if (pe - p < 6) return false;
+        const uint32_t s1 = rd16(p), s2 = rd16(p + 2), s3 = rd16(p + 4);
+        const uint8_t *q = p + 6;
+        const uint64_t total = (uint64_t)(pe - q);
+        if ((uint64_t)s1 + s2 + s3 > total) return false;
+        const uint32_t seg = (regen + 3) / 4;
+        if (regen < 6 || 3 * seg > regen) return false;  // libzstd: >= 6 for 4 streams
+        const uint8_t *st[5] = {q, q + s1, q + s1 + s2, q + s1 + s2 + s3, pe};
+        if (lane == 0) ws->err = OK;
+        warp_sync();
+        for (int k = lane; k < 4; k += nl) {
+            const uint32_t n = k < 3 ? seg : regen - 3 * seg;
+            if (!huf_stream(ws, st[k], st[k + 1], out + (uint64_t)k * seg, n)) ws->err = E_CORRUPT;
+        }
+    }
+    warp_sync();
+    const bool ok = ws->err == OK;
+    warp_sync();
+    return ok;
+}
+
+// Literals section header (RFC 8878 3.1.1.3.1.1) of a compressed block of
+// bsize bytes at b.  False when it is invalid or does not fit the block.
+struct LitHdr {
+    int ltype;         // 0 raw, 1 RLE, 2 compressed, 3 treeless
+    int nstreams;      // Huffman streams (1 or 4)
+    uint32_t regen;    // literal bytes
+    uint32_t csize;    // compressed bytes (types 2, 3)
+    uint32_t hs;       // header bytes
+    uint32_t lsec;     // bytes of the whole literals section
+};
+ZHD bool lit_header(const uint8_t *b, uint32_t bsize, LitHdr *h) {
+    if (bsize < 1) return false;
     const int ltype = b[0] & 3, sfmt = (b[0] >> 2) & 3;
     uint32_t regen = 0, csize = 0, hs = 0;
     int nstreams = 1;
@@ -763,59 +856,68 @@ ZHD int decode_compressed_block(Workspace *ws, const Job &job, const uint8_t *b,
             regen = b[0] >> 3;
         } else if (sfmt == 1) {
             hs = 2;
-            if (bsize < 2) return E_CORRUPT;
+            if (bsize < 2) return false;
             regen = (b[0] >> 4) | ((uint32_t)b[1] << 4);
         } else {
             hs = 3;
-            if (bsize < 3) return E_CORRUPT;
+            if (bsize < 3) return false;
             regen = (b[0] >> 4) | ((uint32_t)b[1] << 4) | ((uint32_t)b[2] << 12);
         }
     } else {  // compressed / treeless
         if (sfmt < 2) {
             hs = 3;
-            if (bsize < 3) return E_CORRUPT;
+            if (bsize < 3) return false;
             const uint32_t v = rd24(b);
             regen = (v >> 4) & 0x3FF;
             csize = (v >> 14) & 0x3FF;
             nstreams = sfmt == 0 ? 1 : 4;
         } else if (sfmt == 2) {
             hs = 4;
-            if (bsize < 4) return E_CORRUPT;
+            if (bsize < 4) return false;
             const uint32_t v = rd32(b);
             regen = (v >> 4) & 0x3FFF;
             csize = (v >> 18) & 0x3FFF;
             nstreams = 4;
         } else {
             hs = 5;
-            if (bsize < 5) return E_CORRUPT;
+            if (bsize < 5) return false;
             const uint64_t v = (uint64_t)rd32(b) | ((uint64_t)b[4] << 32);
             regen = (uint32_t)((v >> 4) & 0x3FFFF);
             csize = (uint32_t)((v >> 22) & 0x3FFFF);
             nstreams = 4;
         }
     }
-    if (regen > BLOCK_MAX) return E_CORRUPT;
+    if (regen > BLOCK_MAX) return false;
+    const uint32_t lsec = ltype == 0 ? hs + regen : (ltype == 1 ? hs + 1 : hs + csize);
+    if (lsec > bsize || (ltype >= 2 && csize == 0)) return false;
+    *h = LitHdr{ltype, nstreams, regen, csize, hs, lsec};
+    return true;
+}
+
+// A compressed block (RFC 8878 3.1.1.3) of bsize bytes at b, its output
+// appended at out (frame output starts at fstart).  Returns an error code.
+ZHD int decode_compressed_block(Workspace *ws, const Job &job, const uint8_t *b, uint32_t bsize,
+                                uint64_t fstart, uint64_t *out, int lane, int nl) {
+    // ---- literals section header
+    LitHdr h;
+    if (!lit_header(b, bsize, &h)) return E_CORRUPT;
+    const int ltype = h.ltype, nstreams = h.nstreams;
+    const uint32_t regen = h.regen, csize = h.csize, hs = h.hs;
     const uint8_t *lit = nullptr;  // the literals, or null for RLE
     uint8_t rle_byte = 0;
-    uint32_t lsec;  // bytes of the literals section
+    const uint32_t lsec = h.lsec;  // bytes of the literals section
     if (ltype == 0) {
-        lsec = hs + regen;
-        if (lsec > bsize) return E_CORRUPT;
         lit = b + hs;
     } else if (ltype == 1) {
-        lsec = hs + 1;
-        if (lsec > bsize) return E_CORRUPT;
         rle_byte = b[hs];
     } else {
-        lsec = hs + csize;
-        if (lsec > bsize || csize == 0) return E_CORRUPT;
         const uint8_t *p = b + hs, *pe = b + hs + csize;
         if (lane == 0) {
             ws->err = OK;
             if (ltype == 2) {
-                const int h = huf_read_table(ws, p, (size_t)(pe - p));
-                if (h < 0) ws->err = E_CORRUPT;
-                else p += h;
+                const int used = huf_read_table(ws, p, (size_t)(pe - p));
+                if (used < 0) ws->err = E_CORRUPT;
+                else p += used;
             } else if (ws->huf_log < 0) {
                 ws->err = E_CORRUPT;  // treeless without an earlier table
             }
@@ -833,27 +935,7 @@ ZHD int decode_compressed_block(Workspace *ws, const Job &job, const uint8_t *b,
         // is its literals: they are decoded straight into the output
         const bool direct = lsec + 1 == bsize && b[lsec] == 0 && *out + regen <= job.cap;
         uint8_t *ld = direct ? job.dst + *out : job.lit;
-        if (nstreams == 1) {
-            if (lane == 0) ws->err = huf_stream(ws, p, pe, ld, regen) ? OK : E_CORRUPT;
-        } else {
-            if (pe - p < 6) return E_CORRUPT;
-            const uint32_t s1 = rd16(p), s2 = rd16(p + 2), s3 = rd16(p + 4);
-            const uint8_t *q = p + 6;
-            const uint64_t total = (uint64_t)(pe - q);
-            if ((uint64_t)s1 + s2 + s3 > total) return E_CORRUPT;
-            const uint32_t seg = (regen + 3) / 4;
-            if (regen < 6 || 3 * seg > regen) return E_CORRUPT;  // libzstd: >= 6 for 4 streams
-            const uint8_t *st[5] = {q, q + s1, q + s1 + s2, q + s1 + s2 + s3, pe};
-            if (lane == 0) ws->err = OK;
-            warp_sync();
-            for (int k = lane; k < 4; k += nl) {
-                const uint32_t n = k < 3 ? seg : regen - 3 * seg;
-                if (!huf_stream(ws, st[k], st[k + 1], ld + (uint64_t)k * seg, n))
-                    ws->err = E_CORRUPT;
-            }
-        }
-        warp_sync();
-        if (ws->err) return ws->err;
+        if (!lit_streams(ws, p, pe, nstreams, regen, ld, lane, nl)) return E_CORRUPT;
         if (direct) {
             *out += regen;
             return OK;
@@ -1130,6 +1212,155 @@ ZHD Result decode(Workspace *ws, const Job &job, int lane, int nl, uint64_t *acc
     }
     r.written = o;
     return r;
+}
+
+// ---- block-parallel frames -----------------------------------------------
+//
+// A frame whose blocks carry no sequences (raw and RLE blocks, compressed
+// blocks whose sequence section is the single byte 0) has every block's
+// output size in its headers, so its blocks decode independently: the plan
+// below walks the block headers (one thread per job) and lists each block
+// with its output offset and the Huffman description it uses (its own, or
+// for treeless literals the last one before it).  Any other job, and any
+// job a block of which fails, goes through decode() whole, which also
+// gives every error its serial code and position.
+
+struct BlockDesc {
+    uint64_t src;   // block content offset in the job's input
+    uint64_t out;   // output offset in the job's output
+    uint64_t tbl;   // Huffman description offset in the job's input (types 2, 3)
+    uint32_t job;
+    uint32_t meta;  // bits 0-17 content bytes (RLE: output bytes), 18-19 block
+                    // type (3: no block), 20-27 description bytes
+};
+
+struct JobPlan {
+    uint64_t total;    // output bytes
+    uint64_t ckpos;    // input offset of the content checksum, or ~0
+    uint64_t lastpos;  // input offset of the last block header
+    uint32_t mode;     // 1: block-parallel
+    uint32_t fail;     // set when a block did not decode
+};
+
+// Bytes of the Huffman description starting with byte hb (RFC 8878 4.2.1).
+ZHD uint32_t huf_desc_bytes(uint8_t hb) {
+    return hb < 128 ? 1u + hb : 1u + ((uint32_t)(hb - 127) + 1) / 2;
+}
+
+// Walks the single zstd frame of a job.  True when it is block-parallel;
+// *count = its blocks, written to d when d is not null.
+ZHD bool plan_job(const uint8_t *src, uint64_t len, uint64_t cap, uint32_t job, JobPlan *jp,
+                  BlockDesc *d, uint32_t *count) {
+    *count = 0;
+    if (len < 4 || rd32(src) != MAGIC) return false;
+    uint64_t p = 4;
+    if (p >= len) return false;
+    const int fhd = src[p++];
+    const int fcs_flag = fhd >> 6, single = (fhd >> 5) & 1, cksum = (fhd >> 2) & 1;
+    if ((fhd & 0x08) || (fhd & 3)) return false;  // reserved bit, dictionary id
+    const int fcs_bytes = fcs_flag == 0 ? (single ? 1 : 0) : (fcs_flag == 1 ? 2 : (fcs_flag == 2 ? 4 : 8));
+    if (len - p < (uint64_t)(single ? 0 : 1) + fcs_bytes) return false;
+    if (!single && 10 + (src[p++] >> 3) > 31) return false;
+    uint64_t fcs = 0;
+    for (int i = 0; i < fcs_bytes; i++) fcs |= (uint64_t)src[p + i] << (8 * i);
+    if (fcs_bytes == 2) fcs += 256;
+    p += fcs_bytes;
+    uint64_t o = 0, tbl = 0;
+    uint32_t tbl_len = 0, n = 0;
+    for (;;) {
+        if (len - p < 3) return false;
+        const uint64_t hdr = p;
+        const uint32_t bh = rd24(src + p);
+        p += 3;
+        const int last = bh & 1, type = (bh >> 1) & 3;
+        const uint32_t bsize = bh >> 3;
+        if (type == 3 || bsize > BLOCK_MAX || (type == 2 && bsize == BLOCK_MAX)) return false;
+        uint64_t bout;
+        uint32_t dlen = 0;
+        if (type == 0) {
+            if (len - p < bsize) return false;
+            bout = bsize;
+        } else if (type == 1) {
+            if (len - p < 1) return false;
+            bout = bsize;
+        } else {
+            if (len - p < bsize) return false;
+            const uint8_t *b = src + p;
+            LitHdr h;
+            if (!lit_header(b, bsize, &h)) return false;
+            if (h.lsec + 1 != bsize || b[h.lsec] != 0) return false;  // sequences
+            if (h.ltype == 2) {
+                tbl = p + h.hs;
+                tbl_len = huf_desc_bytes(b[h.hs]);
+                if (tbl_len > h.csize) return false;
+            } else if (h.ltype == 3 && tbl_len == 0) {
+                return false;  // treeless without an earlier description
+            }
+            if (h.ltype >= 2) dlen = tbl_len;
+            bout = h.regen;
+        }
+        if (o + bout > cap) return false;
+        if (d) {
+            BlockDesc &e = d[n];
+            e.src = p;
+            e.out = o;
+            e.tbl = dlen ? tbl : 0;
+            e.job = job;
+            e.meta = bsize | ((uint32_t)type << 18) | (dlen << 20);
+        }
+        n++;
+        o += bout;
+        p += type == 1 ? 1 : bsize;
+        if (last) {
+            jp->lastpos = hdr;
+            break;
+        }
+    }
+    if (fcs_bytes && o != fcs) return false;
+    jp->ckpos = ~0ull;
+    if (cksum) {
+        if (len - p < 4) return false;
+        jp->ckpos = p;
+        p += 4;
+    }
+    if (p != len) return false;  // one frame per job
+    jp->total = o;
+    *count = n;
+    return true;
+}
+
+// One block of a block-parallel frame into dst (the job's output).  False
+// when it does not decode.  All lanes.
+template <class W>
+ZHD bool decode_block(W *ws, const uint8_t *src, const BlockDesc &e, uint8_t *dst, int lane, int nl) {
+    const uint32_t bsize = e.meta & 0x3FFFF, type = (e.meta >> 18) & 3, dlen = e.meta >> 20;
+    const uint8_t *b = src + e.src;
+    uint8_t *out = dst + e.out;
+    if (type == 0) {
+        coop_copy(out, b, bsize, lane, nl);
+        return true;
+    }
+    if (type == 1) {
+        coop_fill(out, b[0], bsize, lane, nl);
+        return true;
+    }
+    LitHdr h;
+    if (!lit_header(b, bsize, &h)) return false;
+    if (h.ltype == 0) {
+        coop_copy(out, b + h.hs, h.regen, lane, nl);
+        return true;
+    }
+    if (h.ltype == 1) {
+        coop_fill(out, b[h.hs], h.regen, lane, nl);
+        return true;
+    }
+    if (lane == 0) ws->err = huf_read_table(ws, src + e.tbl, dlen) == (int)dlen ? OK : E_CORRUPT;
+    warp_sync();
+    if (ws->err) return false;
+    huf_fill(ws, lane, nl);
+    warp_sync();
+    const uint8_t *p = b + h.hs + (h.ltype == 2 ? dlen : 0);
+    return lit_streams(ws, p, b + h.hs + h.csize, h.nstreams, h.regen, out, lane, nl);
 }
 
 }  // namespace zs

@@ -1,24 +1,106 @@
-// GPU Zstandard decode: one warp per job (a byte range holding one or more
-// concatenated frames), several warps per CTA, persistent over the job list.
-// The decoder itself is zstd_core.cuh; this file holds the kernel and its
-// launcher.  Each warp owns a workspace in shared memory (FSE / Huffman
-// tables, repeat offsets, a batch of decoded sequences) and a literal
-// scratch area of 128 KiB in device memory.
+// GPU Zstandard decode of a list of jobs (a job: a byte range of the input
+// holding one or more concatenated frames, and its output range).  The
+// decoder itself is zstd_core.cuh; this file holds the kernels and the
+// launch sequence:
+//
+//   1. zstd_plan_kernel, a thread per job: a job holding one frame whose
+//      blocks carry no sequences (the usual form of compressed weights:
+//      Huffman-coded literals, raw and RLE blocks) is planned block-parallel
+//      and its blocks appended to a descriptor pool;
+//   2. zstd_block_kernel, a warp per pooled block: the block's literals
+//      straight into the output, with a small workspace (Huffman table) so
+//      that many warps share an SM;
+//   3. zstd_frame_kernel, a warp per job: the content checksum of a
+//      block-parallel job, or the whole serial decode (sequences, repeat
+//      offsets, every frame form) of any other job and of a block-parallel
+//      job one of whose blocks failed, which also reports the error.
+//
+// Each frame-kernel warp owns a workspace in shared memory (FSE / Huffman
+// tables, repeat offsets, a batch of decoded sequences) and 128 KiB of
+// literal scratch in device memory.
 #include "common.cuh"
 #include "zstd_core.cuh"
 
 namespace hct {
 namespace {
 
-constexpr int ZWARPS = 4;  // warps (jobs in flight) per CTA
+constexpr int ZWARPS = 4;  // frame kernel: warps (jobs in flight) per CTA
 #ifndef ZSTD_MIN_CTAS
-#define ZSTD_MIN_CTAS 2  // resident CTAs per SM the register budget allows
+#define ZSTD_MIN_CTAS 3  // resident frame-kernel CTAs per SM the register budget allows
 #endif
 constexpr uint64_t ZSTD_GRID_CAP = 148ull * ZSTD_MIN_CTAS;
+constexpr int BWARPS = 4;     // block kernel: warps per CTA
+constexpr int BMIN_CTAS = 5;  // resident block-kernel CTAs per SM
+constexpr uint32_t PLAN_THREADS = 128;
 
-__global__ void __launch_bounds__(ZWARPS * 32, ZSTD_MIN_CTAS) zstd_decode_kernel(
+// Scratch layout: frame-kernel literal scratch, then the job plans, the
+// pool counter and the block descriptor pool.
+struct ScratchLayout {
+    size_t lit, plans, counter, pool, total;
+    uint32_t pool_cap;
+};
+
+ScratchLayout scratch_layout(uint32_t n) {
+    ScratchLayout L;
+    const uint64_t ctas = ((uint64_t)n + ZWARPS - 1) / ZWARPS;
+    const uint64_t grid = ctas < ZSTD_GRID_CAP ? (ctas ? ctas : 1) : ZSTD_GRID_CAP;
+    L.lit = 0;
+    L.plans = grid * ZWARPS * zs::LIT_SCRATCH;
+    L.counter = L.plans + (((size_t)n * sizeof(zs::JobPlan) + 255) & ~(size_t)255);
+    L.pool = L.counter + 256;
+    L.pool_cap = 4 * n + 16384;  // blocks; a job that does not fit is decoded serially
+    L.total = L.pool + (size_t)L.pool_cap * sizeof(zs::BlockDesc);
+    return L;
+}
+
+__global__ void __launch_bounds__(PLAN_THREADS) zstd_plan_kernel(
     const uint8_t *__restrict__ src, const hct_b200_zstd_job *__restrict__ jobs, uint32_t n,
-    uint8_t *dst, hct_b200_status *__restrict__ status, uint8_t *scratch) {
+    zs::JobPlan *__restrict__ plans, zs::BlockDesc *__restrict__ pool, uint32_t *pool_used,
+    uint32_t pool_cap) {
+    const uint32_t j = blockIdx.x * PLAN_THREADS + threadIdx.x;
+    if (j >= n) return;
+    const hct_b200_zstd_job jd = jobs[j];
+    zs::JobPlan jp{0, ~0ull, 0, 0, 0};
+    uint32_t cnt = 0;
+    bool par = zs::plan_job(src + jd.src_off, jd.src_len, jd.dst_cap, j, &jp, nullptr, &cnt);
+    if (par) {
+        const uint32_t base = atomicAdd(pool_used, cnt);
+        if ((uint64_t)base + cnt <= pool_cap) {
+            zs::plan_job(src + jd.src_off, jd.src_len, jd.dst_cap, j, &jp, pool + base, &cnt);
+        } else {
+            par = false;  // pool full: mark the reserved slots empty
+            for (uint64_t i = base; i < pool_cap && i < (uint64_t)base + cnt; i++)
+                pool[i].meta = 3u << 18;
+        }
+    }
+    jp.mode = par ? 1 : 0;
+    plans[j] = jp;
+}
+
+__global__ void __launch_bounds__(BWARPS * 32, BMIN_CTAS) zstd_block_kernel(
+    const uint8_t *__restrict__ src, const hct_b200_zstd_job *__restrict__ jobs,
+    zs::JobPlan *plans, const zs::BlockDesc *__restrict__ pool, const uint32_t *pool_used,
+    uint32_t pool_cap, uint8_t *dst) {
+    __shared__ zs::HufWs hws[BWARPS];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    zs::HufWs *ws = hws + warp;
+    const uint32_t used0 = *pool_used;
+    const uint32_t used = used0 < pool_cap ? used0 : pool_cap;
+    const uint32_t nw = gridDim.x * BWARPS;
+    for (uint32_t i = blockIdx.x * BWARPS + warp; i < used; i += nw) {
+        const zs::BlockDesc e = pool[i];
+        if (((e.meta >> 18) & 3) == 3) continue;
+        const hct_b200_zstd_job jd = jobs[e.job];
+        const bool ok = zs::decode_block(ws, src + jd.src_off, e, dst + jd.dst_off, lane, 32);
+        if (!ok && lane == 0) plans[e.job].fail = 1;
+        __syncwarp();
+    }
+}
+
+__global__ void __launch_bounds__(ZWARPS * 32, ZSTD_MIN_CTAS) zstd_frame_kernel(
+    const uint8_t *__restrict__ src, const hct_b200_zstd_job *__restrict__ jobs, uint32_t n,
+    const zs::JobPlan *__restrict__ plans, uint8_t *dst, hct_b200_status *__restrict__ status,
+    uint8_t *scratch) {
     extern __shared__ uint8_t zsm[];
     __shared__ uint64_t acc[ZWARPS][4];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -28,8 +110,23 @@ __global__ void __launch_bounds__(ZWARPS * 32, ZSTD_MIN_CTAS) zstd_decode_kernel
     uint8_t *lit = scratch + gw * zs::LIT_SCRATCH;
     for (uint64_t j = gw; j < n; j += nw) {
         const hct_b200_zstd_job jd = jobs[j];
-        const zs::Job job{src + jd.src_off, jd.src_len, dst + jd.dst_off, jd.dst_cap, lit};
-        const zs::Result r = zs::decode(ws, job, lane, 32, acc[warp]);
+        const zs::JobPlan jp = plans[j];
+        zs::Result r;
+        if (jp.mode == 1 && jp.fail == 0) {
+            // block-parallel job: its blocks are decoded; check the checksum
+            r = zs::Result{zs::OK, jp.lastpos, jp.total};
+            if (jp.ckpos != ~0ull) {
+                const uint64_t h = zs::xxh64(dst + jd.dst_off, jp.total, lane, 32, acc[warp],
+                                             reinterpret_cast<uint64_t *>(ws->huf));
+                if ((uint32_t)h != zs::rd32(src + jd.src_off + jp.ckpos)) {
+                    r.code = zs::E_CHECKSUM;
+                    r.pos = jp.ckpos;
+                }
+            }
+        } else {
+            const zs::Job job{src + jd.src_off, jd.src_len, dst + jd.dst_off, jd.dst_cap, lit};
+            r = zs::decode(ws, job, lane, 32, acc[warp]);
+        }
         if (lane == 0) {
             hct_b200_status st;
             st.code = r.code;
@@ -45,25 +142,34 @@ __global__ void __launch_bounds__(ZWARPS * 32, ZSTD_MIN_CTAS) zstd_decode_kernel
 
 }  // namespace
 
-size_t zstd_scratch_bytes(uint32_t n) {
-    const uint64_t ctas = ((uint64_t)n + ZWARPS - 1) / ZWARPS;
-    const uint64_t cap = ZSTD_GRID_CAP;
-    return (size_t)((ctas < cap ? (ctas ? ctas : 1) : cap) * ZWARPS * zs::LIT_SCRATCH);
-}
+size_t zstd_scratch_bytes(uint32_t n) { return scratch_layout(n).total; }
 
 cudaError_t launch_zstd_decode(const uint8_t *d_src, const hct_b200_zstd_job *d_jobs, uint32_t n,
                                uint8_t *d_dst, hct_b200_status *d_status, uint8_t *d_scratch,
                                cudaStream_t s) {
     if (n == 0) return cudaSuccess;
-    const size_t smem = sizeof(zs::Workspace) * ZWARPS;
-    cudaError_t e = cudaFuncSetAttribute(zstd_decode_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const ScratchLayout L = scratch_layout(n);
+    zs::JobPlan *plans = reinterpret_cast<zs::JobPlan *>(d_scratch + L.plans);
+    uint32_t *counter = reinterpret_cast<uint32_t *>(d_scratch + L.counter);
+    zs::BlockDesc *pool = reinterpret_cast<zs::BlockDesc *>(d_scratch + L.pool);
+    cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(uint32_t), s);
     if (e != cudaSuccess) return e;
-    // as many CTAs as zstd_scratch_bytes provides scratch for
+    zstd_plan_kernel<<<(n + PLAN_THREADS - 1) / PLAN_THREADS, PLAN_THREADS, 0, s>>>(
+        d_src, d_jobs, n, plans, pool, counter, L.pool_cap);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    // persistent: every warp loops over the pooled blocks
+    zstd_block_kernel<<<148 * BMIN_CTAS, BWARPS * 32, 0, s>>>(d_src, d_jobs, plans, pool, counter,
+                                                               L.pool_cap, d_dst);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const size_t smem = sizeof(zs::Workspace) * ZWARPS;
+    e = cudaFuncSetAttribute(zstd_frame_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+    if (e != cudaSuccess) return e;
+    // as many CTAs as the literal scratch provides for
     const uint64_t ctas = ((uint64_t)n + ZWARPS - 1) / ZWARPS;
     const uint64_t grid = ctas < ZSTD_GRID_CAP ? ctas : ZSTD_GRID_CAP;
-    zstd_decode_kernel<<<(unsigned)grid, ZWARPS * 32, smem, s>>>(d_src, d_jobs, n, d_dst, d_status,
-                                                                 d_scratch);
+    zstd_frame_kernel<<<(unsigned)grid, ZWARPS * 32, smem, s>>>(d_src, d_jobs, n, plans, d_dst,
+                                                                d_status, d_scratch + L.lit);
     return cudaGetLastError();
 }
 

@@ -113,3 +113,75 @@ def test_corrupted_frames_error_where_libzstd_does(hb):
             else:
                 agree += 1
     assert agree >= 100, (agree, stricter)
+
+
+def _run_jobs(hb, dev, srcs, caps):
+    import torch
+
+    jobs = np.zeros(len(srcs), dtype=hb.ZSTD_JOB)
+    so = do = 0
+    for i, (c, cap) in enumerate(zip(srcs, caps)):
+        jobs[i] = (so, len(c), do, cap)
+        so += (len(c) + 15) // 16 * 16
+        do += (cap + 15) // 16 * 16
+    src = np.zeros(max(so, 16), np.uint8)
+    for i, c in enumerate(srcs):
+        src[jobs[i]["src_off"]: jobs[i]["src_off"] + len(c)] = np.frombuffer(c, np.uint8)
+    d_dst = torch.zeros(max(do, 16), dtype=torch.uint8, device=dev)
+    st = hb.ZstdDecompressor().decompress_jobs(torch.from_numpy(src).to(dev), jobs, d_dst)
+    return jobs, st, d_dst.cpu().numpy()
+
+
+def test_large_frames_block_parallel(hb, dev):
+    """Frames of many 128 KiB blocks (the form of a zstd-compressed weight
+    fragment: sequence-free blocks, decoded block-parallel) beside frames
+    with sequences (decoded whole), checksums on and off, in one launch."""
+    from oracle import zstd_ref as Z
+
+    specs = [("fp16", 8 << 20, 3, True), ("fp16", 6_000_001, 1, False), ("f32", 4 << 20, 9, True),
+             ("zeros", 3 << 20, 3, True), ("random", 1 << 20, 3, False), ("text", 2 << 20, 3, True),
+             ("fp16", 65536, 3, True), ("f32", 777_777, 19, False)]
+    refs = [_data(k, n, 40 + i) for i, (k, n, lv, ck) in enumerate(specs)]
+    srcs = [Z.compress(d, lv, checksum=ck) for d, (k, n, lv, ck) in zip(refs, specs)]
+    jobs, st, out = _run_jobs(hb, dev, srcs, [len(d) + 64 for d in refs])
+    for i, d in enumerate(refs):
+        assert st[i]["code"] == 0, (specs[i], st[i])
+        assert st[i]["written"] == len(d), specs[i]
+        o = int(jobs[i]["dst_off"])
+        assert out[o: o + len(d)].tobytes() == d, specs[i]
+
+
+def test_large_frames_errors(hb, dev):
+    """Block-parallel frames that fail: a damaged block, a damaged checksum,
+    a too-small output; each reports what the serial decode reports."""
+    from oracle import zstd_ref as Z
+
+    d = _data("fp16", 4 << 20, 7)
+    good = Z.compress(d, 3, checksum=True)
+    rng = np.random.default_rng(3)
+    srcs, caps, expect = [], [], []
+    for t in range(6):  # damage inside the block data
+        c = bytearray(good)
+        c[int(rng.integers(len(c) // 4, len(c) - 8))] ^= int(rng.integers(1, 256))
+        srcs.append(bytes(c))
+        caps.append(len(d) + 64)
+        expect.append(Z.decompress(bytes(c), len(d) + 64)[0])
+    c = bytearray(good)
+    c[-2] ^= 0x10  # checksum
+    srcs.append(bytes(c))
+    caps.append(len(d) + 64)
+    expect.append(False)
+    srcs.append(good)  # output one byte short
+    caps.append(len(d) - 1)
+    expect.append(False)
+    jobs, st, out = _run_jobs(hb, dev, srcs, caps)
+    for i, ok in enumerate(expect):
+        if not ok:
+            assert st[i]["code"] != 0, (i, st[i])
+        elif st[i]["code"] == 0:
+            o = int(jobs[i]["dst_off"])
+            assert out[o: o + len(d)].tobytes() == Z.decompress(srcs[i], len(d) + 64)[1]
+    from haagenti_b200 import _lib as L
+
+    assert st[6]["code"] == L.CHECKSUM
+    assert st[7]["code"] == L.BUFFER_TOO_SMALL
