@@ -896,8 +896,11 @@ ZHD bool lit_header(const uint8_t *b, uint32_t bsize, LitHdr *h) {
 
 // A compressed block (RFC 8878 3.1.1.3) of bsize bytes at b, its output
 // appended at out (frame output starts at fstart).  Returns an error code.
+// prelit: the block's Huffman literals, already decoded (the Huffman table
+// is then left as it was).
 ZHD int decode_compressed_block(Workspace *ws, const Job &job, const uint8_t *b, uint32_t bsize,
-                                uint64_t fstart, uint64_t *out, int lane, int nl) {
+                                uint64_t fstart, uint64_t *out, int lane, int nl,
+                                const uint8_t *prelit = nullptr) {
     // ---- literals section header
     LitHdr h;
     if (!lit_header(b, bsize, &h)) return E_CORRUPT;
@@ -910,6 +913,8 @@ ZHD int decode_compressed_block(Workspace *ws, const Job &job, const uint8_t *b,
         lit = b + hs;
     } else if (ltype == 1) {
         rle_byte = b[hs];
+    } else if (prelit) {  // Huffman literals decoded beforehand
+        lit = prelit;
     } else {
         const uint8_t *p = b + hs, *pe = b + hs + csize;
         if (lane == 0) {
@@ -1216,14 +1221,19 @@ ZHD Result decode(Workspace *ws, const Job &job, int lane, int nl, uint64_t *acc
 
 // ---- block-parallel frames -----------------------------------------------
 //
-// A frame whose blocks carry no sequences (raw and RLE blocks, compressed
-// blocks whose sequence section is the single byte 0) has every block's
-// output size in its headers, so its blocks decode independently: the plan
+// Every block of a frame written by zstd's encoder regenerates one block
+// size, min(128 KiB, window), except the last, which regenerates the rest of
+// the frame content size: so its blocks decode independently.  The plan
 // below walks the block headers (one thread per job) and lists each block
 // with its output offset and the Huffman description it uses (its own, or
-// for treeless literals the last one before it).  Any other job, and any
-// job a block of which fails, goes through decode() whole, which also
-// gives every error its serial code and position.
+// for treeless literals the last one before it).  Raw, RLE and
+// sequence-free compressed blocks (whose sizes the headers give) go to the
+// block kernel; blocks with sequences (taken to regenerate one block size)
+// are decoded after them, in order, by the frame kernel, which carries the
+// repeat offsets and sequence tables from one to the next and checks each
+// size.  A job that is not one frame of that form, a block that fails, or a
+// size that differs sends the job through decode() whole, which also gives
+// every error its serial code and position.
 
 struct BlockDesc {
     uint64_t src;   // block content offset in the job's input
@@ -1231,8 +1241,13 @@ struct BlockDesc {
     uint64_t tbl;   // Huffman description offset in the job's input (types 2, 3)
     uint32_t job;
     uint32_t meta;  // bits 0-17 content bytes (RLE: output bytes), 18-19 block
-                    // type (3: no block), 20-27 description bytes
+                    // type (3: no block), 20-27 description bytes, 28: has
+                    // sequences
+    uint32_t slot;  // blocks with sequences: literal slot the block kernel
+                    // decodes the Huffman literals into, or ~0
+    uint32_t pad;
 };
+constexpr uint32_t META_SEQ = 1u << 28;
 
 struct JobPlan {
     uint64_t total;    // output bytes
@@ -1240,6 +1255,10 @@ struct JobPlan {
     uint64_t lastpos;  // input offset of the last block header
     uint32_t mode;     // 1: block-parallel
     uint32_t fail;     // set when a block did not decode
+    uint32_t base;     // its first block descriptor
+    uint32_t count;    // its blocks
+    uint32_t nseq;     // of them with sequences
+    uint32_t bsz;      // one block size (the regenerated size of a block with sequences)
 };
 
 // Bytes of the Huffman description starting with byte hb (RFC 8878 4.2.1).
@@ -1260,13 +1279,20 @@ ZHD bool plan_job(const uint8_t *src, uint64_t len, uint64_t cap, uint32_t job, 
     if ((fhd & 0x08) || (fhd & 3)) return false;  // reserved bit, dictionary id
     const int fcs_bytes = fcs_flag == 0 ? (single ? 1 : 0) : (fcs_flag == 1 ? 2 : (fcs_flag == 2 ? 4 : 8));
     if (len - p < (uint64_t)(single ? 0 : 1) + fcs_bytes) return false;
-    if (!single && 10 + (src[p++] >> 3) > 31) return false;
+    uint64_t window = 0;
+    if (!single) {
+        const int wd = src[p++], wlog = 10 + (wd >> 3);
+        if (wlog > 31) return false;
+        window = (1ull << wlog) + ((1ull << wlog) >> 3) * (wd & 7);
+    }
     uint64_t fcs = 0;
     for (int i = 0; i < fcs_bytes; i++) fcs |= (uint64_t)src[p + i] << (8 * i);
     if (fcs_bytes == 2) fcs += 256;
     p += fcs_bytes;
+    if (single) window = fcs;
+    const uint32_t bsz = (uint32_t)(window < BLOCK_MAX ? window : BLOCK_MAX);
     uint64_t o = 0, tbl = 0;
-    uint32_t tbl_len = 0, n = 0;
+    uint32_t tbl_len = 0, n = 0, nseq = 0;
     for (;;) {
         if (len - p < 3) return false;
         const uint64_t hdr = p;
@@ -1277,6 +1303,7 @@ ZHD bool plan_job(const uint8_t *src, uint64_t len, uint64_t cap, uint32_t job, 
         if (type == 3 || bsize > BLOCK_MAX || (type == 2 && bsize == BLOCK_MAX)) return false;
         uint64_t bout;
         uint32_t dlen = 0;
+        bool seq = false;
         if (type == 0) {
             if (len - p < bsize) return false;
             bout = bsize;
@@ -1288,7 +1315,7 @@ ZHD bool plan_job(const uint8_t *src, uint64_t len, uint64_t cap, uint32_t job, 
             const uint8_t *b = src + p;
             LitHdr h;
             if (!lit_header(b, bsize, &h)) return false;
-            if (h.lsec + 1 != bsize || b[h.lsec] != 0) return false;  // sequences
+            seq = h.lsec + 1 != bsize || b[h.lsec] != 0;
             if (h.ltype == 2) {
                 tbl = p + h.hs;
                 tbl_len = huf_desc_bytes(b[h.hs]);
@@ -1298,6 +1325,12 @@ ZHD bool plan_job(const uint8_t *src, uint64_t len, uint64_t cap, uint32_t job, 
             }
             if (h.ltype >= 2) dlen = tbl_len;
             bout = h.regen;
+            if (seq) {  // one block size; the last block the rest of the content
+                if (last && !fcs_bytes) return false;
+                bout = last ? (fcs >= o ? fcs - o : 0) : bsz;
+                if (bout < h.regen || bout > BLOCK_MAX) return false;
+                nseq++;
+            }
         }
         if (o + bout > cap) return false;
         if (d) {
@@ -1306,7 +1339,9 @@ ZHD bool plan_job(const uint8_t *src, uint64_t len, uint64_t cap, uint32_t job, 
             e.out = o;
             e.tbl = dlen ? tbl : 0;
             e.job = job;
-            e.meta = bsize | ((uint32_t)type << 18) | (dlen << 20);
+            e.meta = bsize | ((uint32_t)type << 18) | (dlen << 20) | (seq ? META_SEQ : 0);
+            e.slot = ~0u;
+            e.pad = 0;
         }
         n++;
         o += bout;
@@ -1325,15 +1360,18 @@ ZHD bool plan_job(const uint8_t *src, uint64_t len, uint64_t cap, uint32_t job, 
     }
     if (p != len) return false;  // one frame per job
     jp->total = o;
+    jp->count = n;
+    jp->nseq = nseq;
+    jp->bsz = bsz;
     *count = n;
     return true;
 }
 
-// One block of a block-parallel frame into dst (the job's output).  False
-// when it does not decode.  All lanes.
+// One block without sequences of a block-parallel frame into dst (the
+// job's output).  False when it does not decode.  All lanes.
 template <class W>
 ZHD bool decode_block(W *ws, const uint8_t *src, const BlockDesc &e, uint8_t *dst, int lane, int nl) {
-    const uint32_t bsize = e.meta & 0x3FFFF, type = (e.meta >> 18) & 3, dlen = e.meta >> 20;
+    const uint32_t bsize = e.meta & 0x3FFFF, type = (e.meta >> 18) & 3, dlen = (e.meta >> 20) & 0xFF;
     const uint8_t *b = src + e.src;
     uint8_t *out = dst + e.out;
     if (type == 0) {
@@ -1361,6 +1399,43 @@ ZHD bool decode_block(W *ws, const uint8_t *src, const BlockDesc &e, uint8_t *ds
     warp_sync();
     const uint8_t *p = b + h.hs + (h.ltype == 2 ? dlen : 0);
     return lit_streams(ws, p, b + h.hs + h.csize, h.nstreams, h.regen, out, lane, nl);
+}
+
+// The blocks with sequences of a block-parallel job, in order, after every
+// other block is in place (matches read earlier blocks' output): the serial
+// block decoder with the frame's repeat offsets and sequence tables carried
+// from one to the next.  False when one fails or regenerates another size
+// than planned.  All lanes.
+ZHD bool decode_seq_blocks(Workspace *ws, const Job &job, const JobPlan &jp, const BlockDesc *d,
+                           const uint8_t *slots, int lane, int nl) {
+    if (lane == 0) {
+        ws->rep[0] = 1;
+        ws->rep[1] = 4;
+        ws->rep[2] = 8;
+        ws->ll_log = ws->ml_log = ws->of_log = ws->huf_log = -1;
+    }
+    warp_sync();
+    uint64_t built = ~0ull;  // description the Huffman table holds
+    for (uint32_t i = 0; i < jp.count; i++) {
+        const BlockDesc e = d[i];
+        if (!(e.meta & META_SEQ)) continue;
+        const uint32_t bsize = e.meta & 0x3FFFF, dlen = (e.meta >> 20) & 0xFF;
+        const uint8_t *b = job.src + e.src;
+        const uint8_t *pre = (b[0] & 3) >= 2 && e.slot != ~0u ? slots + (uint64_t)e.slot * LIT_SCRATCH : nullptr;
+        if (!pre && (b[0] & 3) == 3 && built != e.tbl) {  // treeless: the last description's table
+            if (lane == 0) ws->err = huf_read_table(ws, job.src + e.tbl, dlen) == (int)dlen ? OK : E_CORRUPT;
+            warp_sync();
+            if (ws->err) return false;
+            huf_fill(ws, lane, nl);
+            warp_sync();
+        }
+        if (!pre && (b[0] & 3) >= 2) built = e.tbl;
+        uint64_t o = e.out;
+        if (decode_compressed_block(ws, job, b, bsize, 0, &o, lane, nl, pre) != OK) return false;
+        const uint64_t want = (i + 1 == jp.count) ? jp.total - e.out : jp.bsz;
+        if (o - e.out != want) return false;
+    }
+    return true;
 }
 
 }  // namespace zs

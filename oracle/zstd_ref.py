@@ -87,3 +87,10 @@ def decompress(data: bytes, capacity: int):
     if L.ZSTD_isError(n):
         return False, L.ZSTD_getErrorName(n).decode()
     return True, out.raw[:n]
+
+
+def decompress_into(data: bytes, buf) -> int:
+    """ZSTD_decompress into a preallocated ctypes buffer: bytes written, or -1."""
+    L = lib()
+    n = L.ZSTD_decompress(buf, len(buf), data, len(data))
+    return -1 if L.ZSTD_isError(n) else int(n)
