@@ -35,7 +35,7 @@ __all__ = [
     "Unsupported", "DeviceError", "Context", "Lz4Decompressor", "dequantize_int4",
     "dequantize_int4_mp", "idct_2d",
     "spectral_q4_decode", "HctReader", "HctReaderV2", "HctV3Decoder", "hct_v3_decode",
-    "HoloTensorReader", "ZstdDecompressor", "zstd_decompress", "F32",
+    "HoloTensorReader", "ZstdDecompressor", "ZstdGpuPipeline", "zstd_decompress", "F32",
     "F16", "BF16", "FLAG_SPECTRAL_Q4",
 ]
 
@@ -434,6 +434,77 @@ class ZstdDecompressor:
 def zstd_decompress(data, ctx: Context | None = None) -> bytes:
     """``zstd::decode_all(data)`` on the GPU."""
     return ZstdDecompressor(ctx).decompress(data)
+
+
+class ZstdGpuPipeline:
+    """The reference's GPU zstd pipeline interface
+    (crates/haagenti-cuda/src/zstd_gpu.rs:348-402: is_ready, decompress,
+    decompress_with_dict, decompress_batch, decompress_to_gpu), decoding on the
+    GPU: a batch in one launch, ``decompress_to_gpu`` without a host round trip
+    of the output.  Dictionaries are not supported (Unsupported)."""
+
+    def __init__(self, ctx: Context | None = None):
+        self.z = ZstdDecompressor(ctx)
+
+    @staticmethod
+    def is_ready() -> bool:
+        return True
+
+    def decompress(self, compressed) -> bytes:
+        return self.z.decompress(compressed)
+
+    def decompress_with_dict(self, compressed, dictionary) -> bytes:
+        raise Unsupported("zstd: dictionaries are not supported by the GPU decoder")
+
+    def _device_jobs(self, frames, sizes, stream=None):
+        torch = _torch()
+        dev = torch.device("cuda", self.z.ctx.device)
+        jobs = np.zeros(len(frames), dtype=ZSTD_JOB)
+        so = do = 0
+        for i, (f, n) in enumerate(zip(frames, sizes)):
+            jobs[i] = (so, len(f), do, n)
+            so += (len(f) + 15) // 16 * 16
+            do += (n + 15) // 16 * 16
+        src = np.zeros(max(so, 16), np.uint8)
+        for i, f in enumerate(frames):
+            src[int(jobs[i]["src_off"]): int(jobs[i]["src_off"]) + len(f)] = np.frombuffer(f, np.uint8)
+        d_dst = torch.empty(max(do, 16), dtype=torch.uint8, device=dev)
+        st = self.z.decompress_jobs(torch.from_numpy(src).to(dev), jobs, d_dst, stream)
+        return jobs, st, d_dst
+
+    def decompress_batch(self, frames) -> list:
+        """Every frame of the list in one launch (frames without a recorded
+        content size are decoded one by one with growing capacities)."""
+        frames = [bytes(f) for f in frames]
+        sizes = [self.z.content_size(f) if f else 0 for f in frames]
+        known = [i for i, n in enumerate(sizes) if n is not None]
+        out: list = [None] * len(frames)
+        if known:
+            jobs, st, d_dst = self._device_jobs([frames[i] for i in known],
+                                                [sizes[i] for i in known])
+            host = d_dst.cpu().numpy()
+            for k, i in enumerate(known):
+                _check(int(st[k]["code"]))
+                o = int(jobs[k]["dst_off"])
+                out[i] = host[o: o + int(st[k]["written"])].tobytes()
+        for i, n in enumerate(sizes):
+            if n is None:
+                out[i] = self.z.decompress(frames[i])
+        return out
+
+    def decompress_to_gpu(self, compressed, stream=None):
+        """The decoded bytes as a uint8 tensor on the context's device."""
+        f = bytes(compressed)
+        known = self.z.content_size(f) if f else 0
+        size = known if known is not None else max(4 * len(f), 4096)
+        while True:
+            jobs, st, d_dst = self._device_jobs([f], [size], stream)
+            code = int(st[0]["code"])
+            if code == L.BUFFER_TOO_SMALL and known is None and size < 1 << 32:
+                size *= 2
+                continue
+            _check(code)
+            return d_dst[: int(st[0]["written"])]
 
 
 ZSTD_JOB = np.dtype([("src_off", "<u8"), ("src_len", "<u8"), ("dst_off", "<u8"),

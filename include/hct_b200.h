@@ -290,7 +290,13 @@ int hct_b200_hct_v3_decode(hct_b200_ctx *ctx, const uint8_t *data, size_t len, u
  * libzstd; on corrupted input this decoder reports an error wherever libzstd
  * does and in some cases where libzstd's fast Huffman path returns data
  * (every literal stream must be consumed exactly).
- * jobs: one warp per job on the GPU, several jobs per launch; per-job status
+ * The reference's ZstdGpuPipeline (crates/haagenti-cuda/src/zstd_gpu.rs:
+ * 348-402: decompress, decompress_batch, decompress_to_gpu) maps onto these
+ * three calls (it decodes on the CPU; this decoder runs on the GPU).
+ * jobs: several jobs per launch.  A job holding one frame whose blocks
+ * regenerate the encoder's block size (min(128 KiB, window), the last one the
+ * rest of the content size) is decoded block-parallel, a warp per block;
+ * any other job by one warp.  Per-job status
  * {code, position = input offset of the failing frame or block, provided =
  * dst_cap, written}; codes HCT_B200_ERR_CORRUPTED, _BUFFER_TOO_SMALL,
  * _CHECKSUM, _UNSUPPORTED.  d_src is read only inside each job's range. */
