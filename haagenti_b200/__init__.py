@@ -454,7 +454,7 @@ class ZstdGpuPipeline:
         return self.z.decompress(compressed)
 
     def decompress_with_dict(self, compressed, dictionary) -> bytes:
-        raise Unsupported("zstd: dictionaries are not supported by the GPU decoder")
+        raise Unsupported(L.UNSUPPORTED, "zstd: dictionaries are not supported by the GPU decoder")
 
     def _device_jobs(self, frames, sizes, stream=None):
         torch = _torch()
