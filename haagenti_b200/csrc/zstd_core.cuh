@@ -473,9 +473,7 @@ struct BitWin {
     const uint8_t *s, *e;
     const uint32_t *base;
     int32_t lo, pos, w;
-    uint32_t hi, lo_w;          // words w and w - 1
-    uint32_t q1, q2, q3, q4;    // words w - 2 .. w - 5, loaded ahead (an L2
-                                // round trip is ~17 symbols of decode)
+    uint32_t hi, lo_w, nx;  // words w, w - 1 and (loaded ahead) w - 2
 
     ZHD uint32_t word(int32_t i) const {
 #if defined(__CUDA_ARCH__)
@@ -504,10 +502,7 @@ struct BitWin {
         w = (pos - 1) >> 5;
         hi = word(w);
         lo_w = word(w - 1);
-        q1 = word(w - 2);
-        q2 = word(w - 3);
-        q3 = word(w - 4);
-        q4 = word(w - 5);
+        nx = word(w - 2);
         return true;
     }
     // the next n <= 31 bits (sh reaches 64 only for n == 0, masked to 0)
@@ -516,15 +511,30 @@ struct BitWin {
         return (uint32_t)((((uint64_t)hi << 32) | lo_w) >> sh) & ((1u << n) - 1);
     }
     ZHD void slide() {
-        if (pos <= w * 32) {  // predicated: the lanes of a warp run different streams
-            w--;
-            hi = lo_w;
-            lo_w = q1;
-            q1 = q2;
-            q2 = q3;
-            q3 = q4;
-            q4 = word(w - 5);
-        }
+        // selects, not a branch: the lanes of a warp run different streams
+        const bool c = pos <= w * 32;
+        w -= c ? 1 : 0;
+        hi = c ? lo_w : hi;
+        lo_w = c ? nx : lo_w;
+        nx = word(w - 2);
+    }
+    // the same while w >= 4: word w - 2 lies above the stream's first word
+    // and needs no masking
+    ZHD void slide_inner() {
+        const bool c = pos <= w * 32;
+        w -= c ? 1 : 0;
+        hi = c ? lo_w : hi;
+        lo_w = c ? nx : lo_w;
+#if defined(__CUDA_ARCH__)
+        nx = __ldg(base + (w - 2));
+#else
+        nx = word(w - 2);
+#endif
+    }
+    // peek for 1 <= n <= 31 (the shift then stays below 64)
+    ZHD uint32_t peek1(int n) const {
+        const uint32_t sh = (uint32_t)(pos - n - (w - 1) * 32);
+        return (uint32_t)((((uint64_t)hi << 32) | lo_w) >> sh) & ((1u << n) - 1);
     }
     ZHD uint32_t read(int n) {
         const uint32_t v = peek(n);
@@ -554,20 +564,27 @@ ZHD bool huf_stream(const W *ws, const uint8_t *s, const uint8_t *e, uint8_t *ou
         out[i] = (uint8_t)sym();
         br.slide();
     }
-    for (; i + 8 <= n; i += 8) {
+    // 8 symbols per step while the window stays 4+ words above the stream's
+    // start (8 symbols take at most 3 words)
+    auto sym1 = [&]() -> uint32_t {
+        const uint32_t d = ws->huf[br.peek1(log)];
+        br.pos -= (int32_t)(d >> 8);
+        return d & 0xFF;
+    };
+    for (; i + 8 <= n && br.w >= 8; i += 8) {
         uint32_t v0 = 0, v1 = 0;
 ZUNROLL
         for (int k = 0; k < 4; k += 2) {
-            const uint32_t a = sym();
-            const uint32_t b = sym();
-            br.slide();
+            const uint32_t a = sym1();
+            const uint32_t b = sym1();
+            br.slide_inner();
             v0 |= (a | (b << 8)) << (8 * k);
         }
 ZUNROLL
         for (int k = 0; k < 4; k += 2) {
-            const uint32_t a = sym();
-            const uint32_t b = sym();
-            br.slide();
+            const uint32_t a = sym1();
+            const uint32_t b = sym1();
+            br.slide_inner();
             v1 |= (a | (b << 8)) << (8 * k);
         }
         st_u64(out + i, (uint64_t)v0 | ((uint64_t)v1 << 32));
