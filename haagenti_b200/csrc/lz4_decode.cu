@@ -106,6 +106,42 @@ __device__ __forceinline__ void warp_copy(uint8_t *dst, const uint8_t *src, uint
     if (lane < (int)tail) dst[nw * 4 + lane] = src[nw * 4 + lane];
 }
 
+// Literal copy in device memory (no overlap): bytes up to a 16-byte aligned
+// destination, then 16-byte stores of source words realigned by funnel
+// shifts with 4 chunks in flight per lane (2 KiB per warp: the copy of an
+// incompressible block is latency-bound otherwise), then the tail.  A
+// source word read is an aligned word holding a byte of [src, src + len).
+__device__ __forceinline__ void warp_copy_wide(uint8_t *dst, const uint8_t *src, uint64_t len,
+                                               int lane) {
+    uint64_t head = (16u - ((uintptr_t)dst & 15u)) & 15u;
+    if (head > len) head = len;
+    if ((uint64_t)lane < head) dst[lane] = src[lane];
+    const uint64_t nch = (len - head) >> 4;
+    if (nch) {
+        const uint8_t *s1 = src + head;
+        uint4 *d1 = reinterpret_cast<uint4 *>(dst + head);
+        const uint32_t sh = (uint32_t)((uintptr_t)s1 & 3u) * 8u;
+        const uint32_t *w = reinterpret_cast<const uint32_t *>((uintptr_t)s1 & ~(uintptr_t)3);
+        auto chunk = [&](uint64_t c) -> uint4 {
+            const uint32_t *q = w + 4 * c;
+            const uint32_t a = q[0], b = q[1], e = q[2], f = q[3], g = sh ? q[4] : 0u;
+            return make_uint4(__funnelshift_r(a, b, sh), __funnelshift_r(b, e, sh),
+                              __funnelshift_r(e, f, sh), __funnelshift_r(f, g, sh));
+        };
+        uint64_t c = (uint64_t)lane;
+        for (; c + 96 < nch; c += 128) {
+            const uint4 v0 = chunk(c), v1 = chunk(c + 32), v2 = chunk(c + 64), v3 = chunk(c + 96);
+            d1[c] = v0;
+            d1[c + 32] = v1;
+            d1[c + 64] = v2;
+            d1[c + 96] = v3;
+        }
+        for (; c < nch; c += 32) d1[c] = chunk(c);
+    }
+    const uint64_t t0 = head + 16 * nch;
+    if ((uint64_t)lane < len - t0) dst[t0 + lane] = src[t0 + lane];
+}
+
 // staged compressed bytes per warp: the LZ4 bound of a 16 KiB block
 // (16384 + 16384 / 255 + 16 = 16464), rounded up
 constexpr uint32_t LZ4_STAGE_MAX = 16512;
@@ -229,6 +265,8 @@ __global__ void __launch_bounds__(256) lz4_decode_blocks_kernel(
                 }
                 if (lit <= 32) {  // short run: one byte per lane
                     if ((uint64_t)lane < lit) out[op + lane] = in[ip + lane];
+                } else if (!staged && lit >= 1024) {
+                    warp_copy_wide(out + op, in + ip, lit, lane);
                 } else {
                     warp_copy(out + op, in + ip, lit, lane);
                 }
