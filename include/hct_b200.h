@@ -40,7 +40,7 @@ enum {
     HCT_B200_ERR_INVALID_ARGUMENT = 16,
     HCT_B200_ERR_CORRUPTED = 17,         /* container-level Error::CorruptedData (tensor.rs:334-374, 463-468) */
     HCT_B200_ERR_CHECKSUM = 18,          /* XXH3 mismatch (tensor.rs:857-865, 966-973)                       */
-    HCT_B200_ERR_UNSUPPORTED = 19,       /* e.g. Zstd-compressed container                                  */
+    HCT_B200_ERR_UNSUPPORTED = 19,       /* e.g. a zstd frame that needs a dictionary                      */
     HCT_B200_ERR_CUDA = 20,
     HCT_B200_ERR_NO_DEVICE = 21,
     HCT_B200_ERR_TIMEOUT = 22,           /* a bounded device-side wait expired                              */
