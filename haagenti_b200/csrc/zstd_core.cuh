@@ -14,14 +14,18 @@
 // host):
 //   * frame, block and section headers: every lane parses them (the same
 //     bytes, so the lanes agree without communication);
-//   * FSE and Huffman table construction, Huffman weights and the sequence
-//     bitstream: lane 0, results in the warp's workspace;
+//   * FSE tables, Huffman weights and the sequence bitstream: lane 0,
+//     results in the warp's workspace; the Huffman decoding table is then
+//     filled by all lanes;
 //   * the 4 Huffman literal streams: one lane each;
 //   * raw / RLE blocks, literal copies and match copies: all lanes (a match
 //     with offset < length repeats the period-`offset` pattern, so each output
 //     byte is read from the bytes before the match and no lane waits on
 //     another within a copy);
 //   * XXH64 content checksum: lanes 0-3 run the 4 accumulators.
+// A frame whose blocks regenerate the encoder's block size is also decoded
+// block by block in parallel (plan_job, decode_block, decode_seq_blocks at
+// the end of this file; the kernels are in zstd_decode.cu).
 #pragma once
 
 #include <cstddef>
