@@ -102,9 +102,12 @@ struct Workspace {
 };
 
 // Huffman state of the block-parallel decoder (one per warp, shared memory):
-// the members huf_read_table, huf_fill and huf_stream use.
-struct HufWs {
-    HufEntry huf[1 << HUF_MAX_LOG];
+// the members huf_read_table, huf_fill and huf_stream use, with a table of
+// up to 2^TAB_LOG entries (decode_block fails a block whose table is larger).
+template <int LOG>
+struct HufWsT {
+    static constexpr int TAB_LOG = LOG;
+    HufEntry huf[1 << LOG];
     FseEntry wt[64];
     int16_t norm[256];
     uint16_t next[256];
@@ -113,6 +116,7 @@ struct HufWs {
     uint16_t huf_nsym;
     int err;
 };
+typedef HufWsT<HUF_MAX_LOG> HufWs;  // any table
 
 // ---- small helpers -------------------------------------------------------
 
@@ -1413,7 +1417,10 @@ ZHD bool decode_block(W *ws, const uint8_t *src, const BlockDesc &e, uint8_t *ds
         coop_fill(out, b[h.hs], h.regen, lane, nl);
         return true;
     }
-    if (lane == 0) ws->err = huf_read_table(ws, src + e.tbl, dlen) == (int)dlen ? OK : E_CORRUPT;
+    if (lane == 0)
+        ws->err = huf_read_table(ws, src + e.tbl, dlen) == (int)dlen && ws->huf_log <= W::TAB_LOG
+                      ? OK
+                      : E_CORRUPT;
     warp_sync();
     if (ws->err) return false;
     huf_fill(ws, lane, nl);

@@ -7,8 +7,8 @@
 //      encoder-sized blocks is planned block-parallel and its blocks
 //      appended to a descriptor pool;
 //   2. zstd_block_kernel, a warp per pooled block: the block's literals
-//      straight into the output, with a small workspace (Huffman table) so
-//      that many warps share an SM;
+//      straight into the output, with a small workspace (an 11-bit Huffman
+//      table) so that 28 warps share an SM;
 //   3. zstd_frame_kernel, a warp per job: for a block-parallel job its
 //      blocks with sequences (in order; compressed weights have few) and
 //      the content checksum; the whole serial decode (every frame form) of
@@ -30,7 +30,14 @@ constexpr int ZWARPS = 4;  // frame kernel: warps (jobs in flight) per CTA
 #endif
 constexpr uint64_t ZSTD_GRID_CAP = 148ull * ZSTD_MIN_CTAS;
 constexpr int BWARPS = 4;     // block kernel: warps per CTA
-constexpr int BMIN_CTAS = 5;  // resident block-kernel CTAs per SM
+#ifndef ZSTD_BMIN_CTAS
+#define ZSTD_BMIN_CTAS 7
+#endif
+constexpr int BMIN_CTAS = ZSTD_BMIN_CTAS;  // resident block-kernel CTAs per SM
+// its Huffman tables: zstd's encoders write literal tables of at most 11
+// bits (a block with a 12-bit table fails here and its frame is decoded
+// serially); the smaller workspace lets 7 CTAs share an SM
+typedef zs::HufWsT<11> BlockWs;
 constexpr uint32_t PLAN_THREADS = 128;
 
 // Scratch layout: frame-kernel literal scratch, then the job plans, the
@@ -91,9 +98,9 @@ __global__ void __launch_bounds__(BWARPS * 32, BMIN_CTAS) zstd_block_kernel(
     const uint8_t *__restrict__ src, const hct_b200_zstd_job *__restrict__ jobs,
     zs::JobPlan *plans, const zs::BlockDesc *__restrict__ pool, const uint32_t *pool_used,
     uint32_t pool_cap, uint8_t *dst, uint8_t *slots) {
-    __shared__ zs::HufWs hws[BWARPS];
+    __shared__ BlockWs hws[BWARPS];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    zs::HufWs *ws = hws + warp;
+    BlockWs *ws = hws + warp;
     const uint32_t used0 = *pool_used;
     const uint32_t used = used0 < pool_cap ? used0 : pool_cap;
     const uint32_t nw = gridDim.x * BWARPS;
