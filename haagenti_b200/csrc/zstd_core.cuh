@@ -1035,8 +1035,20 @@ ZHD int decode_compressed_block(Workspace *ws, const Job &job, const uint8_t *b,
                     const int oc = eo.sym, mc = em.sym, lc = el.sym;
                     if (oc > OF_MAX_SYM) { ws->err = E_CORRUPT; break; }
                     const uint64_t ofv = (1ull << oc) + br.read(oc);
-                    const uint32_t ml = ml_base(mc) + (uint32_t)br.read(ml_bits(mc));
-                    const uint32_t ll = ll_base(lc) + (uint32_t)br.read(ll_bits(lc));
+                    // the match- then literal-length extra bits, in one read
+                    // when they fit (a read takes at most 31 bits)
+                    const int mb = ml_bits(mc), lb = ll_bits(lc);
+                    uint32_t mx, lx;
+                    if (mb + lb <= 31) {
+                        const uint32_t x = br.read(mb + lb);
+                        mx = x >> lb;
+                        lx = x & ((1u << lb) - 1);
+                    } else {
+                        mx = br.read(mb);
+                        lx = br.read(lb);
+                    }
+                    const uint32_t ml = ml_base(mc) + mx;
+                    const uint32_t ll = ll_base(lc) + lx;
                     uint64_t off;
                     if (ofv > 3) {
                         off = ofv - 3;
@@ -1069,10 +1081,11 @@ ZHD int decode_compressed_block(Workspace *ws, const Job &job, const uint8_t *b,
                     lused += ll;
                     if (of32 == 0 || (uint64_t)of32 > o - fstart) { ws->err = E_CORRUPT; break; }
                     o += ml;
-                    if (done + i + 1 < nseq) {  // state updates: LL, ML, OF
-                        sll = el.base + (uint32_t)br.read(el.nb);
-                        sml = em.base + (uint32_t)br.read(em.nb);
-                        sof = eo.base + (uint32_t)br.read(eo.nb);
+                    if (done + i + 1 < nseq) {  // state updates LL, ML, OF: one read of <= 26 bits
+                        const uint32_t x = br.read(el.nb + em.nb + eo.nb);
+                        sll = el.base + (x >> (em.nb + eo.nb));
+                        sml = em.base + ((x >> eo.nb) & ((1u << em.nb) - 1));
+                        sof = eo.base + (x & ((1u << eo.nb) - 1));
                     }
                 }
                 ws->rep[0] = r0;
