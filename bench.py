@@ -440,6 +440,32 @@ def run_b200(args):
     d2h = sum(32 * readers[n].num_blocks() + 4 for n in readers)
     e2e_value = world * out_bytes / (e2e_ms / 1e3) / 1e9
 
+    # ---- replicated-weights mode (N > 1 only; not part of the decode) ----
+    # every rank's decoded layer broadcast to every other rank over NCCL;
+    # the ranks decoded the same layer, so each received copy must equal the
+    # rank's own output
+    replicate = None
+    if world > 1:
+        names = [f"{n}@{r}" for r in range(world) for n, _, _ in TENS]
+        owner = {f"{n}@{r}": r for r in range(world) for n, _, _ in TENS}
+        specs = {f"{n}@{r}": ((m, c), torch.bfloat16, dev) for r in range(world) for n, m, c in TENS}
+        mine = {f"{n}@{rank}": outs[n] for n, _, _ in TENS}
+        shard.replicate_units(mine, owner, specs)  # warm-up
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        got = shard.replicate_units(mine, owner, specs)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        rep_ms = shard.max_over_ranks(e0.elapsed_time(e1), dev)
+        same = all(torch.equal(got[k], outs[k.split("@")[0]]) for k in names)
+        recv = (world - 1) * out_bytes
+        replicate = {"ms": round(rep_ms, 3), "bytes_received_per_rank": recv,
+                     "GBps_received_per_rank": round(recv / (rep_ms / 1e3) / 1e9, 2),
+                     "units": len(names), "copies_equal": same,
+                     "path": "shard.replicate_units: one NCCL all-gather per tensor of the layer"}
+        del got
+
     # ---- secondary: LZ4 (config 2) and INT4 (config 1) ------------------
     lz4 = bench_lz4(H, torch, dev, stream, args) if rank == 0 and not args.no_secondary else None
     int4 = bench_int4(H, torch, dev, stream, args) if rank == 0 and not args.no_secondary else None
@@ -520,6 +546,7 @@ def run_b200(args):
             "kernels": kern,
             # the dense-path scatter is two kernels (chunk scan + scatter) under one record
             "gpu_launches": launches_total + ks.get("spectral_scatter", {}).get("launches", 0),
+            "replicate": replicate,
             "lz4": lz4, "int4": int4, "hct_v3": v3, "holotensor": holo, "zstd": zstd,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),

@@ -83,3 +83,53 @@ def test_two_gloo_ranks_shard_without_overlap():
         assert tmax == 11.0
         # every rank computed the same unit placement on its own
         assert all_units[0] == all_units[1]
+
+
+def _replicate_worker(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        # equal-shaped units one per rank (all-gather rounds) and odd ones
+        # (broadcasts)
+        names = ["embed", "layer0.q", "layer0.k", "layer1.q", "layer1.k", "lm_head", "norm"]
+        shapes = {"embed": (7, 5), "layer0.q": (4, 6), "layer1.q": (4, 6), "layer0.k": (2, 6),
+                  "layer1.k": (2, 6), "lm_head": (7, 5), "norm": (9,)}
+        owner = {"embed": 0, "lm_head": 0, "layer0.q": 0, "layer1.q": 1, "layer0.k": 0,
+                 "layer1.k": 1, "norm": 1}
+        specs = {n: (shapes[n], torch.bfloat16, torch.device("cpu")) for n in names}
+
+        def value(n):  # what the owner decoded
+            g = torch.Generator().manual_seed(names.index(n))
+            return torch.randn(shapes[n], generator=g).to(torch.bfloat16)
+
+        mine = {n: value(n) for n in names if owner[n] == rank}
+        got = shard.replicate_units(mine, owner, specs)
+        ok = sorted(got) == sorted(names) and all(torch.equal(got[n], value(n)) for n in names)
+        q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_replicate_decoded_units():
+    """The replicated-weights mode: every rank ends with every unit, bit for
+    bit, whether it travelled in an all-gather round or a broadcast."""
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_replicate_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert [ok for _, ok in res] == [True, True]
+
