@@ -106,11 +106,42 @@ __device__ __forceinline__ void warp_copy(uint8_t *dst, const uint8_t *src, uint
     if (lane < (int)tail) dst[nw * 4 + lane] = src[nw * 4 + lane];
 }
 
+// 16 source bytes starting K words + sh bits into the aligned 32 bytes at q
+// (two 16-byte loads; both granules hold a byte of the 16 wanted when the
+// start is not 16-byte aligned, which is the only case that calls this).
+template <int K>
+__device__ __forceinline__ uint4 src16(const uint4 *q, uint32_t sh) {
+    const uint4 a = q[0], b = q[1];
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    return make_uint4(__funnelshift_r(w[K], w[K + 1], sh), __funnelshift_r(w[K + 1], w[K + 2], sh),
+                      __funnelshift_r(w[K + 2], w[K + 3], sh), __funnelshift_r(w[K + 3], w[K + 4], sh));
+}
+
+// nch 16-byte chunks to the aligned d1 from s1 ((s1 & 15) = 4 K + sh / 8, not 0),
+// 4 chunks in flight per lane
+template <int K>
+__device__ __forceinline__ void wide_chunks(uint4 *d1, const uint8_t *s1, uint64_t nch, int lane) {
+    const uint4 *q = reinterpret_cast<const uint4 *>((uintptr_t)s1 & ~(uintptr_t)15);
+    const uint32_t sh = (uint32_t)((uintptr_t)s1 & 3u) * 8u;
+    uint64_t c = (uint64_t)lane;
+    for (; c + 96 < nch; c += 128) {
+        const uint4 v0 = src16<K>(q + c, sh), v1 = src16<K>(q + c + 32, sh);
+        const uint4 v2 = src16<K>(q + c + 64, sh), v3 = src16<K>(q + c + 96, sh);
+        d1[c] = v0;
+        d1[c + 32] = v1;
+        d1[c + 64] = v2;
+        d1[c + 96] = v3;
+    }
+    for (; c < nch; c += 32) d1[c] = src16<K>(q + c, sh);
+}
+
 // Literal copy in device memory (no overlap): bytes up to a 16-byte aligned
-// destination, then 16-byte stores of source words realigned by funnel
-// shifts with 4 chunks in flight per lane (2 KiB per warp: the copy of an
-// incompressible block is latency-bound otherwise), then the tail.  A
-// source word read is an aligned word holding a byte of [src, src + len).
+// destination, then 16-byte stores with 4 chunks in flight per lane (2 KiB
+// per warp: the copy of an incompressible block is latency-bound
+// otherwise), then the tail.  An aligned source moves with one 16-byte load
+// per chunk; otherwise each chunk is cut from two aligned 16-byte loads, the
+// word offset (the same for the whole run) a compile-time case.  No load
+// reads a 16-byte granule without a byte of [src, src + len).
 __device__ __forceinline__ void warp_copy_wide(uint8_t *dst, const uint8_t *src, uint64_t len,
                                                int lane) {
     uint64_t head = (16u - ((uintptr_t)dst & 15u)) & 15u;
@@ -120,23 +151,26 @@ __device__ __forceinline__ void warp_copy_wide(uint8_t *dst, const uint8_t *src,
     if (nch) {
         const uint8_t *s1 = src + head;
         uint4 *d1 = reinterpret_cast<uint4 *>(dst + head);
-        const uint32_t sh = (uint32_t)((uintptr_t)s1 & 3u) * 8u;
-        const uint32_t *w = reinterpret_cast<const uint32_t *>((uintptr_t)s1 & ~(uintptr_t)3);
-        auto chunk = [&](uint64_t c) -> uint4 {
-            const uint32_t *q = w + 4 * c;
-            const uint32_t a = q[0], b = q[1], e = q[2], f = q[3], g = sh ? q[4] : 0u;
-            return make_uint4(__funnelshift_r(a, b, sh), __funnelshift_r(b, e, sh),
-                              __funnelshift_r(e, f, sh), __funnelshift_r(f, g, sh));
-        };
-        uint64_t c = (uint64_t)lane;
-        for (; c + 96 < nch; c += 128) {
-            const uint4 v0 = chunk(c), v1 = chunk(c + 32), v2 = chunk(c + 64), v3 = chunk(c + 96);
-            d1[c] = v0;
-            d1[c + 32] = v1;
-            d1[c + 64] = v2;
-            d1[c + 96] = v3;
+        const uint32_t o = (uint32_t)((uintptr_t)s1 & 15u);
+        if (o == 0) {
+            const uint4 *q = reinterpret_cast<const uint4 *>(s1);
+            uint64_t c = (uint64_t)lane;
+            for (; c + 96 < nch; c += 128) {
+                const uint4 v0 = q[c], v1 = q[c + 32], v2 = q[c + 64], v3 = q[c + 96];
+                d1[c] = v0;
+                d1[c + 32] = v1;
+                d1[c + 64] = v2;
+                d1[c + 96] = v3;
+            }
+            for (; c < nch; c += 32) d1[c] = q[c];
+        } else {
+            switch (o >> 2) {  // uniform across the warp
+                case 0: wide_chunks<0>(d1, s1, nch, lane); break;
+                case 1: wide_chunks<1>(d1, s1, nch, lane); break;
+                case 2: wide_chunks<2>(d1, s1, nch, lane); break;
+                default: wide_chunks<3>(d1, s1, nch, lane); break;
+            }
         }
-        for (; c < nch; c += 32) d1[c] = chunk(c);
     }
     const uint64_t t0 = head + 16 * nch;
     if ((uint64_t)lane < len - t0) dst[t0 + lane] = src[t0 + lane];
