@@ -202,20 +202,44 @@ def read_traffic(kind):
 
 # ------------------------------------------------------------------ CPU baseline
 
-CPU_SAMPLE = ["k_proj", "v_proj", "q_proj"]
+CPU_SAMPLE = ["k_proj", "v_proj", "q_proj", "o_proj"]
 
 
-def cpu_decode_sample(files: dict, threads: int):
-    """The reference's CPU decode (oracle restatement: LZ4 + INT4 + scatter + Makhoul IDCT)."""
+def cpu_decode_sample(files: dict, threads: int, keep: bool = False):
+    """The reference's CPU decode (oracle restatement: LZ4 + INT4 + scatter + Makhoul
+    IDCT) of the CPU_SAMPLE tensors; with keep, their f32 outputs are returned too."""
     from oracle import hct as OH
 
     t0 = time.perf_counter()
-    elems = 0
+    elems, outs = 0, {}
     for name in CPU_SAMPLE:
         x = OH.decode_spectral_q4_cpu(files[name], threads)
         elems += x.size
+        if keep:
+            outs[name] = x
     dt = time.perf_counter() - t0
-    return elems * 2 / dt / 1e9, dt, elems
+    return elems * 2 / dt / 1e9, dt, elems, outs
+
+
+def cpu_scipy_idct(files: dict, threads: int) -> dict:
+    """scipy.fft.idctn (the orthonormal DCT-III, pocketfft) over the host cores on the
+    dense f32 coefficients of q_proj: a second CPU timing of the IDCT alone."""
+    import scipy.fft
+
+    from oracle import hct as OH
+
+    c = OH.decode_spectral_q4_cpu(files["q_proj"], threads, stage="coeffs")
+    scipy.fft.idctn(c, type=2, norm="ortho", workers=threads)
+    t0 = time.perf_counter()
+    reps = 2
+    for _ in range(reps):
+        scipy.fft.idctn(c, type=2, norm="ortho", workers=threads)
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(c.size * 2 / dt / 1e9, 4), "unit": "GB/s", "cores": threads,
+            "kind": "library",
+            "sample": f"scipy {scipy.__version__} fft.idctn(type=2, norm='ortho', f32, "
+                      f"workers={threads}) of q_proj's dense coefficients (8192x8192): the IDCT "
+                      f"alone, no LZ4/INT4, {dt:.2f} s per call"}
 
 
 def cpu_zstd_sample(frames, total_bytes: int) -> dict:
@@ -249,35 +273,107 @@ def cpu_zstd_sample(frames, total_bytes: int) -> dict:
 
 # ------------------------------------------------------------------ arms
 
+def ref_layer_files() -> dict:
+    """The layer encoded by the oracle's own writer (DCT, top-k, quantize_int4,
+    compress_block; the same seeds, retention and block size as the product
+    arm's files), cached per node.  The reference arm uses only these."""
+    from oracle import hct as OH
+
+    cache = os.path.join(tempfile.gettempdir(),
+                         f"hct_b200_ref_l70b_s{SEED}_r{int(RETENTION * 100)}_oracle")
+    done = os.path.join(cache, "DONE")
+    if not os.path.exists(done):
+        os.makedirs(cache, exist_ok=True)
+        for i, (name, m, n) in enumerate(LAYER_70B):
+            w = OH.gen_weight((m, n), SEED * 100 + i)
+            with open(os.path.join(cache, name + ".hct"), "wb") as f:
+                f.write(OH.encode_spectral_q4(w, RETENTION, version=1))
+            del w
+        with open(done, "w") as f:
+            f.write("ok\n")
+    out = {}
+    for name, _, _ in LAYER_70B:
+        with open(os.path.join(cache, name + ".hct"), "rb") as f:
+            out[name] = f.read()
+    return out
+
+
+REF_BUDGET_S = 150.0  # CPU seconds the reference arm's warm-up + timed steps may take
+
+
 def run_reference(args):
+    """The reference's CPU decode path (the oracle's line-by-line restatement of
+    block.rs, quantization.rs and dct.rs; the Rust crates cannot be built here)
+    on the host cores, on the same workload as the product arm: the 7 tensors of
+    the layer, oracle-encoded.  A step is the whole layer while the run fits
+    REF_BUDGET_S; otherwise each step decodes the next tensors of the layer in
+    turn, about the share of the layer that keeps the run inside the budget."""
+    import shutil
+
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    import oracle
+    from oracle import hct as OH
 
     threads = os.cpu_count() or 1
-    files = layer_files(0, 1, lambda: None)
-    for _ in range(args.warmup):
-        cpu_decode_sample(files, threads)
-    times, elems = [], 0
+    files = ref_layer_files()
+    names = [n for n, _, _ in LAYER_70B]
+    elems = {n: m * c for n, m, c in LAYER_70B}
+    layer_elems = sum(elems.values())
+
+    def decode(ns):
+        t0 = time.perf_counter()
+        for n in ns:
+            OH.decode_spectral_q4_cpu(files[n], threads)
+        return time.perf_counter() - t0
+
+    t_layer = decode(names)  # first warm-up step: the whole layer
+    rest = max(args.warmup - 1, 0) + args.steps
+    frac = min(1.0, REF_BUDGET_S / (rest * t_layer))
+    cursor = [0]
+
+    def next_sample():
+        if frac >= 1.0:
+            return names
+        ns, acc = [], 0
+        while not ns or acc < frac * layer_elems:
+            n = names[cursor[0] % len(names)]
+            cursor[0] += 1
+            ns.append(n)
+            acc += elems[n]
+        return ns
+
+    for _ in range(max(args.warmup - 1, 0)):
+        decode(next_sample())
+    t_sum, e_sum, samples = 0.0, 0, []
     for _ in range(args.steps):
-        gbs, dt, elems = cpu_decode_sample(files, threads)
-        times.append(dt)
-    ms = 1e3 * sum(times) / len(times)
-    value = elems * 2 / (ms / 1e3) / 1e9
+        ns = next_sample()
+        t_sum += decode(ns)
+        e_sum += sum(elems[n] for n in ns)
+        samples.append("+".join(ns))
+    value = e_sum * 2 / t_sum / 1e9
+    ms = 1e3 * t_sum / args.steps
+    sample = ("the whole layer (7 tensors, %d elements) per step" % layer_elems if frac >= 1.0
+              else "per step the next tensors of the layer in turn (%s ...), about %.0f%% of "
+                   "the layer" % (samples[0], 100 * frac))
     line = {
         "impl": "reference", "metric": "decoded_weight_GBps", "value": round(value, 4),
         "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "llama2-70b-layer-hct-q4 (BASELINE config 3), CPU sample "
-                               + "+".join(CPU_SAMPLE), "retention": RETENTION, "seed": SEED},
+        "config": {"workload": "llama2-70b-layer-hct-q4 (BASELINE config 3)",
+                   "tensors": {n: [m, c] for n, m, c in LAYER_70B}, "retention": RETENTION,
+                   "seed": SEED, "block_size": 16384, "same_config": True,
+                   "inputs": "encoded by the oracle's writer (oracle/hct.py encode_spectral_q4)"},
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads,
                          "kind": "port",
-                         "sample": f"{'+'.join(CPU_SAMPLE)} ({elems} elements) per step: LZ4 + "
-                                   "INT4 + bitmap scatter + f32 Makhoul IDCT, OpenMP"},
+                         "sample": sample + ": LZ4 + INT4 + bitmap scatter + f32 Makhoul IDCT "
+                                            "(oracle/hct_oracle.c, OpenMP), bf16-equivalent "
+                                            "bytes out"},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
+        "host": {"cpu_count": threads, "cargo": shutil.which("cargo"),
+                 "rustc": shutil.which("rustc")},
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -507,13 +603,16 @@ def run_b200(args):
                 "rate": round(v["work"] / (v["ms"] / 1e3) / (1e12 if k == "umma_gemm" else 1e9), 2),
                 "rate_unit": "TFLOP/s" if k == "umma_gemm" else "GB/s"} for k, v in ks.items()}
 
-    cpu = None
+    cpu = scipy_idct = oracle_check = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        gbs, dt, elems = cpu_decode_sample(files, threads)
+        gbs, dt, elems, ref = cpu_decode_sample(files, threads, keep=True)
         cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
                "sample": f"{'+'.join(CPU_SAMPLE)} of the layer ({elems} elements, {dt:.1f} s): "
                          "oracle LZ4 + INT4 + scatter + f32 Makhoul IDCT, OpenMP"}
+        scipy_idct = cpu_scipy_idct(files, threads)
+        oracle_check = check_against_oracle(H, torch, dev, readers, outs, ref)
+        del ref
 
     if rank == 0:
         line = {
@@ -549,6 +648,8 @@ def run_b200(args):
             "replicate": replicate,
             "lz4": lz4, "int4": int4, "hct_v3": v3, "holotensor": holo, "zstd": zstd,
             "cpu_baseline": cpu,
+            "cpu_baseline_scipy_idct": scipy_idct,
+            "oracle_check": oracle_check,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
@@ -559,6 +660,30 @@ def run_b200(args):
     if world > 1:
         dist.destroy_process_group()
     return 0
+
+
+def check_against_oracle(H, torch, dev, readers, outs, ref) -> dict:
+    """The checker: the oracle's CPU decode of the sample tensors against the GPU's
+    f32 decode of the same files (max-abs 1e-3, cosine 0.99999) and against the
+    bf16 outputs of the timed steps (the same bound plus the bf16 half-ulp)."""
+    res = {"tensors": sorted(ref), "max_abs_f32": 0.0, "min_cos_f32": 1.0,
+           "max_excess_bf16": -1.0}
+    for n, r in ref.items():
+        g = readers[n].decode(H.F32).cpu().numpy()
+        a, b = g.astype(np.float64).ravel(), r.astype(np.float64).ravel()
+        res["max_abs_f32"] = max(res["max_abs_f32"], float(np.abs(a - b).max()))
+        res["min_cos_f32"] = min(res["min_cos_f32"],
+                                 float((a @ b) / np.sqrt((a @ a) * (b @ b))))
+        gb = outs[n].float().cpu().numpy()
+        ex = np.abs(gb - r) - (1e-3 + np.abs(r) * 2.0 ** -8)
+        res["max_excess_bf16"] = max(res["max_excess_bf16"], float(ex.max()))
+    res["ok"] = (res["max_abs_f32"] <= 1e-3 and res["min_cos_f32"] >= 0.99999
+                 and res["max_excess_bf16"] <= 0.0)
+    if not res["ok"]:
+        raise AssertionError(f"GPU decode differs from the oracle: {res}")
+    for k in ("max_abs_f32", "min_cos_f32", "max_excess_bf16"):
+        res[k] = float(f"{res[k]:.6g}")
+    return res
 
 
 def _data_len(f: bytes) -> int:
@@ -573,8 +698,8 @@ def _data_len(f: bytes) -> int:
 
 
 def bench_v3(H, torch, dev, stream, files, tens, ctx):
-    """the same layer as HCT V3 fragment containers (bitmap + fp16
-    coefficients, one fragment per tensor) decoded to bf16, inputs resident in HBM."""
+    """The same layer as HCT V3 fragment containers (bitmap + fp16 coefficients, one
+    fragment per tensor) decoded to bf16, inputs resident in HBM."""
     decs = {n: H.HctV3Decoder(files[n + ".v3"], m, c, ctx) for n, m, c in tens}
     outs = {n: torch.empty((m, c), dtype=torch.bfloat16, device=dev) for n, m, c in tens}
 
@@ -782,10 +907,36 @@ def bench_lz4(H, torch, dev, stream, args):
     ms = e0.elapsed_time(e1) / reps
     pk = peaks()
     alg = raw.size + packed.size
-    return {"config": "BASELINE config 2 (256 MiB fp16 N(0,0.02) seed 1, 4096 x 64 KiB blocks)",
-            "value": round(raw.size / (ms / 1e3) / 1e9, 2), "unit": "GB/s decompressed",
-            "ms": round(ms, 4), "ratio": round(raw.size / packed.size, 4),
-            "hbm_frac": round(alg / (ms / 1e3) / 1e9 / pk["hbm"], 4), "bytes_checked_ok": ok}
+    out = {"config": "BASELINE config 2 (256 MiB fp16 N(0,0.02) seed 1, 4096 x 64 KiB blocks)",
+           "value": round(raw.size / (ms / 1e3) / 1e9, 2), "unit": "GB/s decompressed",
+           "ms": round(ms, 4), "ratio": round(raw.size / packed.size, 4),
+           "hbm_frac": round(alg / (ms / 1e3) / 1e9 / pk["hbm"], 4), "bytes_checked_ok": ok}
+    if cpu_ok(args):
+        import oracle
+
+        threads = os.cpu_count() or 1
+        d = np.zeros(nb, dtype=oracle.BLOCK_DESC)
+        for f in ("src_off", "dst_off", "src_len", "dst_cap", "out_size"):
+            d[f] = blk[f]
+        oracle.lz4_decompress_batch(packed, d, raw.size, threads)
+        t0 = time.perf_counter()
+        reps_c = 3
+        for _ in range(reps_c):
+            got, st = oracle.lz4_decompress_batch(packed, d, raw.size, threads)
+        dt = (time.perf_counter() - t0) / reps_c
+        assert (st["code"] == 0).all() and np.array_equal(got, raw)
+        out["cpu_baseline"] = {
+            "value": round(raw.size / dt / 1e9, 3), "unit": "GB/s decompressed", "cores": threads,
+            "kind": "port",
+            "sample": f"all 4096 blocks, decompress_block restated (oracle/hct_oracle.c), one "
+                      f"block per task over {threads} OpenMP threads, {dt:.3f} s per pass"}
+    return out
+
+
+def cpu_ok(args) -> bool:
+    """CPU baselines run on rank 0 of a one-GPU run only."""
+    return (not args.no_cpu_baseline and int(os.environ.get("WORLD_SIZE", "1")) == 1
+            and int(os.environ.get("RANK", "0")) == 0)
 
 
 def bench_int4(H, torch, dev, stream, args):
@@ -821,10 +972,28 @@ def bench_int4(H, torch, dev, stream, args):
     ms = e0.elapsed_time(e1) / reps
     alg = q.size + 4 * w.size
     pk = peaks()
-    return {"config": "BASELINE config 1 (4096x4096 seed 0, f32 out)",
-            "value": round(4 * w.size / (ms / 1e3) / 1e9, 2), "unit": "GB/s f32 out",
-            "ms": round(ms, 4), "hbm_frac": round(alg / (ms / 1e3) / 1e9 / pk["hbm"], 4),
-            "l2": "4 rotating input/output pairs (306 MB) > 126 MB L2"}
+    out = {"config": "BASELINE config 1 (4096x4096 seed 0, f32 out)",
+           "value": round(4 * w.size / (ms / 1e3) / 1e9, 2), "unit": "GB/s f32 out",
+           "ms": round(ms, 4), "hbm_frac": round(alg / (ms / 1e3) / 1e9 / pk["hbm"], 4),
+           "l2": "4 rotating input/output pairs (306 MB) > 126 MB L2"}
+    if cpu_ok(args):
+        import oracle
+
+        threads = os.cpu_count() or 1
+        ref = oracle.dequantize_int4_threads(q, w.size, threads)
+        t0 = time.perf_counter()
+        reps_c = 10
+        for _ in range(reps_c):
+            oracle.dequantize_int4_threads(q, w.size, threads)
+        dt = (time.perf_counter() - t0) / reps_c
+        got = outs[(reps - 1) % copies].cpu().numpy()
+        out["bit_exact"] = bool(np.array_equal(got.view(np.uint32), ref.view(np.uint32)))
+        out["cpu_baseline"] = {
+            "value": round(4 * w.size / dt / 1e9, 3), "unit": "GB/s f32 out", "cores": threads,
+            "kind": "port",
+            "sample": f"the whole config-1 tensor, dequantize_int4 restated (oracle/hct_oracle.c) "
+                      f"over {threads} OpenMP threads by 32-element block, {1e3 * dt:.2f} ms"}
+    return out
 
 
 def main():

@@ -74,7 +74,8 @@ cudaError_t launch_basis(const double *d_cos_table, uint64_t n, half_bits *d_bas
 //   mode 1: C stored out_dtype at out[m * ldo + n]         (row-major)
 //   mode 2: DFT stage 1 of the factored IDCT (fdct.cu): row R = (b, k2), the
 //           complex output m1 = column pair (2m1, 2m1+1), times twiddle[k2*m1],
-//           stored as fp16 pair at ((m1 * batch + b) * Q + k2)
+//           stored as fp16 pair at ((m1 * batch + b) * Q + k2); N = 2P (<= 256
+//           on the persistent stage kernel, any even N on the tiled one)
 //   mode 3: DFT stage 2: row R = (m1, b), complex output m2, j = m1 + P*m2,
 //           scaled and scattered to out[(4j + 2 ri) * ldo + b] (j < H/2) or
 //           out[(4(H-1-j) + 3 - 2 ri) * ldo + b] in out_dtype
@@ -101,11 +102,17 @@ struct GemmArgs {
 cudaError_t launch_umma_gemm(const GemmArgs &args, cudaStream_t s);
 
 // ---- factored DCT-III (fdct.cu) -----------------------------------------
-// L even, H = L/2 = P*Q with P, Q multiples of 4 and <= 128.
+// L even, H = L/2 = P*Q: preferably P, Q multiples of 4 and <= 128 (the most
+// balanced such split); otherwise Q the largest multiple of 4 <= 128 dividing
+// H and P = H/Q <= FDCT_MAX_P of any residue (the vocabulary lengths).
+constexpr uint32_t FDCT_MAX_P = 4096;
 bool fdct_factor(uint64_t L, uint32_t *P, uint32_t *Q);
-// rows of length L (fp16, stride ld_in) -> Z[b][k2][k1] complex fp16 pairs.
-// d_tables: the per-k pack coefficients (natural k order) written by
-// launch_pack_tables(L, P, Q).
+// complex values per (b, k2) row of the pack's output Z: P, or P rounded up
+// to a multiple of 8 (zero padded) when P is not a multiple of 4
+uint32_t fdct_padded_p(uint32_t P);
+// rows of length L (fp16, stride ld_in) -> Z[b][k2][k1] complex fp16 pairs,
+// rows of fdct_padded_p(P) values.  d_tables: the per-k pack coefficients
+// (natural k order) written by launch_pack_tables(L, P, Q).
 cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t batch, uint32_t L,
                                 uint32_t P, uint32_t Q, const float *d_tables, half_bits *d_out,
                                 cudaStream_t s);

@@ -242,6 +242,48 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 7 : 3) makhoul_pack_
     }
 }
 
+// Pack for P that is not a multiple of 4 (the vocabulary lengths, e.g.
+// H = 16000 = 125 x 128): the output row of each (b, k2) is padded to
+// Pp = round_up(P, 8) complex values (zeros past P), so that stage 1 reads
+// 16-byte aligned rows of K = 2 Pp.  Each thread writes 4 consecutive k1 of one
+// k2 (one 16-byte store) and computes every Z[k] from its four inputs (no
+// partner sharing: the partner of a run is not an aligned run when P % 4 != 0).
+template <int THREADS>
+__global__ void __launch_bounds__(THREADS) makhoul_pack_generic_kernel(
+    const uint16_t *__restrict__ in, uint64_t ld_in, uint64_t B, uint32_t L, uint32_t P,
+    uint32_t Pp, uint32_t Q, const float4 *__restrict__ coef, uint32_t *__restrict__ out) {
+    extern __shared__ uint4 smem_v[];
+    uint16_t *srow = reinterpret_cast<uint16_t *>(smem_v);
+    const uint32_t H = L / 2, runs = Pp / 4, items = runs * Q;
+    if (threadIdx.x == 0) srow[L] = 0;  // c[L] = 0 (never overwritten)
+    for (uint64_t b = blockIdx.x; b < B; b += gridDim.x) {
+        __syncthreads();  // previous row fully consumed
+        const uint16_t *row = in + b * ld_in;
+        for (uint32_t k = threadIdx.x; k < L; k += THREADS) srow[k] = row[k];
+        __syncthreads();
+        uint32_t *orow = out + b * (uint64_t)Q * Pp;
+        for (uint32_t it = threadIdx.x; it < items; it += THREADS) {
+            const uint32_t k2 = it / runs, g = it - k2 * runs;
+            uint32_t z[4];
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                const uint32_t k1 = 4 * g + t;
+                z[t] = 0;
+                if (k1 < P) {
+                    const uint32_t k = Q * k1 + k2;
+                    const float a = ld_h(srow, k), bb = ld_h(srow, L - k);
+                    const float c = ld_h(srow, H + k), d = ld_h(srow, H - k);
+                    const float4 tt = coef[k];
+                    z[t] = pack_z(fmaf(tt.x, a, fmaf(tt.y, bb, fmaf(tt.z, c, tt.w * d))),
+                                  fmaf(tt.y, a, fmaf(-tt.x, bb, fmaf(tt.w, c, -tt.z * d))));
+                }
+            }
+            *reinterpret_cast<uint4 *>(orow + (uint64_t)k2 * Pp + 4 * g) =
+                make_uint4(z[0], z[1], z[2], z[3]);
+        }
+    }
+}
+
 // Row pack straight from the spectral payload (bitmap ++ INT4): one CTA per
 // row at a time, several CTAs per SM.
 //   A. the row's 64-bit bitmap words into shared memory and their
@@ -498,9 +540,12 @@ __global__ void twiddle_table_kernel(uint32_t H, float2 *out) {
 
 }  // namespace
 
+uint32_t fdct_padded_p(uint32_t P) { return P % 4 == 0 ? P : (P + 7) / 8 * 8; }
+
 bool fdct_factor(uint64_t L, uint32_t *P, uint32_t *Q) {
     if (L < 16 || (L & 1)) return false;
     const uint64_t H = L / 2;
+    if (H > (1ull << 31)) return false;
     uint32_t best_p = 0, best_q = 0;
     auto fast_q = [](uint64_t q) { return q == 16 || q == 32 || q == 64 || q == 128; };
     for (uint32_t p = 4; p <= 128; p += 4) {
@@ -516,7 +561,20 @@ bool fdct_factor(uint64_t L, uint32_t *P, uint32_t *Q) {
             best_q = (uint32_t)q;
         }
     }
-    if (!best_p) return false;
+    if (!best_p) {
+        // no split into two multiples of 4 up to 128 (e.g. H = 16000 = 125 x 128 or
+        // 64128 = 501 x 128): the largest Q (a multiple of 4, <= 128) dividing H,
+        // P = H / Q of any size (stage 1 pads P, and takes the dense-tile
+        // contraction beyond 128)
+        for (uint32_t q = 128; q >= 4; q -= 4) {
+            if (H % q == 0 && H / q <= FDCT_MAX_P) {
+                best_q = q;
+                best_p = (uint32_t)(H / q);
+                break;
+            }
+        }
+        if (!best_p) return false;
+    }
     *P = best_p;
     *Q = best_q;
     return true;
@@ -577,7 +635,20 @@ cudaError_t row_grid(F kern, int threads, size_t smem, uint64_t B, unsigned *gri
 cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t B, uint32_t L,
                                 uint32_t P, uint32_t Q, const float *d_tables, half_bits *d_out,
                                 cudaStream_t s) {
-    if (L % 32 || (uint64_t)P * Q != L / 2 || P % 4 || Q % 4) return cudaErrorInvalidValue;
+    if ((uint64_t)P * Q != L / 2 || Q % 4 || L % 8) return cudaErrorInvalidValue;
+    if (P % 4) {
+        const size_t smem = (size_t)(L + 8) * 2;
+        if (smem > 200 * 1024 || ((uintptr_t)d_out & 15)) return cudaErrorInvalidValue;
+        auto kern = makhoul_pack_generic_kernel<256>;
+        unsigned g = 0;
+        cudaError_t e = row_grid(kern, 256, smem, B, &g);
+        if (e != cudaSuccess) return e;
+        kern<<<g, 256, smem, s>>>(d_in, ld_in, B, L, P, fdct_padded_p(P), Q,
+                                  reinterpret_cast<const float4 *>(d_tables),
+                                  reinterpret_cast<uint32_t *>(d_out));
+        return cudaGetLastError();
+    }
+    if (L % 32) return cudaErrorInvalidValue;
     // the specialised pack writes 32-byte runs: it needs a 32-byte aligned output
     const int qc = ((uintptr_t)d_out & 31) ? 0 : pack_qc(P, Q);
     const size_t smem = (size_t)srow_halves(L, qc) * 2;
@@ -595,7 +666,9 @@ cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t 
 }
 
 bool spectral_pack_supported(uint64_t L) {
-    return L % 64 == 0 && L <= (1u << 20) && spack_smem_bytes((uint32_t)L, 64) <= 200 * 1024;
+    uint32_t P = 0, Q = 0;
+    return L % 64 == 0 && L <= (1u << 20) && spack_smem_bytes((uint32_t)L, 64) <= 200 * 1024 &&
+           fdct_factor(L, &P, &Q) && P % 4 == 0;
 }
 
 cudaError_t launch_spectral_pack(const uint8_t *d_payload, uint64_t bmb, const uint32_t *d_chunk,

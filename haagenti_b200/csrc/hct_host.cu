@@ -175,7 +175,7 @@ struct hct_b200_ctx {
     DevBuf zscratch, zsrc, zdst, zjob, zstatus;  // Zstandard decode
     DevBuf io_in, io_out, io_blk, io_status;
     std::map<uint64_t, std::unique_ptr<Basis>> bases;
-    std::map<uint32_t, std::unique_ptr<DevBuf>> dft_mats;  // realified n-point DFT, fp16
+    std::map<uint64_t, std::unique_ptr<DevBuf>> dft_mats;  // realified n-point DFT (n, ld), fp16
     std::map<uint32_t, std::unique_ptr<DevBuf>> twiddles;  // e^{2 pi i j / H}, complex f32
     std::map<uint32_t, std::unique_ptr<DevBuf>> pack_tabs;  // Makhoul-pack twiddles per length
     DevBuf cos_tbl;
@@ -331,11 +331,20 @@ int get_basis(hct_b200_ctx *ctx, uint64_t n, const Basis **out, cudaStream_t s,
     return HCT_B200_OK;
 }
 
+// Bytes of the pack output Z for `batch` rows of length L (rows of
+// fdct_padded_p(P) complex fp16 per (b, k2)); 0 when L does not factor.
+uint64_t fdct_z_bytes(uint64_t batch, uint64_t L) {
+    uint32_t P = 0, Q = 0;
+    if (!fdct_factor(L, &P, &Q)) return 0;
+    return batch * Q * (uint64_t)fdct_padded_p(P) * 4;
+}
+
 int reserve_spectral(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols,
                      hct_b200_error *err) {
     CK(ctx->dense.reserve(rows * round_up(cols, 8) * 2 + 16));
     CK(ctx->tt.reserve(cols * round_up(rows, 8) * 2 + 16));
-    CK(ctx->za.reserve(rows * cols * 2 + 16));
+    CK(ctx->za.reserve(std::max<uint64_t>(
+        rows * cols * 2, std::max(fdct_z_bytes(rows, cols), fdct_z_bytes(cols, rows))) + 16));
     CK(ctx->zb.reserve(rows * cols * 2 + 16));
     CK(ctx->chunk.reserve(rank_dir_words(rows * cols) * sizeof(uint32_t)));
     CK(ctx->meta.reserve(4 * sizeof(uint64_t)));
@@ -345,18 +354,21 @@ int reserve_spectral(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols,
 
 // The two contractions on a dense fp16 coefficient matrix held in ctx->dense
 // (rows x round_up(cols, 8)).
-int get_dft_matrix(hct_b200_ctx *ctx, uint32_t n, const half_bits **out, cudaStream_t s,
-                   hct_b200_error *err) {
-    auto it = ctx->dft_mats.find(n);
+// Realified n-point DFT matrix, 2n rows of ld >= 2n fp16 (zero columns past 2n).
+int get_dft_matrix(hct_b200_ctx *ctx, uint32_t n, uint32_t ld, const half_bits **out,
+                   cudaStream_t s, hct_b200_error *err) {
+    const uint64_t key = (uint64_t)n | ((uint64_t)ld << 32);
+    auto it = ctx->dft_mats.find(key);
     if (it == ctx->dft_mats.end()) {
         auto b = std::make_unique<DevBuf>();
-        CK(b->reserve((size_t)4 * n * n * 2));
-        CK(launch_dft_matrix(n, 2 * n, 2 * n, b->as<half_bits>(), s));
-        it = ctx->dft_mats.emplace(n, std::move(b)).first;
+        CK(b->reserve((size_t)2 * n * ld * 2));
+        CK(launch_dft_matrix(n, 2 * n, ld, b->as<half_bits>(), s));
+        it = ctx->dft_mats.emplace(key, std::move(b)).first;
     }
     *out = it->second->as<half_bits>();
     return HCT_B200_OK;
 }
+
 
 int get_twiddle(hct_b200_ctx *ctx, uint32_t H, const float **out, cudaStream_t s,
                 hct_b200_error *err) {
@@ -409,10 +421,11 @@ int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint
               const RankDir &dir, uint64_t batch, uint64_t L, uint32_t P, uint32_t Q, void *out,
               uint64_t ldo, int out_dtype, cudaStream_t s, hct_b200_error *err) {
     const uint32_t H = (uint32_t)(L / 2);
+    const uint32_t Pp = fdct_padded_p(P);  // Z rows: Pp complex, zeros past P
     const half_bits *wp = nullptr, *wq = nullptr;
     const float *tw = nullptr;
-    int rc = get_dft_matrix(ctx, P, &wp, s, err);
-    if (!rc) rc = get_dft_matrix(ctx, Q, &wq, s, err);
+    int rc = get_dft_matrix(ctx, P, 2 * Pp, &wp, s, err);
+    if (!rc) rc = get_dft_matrix(ctx, Q, 2 * Q, &wq, s, err);
     if (!rc) rc = get_twiddle(ctx, H, &tw, s, err);
     if (rc) return rc;
     auto pt = ctx->pack_tabs.find((uint32_t)L);
@@ -438,7 +451,7 @@ int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint
         ctx->prof_end(slot, PK_PACK, 4.0 * elems, s);
     }
     CK(ctx->sched.reserve(64));
-    GemmArgs g1{ctx->za.as<half_bits>(), wp, batch * Q, 2ull * P, 2ull * P, 2ull * P, 2ull * P,
+    GemmArgs g1{ctx->za.as<half_bits>(), wp, batch * Q, 2ull * P, 2ull * Pp, 2ull * Pp, 2ull * Pp,
                 ctx->zb.p, 0, 2, HCT_B200_F16, flag};
     g1.tile_counter = ctx->sched.as<uint32_t>();
     g1.P = P;

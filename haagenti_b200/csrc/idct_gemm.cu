@@ -290,7 +290,24 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int col0 = n0 + c;
                 if (!row_ok || col0 >= (int)N) continue;
                 const int ncols = min(32, (int)N - col0);
-                if (mode == 0) {
+                if (mode == 2) {
+                    // DFT stage 1 with P > 128 (the tiled path): this row is data
+                    // row (b, k2), the columns are outputs 2 m1 + ri; the lanes of
+                    // a warp (consecutive k2) store 32 consecutive complex values
+                    const uint32_t Q = sp.Q, b = (uint32_t)row / Q, k2 = (uint32_t)row - b * Q;
+                    uint32_t *g = reinterpret_cast<uint32_t *>(out);
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2) {
+                        if (j < ncols) {
+                            const uint32_t m1 = (uint32_t)(col0 + j) >> 1;
+                            const float2 tw = sp.twiddle[k2 * m1];  // k2 m1 < Q P = H
+                            const float re = __uint_as_float(r[j]), im = __uint_as_float(r[j + 1]);
+                            g[((uint64_t)m1 * sp.batch + b) * Q + k2] =
+                                (uint32_t)f2h(re * tw.x - im * tw.y) |
+                                ((uint32_t)f2h(re * tw.y + im * tw.x) << 16);
+                        }
+                    }
+                } else if (mode == 0) {
                     uint16_t *o = reinterpret_cast<uint16_t *>(out);
 #pragma unroll
                     for (int j = 0; j < 32; j++)
@@ -981,12 +998,15 @@ cudaError_t launch_umma_gemm(const GemmArgs &a, cudaStream_t s) {
     if ((a.lda % 8) || (a.ldb % 8) || a.K == 0) return cudaErrorInvalidValue;
     if (a.M > 0x7fffffffull || a.N > 0x7fffffffull || a.K > 0x7fffffffull)
         return cudaErrorInvalidValue;
-    if ((a.mode == 2 || a.mode == 3) && (!a.P || !a.Q || !a.batch || a.N > 256 ||
-                                         (a.mode == 2 && !a.twiddle)))
+    if ((a.mode == 2 || a.mode == 3) &&
+        (!a.P || !a.Q || !a.batch || (a.mode == 3 && (a.N > 256 || a.K > 256)) ||
+         (a.mode == 2 && (!a.twiddle || (a.N & 1)))))
         return cudaErrorInvalidValue;
     if (a.mode == 2 || a.mode == 3) {
         if (a.N <= 128 && a.K <= 128) return launch_stage_t<1>(a, s);
-        return launch_stage_t<2>(a, s);
+        if (a.N <= 256 && a.K <= 256) return launch_stage_t<2>(a, s);
+        // stage 1 with P > 128: output tiles of the general contraction
+        return launch_bn<256>(a, s);
     }
     if (a.N <= 128) return launch_bn<128>(a, s);
     return launch_bn<256>(a, s);

@@ -231,7 +231,9 @@ int hct_b200_idct_2d(hct_b200_ctx *ctx, const float *d_in, void *d_out, int out_
  * (bitmap ++ quantize_int4(values)), rows x cols, into d_out.  The INT4
  * dequantisation and bitmap scatter run on the GPU and feed the two IDCT
  * contractions (CompressiveSpectralDecoder::reconstruct, crates/haagenti/src/
- * compressive.rs:732-752, with INT4 values in place of FP16). */
+ * compressive.rs:732-752, with INT4 values in place of FP16).  d_payload must
+ * be 16-byte aligned (the kernels read the bitmap in 64-bit and 128-bit
+ * words); an unaligned pointer returns HCT_B200_ERR_INVALID_ARGUMENT. */
 int hct_b200_spectral_q4_decode(hct_b200_ctx *ctx, const uint8_t *d_payload, size_t payload_len,
                                 size_t rows, size_t cols, void *d_out, int out_dtype,
                                 void *stream);
@@ -243,11 +245,15 @@ int hct_b200_spectral_q4_decode(hct_b200_ctx *ctx, const uint8_t *d_payload, siz
  * reference.  It takes no context and allocates nothing: its scratch is one
  * fixed 32 MiB device array inside the library (held on every device that
  * uses the library until the process exits), so rows and cols must each be
- * <= 2048; larger tensors return HCT_B200_ERR_INVALID_ARGUMENT.  The first
- * call on a device looks up that array's device address; make that first
- * call before any stream capture.  All calls share the array: calls whose
- * GPU work overlaps race and must be serialised by the caller.  Synchronises
- * `stream` to report the device-side status. */
+ * <= 2048; larger tensors return HCT_B200_ERR_INVALID_ARGUMENT.
+ * It decodes on the calling thread's current device: d_payload (16-byte
+ * aligned), d_out and stream must belong to that device.  The first call on
+ * a device looks up that array's device address and keeps it for the life of
+ * the process; make that first call before any stream capture begins, and
+ * do not call it again on a device after cudaDeviceReset there.  All calls
+ * share the array: calls whose GPU work overlaps race and must be serialised
+ * by the caller.  Each call copies the device-side status to host memory and
+ * synchronises `stream` before it returns. */
 int hct_b200_spectral_q4_decode_noalloc(const uint8_t *d_payload, size_t payload_len, size_t rows,
                                         size_t cols, void *d_out, int out_dtype, void *stream);
 

@@ -35,13 +35,26 @@ Q4_BLOCK_SIZE = 32
 DEFAULT_BLOCK_SIZE = 16 * 1024  # tensor.rs:74
 
 
+def reference_root() -> str | None:
+    """The haagenti checkout the golden vectors and oracle/_ref come from:
+    $HAAGENTI_REFERENCE, else a ``reference`` directory beside this
+    repository; None when neither exists (as on a GPU box)."""
+    cands = [os.environ.get("HAAGENTI_REFERENCE"),
+             os.path.join(os.path.dirname(os.path.dirname(_HERE)), "reference")]
+    for c in cands:
+        if c and os.path.isdir(os.path.join(c, "ref", "c")):
+            return os.path.abspath(c)
+    return None
+
+
 def build() -> str:
-    """Compile liboracle.so (and the reference C decoder when present)."""
+    """Compile liboracle.so (and the reference C decoder when its checkout is present)."""
     import subprocess
 
     subprocess.run(["make", "-s", "-C", _HERE], check=True)
-    if os.path.isdir("/root/reference/ref/c"):
-        subprocess.run(["make", "-s", "-C", _HERE, "ref"], check=True)
+    ref = reference_root()
+    if ref:
+        subprocess.run(["make", "-s", "-C", _HERE, "ref", f"REF_DIR={ref}/ref/c"], check=True)
     return _LIB_PATH
 
 
@@ -73,6 +86,8 @@ def _load() -> C.CDLL:
     lib.orc_quantize_int4.argtypes = [f32p, sz, u8p]
     lib.orc_dequantize_int4.restype = sz
     lib.orc_dequantize_int4.argtypes = [u8p, sz, sz, f32p]
+    lib.orc_dequantize_int4_threads.restype = sz
+    lib.orc_dequantize_int4_threads.argtypes = [u8p, sz, sz, f32p, C.c_int]
     lib.orc_f32_to_f16_rne.restype = C.c_uint16
     lib.orc_f32_to_f16_rne.argtypes = [C.c_float]
     lib.orc_quantize_int4_mp.restype = None
@@ -244,6 +259,15 @@ def dequantize_int4(data, num_elements: int) -> np.ndarray:
     src = _as_u8(data)
     out = np.zeros(max(num_elements, 1), dtype=np.float32)
     n = lib().orc_dequantize_int4(_u8(src) if src.size else None, src.size, num_elements, _f32(out))
+    return out[:n]
+
+
+def dequantize_int4_threads(data, num_elements: int, threads: int = 0) -> np.ndarray:
+    """dequantize_int4 with OpenMP over 32-element blocks (the CPU baseline)."""
+    src = _as_u8(data)
+    out = np.empty(max(num_elements, 1), dtype=np.float32)
+    n = lib().orc_dequantize_int4_threads(_u8(src) if src.size else None, src.size,
+                                          num_elements, _f32(out), threads)
     return out[:n]
 
 

@@ -210,11 +210,20 @@ def tensor_dims(shape) -> tuple[int, int]:
 
 def encode_spectral_q4(w: np.ndarray, retention: float = 0.30, version: int = 1,
                        block_size: int = DEFAULT_BLOCK_SIZE, threads: int = 0,
-                       return_parts: bool = False):
-    """Encode a tensor as an HCT-Q4 file (DCT -> top-k bitmap -> INT4 -> LZ4 HCT)."""
+                       return_parts: bool = False, dct: str = "f32"):
+    """Encode a tensor as an HCT-Q4 file (DCT -> top-k bitmap -> INT4 -> LZ4 HCT).
+
+    dct: "f32" is the restatement of dct.rs:282-308 (f32 Makhoul FFT); "f64"
+    takes the float64 orthonormal DCT-II (scipy) rounded once to float32, the
+    correctly rounded coefficients, which any float64 DCT reproduces."""
     w = np.ascontiguousarray(w, dtype=np.float32)
     m, n = tensor_dims(w.shape)
-    coeffs = dct_2d(w.reshape(m, n), threads)
+    if dct == "f64":
+        from . import dct_2d_f64_truth
+
+        coeffs = dct_2d_f64_truth(w.reshape(m, n)).astype(np.float32)
+    else:
+        coeffs = dct_2d(w.reshape(m, n), threads)
     total = m * n
     k = retain_count(total, retention)
     bm = topk_bitmap(coeffs, k, threads)
@@ -339,18 +348,34 @@ def decode_hct_v3_cpu(data: bytes, rows: int, cols: int, threads: int = 0) -> np
     return idct_2d(dense.reshape(rows, cols), threads)
 
 
-def gen_weight(shape, seed: int, outlier_frac: float = 0.01, std: float = 0.02) -> np.ndarray:
+def gen_weight(shape, seed: int, outlier_frac: float = 0.01, std: float = 0.02,
+               threads: int = 0) -> np.ndarray:
     """N(0, std) f32: 2^22-element chunks, chunk i from PCG64(SeedSequence(seed).spawn(n)[i]);
-    the first 1% of a default_rng([seed, 1]) column permutation is scaled x10."""
+    the first 1% of a default_rng([seed, 1]) column permutation is scaled x10.
+    Chunks are filled by ``threads`` threads (0: all cores); the result does
+    not depend on the thread count."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+
     shape = tuple(int(s) for s in shape)
     n = int(np.prod(shape))
     chunk = 1 << 22
     nch = max(1, (n + chunk - 1) // chunk)
     w = np.empty(n, np.float32)
-    for i, ss in enumerate(np.random.SeedSequence(seed).spawn(nch)):
+    seqs = np.random.SeedSequence(seed).spawn(nch)
+
+    def fill(i):
         a, b = i * chunk, min(n, (i + 1) * chunk)
-        np.random.Generator(np.random.PCG64(ss)).standard_normal(out=w[a:b], dtype=np.float32)
+        np.random.Generator(np.random.PCG64(seqs[i])).standard_normal(out=w[a:b], dtype=np.float32)
         w[a:b] *= np.float32(std)
+
+    workers = min(nch, threads if threads > 0 else (os.cpu_count() or 1))
+    if workers <= 1:
+        for i in range(nch):
+            fill(i)
+    else:
+        with ThreadPoolExecutor(max_workers=workers) as ex:
+            list(ex.map(fill, range(nch)))
     w = w.reshape(shape)
     if outlier_frac > 0 and len(shape) == 2:
         nout = max(1, int(shape[1] * outlier_frac))

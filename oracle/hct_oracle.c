@@ -393,6 +393,33 @@ size_t orc_dequantize_int4(const uint8_t *data, size_t len, size_t n, float *out
     return w;
 }
 
+/* orc_dequantize_int4 split over OpenMP threads, 32-element block by block:
+ * each element is the same f32 product; written = min(n, 2 * nibble bytes)
+ * (0 when the scales do not fit), as the serial loop stops. */
+size_t orc_dequantize_int4_threads(const uint8_t *data, size_t len, size_t n, float *out,
+                                   int threads) {
+    if (n == 0) return 0;
+    size_t nb = (n + Q4_BLOCK - 1) / Q4_BLOCK;
+    size_t sb = nb * 2;
+    if (len < sb) return 0;
+    const uint8_t *packed = data + sb;
+    size_t plen = len - sb;
+    size_t w = 2 * plen < n ? 2 * plen : n;
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#pragma omp parallel for schedule(static)
+#endif
+    for (long long b = 0; b < (long long)nb; b++) {
+        float scale = orc_f16_bits_to_f32((uint16_t)(data[2 * b] | (data[2 * b + 1] << 8)));
+        size_t s = (size_t)b * Q4_BLOCK, e = s + Q4_BLOCK < w ? s + Q4_BLOCK : w;
+        for (size_t i = s; i < e; i++) {
+            uint8_t nibble = (i & 1) ? (packed[i >> 1] >> 4) & 0x0f : packed[i >> 1] & 0x0f;
+            out[i] = (float)((int8_t)nibble - 8) * scale;
+        }
+    }
+    return w;
+}
+
 /* f32 -> f16 with IEEE round-to-nearest-even, subnormals and overflow to
  * infinity: the conversion of half 2.7.1's f16::from_f32 that
  * mixed_precision.rs:463 stores its scales with (infinity and NaN map to

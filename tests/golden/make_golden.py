@@ -173,8 +173,11 @@ def ref_c_v3(reference: str):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=oracle.reference_root(),
+                    help="haagenti checkout (default: $HAAGENTI_REFERENCE or ../reference)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("no haagenti checkout found; pass --reference")
     oracle.build()
     g = {
         "generator": "tests/golden/make_golden.py",

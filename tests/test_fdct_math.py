@@ -50,7 +50,9 @@ def axis(c, P, Q):
 
 
 @pytest.mark.parametrize("L,P,Q", [(32, 4, 4), (96, 12, 4), (128, 8, 8), (1024, 16, 32),
-                                   (8192, 64, 64), (28672, 112, 128)])
+                                   (8192, 64, 64), (28672, 112, 128),
+                                   # vocabulary lengths: P not a multiple of 4
+                                   (32000, 125, 128), (128256, 501, 128), (80, 1, 40)])
 def test_one_axis_matches_dct_iii(L, P, Q):
     c = np.random.default_rng(L).standard_normal((3, L))
     y = axis(c, P, Q)  # transposed: y[n][b]

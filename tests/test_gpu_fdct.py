@@ -97,3 +97,30 @@ def test_factored_hct_decode_retention(hb, orc, retention):
         err = np.abs(got.astype(np.float64) - ref.astype(np.float64))
         assert (err <= MAX_ABS + tol * np.abs(ref)).all(), f"retention {retention}: {err.max():.3e}"
         assert _cos(got, ref) >= MIN_COS
+
+
+@pytest.mark.parametrize("shape", [(32000, 64), (64, 32000), (128256, 64), (42752, 16),
+                                   (96, 80), (80, 96)])
+def test_factored_vocabulary_lengths(hb, orc, dev, ctxs, shape):
+    """Axis lengths whose half has no split into two multiples of 4 up to 128:
+    32000 (H = 125 x 128, Llama-2's vocabulary), 128256 (H = 501 x 128,
+    Llama-3's; stage 1 on the tiled contraction), 42752 (H = 167 x 128) and 80
+    (H = 1 x 40).  Through the reader (spectral payload -> factored IDCT) against
+    the oracle's decode of the same file, and the bare IDCT against the dense
+    contraction where its basis is small."""
+    import torch
+    from oracle import hct as OH
+
+    w = OH.gen_weight(shape, 43)
+    f = OH.encode_spectral_q4(w)
+    ref = OH.decode_spectral_q4_cpu(f)
+    got = hb.HctReader(f).decode(hb.F32).cpu().numpy()
+    _check(got, ref, f"hct {shape}")
+    auto, dense = ctxs
+    if max(shape) <= 42752:
+        c = OH.decode_spectral_q4_cpu(f, stage="coeffs")
+        x = torch.from_numpy(np.ascontiguousarray(c)).to(dev)
+        a = hb.idct_2d(x, ctx=auto).cpu().numpy()
+        _check(a, ref, f"idct {shape} factored vs oracle")
+        if max(shape) <= 32000:
+            _check(a, hb.idct_2d(x, ctx=dense).cpu().numpy(), f"idct {shape} factored vs dense")

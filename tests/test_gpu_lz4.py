@@ -229,3 +229,36 @@ def test_overlapping_matches_all_periods(hb, orc, dev, staged):
     assert (st["code"] == 0).all()
     assert np.array_equal(st["written"], ref_st["written"])
     assert np.array_equal(dst[:dsz].cpu().numpy(), ref_out[:dsz])
+
+
+@pytest.mark.parametrize("staged", [False, True])
+def test_long_literal_runs_every_alignment_phase(hb, orc, dev, staged):
+    """Literal runs of 1 KiB and more (copied 16 bytes at a time from two
+    aligned loads in the device-memory variant) at every source-minus-
+    destination offset mod 16 and several block starts: same bytes as the oracle."""
+    import torch
+
+    rng = np.random.default_rng(14)
+    comps, sizes = [], []
+    for run in (1024, 1031, 2063, 8200, 9001):
+        for shift in range(16):
+            for lead in (5, 6, 7, 8):
+                head = rng.integers(0, 256, lead, dtype=np.uint8).tobytes()
+                body = rng.integers(0, 256, run, dtype=np.uint8).tobytes()
+                tail = rng.integers(0, 256, 9, dtype=np.uint8).tobytes()
+                # the first match moves the output position by 4 + shift bytes
+                # against the input position; the long run follows it
+                blk = (_lz4_seq(head, 1, 4 + shift) + _lz4_seq(body, 3, 11)
+                       + _lz4_seq(tail))
+                comps.append(blk)
+                sizes.append(lead + 4 + shift + run + 11 + len(tail))
+    d, ssz, dsz = _blocks_for([b"\0" * n for n in sizes], comps)
+    srcnp = np.frombuffer(b"".join(comps), np.uint8)
+    ref_out, ref_st = orc.lz4_decompress_batch(srcnp, d.astype(orc.BLOCK_DESC), dsz)
+    assert (ref_st["code"] == 0).all()
+    src = torch.from_numpy(srcnp.copy()).to(dev)
+    dst = torch.zeros(dsz + 16, dtype=torch.uint8, device=dev)
+    st = hb.Lz4Decompressor().decompress_blocks(src, d, dst, staged=staged)
+    assert (st["code"] == 0).all()
+    assert np.array_equal(st["written"], ref_st["written"])
+    assert np.array_equal(dst[:dsz].cpu().numpy(), ref_out[:dsz])

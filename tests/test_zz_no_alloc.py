@@ -60,12 +60,22 @@ def test_noalloc_matches_context_decode_on_two_calls():
             assert _decode_with_ctx(lib, ctx, p, rows, cols, ref, stream) == 0
             refs.append(ref.cpu().numpy())
             payloads.append(p)
+        # output buffers first, then one call to set up the scratch address on
+        # this device, so that the free-memory reading below brackets only
+        # the decodes themselves
+        bufs = [torch.full((rows, cols), float("nan"), dtype=torch.float32, device=dev)
+                for (rows, cols), _ in cases]
+        warm = torch.empty(cases[0][0], dtype=torch.float32, device=dev)
+        assert _decode_noalloc(lib, payloads[0], *cases[0][0], warm, stream) == 0
+        torch.cuda.synchronize(dev)
+        free_before = torch.cuda.mem_get_info(dev)[0]
         # two calls in a row through the shared scratch array, different shapes
-        outs = []
-        for ((rows, cols), _), p in zip(cases, payloads):
-            out = torch.full((rows, cols), float("nan"), dtype=torch.float32, device=dev)
+        for ((rows, cols), _), p, out in zip(cases, payloads, bufs):
             assert _decode_noalloc(lib, p, rows, cols, out, stream) == 0
-            outs.append(out.cpu().numpy())
+        torch.cuda.synchronize(dev)
+        # the decodes took no device memory (cudaMemGetInfo unchanged)
+        assert torch.cuda.mem_get_info(dev)[0] == free_before
+        outs = [b.cpu().numpy() for b in bufs]
         for got, ref in zip(outs, refs):
             assert np.isfinite(got).all()
             assert np.abs(got - ref).max() <= MAX_ABS
