@@ -3,24 +3,25 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-Workload: one Llama-2-70B-shaped decoder layer -- q/o
-8192x8192, k/v 1024x8192, gate/up 28672x8192, down 8192x28672, N(0,0.02)
-with 1% outlier columns x10, seed 2 -- encoded as HCT-Q4 files (DCT,
-retention 0.30, INT4 coefficients with FP16 block scales, 16 KiB LZ4
-blocks) and decoded to bf16.  A step decodes the whole layer.  Under
-torchrun every rank decodes its own copy of the layer (weak scaling, no
-collective on the data path); the timed region is bracketed by a barrier
-and CUDA events and the reported time is the max over ranks.
+Headline workload: the whole Llama-2-70B -- 80 layers
+(q/o 8192x8192, k/v 1024x8192, gate/up 28672x8192, down 8192x28672, two
+RMSNorm weights), the 32000x8192 embedding and lm_head and the final norm,
+723 tensors, 69.0 G parameters -- as HCT-Q4 files (DCT-II, retention 0.30,
+INT4 coefficients with FP16 block scales, 16 KiB LZ4 blocks) resident in
+HBM, decoded to bf16.  Under torchrun the model is layer-sharded: every rank
+decodes its contiguous layer range (partition.rs create_for_layers) plus its
+share of the other tensors; there is no collective on the decode path.  A
+step decodes the whole model once (strong scaling: the work is fixed as N
+grows); the timed region is bracketed by a barrier and CUDA events and the
+reported time is the max over ranks.
 
-Reported: decoded-weight GB/s (bf16 bytes out) with inputs resident in HBM
-(`value`), the same through the host-buffer path with the H2D copy of the
-compressed files inside the timed region (`e2e`; the copies run on a copy
-stream and overlap the decode of earlier tensors), the roofline of the
-kernel with the largest share of the step (each launch bracketed by CUDA
-events on its launch stream; the factored IDCT's kernels all stream HBM, so
-the bound is the measured copy bandwidth), LZ4 GB/s on BASELINE config 2 and
-INT4 GB/s on config 1, and the reference's CPU decode restated by the oracle
-(`cpu_baseline`).
+Reported beside it: the same decode end to end with each step's compressed
+files copied from pinned host memory (`e2e`), the roofline of the kernel with
+the largest share of the step, the whole Llama-3-8B (config 4), one 70B layer
+per GPU (config 3, with the replicated-weights mode at N > 1), LZ4 on config
+2, INT4 on config 1, the V3 / HoloTensor / Zstandard formats, and the
+reference's CPU decode restated by the oracle (`cpu_baseline`, N = 1), which
+also checks a sample of the GPU's outputs.
 """
 from __future__ import annotations
 
@@ -62,26 +63,36 @@ def peaks():
 
 # ------------------------------------------------------------------ inputs
 
-def layer_files(rank_local: int, world: int, barrier) -> dict:
-    """HCT-Q4 files of the layer, encoded once per node and cached under /tmp."""
+def layer_files(rank_local: int, world: int, barrier, dev) -> dict:
+    """HCT-Q4 (and V3 / HoloTensor) files of the layer, encoded once per node by the
+    torch writer on the GPU (float64 DCT-II) from the seeded numpy weights, and
+    cached under the temporary directory."""
+    import torch
+
     from haagenti_b200 import encode as E
+    from haagenti_b200 import encode_gpu as G
 
     cache = os.path.join(tempfile.gettempdir(),
-                         f"hct_b200_bench_l70b_s{SEED}_r{int(RETENTION*100)}_q4v3holo")
+                         f"hct_b200_bench_l70b_s{SEED}_r{int(RETENTION*100)}_q4v3holo_tw")
     done = os.path.join(cache, "DONE")
     if rank_local == 0 and not os.path.exists(done):
         os.makedirs(cache, exist_ok=True)
         t0 = time.time()
         for i, (name, m, n) in enumerate(LAYER_70B):
             w = E.synthetic_weight((m, n), SEED * 100 + i)
-            c = E.dct_2d(w)  # one DCT for both formats
+            c = G.dct_2d_gpu(torch.from_numpy(w).to(dev))  # one DCT for the three formats
+            bitmap, vals = G.spectral_select_gpu(c, RETENTION)
+            payload = torch.cat([bitmap, G.quantize_int4_gpu(vals)]).cpu().numpy()
+            del bitmap, vals
             with open(os.path.join(cache, name + ".hct"), "wb") as f:
-                f.write(E.encode_spectral_q4(w, RETENTION, version=1, coeffs=c))
+                f.write(E.write_hct(payload, [m, n], E.DTYPE_I4, E.FLAG_SPECTRAL_Q4, 1))
+            c = c.cpu().numpy()
             with open(os.path.join(cache, name + ".v3"), "wb") as f:
                 f.write(E.encode_hct_v3(w, RETENTION, 1, coeffs=c))
             with open(os.path.join(cache, name + ".holo"), "wb") as f:
                 f.write(E.encode_holotensor(w, HOLO_FRAGMENTS, coeffs=c))
             del w, c
+        torch.cuda.empty_cache()
         with open(done, "w") as f:
             f.write(f"{time.time() - t0:.1f}\n")
     barrier()
@@ -273,41 +284,18 @@ def cpu_zstd_sample(frames, total_bytes: int) -> dict:
 
 # ------------------------------------------------------------------ arms
 
-def ref_layer_files() -> dict:
-    """The layer encoded by the oracle's own writer (DCT, top-k, quantize_int4,
-    compress_block; the same seeds, retention and block size as the product
-    arm's files), cached per node.  The reference arm uses only these."""
-    from oracle import hct as OH
-
-    cache = os.path.join(tempfile.gettempdir(),
-                         f"hct_b200_ref_l70b_s{SEED}_r{int(RETENTION * 100)}_oracle")
-    done = os.path.join(cache, "DONE")
-    if not os.path.exists(done):
-        os.makedirs(cache, exist_ok=True)
-        for i, (name, m, n) in enumerate(LAYER_70B):
-            w = OH.gen_weight((m, n), SEED * 100 + i)
-            with open(os.path.join(cache, name + ".hct"), "wb") as f:
-                f.write(OH.encode_spectral_q4(w, RETENTION, version=1))
-            del w
-        with open(done, "w") as f:
-            f.write("ok\n")
-    out = {}
-    for name, _, _ in LAYER_70B:
-        with open(os.path.join(cache, name + ".hct"), "rb") as f:
-            out[name] = f.read()
-    return out
-
-
 REF_BUDGET_S = 150.0  # CPU seconds the reference arm's warm-up + timed steps may take
 
 
 def run_reference(args):
     """The reference's CPU decode path (the oracle's line-by-line restatement of
     block.rs, quantization.rs and dct.rs; the Rust crates cannot be built here)
-    on the host cores, on the same workload as the product arm: the 7 tensors of
-    the layer, oracle-encoded.  A step is the whole layer while the run fits
-    REF_BUDGET_S; otherwise each step decodes the next tensors of the layer in
-    turn, about the share of the layer that keeps the run inside the budget."""
+    on the host cores, on the product arm's workload: the Llama-2-70B model
+    (config 5).  Its inputs are layer 0 of that model, encoded by the oracle's
+    own writer from numpy weights of the same shapes, seeds and distribution.
+    A step decodes the whole layer while the run fits REF_BUDGET_S; otherwise
+    each step decodes the next tensors of the layer in turn, about the share
+    of the layer that keeps the run inside the budget."""
     import shutil
 
     rank = int(os.environ.get("RANK", "0"))
@@ -316,10 +304,10 @@ def run_reference(args):
     from oracle import hct as OH
 
     threads = os.cpu_count() or 1
-    files = ref_layer_files()
-    names = [n for n, _, _ in LAYER_70B]
-    elems = {n: m * c for n, m, c in LAYER_70B}
-    layer_elems = sum(elems.values())
+    files, layer_elems = ref_model_sample_files("llama2-70b", 4)
+    names = list(files)
+    shapes = {n: OH.parse_hct(files[n]).header.shape for n in names}
+    elems = {n: int(np.prod(shapes[n])) for n in names}
 
     def decode(ns):
         t0 = time.perf_counter()
@@ -345,26 +333,29 @@ def run_reference(args):
 
     for _ in range(max(args.warmup - 1, 0)):
         decode(next_sample())
-    t_sum, e_sum, samples = 0.0, 0, []
+    t_sum, e_sum, first = 0.0, 0, None
     for _ in range(args.steps):
         ns = next_sample()
+        first = first or ns
         t_sum += decode(ns)
         e_sum += sum(elems[n] for n in ns)
-        samples.append("+".join(ns))
     value = e_sum * 2 / t_sum / 1e9
     ms = 1e3 * t_sum / args.steps
-    sample = ("the whole layer (7 tensors, %d elements) per step" % layer_elems if frac >= 1.0
-              else "per step the next tensors of the layer in turn (%s ...), about %.0f%% of "
-                   "the layer" % (samples[0], 100 * frac))
+    sample = ("per step all of layer 0 (%d tensors, %d elements)" % (len(names), layer_elems)
+              if frac >= 1.0 else
+              "per step the next tensors of layer 0 in turn (first step: %s), about %.0f%% of "
+              "the layer" % ("+".join(n.split(".", 3)[-1] for n in first), 100 * frac))
     line = {
         "impl": "reference", "metric": "decoded_weight_GBps", "value": round(value, 4),
         "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "llama2-70b-layer-hct-q4 (BASELINE config 3)",
-                   "tensors": {n: [m, c] for n, m, c in LAYER_70B}, "retention": RETENTION,
-                   "seed": SEED, "block_size": 16384, "same_config": True,
-                   "inputs": "encoded by the oracle's writer (oracle/hct.py encode_spectral_q4)"},
+        "config": {"workload": "llama2-70b whole model, HCT-Q4 (BASELINE config 5)",
+                   "retention": RETENTION, "seed": 4, "block_size": 16384,
+                   "inputs": "layer 0 of the model encoded by the oracle's writer "
+                             "(oracle/hct.py encode_spectral_q4) from numpy PCG64 weights "
+                             "N(0,0.02) with 1% outlier columns, seed 4 * 100000 + tensor "
+                             "index"},
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads,
                          "kind": "port",
                          "sample": sample + ": LZ4 + INT4 + bitmap scatter + f32 Makhoul IDCT "
@@ -379,11 +370,253 @@ def run_reference(args):
     return 0
 
 
+def model_files(H, torch, dev, arch: str, seed: int, units) -> tuple[dict, float]:
+    """HCT-Q4 files of this rank's tensors of a whole model, made by the torch
+    writer on the GPU (weights from torch's Philox generator, seed = model seed
+    * 100000 + the tensor's index in the model); the LZ4 + container step of
+    one tensor runs on a host thread while the next is encoded on the GPU."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from haagenti_b200 import encode as E
+    from haagenti_b200 import encode_gpu as G
+    from haagenti_b200 import shard
+
+    index = {n: i for i, (n, _, _) in enumerate(shard.model_units(arch))}
+    t0 = time.time()
+    files, futs = {}, {}
+    with ThreadPoolExecutor(max_workers=1) as ex:
+        for name, shape, _ in units:
+            w = G.synthetic_weight_gpu(shape, seed * 100000 + index[name], dev)
+            rows, cols = E.tensor_dims(shape)
+            payload = G.spectral_payload_gpu(w.reshape(rows, cols), RETENTION).cpu().numpy()
+            del w
+            futs[name] = ex.submit(E.write_hct, payload, list(shape), E.DTYPE_I4,
+                                   E.FLAG_SPECTRAL_Q4, 1)
+        for name, f in futs.items():
+            files[name] = f.result()
+    torch.cuda.empty_cache()
+    return files, time.time() - t0
+
+
+MODEL_WINDOW = 32  # decodes in flight before the loader reads a status back
+RESIDENT_OUT_LIMIT = 100e9  # bf16 bytes a rank keeps resident; beyond, outputs rotate
+
+
+def model_leg(H, torch, dev, args, arch: str, seed: int, world: int, rank: int, local: int,
+              barrier, clocks: bool = False, profile: bool = True) -> dict:
+    """Whole-model decode (BASELINE configs 4 and 5): every rank decodes its own
+    layer range plus its share of the other tensors (shard.rank_units), all
+    HCT-Q4 files resident in HBM; a step decodes all of them once."""
+    from collections import deque
+
+    from haagenti_b200 import encode as E
+    from haagenti_b200 import shard
+
+    units = shard.rank_units(arch, world, rank)
+    files, enc_s = model_files(H, torch, dev, arch, seed, units)
+    barrier()
+    ctxs = (H.Context(local), H.Context(local))
+    stream = torch.cuda.current_stream(dev)
+    stream2 = torch.cuda.Stream(dev)
+    streams = (stream, stream2)
+    copy_stream = torch.cuda.Stream(dev)
+    lane = {n: i % 2 for i, (n, _, _) in enumerate(units)}
+    readers = {n: H.HctReader(files[n], ctxs[lane[n]]) for n, _, _ in units}
+    out_bytes = sum(2 * shard._numel(s) for _, s, _ in units)
+    comp_bytes = sum(len(files[n]) for n, _, _ in units)
+    # outputs: one buffer per tensor when they fit beside the inputs, else the
+    # layers' outputs rotate over two layer-sized pools (layer l and l + 2 keep
+    # their tensors on the same stream, so a buffer is never written twice at once)
+    resident = out_bytes <= RESIDENT_OUT_LIMIT
+    outs = {}
+    pools = {}
+    for n, s, l in units:
+        if resident or l < 0:
+            outs[n] = torch.empty(s, dtype=torch.bfloat16, device=dev)
+        else:
+            key = (l % 2, n.split(".", 3)[-1])
+            if key not in pools:
+                pools[key] = torch.empty(s, dtype=torch.bfloat16, device=dev)
+            outs[n] = pools[key]
+    names = [n for n, _, _ in units]
+    window = max(1, min(MODEL_WINDOW, len(names) - 1))
+    pinned = None
+
+    def run(steps, upload=False, serial=False):
+        pend = deque()
+        for _ in range(steps):
+            for n in names:
+                r = readers[n]
+                if upload:
+                    r.upload(pinned[n], stream=copy_stream)
+                r.decode_async(outs[n], H.BF16, stream=streams[lane[n]])
+                pend.append(r)
+                if serial or len(pend) > window:
+                    pend.popleft().wait()
+        while pend:
+            pend.popleft().wait()
+
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+
+    def timed(steps, upload=False):
+        barrier()
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        stream2.wait_event(e0)
+        copy_stream.wait_event(e0)
+        run(steps, upload)
+        done2 = torch.cuda.Event()
+        done2.record(stream2)
+        stream.wait_event(done2)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        return e0.elapsed_time(e1)
+
+    run(1)
+    torch.cuda.synchronize(dev)
+    for n in names[:4]:
+        v = outs[n].float()
+        assert torch.isfinite(v).all() and 0.001 < v.std().item() < 1.0, n
+    run(max(args.warmup - 1, 2))
+    clk = ClockSampler(local) if clocks else None
+    if clk:
+        clk.__enter__()
+    try:
+        ms_total = timed(args.steps)
+    finally:
+        if clk:
+            clk.__exit__()
+    ms_total = shard.max_over_ranks(ms_total, dev)
+    ms_step = ms_total / args.steps
+    all_bytes = sum(2 * shard._numel(s) for _, s, _ in shard.model_units(arch))
+    value = all_bytes / (ms_step / 1e3) / 1e9
+
+    ks, ms_prof = {}, None
+    if profile:
+        for c in ctxs:
+            set_profiling(c, True)
+        barrier()
+        torch.cuda.synchronize(dev)
+        t_prof = time.perf_counter()
+        run(1, serial=True)
+        torch.cuda.synchronize(dev)
+        ms_prof = 1e3 * (time.perf_counter() - t_prof)
+        barrier()
+        for c in ctxs:
+            for k, v in kernel_stats(H, c).items():
+                a = ks.setdefault(k, dict(launches=0, ms=0.0, work=0.0))
+                a["launches"] += v["launches"]
+                a["ms"] += v["ms"]
+                a["work"] += v["work"]
+            set_profiling(c, False)
+
+    # end to end: each step's compressed files copied from pinned host memory
+    # (copy stream, overlapping earlier tensors' decode) and every status read back
+    pinned = {}
+    for n in names:
+        a = torch.empty(len(files[n]), dtype=torch.uint8, pin_memory=True)
+        a.numpy()[:] = np.frombuffer(files[n], np.uint8)
+        pinned[n] = a.numpy()
+    run(1, upload=True)
+    e2e_ms = shard.max_over_ranks(timed(args.steps, upload=True), dev) / args.steps
+    h2d = sum(_data_len(files[n]) for n in names)
+    d2h = sum(32 * readers[n].num_blocks() + 4 for n in names)
+    e2e_value = all_bytes / (e2e_ms / 1e3) / 1e9
+    # per-rank copy bandwidth of the end-to-end steps
+    h2d_gbs = h2d / (e2e_ms / 1e3) / 1e9
+
+    res = {
+        "arch": arch, "value": round(value, 3), "unit": "GB/s", "ms_per_step": round(ms_step, 3),
+        "per_gpu_GBps": round(value / world, 3),
+        "decoded_bytes_per_step": all_bytes,
+        "this_rank": {"tensors": len(names), "decoded_bytes": out_bytes,
+                      "compressed_bytes": comp_bytes, "encode_s": round(enc_s, 1),
+                      "outputs": "resident" if resident else
+                                 "layer outputs rotate over two layer-sized pools"},
+        "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
+                "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+                "h2d_GBps_per_rank": round(h2d_gbs, 2),
+                "path": "HctReader.upload (pinned host -> HBM, copy stream) + "
+                        "HctReader.decode_async per tensor, statuses read back "
+                        f"{window} tensors behind"},
+        "kernels": ks, "ms_prof": ms_prof, "clocks": clk.summary() if clk else None,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sample = [n for n, _, l in units if l == 0]
+        res["oracle_check"] = check_units_against_oracle(H, torch, readers, files, sample)
+    for r in readers.values():
+        r.close()
+    for c in ctxs:
+        c.close()
+    del outs, pools, pinned
+    torch.cuda.empty_cache()
+    return res
+
+
+def check_units_against_oracle(H, torch, readers, files, names) -> dict:
+    """The checker for a sample of model tensors: the oracle's CPU decode of the
+    product's file against the GPU's f32 decode (max-abs 1e-3, cosine 0.99999)
+    and its bf16 decode (the same bound plus the bf16 half-ulp)."""
+    from oracle import hct as OH
+
+    res = {"tensors": names, "max_abs_f32": 0.0, "min_cos_f32": 1.0, "max_excess_bf16": -1.0}
+    for n in names:
+        r = OH.decode_spectral_q4_cpu(files[n], os.cpu_count() or 1)
+        g = readers[n].decode(H.F32).cpu().numpy().reshape(r.shape)
+        a, b = g.astype(np.float64).ravel(), r.astype(np.float64).ravel()
+        res["max_abs_f32"] = max(res["max_abs_f32"], float(np.abs(a - b).max()))
+        res["min_cos_f32"] = min(res["min_cos_f32"],
+                                 float((a @ b) / np.sqrt((a @ a) * (b @ b))))
+        gb = readers[n].decode(H.BF16).float().cpu().numpy().reshape(r.shape)
+        ex = np.abs(gb - r) - (1e-3 + np.abs(r) * 2.0 ** -8)
+        res["max_excess_bf16"] = max(res["max_excess_bf16"], float(ex.max()))
+    res["ok"] = (res["max_abs_f32"] <= 1e-3 and res["min_cos_f32"] >= 0.99999
+                 and res["max_excess_bf16"] <= 0.0)
+    if not res["ok"]:
+        raise AssertionError(f"GPU decode differs from the oracle: {res}")
+    for k in ("max_abs_f32", "min_cos_f32", "max_excess_bf16"):
+        res[k] = float(f"{res[k]:.6g}")
+    return res
+
+
+def roofline_of(ks: dict, ms_prof, ms_per_step: float, steps: int) -> tuple:
+    """(roofline of the kernel with the largest share, per-kernel table) from the
+    library's per-launch CUDA-event records of `steps` profiled steps; ms_per_step
+    is the uninstrumented step time."""
+    pk = peaks()
+    if not ks:
+        return None, {}
+    top = max(ks, key=lambda k: ks[k]["ms"])
+    t = ks[top]
+    tensor = top == "umma_gemm"
+    scale = 1e12 if tensor else 1e9
+    achieved = t["work"] / (t["ms"] / 1e3) / scale
+    peak = pk["tflops_sustained"] if tensor else pk["hbm"]
+    roof = {
+        "bound": "tensor" if tensor else "hbm", "kernel": KERNEL_NAMES.get(top, top),
+        "achieved": round(achieved, 2), "peak": peak,
+        "unit": "TFLOP/s" if tensor else "GB/s", "frac": round(achieved / peak, 4),
+        "peak_kind": (f"bf16 cuBLAS sustained, of {pk['source']}" if tensor
+                      else f"STREAM copy, of {pk['source']}"),
+        "traffic": read_traffic(top),
+        "algorithmic_per_launch": round(t["work"] / t["launches"]),
+        "launches_per_step": t["launches"] / steps,
+        "share_of_step": round(t["ms"] / ms_prof, 4) if ms_prof else None,
+        "step_hbm_frac": round(sum(v["work"] for k, v in ks.items() if k != "umma_gemm")
+                               / steps / (ms_per_step / 1e3) / 1e9 / pk["hbm"], 4),
+    }
+    kern = {k: {"launches": v["launches"], "ms_total": round(v["ms"], 3),
+                "share": round(v["ms"] / ms_prof, 4) if ms_prof else None,
+                "rate": round(v["work"] / (v["ms"] / 1e3) / (1e12 if k == "umma_gemm" else 1e9), 2),
+                "rate_unit": "TFLOP/s" if k == "umma_gemm" else "GB/s"} for k, v in ks.items()}
+    return roof, kern
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
-
-    TENS = [t for t in LAYER_70B if not args.tensors or t[0] in args.tensors.split(",")]
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -393,20 +626,142 @@ def run_b200(args):
     if world > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=dev)
 
     def barrier():
         if world > 1:
             dist.barrier()
 
     import haagenti_b200 as H
+
+    # ---- headline: the whole Llama-2-70B (config 5), layer-sharded --------
+    m70 = model_leg(H, torch, dev, args, "llama2-70b", 4, world, rank, local, barrier,
+                    clocks=True)
+    # ---- config 4: the whole Llama-3-8B, layer-sharded ----------------------
+    m8 = (model_leg(H, torch, dev, args, "llama3-8b", 3, world, rank, local, barrier,
+                    profile=False) if not args.no_secondary else None)
+    # ---- config 3: one 70B layer per GPU (roofline table, replicate mode) ---
+    layer = layer_leg(H, torch, dev, args, world, rank, local, barrier)
+
+    stream = torch.cuda.current_stream(dev)
+    sec = rank == 0 and not args.no_secondary
+    lz4 = bench_lz4(H, torch, dev, stream, args) if sec else None
+    int4 = bench_int4(H, torch, dev, stream, args) if sec else None
+    v3 = holo = zstd = None
+    if sec:
+        files = layer.pop("_files")
+        ctx = H.Context(local)
+        tens = layer.pop("_tens")
+        v3 = bench_v3(H, torch, dev, stream, files, tens, ctx)
+        holo = bench_holo(H, torch, dev, stream, files, tens, ctx)
+        ctx.close()
+        zstd = bench_zstd(H, torch, dev, stream, args)
+    layer.pop("_files", None)
+    layer.pop("_tens", None)
+
+    cpu = None
+    if cpu_ok(args):
+        # the reference's CPU decode (oracle port) of layer 0 of the same model
+        cpu = cpu_model_sample("llama2-70b", 4)
+
+    roof, kern = roofline_of(m70.pop("kernels"), m70.pop("ms_prof"), m70["ms_per_step"], 1)
+    launches = sum(v["launches"] for v in kern.values()) * args.steps
+    if rank == 0:
+        line = {
+            "metric": "decoded_weight_GBps", "value": m70["value"], "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": m70["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {
+                "workload": "llama2-70b whole model, HCT-Q4 (BASELINE config 5)",
+                "layers": 80, "hidden": 8192, "intermediate": 28672, "heads": 64,
+                "kv_heads": 8, "head_dim": 128, "vocab": 32000, "tensors": 723,
+                "decoded_bytes_per_step": m70["decoded_bytes_per_step"],
+                "retention": RETENTION, "seed": 4, "block_size": 16384, "out_dtype": "bf16",
+                "weights": "N(0,0.02) f32 from torch's Philox generator on the GPU (seed "
+                           "4 * 100000 + tensor index), 1% of columns x10 on 2-D tensors; "
+                           "encoded by the torch writer (float64 DCT-II, top 30%, INT4, LZ4)",
+                "parallelism": f"layer-sharded over {world} GPU(s): contiguous layer ranges "
+                               "(partition.rs create_for_layers), embed/lm_head/norm by size; "
+                               "no collective on the decode path",
+                "pipelining": "every tensor's decode enqueued on one of two decode contexts "
+                              f"(own stream each); statuses read back {MODEL_WINDOW} tensors "
+                              "behind; steps follow each other without a drain",
+                "instrumentation": "value and e2e timed without the per-kernel profiling "
+                                   "hook; kernel times from one more step with it, one tensor "
+                                   "at a time",
+                "l2": "each step reads 20 GB of compressed files and writes 138 GB; no flush",
+            },
+            "e2e": m70["e2e"],
+            "per_gpu_GBps": m70["per_gpu_GBps"],
+            "this_rank": m70["this_rank"],
+            "roofline": roof,
+            "kernels": kern,
+            "gpu_launches": launches,
+            "oracle_check": m70.get("oracle_check"),
+            "cpu_baseline": cpu,
+            "clocks": m70["clocks"],
+            "llama3_8b": m8,
+            "layer70b": layer,
+            "lz4": lz4, "int4": int4, "hct_v3": v3, "holotensor": holo, "zstd": zstd,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def cpu_model_sample(arch: str, seed: int) -> dict:
+    """The reference's CPU decode (oracle: LZ4 + INT4 + scatter + f32 Makhoul IDCT,
+    OpenMP) of layer 0 of the model, encoded by the oracle's writer from numpy
+    weights of the same shapes, seeds and distribution."""
+    files, elems = ref_model_sample_files(arch, seed)
+    threads = os.cpu_count() or 1
+    from oracle import hct as OH
+
+    t0 = time.perf_counter()
+    for f in files.values():
+        OH.decode_spectral_q4_cpu(f, threads)
+    dt = time.perf_counter() - t0
+    return {"value": round(elems * 2 / dt / 1e9, 4), "unit": "GB/s", "cores": threads,
+            "kind": "port",
+            "sample": f"layer 0 of {arch} ({len(files)} tensors, {elems} elements, {dt:.1f} s): "
+                      "oracle LZ4 + INT4 + bitmap scatter + f32 Makhoul IDCT, OpenMP, "
+                      "bf16-equivalent bytes out"}
+
+
+def ref_model_sample_files(arch: str, seed: int) -> tuple[dict, int]:
+    """Layer 0 of the model encoded by the oracle's writer (cached per node)."""
+    from haagenti_b200 import shard
+    from oracle import hct as OH
+
+    units = shard.model_units(arch)
+    index = {n: i for i, (n, _, _) in enumerate(units)}
+    sample = [(n, s) for n, s, l in units if l == 0]
+    cache = os.path.join(tempfile.gettempdir(), f"hct_b200_ref_{arch}_s{seed}_layer0_oracle")
+    done = os.path.join(cache, "DONE")
+    if not os.path.exists(done):
+        os.makedirs(cache, exist_ok=True)
+        for n, s in sample:
+            w = OH.gen_weight(s, seed * 100000 + index[n])
+            with open(os.path.join(cache, n), "wb") as f:
+                f.write(OH.encode_spectral_q4(w, RETENTION, version=1))
+        with open(done, "w") as f:
+            f.write("ok\n")
+    files = {}
+    for n, _ in sample:
+        with open(os.path.join(cache, n), "rb") as f:
+            files[n] = f.read()
+    return files, sum(shard._numel(s) for _, s in sample)
+
+
+def layer_leg(H, torch, dev, args, world: int, rank: int, local: int, barrier) -> dict:
+    """every rank decodes its own copy of one 70B layer per step
+    (the round-1 workload, kept for its per-kernel table and the replicate mode)."""
     from haagenti_b200 import shard
 
-    files = layer_files(local, world, barrier)
-    # Two decode contexts, each with its own stream and scratch: consecutive
-    # tensors of the step (largest first) alternate between them, so that one
-    # tensor's pack kernels (L1- and issue-bound) run beside another's DFT
-    # stages (HBM-bound).
+    TENS = [t for t in LAYER_70B if not args.tensors or t[0] in args.tensors.split(",")]
+    files = layer_files(local, world, barrier, dev)
     idct_mode = {"auto": H.IDCT_AUTO, "scatter": H.IDCT_SCATTER, "dense": H.IDCT_DENSE}[args.idct]
     ctx = H.Context(local)
     ctx2 = H.Context(local)
@@ -421,11 +776,6 @@ def run_b200(args):
     outs = {n: torch.empty((m, c), dtype=torch.bfloat16, device=dev) for n, m, c in TENS}
     out_bytes = sum(2 * m * c for _, m, c in TENS)
     comp_bytes = sum(len(files[n]) for n, _, _ in TENS)
-
-    # Two reader sets alternate between steps, as a loader streaming layers
-    # would: step k+1 (another layer) is enqueued before step k's statuses
-    # are read, so no step waits for the host.  Every tensor of a step is
-    # enqueued back to back (decode_async); wait() reads its statuses.
     readers_b = {n: H.HctReader(files[n], ctxs[lane[n]]) for n, _, _ in TENS}
     outs_b = {n: torch.empty((m, c), dtype=torch.bfloat16, device=dev) for n, m, c in TENS}
     sets = [(readers, outs), (readers_b, outs_b)]
@@ -435,7 +785,7 @@ def run_b200(args):
     def issue(k, upload):
         rs, os_ = sets[k % 2]
         for n, _, _ in TENS:
-            if upload:  # copy stream; each reader orders its buffer against its decodes
+            if upload:
                 rs[n].upload(pinned[n], stream=copy_stream)
             rs[n].decode_async(os_[n], H.BF16, stream=streams[lane[n]])
 
@@ -451,7 +801,6 @@ def run_b200(args):
                 wait(k - 1)
         wait(steps - 1)
 
-    # correctness guard on the timed configuration: finite output, sane scale
     run(2)
     torch.cuda.synchronize(dev)
     for n in outs:
@@ -459,14 +808,10 @@ def run_b200(args):
         assert torch.isfinite(v).all() and 0.005 < v.std().item() < 1.0, n
         assert torch.equal(outs[n], outs_b[n]), n
     run(max(args.warmup, 3))
-
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
 
     def timed(steps, upload=False):
-        """Device time of `steps` steps: e0 on the main stream before any of
-        their work (both decode streams and the copy stream wait on it), e1
-        after all of it."""
         barrier()
         torch.cuda.synchronize(dev)
         e0.record(stream)
@@ -481,19 +826,14 @@ def run_b200(args):
         barrier()
         return e0.elapsed_time(e1)
 
-    # ---- device-resident timing (value), no instrumentation ------------
-    with ClockSampler(local) as clk:
-        ms_total = timed(args.steps)
-    ms_total = shard.max_over_ranks(ms_total, dev)
-    ms_step = ms_total / args.steps
+    # enough steps for a timed region of about a second
+    steps = max(args.steps, 200)
+    ms_total = shard.max_over_ranks(timed(steps), dev)
+    ms_step = ms_total / steps
     value = world * out_bytes / (ms_step / 1e3) / 1e9
 
-    # ---- per-kernel device times: the same steps again with the library's
-    # profiling hook (CUDA events around each launch, on its stream), one
-    # tensor at a time so that no kernel of the other context overlaps the
-    # one being timed
-    def run_serial(steps):
-        for k in range(steps):
+    def run_serial(nsteps):
+        for k in range(nsteps):
             rs, os_ = sets[k % 2]
             for n, _, _ in TENS:
                 rs[n].decode_async(os_[n], H.BF16, stream=streams[lane[n]])
@@ -506,7 +846,7 @@ def run_b200(args):
     t_prof = time.perf_counter()
     run_serial(args.steps)
     torch.cuda.synchronize(dev)
-    ms_prof = 1e3 * (time.perf_counter() - t_prof)  # host time of the serial steps
+    ms_prof = 1e3 * (time.perf_counter() - t_prof)
     barrier()
     ks = {}
     for c in ctxs:
@@ -516,11 +856,8 @@ def run_b200(args):
             a["ms"] += v["ms"]
             a["work"] += v["work"]
         set_profiling(c, False)
+    roof, kern = roofline_of(ks, ms_prof, ms_step, args.steps)
 
-    # ---- end to end through the host-buffer API ------------------------
-    # the same stream of layers with each step's compressed bytes copied from
-    # pinned host memory inside the timed region (step k+1's copies overlap
-    # step k's decode) and every step's statuses read back
     pinned = {}
     for n, _, _ in TENS:
         a = torch.empty(len(files[n]), dtype=torch.uint8, pin_memory=True)
@@ -528,25 +865,21 @@ def run_b200(args):
         pinned[n] = a.numpy()
     run(2, upload=True)
     e2e_ms = shard.max_over_ranks(timed(args.steps, upload=True), dev) / args.steps
-    for n in outs_b:  # both sets decoded the same layer
+    for n in outs_b:
         assert torch.equal(outs_b[n], outs[n]), n
     for r in readers_b.values():
         r.close()
-    h2d = sum(_data_len(files[n]) for n, _, _ in TENS)  # compressed data sections
+    h2d = sum(_data_len(files[n]) for n, _, _ in TENS)
     d2h = sum(32 * readers[n].num_blocks() + 4 for n in readers)
     e2e_value = world * out_bytes / (e2e_ms / 1e3) / 1e9
 
-    # ---- replicated-weights mode (N > 1 only; not part of the decode) ----
-    # every rank's decoded layer broadcast to every other rank over NCCL;
-    # the ranks decoded the same layer, so each received copy must equal the
-    # rank's own output
     replicate = None
     if world > 1:
         names = [f"{n}@{r}" for r in range(world) for n, _, _ in TENS]
         owner = {f"{n}@{r}": r for r in range(world) for n, _, _ in TENS}
         specs = {f"{n}@{r}": ((m, c), torch.bfloat16, dev) for r in range(world) for n, m, c in TENS}
         mine = {f"{n}@{rank}": outs[n] for n, _, _ in TENS}
-        shard.replicate_units(mine, owner, specs)  # warm-up
+        shard.replicate_units(mine, owner, specs)
         barrier()
         torch.cuda.synchronize(dev)
         e0.record(stream)
@@ -562,104 +895,31 @@ def run_b200(args):
                      "path": "shard.replicate_units: one NCCL all-gather per tensor of the layer"}
         del got
 
-    # ---- secondary: LZ4 (config 2) and INT4 (config 1) ------------------
-    lz4 = bench_lz4(H, torch, dev, stream, args) if rank == 0 and not args.no_secondary else None
-    int4 = bench_int4(H, torch, dev, stream, args) if rank == 0 and not args.no_secondary else None
-    v3 = (bench_v3(H, torch, dev, stream, files, TENS, ctx)
-          if rank == 0 and not args.no_secondary else None)
-    holo = (bench_holo(H, torch, dev, stream, files, TENS, ctx)
-            if rank == 0 and not args.no_secondary else None)
-    zstd = bench_zstd(H, torch, dev, stream, args) if rank == 0 and not args.no_secondary else None
-
-    # ---- roofline of the dominant kernel --------------------------------
-    pk = peaks()
-    launches_total = sum(v["launches"] for v in ks.values())
-    top = max(ks, key=lambda k: ks[k]["ms"]) if ks else None
-    roofline = None
-    if top:
-        t = ks[top]
-        tensor = top == "umma_gemm"  # the dense-basis contraction; every other kernel streams HBM
-        scale = 1e12 if tensor else 1e9
-        achieved = t["work"] / (t["ms"] / 1e3) / scale
-        peak = pk["tflops_sustained"] if tensor else pk["hbm"]
-        roofline = {
-            "bound": "tensor" if tensor else "hbm", "kernel": KERNEL_NAMES.get(top, top),
-            "achieved": round(achieved, 2), "peak": peak,
-            "unit": "TFLOP/s" if tensor else "GB/s", "frac": round(achieved / peak, 4),
-            "peak_kind": (f"bf16 cuBLAS sustained ({pk['source']})" if tensor
-                          else f"STREAM copy ({pk['source']})"),
-            "traffic": read_traffic(top),
-            "algorithmic_per_launch": round(t["work"] / t["launches"]),
-            "launches_per_step": t["launches"] / args.steps,
-            # of the instrumented, one-tensor-at-a-time steps
-            "share_of_step": round(t["ms"] / ms_prof, 4),
-            # every kernel of the step against the copy roofline: algorithmic
-            # bytes / uninstrumented step time
-            "step_hbm_frac": round(sum(v["work"] for k, v in ks.items() if k != "umma_gemm")
-                                   / (ms_total / 1e3) / 1e9 / pk["hbm"], 4),
-        }
-    kern = {k: {"launches": v["launches"], "ms_total": round(v["ms"], 3),
-                "share": round(v["ms"] / ms_prof, 4),
-                "rate": round(v["work"] / (v["ms"] / 1e3) / (1e12 if k == "umma_gemm" else 1e9), 2),
-                "rate_unit": "TFLOP/s" if k == "umma_gemm" else "GB/s"} for k, v in ks.items()}
-
-    cpu = scipy_idct = oracle_check = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    res = {"config": "llama2-70b layer (BASELINE config 3), one copy per GPU"
+                     + (f", subset {args.tensors}" if args.tensors else ""),
+           "value": round(value, 3), "unit": "GB/s", "ms_per_step": round(ms_step, 3),
+           "steps_timed": steps, "scaling": "weak",
+           "decoded_bytes_per_gpu_step": out_bytes, "compressed_bytes_per_gpu_step": comp_bytes,
+           "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
+                   "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
+           "roofline": roof, "kernels": kern, "replicate": replicate}
+    if cpu_ok(args):
         threads = os.cpu_count() or 1
         gbs, dt, elems, ref = cpu_decode_sample(files, threads, keep=True)
-        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"{'+'.join(CPU_SAMPLE)} of the layer ({elems} elements, {dt:.1f} s): "
-                         "oracle LZ4 + INT4 + scatter + f32 Makhoul IDCT, OpenMP"}
-        scipy_idct = cpu_scipy_idct(files, threads)
-        oracle_check = check_against_oracle(H, torch, dev, readers, outs, ref)
+        res["cpu_baseline"] = {
+            "value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{'+'.join(CPU_SAMPLE)} of the layer ({elems} elements, {dt:.1f} s): "
+                      "oracle LZ4 + INT4 + scatter + f32 Makhoul IDCT, OpenMP"}
+        res["cpu_baseline_scipy_idct"] = cpu_scipy_idct(files, threads)
+        res["oracle_check"] = check_against_oracle(H, torch, dev, readers, outs, ref)
         del ref
-
-    if rank == 0:
-        line = {
-            "metric": "decoded_weight_GBps", "value": round(value, 3), "unit": "GB/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms_step, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "llama2-70b-layer-hct-q4 (BASELINE config 3)"
-                                   + (f" subset {args.tensors}" if args.tensors else ""),
-                       "tensors": {n: [m, c] for n, m, c in TENS}, "retention": RETENTION,
-                       "seed": SEED, "block_size": 16384, "out_dtype": "bf16",
-                       "decoded_bytes_per_gpu_step": out_bytes,
-                       "compressed_bytes_per_gpu_step": comp_bytes,
-                       "parallelism": f"replicas x{world}, layer per GPU, no collective",
-                       "pipelining": "steps alternate two reader sets; step k+1 is enqueued "
-                                     "before step k's statuses are read; the step's tensors "
-                                     "(largest first) alternate between two decode contexts, "
-                                     "each on its own stream",
-                       "instrumentation": "value and e2e timed without the per-kernel "
-                                          "profiling hook; kernel times from a separate run "
-                                          "of the same steps with it, one tensor at a time",
-                       "l2": "inputs + outputs per step (1.96 GB) exceed the 126 MB L2; no flush"},
-            "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "path": "HctReader.upload (pinned host -> HBM, copy stream) + "
-                            "HctReader.decode_async per tensor; layers streamed: step k+1 is "
-                            "enqueued (copies included) before step k's statuses are read "
-                            "back (two reader sets)"},
-            "roofline": roofline,
-            "kernels": kern,
-            # the dense-path scatter is two kernels (chunk scan + scatter) under one record
-            "gpu_launches": launches_total + ks.get("spectral_scatter", {}).get("launches", 0),
-            "replicate": replicate,
-            "lz4": lz4, "int4": int4, "hct_v3": v3, "holotensor": holo, "zstd": zstd,
-            "cpu_baseline": cpu,
-            "cpu_baseline_scipy_idct": scipy_idct,
-            "oracle_check": oracle_check,
-            "clocks": clk.summary(),
-        }
-        print(json.dumps(line), flush=True)
     for r in readers.values():
         r.close()
     ctx.close()
     ctx2.close()
-    if world > 1:
-        dist.destroy_process_group()
-    return 0
+    res["_files"] = files
+    res["_tens"] = TENS
+    return res
 
 
 def check_against_oracle(H, torch, dev, readers, outs, ref) -> dict:
@@ -972,10 +1232,34 @@ def bench_int4(H, torch, dev, stream, args):
     ms = e0.elapsed_time(e1) / reps
     alg = q.size + 4 * w.size
     pk = peaks()
+    # the four copies in one batched launch (hct_b200_dequantize_int4_batch), as a
+    # loader decoding a model of plain INT4 tensors would call it
+    jobs = (L.Int4Job * copies)()
+    for i in range(copies):
+        jobs[i] = L.Int4Job(d_q[i].data_ptr(), q.size, w.size, outs[i].data_ptr())
+    wr = (C.c_size_t * copies)()
+
+    def launch_batch():
+        rc = lib.hct_b200_dequantize_int4_batch(jobs, copies, L.F32, wr, sp)
+        assert rc == 0
+
+    for _ in range(3):
+        launch_batch()
+    reps_b = 12
+    e0.record(stream)
+    for _ in range(reps_b):
+        launch_batch()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms_b = e0.elapsed_time(e1) / reps_b / copies  # per tensor
     out = {"config": "BASELINE config 1 (4096x4096 seed 0, f32 out)",
            "value": round(4 * w.size / (ms / 1e3) / 1e9, 2), "unit": "GB/s f32 out",
            "ms": round(ms, 4), "hbm_frac": round(alg / (ms / 1e3) / 1e9 / pk["hbm"], 4),
-           "l2": "4 rotating input/output pairs (306 MB) > 126 MB L2"}
+           "l2": "4 rotating input/output pairs (306 MB) > 126 MB L2",
+           "batched": {"value": round(4 * w.size / (ms_b / 1e3) / 1e9, 2),
+                       "unit": "GB/s f32 out", "ms_per_tensor": round(ms_b, 4),
+                       "hbm_frac": round(alg / (ms_b / 1e3) / 1e9 / pk["hbm"], 4),
+                       "path": f"{copies} tensors per hct_b200_dequantize_int4_batch launch"}}
     if cpu_ok(args):
         import oracle
 

@@ -260,6 +260,25 @@ def dequantize_int4(data, num_elements: int, out_dtype: int = F32, device=None, 
     return out[: written.value]
 
 
+def dequantize_int4_batch(items, out_dtype: int = F32, outs=None, stream=None):
+    """Many dequantize_int4 calls in few launches: ``items`` is a list of
+    (CUDA uint8 tensor, num_elements); returns one CUDA tensor of ``written``
+    elements per item (into ``outs`` when given)."""
+    torch = _torch()
+    n = len(items)
+    jobs = (L.Int4Job * max(n, 1))()
+    res = []
+    for i, (data, num) in enumerate(items):
+        out = (outs[i] if outs is not None else
+               torch.empty(max(num, 1), dtype=_torch_dtype(out_dtype), device=data.device))
+        jobs[i] = L.Int4Job(data.data_ptr(), data.numel(), num, out.data_ptr())
+        res.append(out)
+    written = (C.c_size_t * max(n, 1))()
+    _check(L.load().hct_b200_dequantize_int4_batch(jobs, n, out_dtype, written,
+                                                   _stream_ptr(stream)))
+    return [r[: written[i]] for i, r in enumerate(res)]
+
+
 def dequantize_int4_mp(data, num_elements: int, out_dtype: int = F32, device=None, stream=None):
     """mixed_precision.rs:489-539 on the GPU: ``num_elements`` values, zero where
     the data runs short (an empty tensor for ``num_elements == 0`` or empty data)."""

@@ -63,6 +63,11 @@ class HoloInfo(C.Structure):
                 ("rows", C.c_uint64), ("cols", C.c_uint64)]
 
 
+class Int4Job(C.Structure):
+    _fields_ = [("d_data", C.c_void_p), ("data_len", C.c_uint64), ("num_elements", C.c_uint64),
+                ("d_out", C.c_void_p)]
+
+
 class KernelStats(C.Structure):
     _fields_ = [("name", C.c_char * 32), ("launches", C.c_uint64), ("total_ms", C.c_double),
                 ("work", C.c_double)]
@@ -98,6 +103,8 @@ SIGNATURES = {
                                            C.POINTER(C.c_size_t), _vp]),
     "hct_b200_dequantize_int4_mp": (C.c_int, [_vp, _sz, _sz, _vp, C.c_int,
                                               C.POINTER(C.c_size_t), _vp]),
+    "hct_b200_dequantize_int4_batch": (C.c_int, [C.POINTER(Int4Job), C.c_uint32, C.c_int,
+                                                 C.POINTER(C.c_size_t), _vp]),
     "hct_b200_idct_2d": (C.c_int, [_vp, _vp, _vp, C.c_int, _sz, _sz, _vp]),
     "hct_b200_spectral_q4_decode": (C.c_int, [_vp, _vp, _sz, _sz, _sz, _vp, C.c_int, _vp]),
     "hct_b200_spectral_q4_decode_noalloc": (C.c_int, [_vp, _sz, _sz, _sz, _vp, C.c_int, _vp]),

@@ -22,9 +22,21 @@ cudaError_t launch_lz4_blocks(const uint8_t *d_src, const hct_b200_lz4_block *d_
 
 // ---- INT4 / spectral scatter (int4_dequant.cu) -------------------------
 // n_written elements are produced (the reference's short-input rule is
-// applied by the caller), out_dtype one of HCT_B200_F32/F16/BF16.
+// applied by the caller), out_dtype one of HCT_B200_F32/F16/BF16.  d_flag
+// receives HCT_B200_ERR_TIMEOUT if a bounded wait on a staged copy expires.
 cudaError_t launch_dequant_int4(const uint8_t *d_data, size_t data_len, size_t n_written,
-                                size_t num_elements, void *d_out, int out_dtype, cudaStream_t s);
+                                size_t num_elements, void *d_out, int out_dtype, int *d_flag,
+                                cudaStream_t s);
+// Many tensors in few launches (DQ_MAX_JOBS per launch).
+struct Int4Job {
+    const uint8_t *data;   // scales then nibbles (the quantize_int4 layout)
+    void *out;
+    uint64_t num_elements; // sets the scale section: 2 * ceil(num_elements / 32) bytes
+    uint64_t n_written;    // elements to produce (<= num_elements)
+};
+constexpr uint32_t DQ_MAX_JOBS = 64;
+cudaError_t launch_dequant_int4_batch(const Int4Job *jobs, uint32_t njobs, int out_dtype,
+                                      int *d_flag, cudaStream_t s);
 
 // Number of 1024-bit chunks the spectral scatter scans.
 __host__ __device__ inline constexpr uint64_t spectral_chunks(uint64_t total) {

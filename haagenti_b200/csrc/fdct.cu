@@ -31,6 +31,7 @@
 // (one float4 per k, computed once per length in f64).
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cmath>
 
 #include "common.cuh"
@@ -243,27 +244,25 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 7 : 3) makhoul_pack_
 }
 
 // Pack for P that is not a multiple of 4 (the vocabulary lengths, e.g.
-// H = 16000 = 125 x 128): the output row of each (b, k2) is padded to
-// Pp = round_up(P, 8) complex values (zeros past P), so that stage 1 reads
-// 16-byte aligned rows of K = 2 Pp.  Each thread writes 4 consecutive k1 of one
-// k2 (one 16-byte store) and computes every Z[k] from its four inputs (no
-// partner sharing: the partner of a run is not an aligned run when P % 4 != 0).
-template <int THREADS>
-__global__ void __launch_bounds__(THREADS) makhoul_pack_generic_kernel(
+// H = 16000 = 125 x 128 or 64128 = 501 x 128): the output row of each
+// (b, k2) is padded to Pp = round_up(P, 8) complex values (zeros past P), so
+// that stage 1 reads 16-byte aligned rows of K = 2 Pp.  Each thread writes 4
+// consecutive k1 of one k2 (one 16-byte store) and computes every Z[k] from
+// its four inputs (no partner sharing: the partner of a run is not an aligned
+// run when P % 4 != 0).  The inputs are read from global memory (a row of up
+// to 2^20 elements, cached in L1/L2): consecutive threads take consecutive
+// k2, so each of the four reads of a warp is contiguous.
+__global__ void __launch_bounds__(256) makhoul_pack_generic_kernel(
     const uint16_t *__restrict__ in, uint64_t ld_in, uint64_t B, uint32_t L, uint32_t P,
     uint32_t Pp, uint32_t Q, const float4 *__restrict__ coef, uint32_t *__restrict__ out) {
-    extern __shared__ uint4 smem_v[];
-    uint16_t *srow = reinterpret_cast<uint16_t *>(smem_v);
-    const uint32_t H = L / 2, runs = Pp / 4, items = runs * Q;
-    if (threadIdx.x == 0) srow[L] = 0;  // c[L] = 0 (never overwritten)
-    for (uint64_t b = blockIdx.x; b < B; b += gridDim.x) {
-        __syncthreads();  // previous row fully consumed
+    const uint32_t H = L / 2, runs = Pp / 4;
+    const uint64_t items = (uint64_t)runs * Q;
+    for (uint64_t b = blockIdx.y; b < B; b += gridDim.y) {
         const uint16_t *row = in + b * ld_in;
-        for (uint32_t k = threadIdx.x; k < L; k += THREADS) srow[k] = row[k];
-        __syncthreads();
         uint32_t *orow = out + b * (uint64_t)Q * Pp;
-        for (uint32_t it = threadIdx.x; it < items; it += THREADS) {
-            const uint32_t k2 = it / runs, g = it - k2 * runs;
+        for (uint64_t it = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; it < items;
+             it += (uint64_t)gridDim.x * blockDim.x) {
+            const uint32_t g = (uint32_t)(it / Q), k2 = (uint32_t)(it - (uint64_t)g * Q);
             uint32_t z[4];
 #pragma unroll
             for (int t = 0; t < 4; t++) {
@@ -271,8 +270,8 @@ __global__ void __launch_bounds__(THREADS) makhoul_pack_generic_kernel(
                 z[t] = 0;
                 if (k1 < P) {
                     const uint32_t k = Q * k1 + k2;
-                    const float a = ld_h(srow, k), bb = ld_h(srow, L - k);
-                    const float c = ld_h(srow, H + k), d = ld_h(srow, H - k);
+                    const float a = ld_h(row, k), bb = k ? ld_h(row, L - k) : 0.0f;
+                    const float c = ld_h(row, H + k), d = ld_h(row, H - k);
                     const float4 tt = coef[k];
                     z[t] = pack_z(fmaf(tt.x, a, fmaf(tt.y, bb, fmaf(tt.z, c, tt.w * d))),
                                   fmaf(tt.y, a, fmaf(-tt.x, bb, fmaf(tt.w, c, -tt.z * d))));
@@ -637,15 +636,13 @@ cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t 
                                 cudaStream_t s) {
     if ((uint64_t)P * Q != L / 2 || Q % 4 || L % 8) return cudaErrorInvalidValue;
     if (P % 4) {
-        const size_t smem = (size_t)(L + 8) * 2;
-        if (smem > 200 * 1024 || ((uintptr_t)d_out & 15)) return cudaErrorInvalidValue;
-        auto kern = makhoul_pack_generic_kernel<256>;
-        unsigned g = 0;
-        cudaError_t e = row_grid(kern, 256, smem, B, &g);
-        if (e != cudaSuccess) return e;
-        kern<<<g, 256, smem, s>>>(d_in, ld_in, B, L, P, fdct_padded_p(P), Q,
-                                  reinterpret_cast<const float4 *>(d_tables),
-                                  reinterpret_cast<uint32_t *>(d_out));
+        if ((uintptr_t)d_out & 15) return cudaErrorInvalidValue;
+        const uint64_t items = (uint64_t)(fdct_padded_p(P) / 4) * Q;
+        const unsigned gx = (unsigned)std::min<uint64_t>((items + 255) / 256, 64);
+        const unsigned gy = (unsigned)std::min<uint64_t>(B, 65535);
+        makhoul_pack_generic_kernel<<<dim3(gx, gy), 256, 0, s>>>(
+            d_in, ld_in, B, L, P, fdct_padded_p(P), Q, reinterpret_cast<const float4 *>(d_tables),
+            reinterpret_cast<uint32_t *>(d_out));
         return cudaGetLastError();
     }
     if (L % 32) return cudaErrorInvalidValue;

@@ -769,10 +769,33 @@ int hct_b200_dequantize_int4(const uint8_t *d_data, size_t data_len, size_t num_
     const size_t n = std::min<size_t>(num_elements, 2 * (data_len - sb));  // :113-115
     if (n && (!d_data || !d_out)) return HCT_B200_ERR_INVALID_ARGUMENT;
     cudaError_t e = launch_dequant_int4(d_data, data_len, n, num_elements, d_out, out_dtype,
-                                        (cudaStream_t)stream);
+                                        nullptr, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_code(e);
     *written = n;
     return HCT_B200_OK;
+}
+
+int hct_b200_dequantize_int4_batch(const hct_b200_int4_job *jobs, uint32_t num_jobs,
+                                   int out_dtype, size_t *written, void *stream) {
+    if (num_jobs && (!jobs || !written)) return HCT_B200_ERR_INVALID_ARGUMENT;
+    if (out_dtype < HCT_B200_F32 || out_dtype > HCT_B200_BF16) return HCT_B200_ERR_INVALID_ARGUMENT;
+    std::vector<Int4Job> v;
+    v.reserve(num_jobs);
+    for (uint32_t i = 0; i < num_jobs; i++) {
+        const hct_b200_int4_job &j = jobs[i];
+        written[i] = 0;
+        if (j.num_elements == 0) continue;                      // quantization.rs:83-85
+        const uint64_t sb = (j.num_elements + 31) / 32 * 2;
+        if (j.data_len < sb) continue;                          // quantization.rs:90-92
+        const uint64_t n = std::min<uint64_t>(j.num_elements, 2 * (j.data_len - sb));  // :113-115
+        if (n && (!j.d_data || !j.d_out)) return HCT_B200_ERR_INVALID_ARGUMENT;
+        written[i] = n;
+        if (n) v.push_back(Int4Job{j.d_data, j.d_out, j.num_elements, n});
+    }
+    if (v.empty()) return HCT_B200_OK;
+    cudaError_t e = launch_dequant_int4_batch(v.data(), (uint32_t)v.size(), out_dtype, nullptr,
+                                              (cudaStream_t)stream);
+    return e == cudaSuccess ? HCT_B200_OK : cuda_code(e);
 }
 
 int hct_b200_dequantize_int4_mp(const uint8_t *d_data, size_t data_len, size_t num_elements,
@@ -788,7 +811,8 @@ int hct_b200_dequantize_int4_mp(const uint8_t *d_data, size_t data_len, size_t n
     // all zero when the scales do not fit (:497-499), zero past the nibbles (:510-514)
     const size_t n = data_len < sb ? 0 : std::min<size_t>(num_elements, 2 * (data_len - sb));
     if (n) {
-        cudaError_t e = launch_dequant_int4(d_data, data_len, n, num_elements, d_out, out_dtype, s);
+        cudaError_t e =
+            launch_dequant_int4(d_data, data_len, n, num_elements, d_out, out_dtype, nullptr, s);
         if (e != cudaSuccess) return cuda_code(e);
     }
     if (n < num_elements) {

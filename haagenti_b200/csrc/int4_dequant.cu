@@ -8,6 +8,8 @@
 // conversion is done on the bits (quantization.rs:166-197), so the f32
 // product is the same single rounding the reference performs.
 #include <cuda_bf16.h>
+
+#include <algorithm>
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -54,67 +56,248 @@ __device__ __forceinline__ uint32_t ld_u32_any(const uint8_t *p) {
     return __funnelshift_r(w[0], w[1], 8u * sh);
 }
 
+// ---- dequant_int4: 16 KiB-element tiles staged by cp.async.bulk ----------
+//
+// A launch dequantises a batch of tensors ("jobs").  Each job is cut into
+// tiles of DQ_TILE elements; CTAs take tiles t = blockIdx.x + i * gridDim.x
+// over the whole batch.  A tile's 8 KiB of nibbles and 1 KiB of f16 scales
+// are copied into shared memory by two 1-D bulk copies (cp.async.bulk, no
+// multicast) issued by thread 0 up to DQ_STAGES tiles ahead and completed
+// on an mbarrier; a job whose nibble section is not 16-byte aligned, and the
+// last partial tile of every job, are read from global memory directly.
+// Within a tile, warp w takes elements [2048 w, 2048 w + 2048); lane l of
+// step j takes the 8 elements at 2048 w + 256 j + 8 l (one nibble word, one
+// scale), so every store instruction of a warp writes 1 KiB (f32) or 512 B
+// (f16/bf16) of contiguous output with 32- or 16-byte stores.
+constexpr int DQ_THREADS = 256;
+constexpr int DQ_TILE = 16384;
+constexpr int DQ_NIB = DQ_TILE / 2;   // nibble bytes per tile
+constexpr int DQ_SC = DQ_TILE / 16;   // scale bytes per tile (f16 per 32 elements)
+constexpr int DQ_STAGES = 3;
+constexpr int DQ_STAGE_BYTES = DQ_NIB + DQ_SC;
+constexpr uint64_t DQ_WAIT_NS = 2000000000ull;
+
+struct DqJob {
+    const uint8_t *data;  // f16 scales at data, nibbles at data + sb
+    void *out;
+    uint64_t sb;          // 2 * ceil(num_elements / 32)
+    uint64_t n;           // elements written
+    uint64_t tile0;       // first tile of the job within the launch
+    uint64_t bulk_tiles;  // leading whole tiles staged by the bulk copies
+    uint32_t vec;         // out is aligned for 32-byte (f32) / 16-byte (f16, bf16) stores
+    uint32_t pad;
+};
+struct DqBatch {
+    DqJob job[DQ_MAX_JOBS];
+    uint32_t njobs;
+    uint64_t total_tiles;
+};
+
+__device__ __forceinline__ uint32_t dq_smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ bool dq_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase (iteration count and %globaltimer).
+__device__ __forceinline__ bool dq_wait(uint32_t bar, uint32_t parity) {
+    if (dq_try_wait(bar, parity)) return true;
+    uint64_t t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (uint32_t i = 1; i < (1u << 30); ++i) {
+        if (dq_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0) {
+            uint64_t t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            if (t - t0 > DQ_WAIT_NS) return false;
+        }
+    }
+    return false;
+}
+
+__device__ __forceinline__ uint32_t dq_job_of(const DqBatch &b, uint64_t t) {
+    uint32_t lo = 0, hi = b.njobs - 1;
+    while (lo < hi) {  // last job whose tile0 <= t
+        const uint32_t mid = (lo + hi + 1) / 2;
+        if (b.job[mid].tile0 <= t) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+// thread 0: the two bulk copies of tile `local` of job j into stage `slot`
+__device__ __forceinline__ void dq_issue(const DqJob &jb, uint64_t local, uint8_t *stage,
+                                         uint32_t bar) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                 "r"((uint32_t)DQ_STAGE_BYTES)
+                 : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            dq_smem_u32(stage)),
+        "l"(jb.data + jb.sb + local * DQ_NIB), "r"((uint32_t)DQ_NIB), "r"(bar)
+        : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            dq_smem_u32(stage + DQ_NIB)),
+        "l"(jb.data + local * DQ_SC), "r"((uint32_t)DQ_SC), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void st_v8_f32(float *p, const float (&v)[8]) {
+    asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "f"(v[0]),
+                 "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+                 : "memory");
+}
+
+// 8 elements from one nibble word (low nibble first) and their f32 scale:
+// (nibble - 8) as an exact float is (2^23 + nibble) - (2^23 + 8).
 template <int DT>
-__device__ __forceinline__ void store8(void *out, uint64_t e, const float v[8], bool vec) {
-    if (DT == HCT_B200_F32) {
-        float *o = reinterpret_cast<float *>(out) + e;
-        if (vec) {
-            reinterpret_cast<float4 *>(o)[0] = make_float4(v[0], v[1], v[2], v[3]);
-            reinterpret_cast<float4 *>(o)[1] = make_float4(v[4], v[5], v[6], v[7]);
-        } else {
+__device__ __forceinline__ void dq_store1(void *out, uint64_t e, float v) {
+    if (DT == HCT_B200_F32) reinterpret_cast<float *>(out)[e] = v;
+    else if (DT == HCT_B200_F16) reinterpret_cast<uint16_t *>(out)[e] = to_f16(v);
+    else reinterpret_cast<uint16_t *>(out)[e] = to_bf16(v);
+}
+
+template <int DT>
+__device__ __forceinline__ void dq_emit8(void *out, uint64_t e, uint32_t w, float scale,
+                                         bool vec) {
+    float v[8];
 #pragma unroll
-            for (int j = 0; j < 8; j++) o[j] = v[j];
-        }
+    for (int k = 0; k < 8; k++)
+        v[k] = __fmul_rn(__int_as_float(0x4B000000 | ((w >> (4 * k)) & 0xfu)) - 8388616.0f, scale);
+    if (!vec) {
+#pragma unroll
+        for (int k = 0; k < 8; k++) dq_store1<DT>(out, e + k, v[k]);
+    } else if (DT == HCT_B200_F32) {
+        st_v8_f32(reinterpret_cast<float *>(out) + e, v);
     } else {
-        uint16_t h[8];
+        uint32_t h[4];
 #pragma unroll
-        for (int j = 0; j < 8; j++) h[j] = DT == HCT_B200_F16 ? to_f16(v[j]) : to_bf16(v[j]);
-        uint16_t *o = reinterpret_cast<uint16_t *>(out) + e;
-        if (vec) {
-            uint4 u;
-            u.x = h[0] | ((uint32_t)h[1] << 16);
-            u.y = h[2] | ((uint32_t)h[3] << 16);
-            u.z = h[4] | ((uint32_t)h[5] << 16);
-            u.w = h[6] | ((uint32_t)h[7] << 16);
-            *reinterpret_cast<uint4 *>(o) = u;
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; j++) o[j] = h[j];
+        for (int k = 0; k < 4; k++) {
+            const uint32_t a = DT == HCT_B200_F16 ? to_f16(v[2 * k]) : to_bf16(v[2 * k]);
+            const uint32_t c = DT == HCT_B200_F16 ? to_f16(v[2 * k + 1]) : to_bf16(v[2 * k + 1]);
+            h[k] = a | (c << 16);
         }
+        *reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(out) + e) =
+            make_uint4(h[0], h[1], h[2], h[3]);
     }
 }
 
-// One thread per group of 8 elements (4 nibble bytes, one scale).
 template <int DT>
-__global__ void __launch_bounds__(256) dequant_int4_kernel(const uint8_t *__restrict__ data,
-                                                           uint64_t sb, uint64_t n_written,
-                                                           void *__restrict__ out, bool vec_ok) {
-    const uint8_t *nib = data + sb;
-    const uint64_t full_groups = n_written / 8;
-    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    for (uint64_t g = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; g < full_groups;
-         g += stride) {
-        const uint32_t w = ld_u32_any(nib + 4 * g);
-        const uint64_t blk = g >> 2;  // 8*g / 32
-        const float scale = f16_bits_to_f32((uint32_t)data[2 * blk] | ((uint32_t)data[2 * blk + 1] << 8));
-        float v[8];
-#pragma unroll
-        for (int j = 0; j < 8; j++) v[j] = deq((w >> (4 * j)) & 0xfu, scale);
-        store8<DT>(out, 8 * g, v, vec_ok);
+__global__ void __launch_bounds__(DQ_THREADS) dequant_int4_tiles_kernel(
+    const __grid_constant__ DqBatch b, int *flag) {
+    extern __shared__ __align__(128) uint8_t dq_smem[];
+    __shared__ __align__(8) uint64_t bar[DQ_STAGES];
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < DQ_STAGES; s++)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(dq_smem_u32(&bar[s]))
+                         : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    // ragged tail (< 8 elements), byte-wise
-    const uint64_t tail0 = full_groups * 8;
-    const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (gid < n_written - tail0) {
-        const uint64_t e = tail0 + gid;
-        const uint32_t byte = nib[e >> 1];
-        const uint32_t nibble = (e & 1) ? (byte >> 4) & 0xfu : byte & 0xfu;
-        const uint64_t blk = e >> 5;
-        const float scale = f16_bits_to_f32((uint32_t)data[2 * blk] | ((uint32_t)data[2 * blk + 1] << 8));
-        const float v = deq(nibble, scale);
-        if (DT == HCT_B200_F32) reinterpret_cast<float *>(out)[e] = v;
-        else if (DT == HCT_B200_F16) reinterpret_cast<uint16_t *>(out)[e] = to_f16(v);
-        else reinterpret_cast<uint16_t *>(out)[e] = to_bf16(v);
+    __syncthreads();
+    const uint64_t T = b.total_tiles;
+    auto bulk_at = [&](uint64_t i, uint32_t *jo, uint64_t *lo) -> bool {
+        const uint64_t t = blockIdx.x + i * gridDim.x;
+        if (t >= T) return false;
+        const uint32_t j = dq_job_of(b, t);
+        *jo = j;
+        *lo = t - b.job[j].tile0;
+        return *lo < b.job[j].bulk_tiles;
+    };
+    // armed[s]: a copy into stage s is in flight (thread 0's view)
+    uint32_t armed = 0, phase = 0;
+    if (tid == 0) {
+        for (int i = 0; i < DQ_STAGES; i++) {
+            uint32_t j;
+            uint64_t lo;
+            if (bulk_at(i, &j, &lo)) {
+                dq_issue(b.job[j], lo, dq_smem + i * DQ_STAGE_BYTES, dq_smem_u32(&bar[i]));
+                armed |= 1u << i;
+            }
+        }
+    }
+    bool aborted = false;
+    for (uint64_t i = 0;; i++) {
+        const uint64_t t = blockIdx.x + i * gridDim.x;
+        if (t >= T) break;
+        const uint32_t j = dq_job_of(b, t);
+        const DqJob &jb = b.job[j];
+        const uint64_t local = t - jb.tile0;
+        const uint64_t e0 = local * DQ_TILE;  // first element of the tile within the job
+        const int slot = (int)(i % DQ_STAGES);
+        if (local < jb.bulk_tiles) {
+            const bool ok = dq_wait(dq_smem_u32(&bar[slot]), (phase >> slot) & 1u);
+            if (__syncthreads_or(!ok)) {
+                if (tid == 0 && flag) atomicExch(flag, HCT_B200_ERR_TIMEOUT);
+                aborted = true;
+                break;
+            }
+            phase ^= 1u << slot;
+            const uint8_t *st = dq_smem + slot * DQ_STAGE_BYTES;
+            uint32_t w[8];
+            float sc[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                const uint32_t wi = 256 * warp + 32 * k + lane;  // nibble word of the tile
+                w[k] = reinterpret_cast<const uint32_t *>(st)[wi];
+                sc[k] = f16_bits_to_f32(
+                    reinterpret_cast<const uint16_t *>(st + DQ_NIB)[wi >> 2]);
+            }
+            __syncthreads();  // stage consumed: refill it
+            if (tid == 0) {
+                armed &= ~(1u << slot);
+                uint32_t jn;
+                uint64_t ln;
+                if (bulk_at(i + DQ_STAGES, &jn, &ln)) {
+                    dq_issue(b.job[jn], ln, dq_smem + slot * DQ_STAGE_BYTES,
+                             dq_smem_u32(&bar[slot]));
+                    armed |= 1u << slot;
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                dq_emit8<DT>(jb.out, e0 + 2048 * warp + 256 * k + 8 * lane, w[k], sc[k], true);
+        } else {
+            // direct loads: a misaligned job, or the job's last (partial) tile
+            const uint8_t *nib = jb.data + jb.sb;
+#pragma unroll 2
+            for (int k = 0; k < 8; k++) {
+                const uint64_t e = e0 + 2048 * warp + 256 * k + 8 * lane;
+                if (e >= jb.n) continue;
+                const uint64_t blk = e >> 5;
+                const float scale = f16_bits_to_f32((uint32_t)jb.data[2 * blk] |
+                                                    ((uint32_t)jb.data[2 * blk + 1] << 8));
+                if (e + 8 <= jb.n) {
+                    dq_emit8<DT>(jb.out, e, ld_u32_any(nib + (e >> 1)), scale, jb.vec != 0);
+                } else {
+                    for (uint64_t x = e; x < jb.n; x++) {
+                        const uint32_t byte = nib[x >> 1];
+                        const uint32_t nb = (x & 1) ? byte >> 4 : byte & 0xfu;
+                        dq_store1<DT>(jb.out, x, deq(nb, scale));
+                    }
+                }
+            }
+        }
+    }
+    // teardown: copies still in flight into this CTA's stages (abort path only)
+    if (aborted && tid == 0) {
+        for (int s = 0; s < DQ_STAGES; s++)
+            if (armed & (1u << s)) {
+                if (!dq_wait(dq_smem_u32(&bar[s]), (phase >> s) & 1u) && flag)
+                    atomicExch(flag, HCT_B200_ERR_TIMEOUT);
+            }
     }
 }
 
@@ -404,27 +587,81 @@ inline unsigned grid_for(uint64_t work, unsigned threads, unsigned max_ctas = 14
 
 }  // namespace
 
+namespace {
+
+int dq_max_grid() {
+    static int g = 0;
+    if (!g) {
+        int dev = 0, sms = 148, per = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess)
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const size_t smem = (size_t)DQ_STAGES * DQ_STAGE_BYTES;
+        if (cudaFuncSetAttribute(dequant_int4_tiles_kernel<HCT_B200_F32>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ||
+            cudaFuncSetAttribute(dequant_int4_tiles_kernel<HCT_B200_F16>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ||
+            cudaFuncSetAttribute(dequant_int4_tiles_kernel<HCT_B200_BF16>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                &per, dequant_int4_tiles_kernel<HCT_B200_F32>, DQ_THREADS, smem) ||
+            per < 1)
+            per = 4;
+        g = sms * per;
+    }
+    return g;
+}
+
+}  // namespace
+
+cudaError_t launch_dequant_int4_batch(const Int4Job *jobs, uint32_t njobs, int dtype, int *d_flag,
+                                      cudaStream_t s) {
+    const size_t esz = dtype == HCT_B200_F32 ? 4 : 2;
+    for (uint32_t j0 = 0; j0 < njobs; j0 += DQ_MAX_JOBS) {
+        DqBatch b{};
+        uint64_t tiles = 0;
+        for (uint32_t j = j0; j < njobs && b.njobs < DQ_MAX_JOBS; j++) {
+            const Int4Job &in = jobs[j];
+            if (in.n_written == 0) continue;
+            if ((uintptr_t)in.out % esz) return cudaErrorInvalidValue;
+            DqJob &d = b.job[b.njobs++];
+            d.data = in.data;
+            d.out = in.out;
+            d.sb = (in.num_elements + 31) / 32 * 2;
+            d.n = in.n_written;
+            d.tile0 = tiles;
+            d.vec = (uintptr_t)in.out % (dtype == HCT_B200_F32 ? 32 : 16) == 0;
+            const bool aligned = ((uintptr_t)in.data % 16 == 0) && (d.sb % 16 == 0) && d.vec;
+            d.bulk_tiles = aligned ? in.n_written / DQ_TILE : 0;
+            tiles += (in.n_written + DQ_TILE - 1) / DQ_TILE;
+        }
+        if (!b.njobs) continue;
+        b.total_tiles = tiles;
+        const unsigned grid = (unsigned)std::min<uint64_t>(tiles, (uint64_t)dq_max_grid());
+        const size_t smem = (size_t)DQ_STAGES * DQ_STAGE_BYTES;
+        switch (dtype) {
+            case HCT_B200_F32:
+                dequant_int4_tiles_kernel<HCT_B200_F32><<<grid, DQ_THREADS, smem, s>>>(b, d_flag);
+                break;
+            case HCT_B200_F16:
+                dequant_int4_tiles_kernel<HCT_B200_F16><<<grid, DQ_THREADS, smem, s>>>(b, d_flag);
+                break;
+            default:
+                dequant_int4_tiles_kernel<HCT_B200_BF16><<<grid, DQ_THREADS, smem, s>>>(b, d_flag);
+                break;
+        }
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
 cudaError_t launch_dequant_int4(const uint8_t *d_data, size_t data_len, size_t n_written,
-                                size_t num_elements, void *d_out, int dtype, cudaStream_t s) {
+                                size_t num_elements, void *d_out, int dtype, int *d_flag,
+                                cudaStream_t s) {
     (void)data_len;
     if (n_written == 0) return cudaSuccess;
-    const uint64_t nb = (num_elements + 31) / 32;
-    const uint64_t sb = nb * 2;
-    const bool vec = ((uintptr_t)d_out & 15u) == 0;
-    const uint64_t groups = n_written / 8 > 0 ? n_written / 8 : 1;
-    const unsigned g = grid_for(groups, 256);
-    switch (dtype) {
-        case HCT_B200_F32:
-            dequant_int4_kernel<HCT_B200_F32><<<g, 256, 0, s>>>(d_data, sb, n_written, d_out, vec);
-            break;
-        case HCT_B200_F16:
-            dequant_int4_kernel<HCT_B200_F16><<<g, 256, 0, s>>>(d_data, sb, n_written, d_out, vec);
-            break;
-        default:
-            dequant_int4_kernel<HCT_B200_BF16><<<g, 256, 0, s>>>(d_data, sb, n_written, d_out, vec);
-            break;
-    }
-    return cudaGetLastError();
+    Int4Job j{d_data, d_out, num_elements, n_written};
+    return launch_dequant_int4_batch(&j, 1, dtype, d_flag, s);
 }
 
 cudaError_t launch_spectral_scatter(const uint8_t *d_payload, size_t payload_len, uint64_t rows,

@@ -122,3 +122,70 @@ def replicate_units(units: dict, owner: dict, specs: dict) -> dict:
                 dist.broadcast(t, src=r)
                 out[n] = t
     return out
+
+
+# ------------------------------------------------------------------ models
+
+# Decoder architectures of the whole-model decode (shapes as the reference's
+# safetensors_to_int4_hct example sees a checkpoint: [out, in] row-major, the
+# RMSNorm weights 1-D).
+ARCHS = {
+    "llama2-70b": dict(layers=80, hidden=8192, intermediate=28672, heads=64, kv_heads=8,
+                       head_dim=128, vocab=32000),
+    "llama3-8b": dict(layers=32, hidden=4096, intermediate=14336, heads=32, kv_heads=8,
+                      head_dim=128, vocab=128256),
+}
+
+
+def model_units(arch: str) -> list[tuple[str, tuple, int]]:
+    """Every tensor of the model as (name, shape, layer); layer -1 for the
+    embedding, the final norm and lm_head."""
+    a = ARCHS[arch]
+    h, i, q = a["hidden"], a["intermediate"], a["heads"] * a["head_dim"]
+    kv = a["kv_heads"] * a["head_dim"]
+    out = [("model.embed_tokens.weight", (a["vocab"], h), -1)]
+    for l in range(a["layers"]):
+        p = f"model.layers.{l}."
+        out += [(p + "self_attn.q_proj.weight", (q, h), l),
+                (p + "self_attn.k_proj.weight", (kv, h), l),
+                (p + "self_attn.v_proj.weight", (kv, h), l),
+                (p + "self_attn.o_proj.weight", (h, q), l),
+                (p + "mlp.gate_proj.weight", (i, h), l),
+                (p + "mlp.up_proj.weight", (i, h), l),
+                (p + "mlp.down_proj.weight", (h, i), l),
+                (p + "input_layernorm.weight", (h,), l),
+                (p + "post_attention_layernorm.weight", (h,), l)]
+    out += [("model.norm.weight", (h,), -1), ("lm_head.weight", (a["vocab"], h), -1)]
+    return out
+
+
+def rank_units(arch: str, world: int, rank: int) -> list[tuple[str, tuple, int]]:
+    """This rank's tensors: its contiguous layer range (layer_ranges) plus the
+    non-layer tensors placed by element count (assign_units), in model order."""
+    units = model_units(arch)
+    layers = set(layer_ranges(ARCHS[arch]["layers"], world)[rank])
+    extra = {n: float(_numel(s)) for n, s, l in units if l < 0}
+    # the layer ranges already load the ranks: count them in before placing the rest
+    mine_extra = set(_assign_with_base(extra, units, world)[rank])
+    return [u for u in units if (u[2] in layers) or (u[2] < 0 and u[0] in mine_extra)]
+
+
+def _numel(shape) -> int:
+    n = 1
+    for d in shape:
+        n *= int(d)
+    return n
+
+
+def _assign_with_base(extra: dict, units, world: int) -> list[list]:
+    """assign_units for the non-layer tensors, starting from each rank's layer load."""
+    arch_layers = max(l for _, _, l in units) + 1
+    load = [0.0] * world
+    for r, rng in enumerate(layer_ranges(arch_layers, world)):
+        load[r] = float(sum(_numel(s) for _, s, l in units if l in rng))
+    out: list[list] = [[] for _ in range(world)]
+    for name, cost in sorted(extra.items(), key=lambda kv: (-kv[1], str(kv[0]))):
+        r = min(range(world), key=lambda i: (load[i], i))
+        out[r].append(name)
+        load[r] += cost
+    return out

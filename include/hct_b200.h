@@ -210,6 +210,20 @@ int hct_b200_spectral_select(const float *coeffs, size_t n, size_t k, uint8_t *b
  * F16/BF16 outputs are the round-to-nearest-even of that f32 value. */
 int hct_b200_dequantize_int4(const uint8_t *d_data, size_t data_len, size_t num_elements,
                              void *d_out, int out_dtype, size_t *written, void *stream);
+/* Many dequantize_int4 calls in few launches (no single reference
+ * counterpart: each job is haagenti::testing::dequantize_int4,
+ * crates/haagenti/src/testing/quantization.rs:82-131, with the same short-input
+ * rules; written[i] receives job i's element count).  For a loader decoding a
+ * model of plain INT4 tensors (examples/safetensors_to_int4_hct.rs) without a
+ * launch per tensor.  Stream-ordered, no host synchronisation. */
+typedef struct {
+    const uint8_t *d_data;   /* f16 scales, then nibbles (the quantize_int4 layout) */
+    uint64_t data_len;
+    uint64_t num_elements;
+    void *d_out;             /* num_elements of out_dtype */
+} hct_b200_int4_job;
+int hct_b200_dequantize_int4_batch(const hct_b200_int4_job *jobs, uint32_t num_jobs,
+                                   int out_dtype, size_t *written, void *stream);
 /* The private INT4 pair of haagenti::mixed_precision (crates/haagenti/src/
  * mixed_precision.rs:489-539): the same values, but always num_elements of
  * them -- all zero when the scales do not fit, zero past the end of the

@@ -70,3 +70,15 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(L, "_lib", None)
     with pytest.raises(ImportError, match="no CPU fallback"):
         L.load()
+
+
+def test_rust_sys_crate_declares_every_header_symbol():
+    """The Rust binding (rust/haagenti-b200-sys, not compiled here: no Rust
+    toolchain) declares exactly the functions the header declares."""
+    import re
+
+    hdr = open(os.path.join(REPO, "include", "hct_b200.h")).read()
+    rs = open(os.path.join(REPO, "rust", "haagenti-b200-sys", "src", "lib.rs")).read()
+    want = set(re.findall(r"\b(hct_b200_[a-z0-9_]+)\s*\(", hdr))
+    got = set(re.findall(r"pub fn (hct_b200_[a-z0-9_]+)\(", rs))
+    assert got == want

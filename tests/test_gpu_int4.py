@@ -96,3 +96,55 @@ def test_dequantize_int4_mp_vs_oracle(hb, orc):
         assert torch.equal(bf, torch.from_numpy(ref).to(torch.bfloat16))
     assert hb.dequantize_int4_mp(q, 0).numel() == 0
     assert hb.dequantize_int4_mp(b"", 10).numel() == 0
+
+
+@pytest.mark.parametrize("n", [16384, 16385, 3 * 16384 + 5, 5 * 16384 - 8, 262144 + 31,
+                               1_000_003])
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+def test_staged_tiles_and_tails(hb, orc, dev, n, dt):
+    """Sizes around the 16384-element tile of the bulk-staged path (whole tiles
+    copied by cp.async.bulk, the partial last tile read directly), every output
+    type: f32 bit-exact, f16/bf16 the RNE of that f32."""
+    import torch
+
+    rng = np.random.default_rng(n)
+    w = (rng.standard_normal(n) * 0.05).astype(np.float32)
+    q = orc.quantize_int4(w)
+    ref = orc.dequantize_int4(q, n)
+    code = {"f32": hb.F32, "f16": hb.F16, "bf16": hb.BF16}[dt]
+    got = hb.dequantize_int4(torch.from_numpy(np.frombuffer(q, np.uint8).copy()).to(dev), n,
+                             code).float().cpu().numpy()
+    if dt == "f32":
+        assert np.array_equal(_bits(got), _bits(ref))
+    else:
+        want = torch.from_numpy(ref).to(torch.float16 if dt == "f16" else torch.bfloat16)
+        assert np.array_equal(got, want.float().numpy())
+
+
+def test_batch_mixed_jobs_and_alignments(hb, orc, dev):
+    """One batched call: jobs of many sizes, data at odd offsets (the direct-load
+    path), outputs at offsets that rule out vector stores, short inputs and an
+    empty job; every job bit-exact with its own dequantize_int4."""
+    import torch
+
+    rng = np.random.default_rng(5)
+    sizes = [1, 33, 16384, 16384 * 2 + 7, 40000, 65536 * 3, 100001, 0, 70000]
+    items, refs, outs = [], [], []
+    for i, n in enumerate(sizes):
+        w = (rng.standard_normal(n) * 0.03).astype(np.float32)
+        q = np.frombuffer(orc.quantize_int4(w), np.uint8)
+        if i == 8:
+            q = q[: len(q) - 999]  # nibbles run out: fewer elements written
+        off = [0, 2, 0, 6, 16, 0, 4, 0, 0][i]  # byte offset of the data in its buffer
+        buf = torch.zeros(len(q) + off + 16, dtype=torch.uint8, device=dev)
+        buf[off: off + len(q)] = torch.from_numpy(q.copy()).to(dev)
+        items.append((buf[off: off + len(q)], n))
+        refs.append(orc.dequantize_int4(q.tobytes(), n))
+        o_off = [0, 1, 0, 3, 0, 0, 5, 0, 0][i]  # element offset of the output
+        ob = torch.full((max(n, 1) + o_off,), float("nan"), dtype=torch.float32, device=dev)
+        outs.append(ob[o_off:])
+    got = hb.dequantize_int4_batch(items, hb.F32, outs=outs)
+    for g, r, n in zip(got, refs, sizes):
+        g = g.cpu().numpy()
+        assert g.size == r.size, n
+        assert np.array_equal(_bits(g), _bits(r)), n

@@ -133,3 +133,23 @@ def test_two_gloo_ranks_replicate_decoded_units():
         assert p.exitcode == 0
     assert [ok for _, ok in res] == [True, True]
 
+
+
+@pytest.mark.parametrize("arch", sorted(shard.ARCHS))
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_rank_units_cover_the_model_once(arch, world):
+    units = shard.model_units(arch)
+    names = [n for n, _, _ in units]
+    assert len(names) == len(set(names))
+    got = [shard.rank_units(arch, world, r) for r in range(world)]
+    flat = sorted(n for g in got for n, _, _ in g)
+    assert flat == sorted(names)
+    ranges = shard.layer_ranges(shard.ARCHS[arch]["layers"], world)
+    for r, g in enumerate(got):
+        assert {l for _, _, l in g if l >= 0} <= set(ranges[r])
+
+
+def test_model_sizes_match_the_architectures():
+    tot = {a: sum(shard._numel(s) for _, s, _ in shard.model_units(a)) for a in shard.ARCHS}
+    assert tot["llama2-70b"] == 68_976_648_192
+    assert tot["llama3-8b"] == 8_030_261_248
