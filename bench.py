@@ -196,13 +196,16 @@ KERNEL_NAMES = {  # profile record -> kernel
 TRAFFIC_PROFILE = os.path.join(REPO, "profiles", "hct_decode_layer70b.md")
 
 
-def read_traffic(kind):
-    """DRAM bytes per launch of one kernel (ncu dram__bytes_read + write), from the
+MODEL_TRAFFIC_PROFILE = os.path.join(REPO, "profiles", "hct_decode_llama2_70b.md")
+
+
+def read_traffic(kind, path=TRAFFIC_PROFILE):
+    """DRAM bytes per launch of one kernel (ncu dram__bytes_read + write), from a
     committed profile summary: a line `traffic_bytes_per_launch[<record>]: <bytes>`."""
-    if not os.path.exists(TRAFFIC_PROFILE):
+    if not os.path.exists(path):
         return None
     key = f"traffic_bytes_per_launch[{kind}]:"
-    for line in open(TRAFFIC_PROFILE):
+    for line in open(path):
         if line.startswith(key):
             try:
                 return float(line.split(":", 1)[1].strip())
@@ -521,6 +524,18 @@ def model_leg(H, torch, dev, args, arch: str, seed: int, world: int, rank: int, 
         pinned[n] = a.numpy()
     run(1, upload=True)
     e2e_ms = shard.max_over_ranks(timed(args.steps, upload=True), dev) / args.steps
+    # the copies alone, every rank at once: this box's concurrent pinned -> HBM ceiling
+    barrier()
+    torch.cuda.synchronize(dev)
+    c0 = torch.cuda.Event(enable_timing=True)
+    c1 = torch.cuda.Event(enable_timing=True)
+    c0.record(copy_stream)
+    for n in names:
+        readers[n].upload(pinned[n], stream=copy_stream)
+    c1.record(copy_stream)
+    torch.cuda.synchronize(dev)
+    copy_ms = shard.max_over_ranks(c0.elapsed_time(c1), dev)
+    barrier()
     h2d = sum(_data_len(files[n]) for n in names)
     d2h = sum(32 * readers[n].num_blocks() + 4 for n in names)
     e2e_value = all_bytes / (e2e_ms / 1e3) / 1e9
@@ -538,6 +553,9 @@ def model_leg(H, torch, dev, args, arch: str, seed: int, world: int, rank: int, 
         "e2e": {"value": round(e2e_value, 3), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
                 "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
                 "h2d_GBps_per_rank": round(h2d_gbs, 2),
+                "h2d_ceiling_GBps_per_rank": round(h2d / (copy_ms / 1e3) / 1e9, 2),
+                "h2d_ceiling_note": "the same uploads alone on every rank at once (copy "
+                                    "stream, no decode), the slowest rank",
                 "path": "HctReader.upload (pinned host -> HBM, copy stream) + "
                         "HctReader.decode_async per tensor, statuses read back "
                         f"{window} tensors behind"},
@@ -581,7 +599,8 @@ def check_units_against_oracle(H, torch, readers, files, names) -> dict:
     return res
 
 
-def roofline_of(ks: dict, ms_prof, ms_per_step: float, steps: int) -> tuple:
+def roofline_of(ks: dict, ms_prof, ms_per_step: float, steps: int,
+                traffic_file: str = TRAFFIC_PROFILE) -> tuple:
     """(roofline of the kernel with the largest share, per-kernel table) from the
     library's per-launch CUDA-event records of `steps` profiled steps; ms_per_step
     is the uninstrumented step time."""
@@ -600,7 +619,8 @@ def roofline_of(ks: dict, ms_prof, ms_per_step: float, steps: int) -> tuple:
         "unit": "TFLOP/s" if tensor else "GB/s", "frac": round(achieved / peak, 4),
         "peak_kind": (f"bf16 cuBLAS sustained, of {pk['source']}" if tensor
                       else f"STREAM copy, of {pk['source']}"),
-        "traffic": read_traffic(top),
+        "traffic": read_traffic(top, traffic_file),
+        "traffic_source": os.path.relpath(traffic_file, REPO),
         "algorithmic_per_launch": round(t["work"] / t["launches"]),
         "launches_per_step": t["launches"] / steps,
         "share_of_step": round(t["ms"] / ms_prof, 4) if ms_prof else None,
@@ -664,7 +684,8 @@ def run_b200(args):
         # the reference's CPU decode (oracle port) of layer 0 of the same model
         cpu = cpu_model_sample("llama2-70b", 4)
 
-    roof, kern = roofline_of(m70.pop("kernels"), m70.pop("ms_prof"), m70["ms_per_step"], 1)
+    roof, kern = roofline_of(m70.pop("kernels"), m70.pop("ms_prof"), m70["ms_per_step"], 1,
+                             MODEL_TRAFFIC_PROFILE)
     launches = sum(v["launches"] for v in kern.values()) * args.steps
     if rank == 0:
         line = {
@@ -1291,7 +1312,8 @@ def main():
     ap.add_argument("--tensors", default="", help="comma list of layer tensors (default: all)")
     ap.add_argument("--idct", choices=["auto", "scatter", "dense"], default="auto",
                     help="IDCT mode of the decode context (hct_b200_ctx_set_idct)")
-    ap.add_argument("--leg", choices=["zstd", "lz4", "int4"], default="",
+    ap.add_argument("--leg", choices=["zstd", "lz4", "int4", "layer", "model", "model8b"],
+                    default="",
                     help="run only this secondary measurement on cuda:0 and print its object")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -1312,6 +1334,17 @@ def run_leg(args):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     stream = torch.cuda.current_stream(dev)
+    if args.leg in ("model", "model8b", "layer"):
+        # the decode legs alone on one GPU (profiling runs of their kernels)
+        if args.leg == "layer":
+            res = layer_leg(H, torch, dev, args, 1, 0, 0, lambda: None)
+            res.pop("_files")
+            res.pop("_tens")
+        else:
+            arch, seed = ("llama2-70b", 4) if args.leg == "model" else ("llama3-8b", 3)
+            res = model_leg(H, torch, dev, args, arch, seed, 1, 0, 0, lambda: None)
+        print(json.dumps({"leg": args.leg, **res}), flush=True)
+        return 0
     fn = {"zstd": bench_zstd, "lz4": bench_lz4, "int4": bench_int4}[args.leg]
     print(json.dumps({"leg": args.leg, **fn(H, torch, dev, stream, args)}), flush=True)
     return 0

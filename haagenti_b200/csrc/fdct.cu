@@ -95,14 +95,24 @@ __device__ __forceinline__ float ld_h(const uint16_t *s, uint32_t i) {
 // k != 0, so the table is read once per pair).  Z[H-k] lies in row Q - k2
 // at k1' = P - 1 - k1: two runs of J contiguous outputs.  The row k2 = Q/2 is
 // its own partner row; its runs write only Z[k], which covers it.
+// The coefficients of a run follow from those of its first k by recurrence:
+// with u = e^{i pi k / 2L} and v = e^{i 5 pi k / 2L} (k >= 1),
+//   alpha_k = (u + i v) / 2,   beta_k = e^{i pi / 4} (u - i v) / 2,
+// and k -> k + Q multiplies u by rot.(x, y) = e^{i pi Q / 2L} and v by
+// rot.(z, w) = e^{i 5 pi Q / 2L}; u and v of the first k are recovered from its
+// table entry, so a run of J outputs loads one float4 instead of J.
 template <int QC, int J>
 __device__ __forceinline__ void pack_run(const uint16_t *s, const float4 *__restrict__ coef,
-                                         uint32_t L, uint32_t P, uint32_t Q, uint32_t g,
-                                         uint32_t k2, uint32_t *__restrict__ orow) {
+                                         float4 rot, uint32_t L, uint32_t P, uint32_t Q,
+                                         uint32_t g, uint32_t k2, uint32_t *__restrict__ orow) {
     constexpr float RS2 = 0.70710678118654752440f;
+    constexpr float RS2H = 0.35355339059327376220f;  // sqrt(2) / 4
     const uint32_t H = L / 2, k1a = J * g;
     const uint32_t ka = Q * k1a + k2;  // k of the run's first element
-    const float4 *ct = coef + ka;
+    const float4 t0 = coef[ka];
+    // gamma = e^{-i pi / 4} beta;  u = alpha + gamma,  v = -i (alpha - gamma)
+    const float gr = RS2 * (t0.z + t0.w), gi = RS2 * (t0.w - t0.z);
+    float ur = t0.x + gr, ui = t0.y + gi, vr = t0.y - gi, vi = gr - t0.x;
     uint32_t *zd = orow + k2 * P + k1a;
     uint32_t *yd = orow + (Q - k2) * P + (P - J - k1a);
     const bool partner = 2 * k2 != Q;
@@ -127,7 +137,16 @@ __device__ __forceinline__ void pack_run(const uint16_t *s, const float4 *__rest
                 id = spad<QC>(H - k);
             }
             const float a = ld_h(s, ia), b = ld_h(s, ib), c = ld_h(s, ic), d = ld_h(s, id);
-            const float4 tt = ct[Q * j];  // (alpha.re, alpha.im, beta.re, beta.im) of k
+            float4 tt;  // (alpha.re, alpha.im, beta.re, beta.im) of k
+            {
+                const float x = ur + vi, y = ui - vr;
+                tt = make_float4(0.5f * (ur - vi), 0.5f * (ui + vr), RS2H * (x - y), RS2H * (x + y));
+                const float nur = ur * rot.x - ui * rot.y, nvr = vr * rot.z - vi * rot.w;
+                ui = ur * rot.y + ui * rot.x;
+                vi = vr * rot.w + vi * rot.z;
+                ur = nur;
+                vr = nvr;
+            }
             zo[j] = pack_z(fmaf(tt.x, a, fmaf(tt.y, b, fmaf(tt.z, c, tt.w * d))),
                            fmaf(tt.y, a, fmaf(-tt.x, b, fmaf(tt.w, c, -tt.z * d))));
             const float s1 = d + c, s2 = d - c, s3 = a - b, s4 = a + b;
@@ -177,7 +196,7 @@ __device__ __forceinline__ void pack_k2_zero(const uint16_t *s, const float4 *__
 // the remaining tasks cover row k2 = 0.
 template <int QC, int J>
 __device__ __forceinline__ void pack_row(const uint16_t *s, const float4 *__restrict__ coef,
-                                         uint32_t L, uint32_t P, uint32_t Q,
+                                         float4 rot, uint32_t L, uint32_t P, uint32_t Q,
                                          uint32_t *__restrict__ orow, uint32_t warp,
                                          uint32_t nwarps, uint32_t lane) {
     const uint32_t half = QC ? (uint32_t)QC / 2 : Q / 2;
@@ -191,12 +210,12 @@ __device__ __forceinline__ void pack_row(const uint16_t *s, const float4 *__rest
             if (QC) {
                 const uint32_t kg = tau % (half / 8), og = tau / (half / 8);
                 const uint32_t g = 4 * og + (lane >> 3);
-                if (g < runs) pack_run<QC, J>(s, coef, L, P, QC, g, 8 * kg + 1 + (lane & 7), orow);
+                if (g < runs) pack_run<QC, J>(s, coef, rot, L, P, QC, g, 8 * kg + 1 + (lane & 7), orow);
             } else {
                 const uint32_t i = 32 * tau + lane;
                 if (i < runs * half) {
                     const uint32_t g = i / half;
-                    pack_run<0, J>(s, coef, L, P, Q, g, 1 + i - g * half, orow);
+                    pack_run<0, J>(s, coef, rot, L, P, Q, g, 1 + i - g * half, orow);
                 }
             }
         } else {
@@ -219,7 +238,7 @@ __device__ __forceinline__ void cp_async_wait_all() {
 template <int THREADS, int QC, int J>
 __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 7 : 3) makhoul_pack_kernel(
     const uint16_t *__restrict__ in, uint64_t ld_in, uint64_t B, uint32_t L, uint32_t P,
-    uint32_t Q, const float4 *__restrict__ coef, uint32_t *__restrict__ out) {
+    uint32_t Q, const float4 *__restrict__ coef, float4 rot, uint32_t *__restrict__ out) {
     extern __shared__ uint4 smem_v[];
     uint16_t *srow = reinterpret_cast<uint16_t *>(smem_v);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -238,7 +257,7 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 7 : 3) makhoul_pack_
             for (uint32_t k = threadIdx.x; k < L; k += THREADS) srow[spad<QC>(k)] = row[k];
         }
         __syncthreads();
-        pack_row<QC, J>(srow, coef, L, P, Q, out + b * (uint64_t)(L / 2), warp, THREADS / 32,
+        pack_row<QC, J>(srow, coef, rot, L, P, Q, out + b * (uint64_t)(L / 2), warp, THREADS / 32,
                         lane);
     }
 }
@@ -337,7 +356,7 @@ template <int THREADS, int QC, int J>
 __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack_kernel(
     const uint8_t *__restrict__ payload, uint64_t bmb, const uint32_t *__restrict__ chunk_base,
     uint64_t group_off, const uint64_t *__restrict__ meta, uint64_t B, uint32_t L, uint32_t P,
-    uint32_t Q, const float4 *__restrict__ coef, uint32_t *__restrict__ out) {
+    uint32_t Q, const float4 *__restrict__ coef, float4 rot, uint32_t *__restrict__ out) {
     constexpr uint32_t NW = THREADS / 32;
     extern __shared__ uint4 smem_v[];
     __shared__ uint32_t warp_tot[NW];
@@ -483,7 +502,7 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack
             }
         }
         __syncthreads();
-        pack_row<QC, J>(srow, coef, L, P, Q, out + b * (uint64_t)(L / 2), warp, NW, lane);
+        pack_row<QC, J>(srow, coef, rot, L, P, Q, out + b * (uint64_t)(L / 2), warp, NW, lane);
     }
 }
 
@@ -589,10 +608,17 @@ int pack_qc(uint32_t P, uint32_t Q) {
 }
 
 using MakhoulFn = void (*)(const uint16_t *, uint64_t, uint64_t, uint32_t, uint32_t, uint32_t,
-                           const float4 *, uint32_t *);
+                           const float4 *, float4, uint32_t *);
 using SpectralFn = void (*)(const uint8_t *, uint64_t, const uint32_t *, uint64_t,
                             const uint64_t *, uint64_t, uint32_t, uint32_t, uint32_t,
-                            const float4 *, uint32_t *);
+                            const float4 *, float4, uint32_t *);
+
+// (e^{i pi Q / 2L}, e^{i 5 pi Q / 2L}): the steps of u and v along k1 (pack_run)
+float4 pack_rot(uint32_t L, uint32_t Q) {
+    const double a = M_PI * (double)Q / (2.0 * (double)L);
+    return make_float4((float)std::cos(a), (float)std::sin(a), (float)std::cos(5.0 * a),
+                       (float)std::sin(5.0 * a));
+}
 
 template <int T>
 MakhoulFn makhoul_fn(int qc) {
@@ -657,7 +683,7 @@ cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t 
     cudaError_t e = row_grid(kern, threads, smem, B, &g);
     if (e != cudaSuccess) return e;
     kern<<<g, threads, smem, s>>>(d_in, ld_in, B, L, P, Q,
-                                  reinterpret_cast<const float4 *>(d_tables),
+                                  reinterpret_cast<const float4 *>(d_tables), pack_rot(L, Q),
                                   reinterpret_cast<uint32_t *>(d_out));
     return cudaGetLastError();
 }
@@ -684,7 +710,7 @@ cudaError_t launch_spectral_pack(const uint8_t *d_payload, uint64_t bmb, const u
     if (e != cudaSuccess) return e;
     kern<<<g, threads, smem, s>>>(d_payload, bmb, d_chunk, rank_group_offset(B * (uint64_t)L),
                                   d_meta, B, L, P, Q, reinterpret_cast<const float4 *>(d_tables),
-                                  reinterpret_cast<uint32_t *>(d_out));
+                                  pack_rot(L, Q), reinterpret_cast<uint32_t *>(d_out));
     return cudaGetLastError();
 }
 
