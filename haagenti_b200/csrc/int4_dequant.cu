@@ -14,6 +14,10 @@
 
 #include "common.cuh"
 
+#ifndef DQ_TILE_ELEMS
+#define DQ_TILE_ELEMS 16384
+#endif
+
 namespace hct {
 namespace {
 
@@ -70,7 +74,9 @@ __device__ __forceinline__ uint32_t ld_u32_any(const uint8_t *p) {
 // scale), so every store instruction of a warp writes 1 KiB (f32) or 512 B
 // (f16/bf16) of contiguous output with 32- or 16-byte stores.
 constexpr int DQ_THREADS = 256;
-constexpr int DQ_TILE = 16384;
+constexpr int DQ_TILE = DQ_TILE_ELEMS;
+constexpr int DQ_STEPS = DQ_TILE / 2048;  // 8-element steps per lane within a tile
+constexpr int DQ_WARP_SPAN = 256 * DQ_STEPS;  // elements per warp per tile
 constexpr int DQ_NIB = DQ_TILE / 2;   // nibble bytes per tile
 constexpr int DQ_SC = DQ_TILE / 16;   // scale bytes per tile (f16 per 32 elements)
 constexpr int DQ_STAGES = 3;
@@ -246,11 +252,11 @@ __global__ void __launch_bounds__(DQ_THREADS) dequant_int4_tiles_kernel(
             }
             phase ^= 1u << slot;
             const uint8_t *st = dq_smem + slot * DQ_STAGE_BYTES;
-            uint32_t w[8];
-            float sc[8];
+            uint32_t w[DQ_STEPS];
+            float sc[DQ_STEPS];
 #pragma unroll
-            for (int k = 0; k < 8; k++) {
-                const uint32_t wi = 256 * warp + 32 * k + lane;  // nibble word of the tile
+            for (int k = 0; k < DQ_STEPS; k++) {
+                const uint32_t wi = (DQ_WARP_SPAN / 8) * warp + 32 * k + lane;  // nibble word
                 w[k] = reinterpret_cast<const uint32_t *>(st)[wi];
                 sc[k] = f16_bits_to_f32(
                     reinterpret_cast<const uint16_t *>(st + DQ_NIB)[wi >> 2]);
@@ -267,14 +273,15 @@ __global__ void __launch_bounds__(DQ_THREADS) dequant_int4_tiles_kernel(
                 }
             }
 #pragma unroll
-            for (int k = 0; k < 8; k++)
-                dq_emit8<DT>(jb.out, e0 + 2048 * warp + 256 * k + 8 * lane, w[k], sc[k], true);
+            for (int k = 0; k < DQ_STEPS; k++)
+                dq_emit8<DT>(jb.out, e0 + DQ_WARP_SPAN * warp + 256 * k + 8 * lane, w[k], sc[k],
+                             true);
         } else {
             // direct loads: a misaligned job, or the job's last (partial) tile
             const uint8_t *nib = jb.data + jb.sb;
 #pragma unroll 2
-            for (int k = 0; k < 8; k++) {
-                const uint64_t e = e0 + 2048 * warp + 256 * k + 8 * lane;
+            for (int k = 0; k < DQ_STEPS; k++) {
+                const uint64_t e = e0 + DQ_WARP_SPAN * warp + 256 * k + 8 * lane;
                 if (e >= jb.n) continue;
                 const uint64_t blk = e >> 5;
                 const float scale = f16_bits_to_f32((uint32_t)jb.data[2 * blk] |

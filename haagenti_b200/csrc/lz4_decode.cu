@@ -300,6 +300,11 @@ __global__ void __launch_bounds__(256) lz4_decode_blocks_kernel(
                 if (lit <= 32) {  // short run: one byte per lane
                     if ((uint64_t)lane < lit) out[op + lane] = in[ip + lane];
                 } else if (!staged && lit >= 1024) {
+                    // the bytes after the run (offset, next token, its length
+                    // bytes, the next short sequences) are the next reads of the
+                    // serial walk: ask for their 4 lines while the run is copied
+                    if (lane < 4 && ip + lit + 128ull * lane < in_len)
+                        asm volatile("prefetch.global.L1 [%0];" ::"l"(in + ip + lit + 128ull * lane));
                     warp_copy_wide(out + op, in + ip, lit, lane);
                 } else {
                     warp_copy(out + op, in + ip, lit, lane);
