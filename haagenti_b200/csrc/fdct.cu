@@ -100,8 +100,11 @@ __device__ __forceinline__ float ld_h(const uint16_t *s, uint32_t i) {
 //   alpha_k = (u + i v) / 2,   beta_k = e^{i pi / 4} (u - i v) / 2,
 // and k -> k + Q multiplies u by rot.(x, y) = e^{i pi Q / 2L} and v by
 // rot.(z, w) = e^{i 5 pi Q / 2L}; u and v of the first k are recovered from its
-// table entry, so a run of J outputs loads one float4 instead of J.
-template <int QC, int J>
+// table entry, so a run of J outputs loads one float4 instead of J.  REC
+// selects that recurrence (fewer L1 wavefronts, for the L1-bound column pack)
+// or one table load per k (fewer instructions, for the issue-bound row pack
+// that also decodes the payload).
+template <int QC, int J, bool REC>
 __device__ __forceinline__ void pack_run(const uint16_t *s, const float4 *__restrict__ coef,
                                          float4 rot, uint32_t L, uint32_t P, uint32_t Q,
                                          uint32_t g, uint32_t k2, uint32_t *__restrict__ orow) {
@@ -138,7 +141,9 @@ __device__ __forceinline__ void pack_run(const uint16_t *s, const float4 *__rest
             }
             const float a = ld_h(s, ia), b = ld_h(s, ib), c = ld_h(s, ic), d = ld_h(s, id);
             float4 tt;  // (alpha.re, alpha.im, beta.re, beta.im) of k
-            {
+            if (!REC) {
+                tt = coef[ka + Q * (uint32_t)j];
+            } else {
                 const float x = ur + vi, y = ui - vr;
                 tt = make_float4(0.5f * (ur - vi), 0.5f * (ui + vr), RS2H * (x - y), RS2H * (x + y));
                 const float nur = ur * rot.x - ui * rot.y, nvr = vr * rot.z - vi * rot.w;
@@ -194,7 +199,7 @@ __device__ __forceinline__ void pack_k2_zero(const uint16_t *s, const float4 *__
 //     touches 8 rows;
 //   QC = 0 (any Q, runs of 4): lane items (run g, row k2), k2 fastest;
 // the remaining tasks cover row k2 = 0.
-template <int QC, int J>
+template <int QC, int J, bool REC>
 __device__ __forceinline__ void pack_row(const uint16_t *s, const float4 *__restrict__ coef,
                                          float4 rot, uint32_t L, uint32_t P, uint32_t Q,
                                          uint32_t *__restrict__ orow, uint32_t warp,
@@ -210,12 +215,13 @@ __device__ __forceinline__ void pack_row(const uint16_t *s, const float4 *__rest
             if (QC) {
                 const uint32_t kg = tau % (half / 8), og = tau / (half / 8);
                 const uint32_t g = 4 * og + (lane >> 3);
-                if (g < runs) pack_run<QC, J>(s, coef, rot, L, P, QC, g, 8 * kg + 1 + (lane & 7), orow);
+                if (g < runs)
+                    pack_run<QC, J, REC>(s, coef, rot, L, P, QC, g, 8 * kg + 1 + (lane & 7), orow);
             } else {
                 const uint32_t i = 32 * tau + lane;
                 if (i < runs * half) {
                     const uint32_t g = i / half;
-                    pack_run<0, J>(s, coef, rot, L, P, Q, g, 1 + i - g * half, orow);
+                    pack_run<0, J, REC>(s, coef, rot, L, P, Q, g, 1 + i - g * half, orow);
                 }
             }
         } else {
@@ -257,7 +263,8 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 7 : 3) makhoul_pack_
             for (uint32_t k = threadIdx.x; k < L; k += THREADS) srow[spad<QC>(k)] = row[k];
         }
         __syncthreads();
-        pack_row<QC, J>(srow, coef, rot, L, P, Q, out + b * (uint64_t)(L / 2), warp, THREADS / 32,
+        pack_row<QC, J, true>(srow, coef, rot, L, P, Q, out + b * (uint64_t)(L / 2), warp,
+                                 THREADS / 32,
                         lane);
     }
 }
@@ -502,7 +509,7 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack
             }
         }
         __syncthreads();
-        pack_row<QC, J>(srow, coef, rot, L, P, Q, out + b * (uint64_t)(L / 2), warp, NW, lane);
+        pack_row<QC, J, false>(srow, coef, rot, L, P, Q, out + b * (uint64_t)(L / 2), warp, NW, lane);
     }
 }
 
