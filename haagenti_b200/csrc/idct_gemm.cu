@@ -195,7 +195,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     SmemCtl *ctl = reinterpret_cast<SmemCtl *>(smem + (size_t)STAGES * STAGE_BYTES);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t m_tile = blockIdx.x % m_tiles, n_tile = blockIdx.x / m_tiles;
+    // mode 2 (DFT stage 1 with P > 128: a tall A against a short B) walks the
+    // few n-tiles of one m-tile in consecutive CTAs, so that the A tile they
+    // share is read from DRAM once and found in L2 by the others
+    const uint32_t n_tiles = (N + BN - 1) / BN;
+    const uint32_t m_tile = mode == 2 ? blockIdx.x / n_tiles : blockIdx.x % m_tiles;
+    const uint32_t n_tile = mode == 2 ? blockIdx.x % n_tiles : blockIdx.x / m_tiles;
     const int m0 = (int)(m_tile * BM), n0 = (int)(n_tile * BN);
     const int num_kb = (int)((K + BK - 1) / BK);
 

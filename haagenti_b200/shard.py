@@ -137,10 +137,11 @@ ARCHS = {
 }
 
 
-def model_units(arch: str) -> list[tuple[str, tuple, int]]:
+def model_units(arch) -> list[tuple[str, tuple, int]]:
     """Every tensor of the model as (name, shape, layer); layer -1 for the
-    embedding, the final norm and lm_head."""
-    a = ARCHS[arch]
+    embedding, the final norm and lm_head.  ``arch`` names an entry of ARCHS
+    or is a dict with the same keys."""
+    a = ARCHS[arch] if isinstance(arch, str) else arch
     h, i, q = a["hidden"], a["intermediate"], a["heads"] * a["head_dim"]
     kv = a["kv_heads"] * a["head_dim"]
     out = [("model.embed_tokens.weight", (a["vocab"], h), -1)]
@@ -159,11 +160,12 @@ def model_units(arch: str) -> list[tuple[str, tuple, int]]:
     return out
 
 
-def rank_units(arch: str, world: int, rank: int) -> list[tuple[str, tuple, int]]:
+def rank_units(arch, world: int, rank: int) -> list[tuple[str, tuple, int]]:
     """This rank's tensors: its contiguous layer range (layer_ranges) plus the
     non-layer tensors placed by element count (assign_units), in model order."""
     units = model_units(arch)
-    layers = set(layer_ranges(ARCHS[arch]["layers"], world)[rank])
+    a = ARCHS[arch] if isinstance(arch, str) else arch
+    layers = set(layer_ranges(a["layers"], world)[rank])
     extra = {n: float(_numel(s)) for n, s, l in units if l < 0}
     # the layer ranges already load the ranks: count them in before placing the rest
     mine_extra = set(_assign_with_base(extra, units, world)[rank])
