@@ -301,16 +301,23 @@ __global__ void __launch_bounds__(THREADS, 1)
                     // a warp (consecutive k2) store 32 consecutive complex values
                     const uint32_t Q = sp.Q, b = (uint32_t)row / Q, k2 = (uint32_t)row - b * Q;
                     uint32_t *g = reinterpret_cast<uint32_t *>(out);
+                    // e^{2 pi i k2 m1 / H} for the chunk's first m1 (k2 m1 < Q P = H),
+                    // then stepped by e^{2 pi i k2 / H} along m1
+                    const uint32_t m1a = (uint32_t)col0 >> 1;
+                    float2 tw = sp.twiddle[k2 * m1a];
+                    const float2 st = sp.twiddle[k2];
 #pragma unroll
                     for (int j = 0; j < 32; j += 2) {
                         if (j < ncols) {
-                            const uint32_t m1 = (uint32_t)(col0 + j) >> 1;
-                            const float2 tw = sp.twiddle[k2 * m1];  // k2 m1 < Q P = H
+                            const uint32_t m1 = m1a + (uint32_t)(j >> 1);
                             const float re = __uint_as_float(r[j]), im = __uint_as_float(r[j + 1]);
                             g[((uint64_t)m1 * sp.batch + b) * Q + k2] =
                                 (uint32_t)f2h(re * tw.x - im * tw.y) |
                                 ((uint32_t)f2h(re * tw.y + im * tw.x) << 16);
                         }
+                        const float tx = tw.x * st.x - tw.y * st.y;
+                        tw.y = tw.x * st.y + tw.y * st.x;
+                        tw.x = tx;
                     }
                 } else if (mode == 0) {
                     uint16_t *o = reinterpret_cast<uint16_t *>(out);
