@@ -91,6 +91,12 @@ cudaError_t launch_basis(const double *d_cos_table, uint64_t n, half_bits *d_bas
 //   mode 3: DFT stage 2: row R = (m1, b), complex output m2, j = m1 + P*m2,
 //           scaled and scattered to out[(4j + 2 ri) * ldo + b] (j < H/2) or
 //           out[(4(H-1-j) + 3 - 2 ri) * ldo + b] in out_dtype
+//   mode 4: DFT stage 1 with the twiddle folded into per-k2 matrices: A holds
+//           Z as [k2][b][k1] (rows (k2, b), batch % 128 == 0), B is a table of
+//           Q matrices of stage_w_rows(N, K) rows each (N = 2P live rows);
+//           output G[m1][k2][ri][b] fp16
+//   mode 5: DFT stage 2 reading that G as an MN-major operand (A = G, lda =
+//           batch, K = 2Q a multiple of 64); output as mode 3
 struct GemmArgs {
     const half_bits *A;
     const half_bits *B;
@@ -112,6 +118,13 @@ struct GemmArgs {
     uint32_t *tile_counter = nullptr;
 };
 cudaError_t launch_umma_gemm(const GemmArgs &args, cudaStream_t s);
+// rows of each per-k2 matrix of mode 4 (the stage kernel's resident W height)
+uint32_t stage_w_rows(uint64_t N, uint64_t K);
+// The mode-4 table: for k2 < Q, rows o = 2 m1 + ri (< 2P; zero up to w_rows)
+// and columns k = 2 k1 + rk (< 2P; zero up to ld), the realified
+// e^{2 pi i m1 (Q k1 + k2) / H}.
+cudaError_t launch_twiddled_dft_table(uint32_t P, uint32_t Q, uint32_t w_rows, uint32_t ld,
+                                      half_bits *d_out, cudaStream_t s);
 
 // ---- factored DCT-III (fdct.cu) -----------------------------------------
 // L even, H = L/2 = P*Q: preferably P, Q multiples of 4 and <= 128 (the most
@@ -125,9 +138,10 @@ uint32_t fdct_padded_p(uint32_t P);
 // rows of length L (fp16, stride ld_in) -> Z[b][k2][k1] complex fp16 pairs,
 // rows of fdct_padded_p(P) values.  d_tables: the per-k pack coefficients
 // (natural k order) written by launch_pack_tables(L, P, Q).
+// k2_major: Z laid out [k2][b][k1] instead (the input of DFT stage mode 4).
 cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t batch, uint32_t L,
                                 uint32_t P, uint32_t Q, const float *d_tables, half_bits *d_out,
-                                cudaStream_t s);
+                                bool k2_major, cudaStream_t s);
 // L/2 float4 (alpha_k, beta_k) in natural k order (P Q = L/2).
 cudaError_t launch_pack_tables(uint32_t L, uint32_t P, uint32_t Q, float *d_tables,
                                cudaStream_t s);
@@ -141,7 +155,7 @@ bool spectral_pack_supported(uint64_t L);
 cudaError_t launch_spectral_pack(const uint8_t *d_payload, uint64_t bmb, const uint32_t *d_chunk,
                                  const uint64_t *d_meta, uint64_t batch, uint32_t L, uint32_t P,
                                  uint32_t Q, const float *d_tables, half_bits *d_out,
-                                 cudaStream_t s);
+                                 bool k2_major, cudaStream_t s);
 // ---- HoloTensor SV03 fragments (holo.cu) ---------------------------------
 // One residue class r of the raster positions p = r + F i: fragment values
 // vals[src + i - q0] for q0 <= i < q0 + count, no fragment when count == 0.

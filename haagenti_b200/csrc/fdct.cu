@@ -107,7 +107,8 @@ __device__ __forceinline__ float ld_h(const uint16_t *s, uint32_t i) {
 template <int QC, int J, bool REC>
 __device__ __forceinline__ void pack_run(const uint16_t *s, const float4 *__restrict__ coef,
                                          float4 rot, uint32_t L, uint32_t P, uint32_t Q,
-                                         uint32_t g, uint32_t k2, uint32_t *__restrict__ orow) {
+                                         uint32_t g, uint32_t k2, uint32_t *__restrict__ orow,
+                                         uint64_t ks) {
     constexpr float RS2 = 0.70710678118654752440f;
     constexpr float RS2H = 0.35355339059327376220f;  // sqrt(2) / 4
     const uint32_t H = L / 2, k1a = J * g;
@@ -116,8 +117,8 @@ __device__ __forceinline__ void pack_run(const uint16_t *s, const float4 *__rest
     // gamma = e^{-i pi / 4} beta;  u = alpha + gamma,  v = -i (alpha - gamma)
     const float gr = RS2 * (t0.z + t0.w), gi = RS2 * (t0.w - t0.z);
     float ur = t0.x + gr, ui = t0.y + gi, vr = t0.y - gi, vi = gr - t0.x;
-    uint32_t *zd = orow + k2 * P + k1a;
-    uint32_t *yd = orow + (Q - k2) * P + (P - J - k1a);
+    uint32_t *zd = orow + (uint64_t)k2 * ks + k1a;
+    uint32_t *yd = orow + (uint64_t)(Q - k2) * ks + (P - J - k1a);
     const bool partner = 2 * k2 != Q;
     const uint32_t pa = spad<QC>(ka), pb = spad<QC>(L - ka), pc = spad<QC>(H + ka), pd = spad<QC>(H - ka);
     uint32_t zo[J], yo[J];
@@ -202,7 +203,7 @@ __device__ __forceinline__ void pack_k2_zero(const uint16_t *s, const float4 *__
 template <int QC, int J, bool REC>
 __device__ __forceinline__ void pack_row(const uint16_t *s, const float4 *__restrict__ coef,
                                          float4 rot, uint32_t L, uint32_t P, uint32_t Q,
-                                         uint32_t *__restrict__ orow, uint32_t warp,
+                                         uint32_t *__restrict__ orow, uint64_t ks, uint32_t warp,
                                          uint32_t nwarps, uint32_t lane) {
     const uint32_t half = QC ? (uint32_t)QC / 2 : Q / 2;
     const uint32_t runs = P / J;
@@ -216,12 +217,12 @@ __device__ __forceinline__ void pack_row(const uint16_t *s, const float4 *__rest
                 const uint32_t kg = tau % (half / 8), og = tau / (half / 8);
                 const uint32_t g = 4 * og + (lane >> 3);
                 if (g < runs)
-                    pack_run<QC, J, REC>(s, coef, rot, L, P, QC, g, 8 * kg + 1 + (lane & 7), orow);
+                    pack_run<QC, J, REC>(s, coef, rot, L, P, QC, g, 8 * kg + 1 + (lane & 7), orow, ks);
             } else {
                 const uint32_t i = 32 * tau + lane;
                 if (i < runs * half) {
                     const uint32_t g = i / half;
-                    pack_run<0, J, REC>(s, coef, rot, L, P, Q, g, 1 + i - g * half, orow);
+                    pack_run<0, J, REC>(s, coef, rot, L, P, Q, g, 1 + i - g * half, orow, ks);
                 }
             }
         } else {
@@ -244,7 +245,8 @@ __device__ __forceinline__ void cp_async_wait_all() {
 template <int THREADS, int QC, int J>
 __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 7 : 3) makhoul_pack_kernel(
     const uint16_t *__restrict__ in, uint64_t ld_in, uint64_t B, uint32_t L, uint32_t P,
-    uint32_t Q, const float4 *__restrict__ coef, float4 rot, uint32_t *__restrict__ out) {
+    uint32_t Q, const float4 *__restrict__ coef, float4 rot, uint32_t *__restrict__ out,
+    uint64_t bs, uint64_t ks) {
     extern __shared__ uint4 smem_v[];
     uint16_t *srow = reinterpret_cast<uint16_t *>(smem_v);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -263,7 +265,7 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 7 : 3) makhoul_pack_
             for (uint32_t k = threadIdx.x; k < L; k += THREADS) srow[spad<QC>(k)] = row[k];
         }
         __syncthreads();
-        pack_row<QC, J, true>(srow, coef, rot, L, P, Q, out + b * (uint64_t)(L / 2), warp,
+        pack_row<QC, J, true>(srow, coef, rot, L, P, Q, out + b * bs, ks, warp,
                                  THREADS / 32,
                         lane);
     }
@@ -280,12 +282,13 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 7 : 3) makhoul_pack_
 // k2, so each of the four reads of a warp is contiguous.
 __global__ void __launch_bounds__(256) makhoul_pack_generic_kernel(
     const uint16_t *__restrict__ in, uint64_t ld_in, uint64_t B, uint32_t L, uint32_t P,
-    uint32_t Pp, uint32_t Q, const float4 *__restrict__ coef, uint32_t *__restrict__ out) {
+    uint32_t Pp, uint32_t Q, const float4 *__restrict__ coef, uint32_t *__restrict__ out,
+    uint64_t bs, uint64_t ks) {
     const uint32_t H = L / 2, runs = Pp / 4;
     const uint64_t items = (uint64_t)runs * Q;
     for (uint64_t b = blockIdx.y; b < B; b += gridDim.y) {
         const uint16_t *row = in + b * ld_in;
-        uint32_t *orow = out + b * (uint64_t)Q * Pp;
+        uint32_t *orow = out + b * bs;
         for (uint64_t it = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; it < items;
              it += (uint64_t)gridDim.x * blockDim.x) {
             const uint32_t g = (uint32_t)(it / Q), k2 = (uint32_t)(it - (uint64_t)g * Q);
@@ -303,7 +306,7 @@ __global__ void __launch_bounds__(256) makhoul_pack_generic_kernel(
                                   fmaf(tt.y, a, fmaf(-tt.x, bb, fmaf(tt.w, c, -tt.z * d))));
                 }
             }
-            *reinterpret_cast<uint4 *>(orow + (uint64_t)k2 * Pp + 4 * g) =
+            *reinterpret_cast<uint4 *>(orow + (uint64_t)k2 * ks + 4 * g) =
                 make_uint4(z[0], z[1], z[2], z[3]);
         }
     }
@@ -363,7 +366,8 @@ template <int THREADS, int QC, int J>
 __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack_kernel(
     const uint8_t *__restrict__ payload, uint64_t bmb, const uint32_t *__restrict__ chunk_base,
     uint64_t group_off, const uint64_t *__restrict__ meta, uint64_t B, uint32_t L, uint32_t P,
-    uint32_t Q, const float4 *__restrict__ coef, float4 rot, uint32_t *__restrict__ out) {
+    uint32_t Q, const float4 *__restrict__ coef, float4 rot, uint32_t *__restrict__ out,
+    uint64_t bs, uint64_t ks) {
     constexpr uint32_t NW = THREADS / 32;
     extern __shared__ uint4 smem_v[];
     __shared__ uint32_t warp_tot[NW];
@@ -509,7 +513,7 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack
             }
         }
         __syncthreads();
-        pack_row<QC, J, false>(srow, coef, rot, L, P, Q, out + b * (uint64_t)(L / 2), warp, NW, lane);
+        pack_row<QC, J, false>(srow, coef, rot, L, P, Q, out + b * bs, ks, warp, NW, lane);
     }
 }
 
@@ -549,6 +553,31 @@ __global__ void dft_matrix_kernel(uint32_t n, uint32_t rows_pad, uint32_t ld, ui
             sincospi(2.0 * (double)j / (double)n, &s, &co);
             if ((r & 1) == 0) v = (c & 1) == 0 ? (float)co : (float)-s;
             else v = (c & 1) == 0 ? (float)s : (float)co;
+        }
+        out[idx] = f2h(v);
+    }
+}
+
+// Per-k2 stage-1 matrices with the twiddle folded in (mode 4 of the stage
+// kernel): entry (k2, o = 2 m1 + ri, k = 2 k1 + rk) is the realified
+// e^{2 pi i m1 (Q k1 + k2) / H} (rows [cos, -sin], [sin, cos] as in
+// dft_matrix_kernel), the angle reduced exactly in integers and evaluated in f64.
+__global__ void twiddled_dft_kernel(uint32_t P, uint32_t Q, uint32_t w_rows, uint32_t ld,
+                                    uint16_t *out) {
+    const uint64_t H = (uint64_t)P * Q;
+    const uint64_t per_k2 = (uint64_t)w_rows * ld, total = per_k2 * Q;
+    for (uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t k2 = idx / per_k2, rem = idx - k2 * per_k2;
+        const uint32_t o = (uint32_t)(rem / ld), k = (uint32_t)(rem - (uint64_t)o * ld);
+        float v = 0.0f;
+        if (o < 2 * P && k < 2 * P) {
+            const uint64_t m1 = o >> 1, k1 = k >> 1;
+            const uint64_t j = (m1 * (Q * k1 + k2)) % H;
+            double sn, cs;
+            sincospi(2.0 * (double)j / (double)H, &sn, &cs);
+            if ((o & 1) == 0) v = (k & 1) == 0 ? (float)cs : (float)-sn;
+            else v = (k & 1) == 0 ? (float)sn : (float)cs;
         }
         out[idx] = f2h(v);
     }
@@ -615,10 +644,10 @@ int pack_qc(uint32_t P, uint32_t Q) {
 }
 
 using MakhoulFn = void (*)(const uint16_t *, uint64_t, uint64_t, uint32_t, uint32_t, uint32_t,
-                           const float4 *, float4, uint32_t *);
+                           const float4 *, float4, uint32_t *, uint64_t, uint64_t);
 using SpectralFn = void (*)(const uint8_t *, uint64_t, const uint32_t *, uint64_t,
                             const uint64_t *, uint64_t, uint32_t, uint32_t, uint32_t,
-                            const float4 *, float4, uint32_t *);
+                            const float4 *, float4, uint32_t *, uint64_t, uint64_t);
 
 // (e^{i pi Q / 2L}, e^{i 5 pi Q / 2L}): the steps of u and v along k1 (pack_run)
 float4 pack_rot(uint32_t L, uint32_t Q) {
@@ -666,8 +695,11 @@ cudaError_t row_grid(F kern, int threads, size_t smem, uint64_t B, unsigned *gri
 
 cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t B, uint32_t L,
                                 uint32_t P, uint32_t Q, const float *d_tables, half_bits *d_out,
-                                cudaStream_t s) {
+                                bool k2_major, cudaStream_t s) {
     if ((uint64_t)P * Q != L / 2 || Q % 4 || L % 8) return cudaErrorInvalidValue;
+    const uint64_t Pp = fdct_padded_p(P);
+    // Z[b][k2][k1] (b stride Q Pp, k2 stride Pp) or Z[k2][b][k1] (Pp, B Pp)
+    const uint64_t bs = k2_major ? Pp : (uint64_t)Q * Pp, ks = k2_major ? B * Pp : Pp;
     if (P % 4) {
         if ((uintptr_t)d_out & 15) return cudaErrorInvalidValue;
         const uint64_t items = (uint64_t)(fdct_padded_p(P) / 4) * Q;
@@ -675,7 +707,7 @@ cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t 
         const unsigned gy = (unsigned)std::min<uint64_t>(B, 65535);
         makhoul_pack_generic_kernel<<<dim3(gx, gy), 256, 0, s>>>(
             d_in, ld_in, B, L, P, fdct_padded_p(P), Q, reinterpret_cast<const float4 *>(d_tables),
-            reinterpret_cast<uint32_t *>(d_out));
+            reinterpret_cast<uint32_t *>(d_out), bs, ks);
         return cudaGetLastError();
     }
     if (L % 32) return cudaErrorInvalidValue;
@@ -691,7 +723,7 @@ cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t 
     if (e != cudaSuccess) return e;
     kern<<<g, threads, smem, s>>>(d_in, ld_in, B, L, P, Q,
                                   reinterpret_cast<const float4 *>(d_tables), pack_rot(L, Q),
-                                  reinterpret_cast<uint32_t *>(d_out));
+                                  reinterpret_cast<uint32_t *>(d_out), bs, ks);
     return cudaGetLastError();
 }
 
@@ -704,9 +736,10 @@ bool spectral_pack_supported(uint64_t L) {
 cudaError_t launch_spectral_pack(const uint8_t *d_payload, uint64_t bmb, const uint32_t *d_chunk,
                                  const uint64_t *d_meta, uint64_t B, uint32_t L, uint32_t P,
                                  uint32_t Q, const float *d_tables, half_bits *d_out,
-                                 cudaStream_t s) {
+                                 bool k2_major, cudaStream_t s) {
     if (!spectral_pack_supported(L) || (uint64_t)P * Q != L / 2 || P % 4 || Q % 4)
         return cudaErrorInvalidValue;
+    const uint64_t bs = k2_major ? P : (uint64_t)Q * P, ks = k2_major ? B * P : P;
     const int qc = ((uintptr_t)d_out & 31) ? 0 : pack_qc(P, Q);
     const size_t smem = spack_smem_bytes(L, qc);
     const bool small = L <= 16384;
@@ -717,7 +750,7 @@ cudaError_t launch_spectral_pack(const uint8_t *d_payload, uint64_t bmb, const u
     if (e != cudaSuccess) return e;
     kern<<<g, threads, smem, s>>>(d_payload, bmb, d_chunk, rank_group_offset(B * (uint64_t)L),
                                   d_meta, B, L, P, Q, reinterpret_cast<const float4 *>(d_tables),
-                                  pack_rot(L, Q), reinterpret_cast<uint32_t *>(d_out));
+                                  pack_rot(L, Q), reinterpret_cast<uint32_t *>(d_out), bs, ks);
     return cudaGetLastError();
 }
 
@@ -732,6 +765,14 @@ cudaError_t launch_dft_matrix(uint32_t n, uint32_t rows_pad, uint32_t ld, half_b
                               cudaStream_t s) {
     const uint32_t total = rows_pad * ld;
     dft_matrix_kernel<<<(total + 255) / 256, 256, 0, s>>>(n, rows_pad, ld, d_out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_twiddled_dft_table(uint32_t P, uint32_t Q, uint32_t w_rows, uint32_t ld,
+                                      half_bits *d_out, cudaStream_t s) {
+    const uint64_t total = (uint64_t)Q * w_rows * ld;
+    const uint64_t g = std::min<uint64_t>((total + 255) / 256, 148ull * 64);
+    twiddled_dft_kernel<<<(unsigned)g, 256, 0, s>>>(P, Q, w_rows, ld, d_out);
     return cudaGetLastError();
 }
 

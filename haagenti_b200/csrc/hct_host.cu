@@ -178,6 +178,7 @@ struct hct_b200_ctx {
     std::map<uint64_t, std::unique_ptr<DevBuf>> dft_mats;  // realified n-point DFT (n, ld), fp16
     std::map<uint32_t, std::unique_ptr<DevBuf>> twiddles;  // e^{2 pi i j / H}, complex f32
     std::map<uint32_t, std::unique_ptr<DevBuf>> pack_tabs;  // Makhoul-pack twiddles per length
+    std::map<uint64_t, std::unique_ptr<DevBuf>> fold_tabs;  // per-k2 stage-1 matrices (P, Q, rows)
     DevBuf cos_tbl;
     int idct_mode = HCT_B200_IDCT_AUTO;
     bool profiling = false;
@@ -301,6 +302,11 @@ struct hct_b200_reader {
 };
 
 namespace {
+
+// Stage 1 with the twiddle folded into per-k2 matrices where the shapes allow.
+#ifndef FDCT_FOLD_TWIDDLE
+#define FDCT_FOLD_TWIDDLE 1
+#endif
 
 int ensure_device(hct_b200_ctx *ctx) {
     cudaError_t e = cudaSetDevice(ctx->device);
@@ -437,22 +443,42 @@ int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint
     }
     int *flag = dir.flag;
     const double elems = (double)batch * (double)L;
+    // Twiddle folded into per-k2 stage-1 matrices (stage modes 4 and 5): Z is
+    // written k2-major, stage 1 multiplies 128 lines of one k2 by that k2's
+    // matrix and stores G[m1][k2][ri][b] without any epilogue arithmetic, and
+    // stage 2 reads G as an MN-major operand.  Needs whole 128-line tiles per
+    // k2 and K-row blocks of 64 (Q % 32 == 0) inside the stage kernel's sizes.
+    const bool fold = FDCT_FOLD_TWIDDLE && batch % 128 == 0 && Q % 32 == 0 && 2 * Q <= 256 &&
+                      2 * Pp <= 256;
+    const half_bits *w4 = nullptr;
+    if (fold) {
+        const uint32_t wr = stage_w_rows(2ull * P, 2ull * Pp);
+        const uint64_t key = ((uint64_t)P << 32) | ((uint64_t)Q << 16) | wr;
+        auto it = ctx->fold_tabs.find(key);
+        if (it == ctx->fold_tabs.end()) {
+            auto b = std::make_unique<DevBuf>();
+            CK(b->reserve((size_t)Q * wr * 2 * Pp * 2));
+            CK(launch_twiddled_dft_table(P, Q, wr, 2 * Pp, b->as<half_bits>(), s));
+            it = ctx->fold_tabs.emplace(key, std::move(b)).first;
+        }
+        w4 = it->second->as<half_bits>();
+    }
     int slot = ctx->prof_begin(s);
     if (payload) {
         const uint64_t bmb = (batch * L + 7) / 8;
         CK(launch_spectral_pack(payload, bmb, dir.chunk, dir.meta,
                                 batch, (uint32_t)L, P, Q, pt->second->as<float>(),
-                                ctx->za.as<half_bits>(), s));
+                                ctx->za.as<half_bits>(), fold, s));
         // bitmap + ~0.3 of the INT4 section read, fp16 pairs written
         ctx->prof_end(slot, PK_SPACK, (double)bmb + 0.17 * elems + 2.0 * elems, s);
     } else {
         CK(launch_makhoul_pack(in, ld_in, batch, (uint32_t)L, P, Q, pt->second->as<float>(),
-                               ctx->za.as<half_bits>(), s));
+                               ctx->za.as<half_bits>(), fold, s));
         ctx->prof_end(slot, PK_PACK, 4.0 * elems, s);
     }
     CK(ctx->sched.reserve(64));
-    GemmArgs g1{ctx->za.as<half_bits>(), wp, batch * Q, 2ull * P, 2ull * Pp, 2ull * Pp, 2ull * Pp,
-                ctx->zb.p, 0, 2, HCT_B200_F16, flag};
+    GemmArgs g1{ctx->za.as<half_bits>(), fold ? w4 : wp, batch * Q, 2ull * P, 2ull * Pp, 2ull * Pp,
+                2ull * Pp, ctx->zb.p, 0, fold ? 4 : 2, HCT_B200_F16, flag};
     g1.tile_counter = ctx->sched.as<uint32_t>();
     g1.P = P;
     g1.Q = Q;
@@ -462,8 +488,8 @@ int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint
     slot = ctx->prof_begin(s);
     CK(launch_umma_gemm(g1, s));
     ctx->prof_end(slot, PK_DFT1, 4.0 * elems, s);
-    GemmArgs g2{ctx->zb.as<half_bits>(), wq, (uint64_t)P * batch, 2ull * Q, 2ull * Q, 2ull * Q,
-                2ull * Q, out, ldo, 3, out_dtype, flag};
+    GemmArgs g2{ctx->zb.as<half_bits>(), wq, (uint64_t)P * batch, 2ull * Q, 2ull * Q,
+                fold ? batch : 2ull * Q, 2ull * Q, out, ldo, fold ? 5 : 3, out_dtype, flag};
     g2.tile_counter = ctx->sched.as<uint32_t>() + 1;
     g2.P = P;
     g2.Q = Q;

@@ -67,6 +67,8 @@ struct StageParams {
     uint64_t batch;
     const float2 *twiddle;
     float scale;
+    // modes 4 and 5: data tiles per k2 (mode 4) or per m1 (mode 5), batch / 128
+    uint32_t tiles_per_group;
 };
 
 constexpr uint64_t WAIT_TIMEOUT_NS = 2000000000ull;  // 2 s per wait
@@ -128,6 +130,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
     return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
            (2ull << 61);
+}
+
+// UMMA shared-memory descriptor, MN-major, 128B swizzle: atoms of 8 K-rows x
+// 64 MN elements (128 bytes per row), 8-row K groups 1024 bytes apart (SBO),
+// 64-element MN chunks lbo bytes apart (LBO), version 1.
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t saddr, uint32_t lbo) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           (64ull << 32) | (1ull << 46) | (2ull << 61);
 }
 
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
@@ -409,12 +419,14 @@ struct StageCtl {
     uint64_t drain;
     uint64_t tid_full[TILE_SLOTS];   // tile index published (producer arrives)
     uint64_t tid_empty[TILE_SLOTS];  // tile index read (MMA thread + 8 epilogue warps)
+    uint64_t wempty;                 // mode 4: the MMAs that read the current W are done
     int tiles[TILE_SLOTS];           // tile index, -1 = no more tiles
     uint32_t tmem_base;
     int abort;
     int issued;    // ring slots the producer filled
     int consumed;  // ring slots whose "full" phase the MMA thread observed
-    int w_waited;  // the MMA thread observed the W load
+    int w_issued;  // W loads the producer issued (one per k2 in mode 4, else one)
+    int w_waited;  // W loads whose "wfull" phase the MMA thread observed
 };
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
@@ -555,6 +567,41 @@ __device__ __forceinline__ void stage1_chunk_t(const uint32_t (&r)[32], uint32_t
     __syncwarp();
 }
 
+// Stage 1 chunk of mode 4 (twiddle folded into the per-k2 W): lane o = 2 m1 + ri
+// holds columns c..c+31 of the tile, the 32 consecutive b at (tile % tpg) * 128
+// + c of one k2 = tile / tpg; each output row is 64 contiguous bytes of
+// G[m1][k2][ri][b], the MN-major layout stage 2 (mode 5) reads.  The warp's 32
+// rows are staged as 64-byte rows (16-byte pieces XOR-swizzled as in stage 2)
+// and stored 4 lanes per row, so every store instruction writes 8 whole rows.
+__device__ __forceinline__ void stage1_chunk_g4(const uint32_t (&r)[32], uint32_t o, uint32_t tile,
+                                                uint32_t c, void *out, const StageParams &sp,
+                                                uint8_t *xs, int lane) {
+    const uint32_t k2 = tile / sp.tiles_per_group;
+    const uint64_t b0 = (uint64_t)(tile - k2 * sp.tiles_per_group) * 128 + c;
+    const uint32_t wsw = ((uint32_t)lane >> 1) & 3;
+#pragma unroll
+    for (int t = 0; t < 4; t++)
+        *reinterpret_cast<uint4 *>(xs + lane * 64 + ((t ^ wsw) * 16)) = make_uint4(
+            pack_h2(__uint_as_float(r[8 * t]), __uint_as_float(r[8 * t + 1])),
+            pack_h2(__uint_as_float(r[8 * t + 2]), __uint_as_float(r[8 * t + 3])),
+            pack_h2(__uint_as_float(r[8 * t + 4]), __uint_as_float(r[8 * t + 5])),
+            pack_h2(__uint_as_float(r[8 * t + 6]), __uint_as_float(r[8 * t + 7])));
+    __syncwarp();
+    const uint32_t o_base = o - (uint32_t)lane, piece = lane & 3;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const uint32_t row = (uint32_t)(lane >> 2) + 8 * i;
+        const uint32_t oo = o_base + row, m1 = oo >> 1, ri = oo & 1u;
+        const uint4 val =
+            *reinterpret_cast<const uint4 *>(xs + row * 64 + ((piece ^ ((row >> 1) & 3)) * 16));
+        if (m1 < sp.P)
+            *reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(out) +
+                                       (((uint64_t)m1 * sp.Q + k2) * 2 + ri) * sp.batch + b0 +
+                                       8 * piece) = val;
+    }
+    __syncwarp();
+}
+
 // Stage 2 chunk: lane o = 2 m2 + ri holds columns rT..rT+31 = rows (m1, b).
 // With batch % 32 == 0 the chunk is one m1 and b0..b0+31: each output row
 // n(j, ri) receives 32 contiguous values, staged as 64-byte rows (two
@@ -665,6 +712,7 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
             mbar_init(smem_u32(&ctl->tempty[b]), 8);  // one arrive per epilogue warp
         }
         mbar_init(smem_u32(&ctl->drain), 1);
+        mbar_init(smem_u32(&ctl->wempty), 1);
         for (int t = 0; t < TILE_SLOTS; t++) {
             mbar_init(smem_u32(&ctl->tid_full[t]), 1);
             mbar_init(smem_u32(&ctl->tid_empty[t]), 9);  // MMA thread + 8 epilogue warps
@@ -672,10 +720,15 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
         ctl->abort = 0;
         ctl->issued = 0;
         ctl->consumed = 0;
+        ctl->w_issued = 0;
         ctl->w_waited = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
+    // mode 4: each CTA takes a contiguous range of tiles, so that the k2 of
+    // consecutive tiles (and with it the W in shared memory) rarely changes
+    const uint32_t per_cta = (m_tiles + gridDim.x - 1) / gridDim.x;
+    const uint32_t tpg = sp.tiles_per_group;
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(&ctl->tmem_base)),
@@ -693,14 +746,22 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmD))
                          : "memory");
             const uint32_t wb = smem_u32(&ctl->wfull);
-            mbar_expect_tx(wb, (uint32_t)(kbs * SC::W_KB_BYTES));
-            for (int kb = 0; kb < kbs; kb++)
-                tma_load_2d(smem_u32(w_smem + (size_t)kb * SC::W_KB_BYTES), &tmW, wb, kb * BK, 0);
-            int it = 0;
+            // mode 4: the per-k2 W is loaded when the k2 of the tiles changes
+            if (mode != 4) {
+                mbar_expect_tx(wb, (uint32_t)(kbs * SC::W_KB_BYTES));
+                for (int kb = 0; kb < kbs; kb++)
+                    tma_load_2d(smem_u32(w_smem + (size_t)kb * SC::W_KB_BYTES), &tmW, wb, kb * BK,
+                                0);
+                *(volatile int *)&ctl->w_issued = 1;
+            }
+            int it = 0, w_issued = 0;
+            uint32_t cur_g = 0xffffffffu;
             for (uint32_t i = 0;; i++) {
-                // the next tile: from the counter, or every gridDim.x-th
-                const uint32_t t = tile_counter ? atomicAdd(tile_counter, 1u)
-                                                : blockIdx.x + i * gridDim.x;
+                // the next tile: the CTA's range (mode 4), the counter, or every
+                // gridDim.x-th
+                const uint32_t t =
+                    mode == 4 ? (i < per_cta ? blockIdx.x * per_cta + i : m_tiles)
+                              : (tile_counter ? atomicAdd(tile_counter, 1u) : blockIdx.x + i * gridDim.x);
                 const int slot = (int)(i % TILE_SLOTS);
                 if (*(volatile int *)&ctl->abort) break;
                 if (!mbar_wait(smem_u32(&ctl->tid_empty[slot]), ((i / TILE_SLOTS) & 1u) ^ 1u)) {
@@ -712,6 +773,21 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
                 mbar_arrive(smem_u32(&ctl->tid_full[slot]));
                 if (t >= m_tiles) break;
                 const int r0 = (int)(t * NT);
+                if (mode == 4 && t / tpg != cur_g) {
+                    // the previous W must no longer be read by any MMA
+                    if (w_issued > 0 &&
+                        !mbar_wait(smem_u32(&ctl->wempty), (uint32_t)(w_issued - 1) & 1u)) {
+                        atomicExch(flag, HCT_B200_ERR_TIMEOUT);
+                        atomicExch(&ctl->abort, 1);
+                        break;
+                    }
+                    cur_g = t / tpg;
+                    mbar_expect_tx(wb, (uint32_t)(kbs * SC::W_KB_BYTES));
+                    for (int kb = 0; kb < kbs; kb++)
+                        tma_load_2d(smem_u32(w_smem + (size_t)kb * SC::W_KB_BYTES), &tmW, wb,
+                                    kb * BK, (int)(cur_g * SC::WROWS));
+                    *(volatile int *)&ctl->w_issued = ++w_issued;
+                }
                 bool stop = false;
                 for (int kb = 0; kb < kbs; kb++, it++) {
                     const int s = it % RING;
@@ -725,8 +801,17 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
                     }
                     const uint32_t fb = smem_u32(&ctl->full[s]);
                     mbar_expect_tx(fb, SC::B_TILE_BYTES);
-                    tma_load_2d(smem_u32(d_smem + (size_t)s * SC::B_TILE_BYTES), &tmD, fb, kb * BK,
-                                r0);
+                    uint8_t *slot_p = d_smem + (size_t)s * SC::B_TILE_BYTES;
+                    if (mode == 5) {
+                        // MN-major tile: K rows (k2, ri) of m1, 128 b as two 64-wide boxes
+                        const uint32_t m1 = t / tpg, b0 = (t - m1 * tpg) * NT;
+                        const int y = (int)(m1 * K) + kb * BK;
+                        tma_load_2d(smem_u32(slot_p), &tmD, fb, (int)b0, y);
+                        tma_load_2d(smem_u32(slot_p + SC::B_TILE_BYTES / 2), &tmD, fb, (int)b0 + 64,
+                                    y);
+                    } else {
+                        tma_load_2d(smem_u32(slot_p), &tmD, fb, kb * BK, r0);
+                    }
                     *(volatile int *)&ctl->issued = it + 1;
                 }
                 if (stop) break;
@@ -734,8 +819,14 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            bool ok = mbar_wait(smem_u32(&ctl->wfull), 0);
-            if (ok) *(volatile int *)&ctl->w_waited = 1;
+            bool ok = true;
+            int w_waited = 0;
+            uint32_t cur_g = 0xffffffffu;
+            if (mode != 4) {
+                ok = mbar_wait(smem_u32(&ctl->wfull), 0);
+                if (ok) *(volatile int *)&ctl->w_waited = w_waited = 1;
+            }
+            const uint32_t idesc = mode == 5 ? SC::IDESC | (1u << 16) : SC::IDESC;  // B MN-major
             int it = 0;
             for (uint32_t i = 0; ok; i++) {
                 const int buf = (int)(i & 1u);
@@ -749,6 +840,14 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
                 const int tile = *(volatile int *)&ctl->tiles[slot];
                 mbar_arrive(smem_u32(&ctl->tid_empty[slot]));
                 if (tile < 0) break;
+                if (mode == 4 && (uint32_t)tile / tpg != cur_g) {
+                    if (!mbar_wait(smem_u32(&ctl->wfull), (uint32_t)w_waited & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    *(volatile int *)&ctl->w_waited = ++w_waited;
+                    cur_g = (uint32_t)tile / tpg;
+                }
                 if (!mbar_wait(smem_u32(&ctl->tempty[buf]), (use & 1u) ^ 1u)) { ok = false; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t d = tmem + (uint32_t)(buf * MT * NT);
@@ -758,7 +857,11 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
                     if (!mbar_wait(smem_u32(&ctl->full[s]), ph)) { ok = false; break; }
                     *(volatile int *)&ctl->consumed = it + 1;
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint64_t db = umma_desc_sw128(smem_u32(d_smem + (size_t)s * SC::B_TILE_BYTES));
+                    const uint32_t sb = smem_u32(d_smem + (size_t)s * SC::B_TILE_BYTES);
+                    // K-major: +32 bytes per 16 K; MN-major: +16 rows of 128 bytes
+                    const uint64_t db = mode == 5 ? umma_desc_sw128_mn(sb, SC::B_TILE_BYTES / 2)
+                                                  : umma_desc_sw128(sb);
+                    const uint32_t dstep = mode == 5 ? 128u : 2u;
 #pragma unroll
                     for (int hh = 0; hh < MT; hh++) {
                         // rows 128 hh.. of the k-block: 16 core groups of 1 KB further
@@ -766,13 +869,19 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
                             smem_u32(w_smem + (size_t)kb * SC::W_KB_BYTES + (size_t)hh * 128 * 128));
 #pragma unroll
                         for (int k = 0; k < BK / 16; k++)
-                            umma_f16(d + (uint32_t)(hh * NT), da + 2 * k, db + 2 * k, SC::IDESC,
+                            umma_f16(d + (uint32_t)(hh * NT), da + 2 * k, db + dstep * k, idesc,
                                      (kb | k) != 0);
                     }
                     umma_commit(smem_u32(&ctl->empty[s]));
                 }
                 if (!ok) break;
                 umma_commit(smem_u32(&ctl->tfull[buf]));
+                if (mode == 4) {
+                    // the last tile of this W: release it to the producer once read
+                    const uint32_t nx = (uint32_t)tile + 1;
+                    const bool last = i + 1 >= per_cta || nx >= m_tiles || nx / tpg != cur_g;
+                    if (last) umma_commit(smem_u32(&ctl->wempty));
+                }
             }
             if (!ok) {
                 atomicExch(flag, HCT_B200_ERR_TIMEOUT);
@@ -832,7 +941,9 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
                 const int c = c_begin + 32 * ci;
                 uint32_t r[32];
                 tmem_ld32(taddr + (uint32_t)c, r);
-                if (mode == 2) {
+                if (mode == 4) {
+                    stage1_chunk_g4(r, o, (uint32_t)tile, (uint32_t)c, out, sp, xs, lane);
+                } else if (mode == 2) {
                     stage1_chunk_t(r, o, r0 + c, M, out, sp, xs, lane, tw_first[ci], tw_step,
                                    tw_fixed);
                 } else if (out_dtype == HCT_B200_F16) {
@@ -852,7 +963,9 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
     // ---- teardown: drain this CTA's copies and MMAs, then free TMEM ------
     __syncthreads();
     if (threadIdx.x == 0) {
-        if (!*(volatile int *)&ctl->w_waited && !mbar_wait(smem_u32(&ctl->wfull), 0))
+        // a W load nobody waited for (abort path): at most the latest one
+        const int wi = *(volatile int *)&ctl->w_issued, ww = *(volatile int *)&ctl->w_waited;
+        if (ww < wi && !mbar_wait(smem_u32(&ctl->wfull), (uint32_t)(wi - 1) & 1u))
             atomicExch(flag, HCT_B200_ERR_TIMEOUT);
         const int issued = *(volatile int *)&ctl->issued;
         const int consumed = *(volatile int *)&ctl->consumed;
@@ -956,7 +1069,8 @@ cudaError_t launch_bn(const GemmArgs &a, cudaStream_t s) {
     const uint32_t n_tiles = (uint32_t)((a.N + BN - 1) / BN);
     const uint64_t ctas = (uint64_t)m_tiles * n_tiles;
     if (ctas > 0x7fffffffull) return cudaErrorInvalidValue;
-    StageParams sp{a.P, a.Q, a.H, 0, a.batch, reinterpret_cast<const float2 *>(a.twiddle), a.scale};
+    StageParams sp{a.P, a.Q, a.H, 0, a.batch, reinterpret_cast<const float2 *>(a.twiddle), a.scale,
+                   0};
     umma_gemm_kernel<BN><<<(unsigned)ctas, THREADS, C::SMEM_BYTES, s>>>(
         ta, tb, (uint32_t)a.M, (uint32_t)a.N, (uint32_t)a.K, m_tiles, a.out, a.ldo, a.mode,
         a.out_dtype, a.d_flag, sp);
@@ -978,9 +1092,19 @@ template <int MT>
 cudaError_t launch_stage_t(const GemmArgs &a, cudaStream_t s) {
     using SC = StageTCfg<MT>;
     if (a.K > (uint64_t)SC::KB_MAX * BK || a.N > (uint64_t)SC::WROWS) return cudaErrorInvalidValue;
+    if ((a.mode == 4 || a.mode == 5) && a.batch % SC::NT) return cudaErrorInvalidValue;
+    if (a.mode == 5 && a.K % BK) return cudaErrorInvalidValue;  // K-row boxes stay in one m1
     alignas(64) CUtensorMap td, tw;
-    if (!make_operand_map(&td, a.A, a.M, a.K, a.lda, SC::NT)) return cudaErrorInvalidValue;
-    if (!make_operand_map(&tw, a.B, a.N, a.K, a.ldb, SC::WROWS)) return cudaErrorInvalidValue;
+    if (a.mode == 5) {
+        // G[m1][k2][ri][b]: P * 2Q rows of batch b, read as 64 x 64 MN-major boxes
+        if (!make_operand_map(&td, a.A, (uint64_t)a.P * a.K, a.batch, a.lda, BK))
+            return cudaErrorInvalidValue;
+    } else if (!make_operand_map(&td, a.A, a.M, a.K, a.lda, SC::NT)) {
+        return cudaErrorInvalidValue;
+    }
+    // mode 4: the table of per-k2 matrices, WROWS rows each
+    const uint64_t w_rows = a.mode == 4 ? (uint64_t)a.Q * SC::WROWS : a.N;
+    if (!make_operand_map(&tw, a.B, w_rows, a.K, a.ldb, SC::WROWS)) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(dft_stage_t_kernel<MT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)SC::SMEM_BYTES);
@@ -992,7 +1116,7 @@ cudaError_t launch_stage_t(const GemmArgs &a, cudaStream_t s) {
     // 16-byte output runs need an aligned base and row stride (stage 2)
     const uint32_t vec = ((uintptr_t)a.out % 16 == 0) && (a.ldo % 8 == 0);
     StageParams sp{a.P, a.Q, a.H, vec, a.batch, reinterpret_cast<const float2 *>(a.twiddle),
-                   a.scale};
+                   a.scale, (uint32_t)(a.batch / SC::NT)};
     if (a.tile_counter) {
         e = cudaMemsetAsync(a.tile_counter, 0, sizeof(uint32_t), s);
         if (e != cudaSuccess) return e;
@@ -1004,6 +1128,8 @@ cudaError_t launch_stage_t(const GemmArgs &a, cudaStream_t s) {
 }
 
 }  // namespace
+
+uint32_t stage_w_rows(uint64_t N, uint64_t K) { return N <= 128 && K <= 128 ? 128u : 256u; }
 
 cudaError_t launch_umma_gemm(const GemmArgs &a, cudaStream_t s) {
     if (a.M == 0 || a.N == 0) return cudaSuccess;
@@ -1019,6 +1145,11 @@ cudaError_t launch_umma_gemm(const GemmArgs &a, cudaStream_t s) {
         if (a.N <= 256 && a.K <= 256) return launch_stage_t<2>(a, s);
         // stage 1 with P > 128: output tiles of the general contraction
         return launch_bn<256>(a, s);
+    }
+    if (a.mode == 4 || a.mode == 5) {
+        if (!a.P || !a.Q || !a.batch || a.N > 256 || a.K > 256) return cudaErrorInvalidValue;
+        if (stage_w_rows(a.N, a.K) == 128) return launch_stage_t<1>(a, s);
+        return launch_stage_t<2>(a, s);
     }
     if (a.N <= 128) return launch_bn<128>(a, s);
     return launch_bn<256>(a, s);
