@@ -187,11 +187,13 @@ KERNEL_NAMES = {  # profile record -> kernel
     "spectral_rank": "hct::chunk_rank_kernel + hct::chunk_scan_kernel",
     "spectral_pack": "hct::spectral_pack_kernel (bitmap/INT4 decode + Makhoul pack, row axis)",
     "makhoul_pack": "hct::makhoul_pack_kernel (Makhoul pack, column axis)",
-    "dft_stage1": "hct::dft_stage_t_kernel mode 2 (tcgen05 DFT over k1, twiddled)",
-    "dft_stage2": "hct::dft_stage_t_kernel mode 3 (tcgen05 DFT over k2, quartet store)",
+    "dft_stage1": "hct::dft_stage_t_kernel modes 4/6 (tcgen05 DFT over k1, twiddle and, "
+                  "on column passes with 2P <= 128, the Makhoul pack folded into per-k2 matrices)",
+    "dft_stage2": "hct::dft_stage_t_kernel mode 5 (tcgen05 DFT over k2 from the MN-major "
+                  "intermediate, quartet store)",
     "umma_gemm": "hct::umma_gemm_kernel (dense-basis tcgen05 IDCT contraction)",
     "spectral_scatter": "hct::chunk_scan_kernel + hct::spectral_scatter_kernel",
-    "dequant_int4": "hct::dequant_int4_kernel",
+    "dequant_int4": "hct::dequant_int4_tiles_kernel (bulk-staged INT4 dequant)",
 }
 TRAFFIC_PROFILE = os.path.join(REPO, "profiles", "hct_decode_layer70b.md")
 

@@ -97,6 +97,12 @@ cudaError_t launch_basis(const double *d_cos_table, uint64_t n, half_bits *d_bas
 //           output G[m1][k2][ri][b] fp16
 //   mode 5: DFT stage 2 reading that G as an MN-major operand (A = G, lda =
 //           batch, K = 2Q a multiple of 64); output as mode 3
+//   mode 6: DFT stage 1 with the Makhoul pack and the twiddle folded into
+//           per-pair matrices: A holds the lines x as T'[n][k2][r] = x[Q r + k2]
+//           (batch lines of stride lda, 64 <= 2P <= 128, P % 4 == 0), a tile
+//           reads columns u and (Q - u) mod Q of 128 lines, B is the table of
+//           launch_makhoul_fold_table (N = 256 rows per pair, K = 128 kbc),
+//           M = (Q/2 + 1) batch; output G[m1][k2][ri][b] fp16 as mode 4
 struct GemmArgs {
     const half_bits *A;
     const half_bits *B;
@@ -125,6 +131,11 @@ uint32_t stage_w_rows(uint64_t N, uint64_t K);
 // e^{2 pi i m1 (Q k1 + k2) / H}.
 cudaError_t launch_twiddled_dft_table(uint32_t P, uint32_t Q, uint32_t w_rows, uint32_t ld,
                                       half_bits *d_out, cudaStream_t s);
+// The mode-6 table: for each pair u in [0, Q/2], 256 rows (G of k2 = u, then
+// of k2 = Q - u) x 128 kbc columns (kbc = ceil(2P / 64) values of column u,
+// then of column (Q - u) mod Q), fp16; (Q/2 + 1) 256 128 kbc entries.
+cudaError_t launch_makhoul_fold_table(uint32_t P, uint32_t Q, uint32_t kbc, half_bits *d_out,
+                                      cudaStream_t s);
 
 // ---- factored DCT-III (fdct.cu) -----------------------------------------
 // L even, H = L/2 = P*Q: preferably P, Q multiples of 4 and <= 128 (the most
@@ -139,9 +150,12 @@ uint32_t fdct_padded_p(uint32_t P);
 // rows of fdct_padded_p(P) values.  d_tables: the per-k pack coefficients
 // (natural k order) written by launch_pack_tables(L, P, Q).
 // k2_major: Z laid out [k2][b][k1] instead (the input of DFT stage mode 4).
+// perm_q != 0: line b is written at slot (b % perm_q) perm_2p + b / perm_q
+// (perm_q perm_2p == batch), the order whose transposed result the next
+// pass reads with stage mode 6 (Q = perm_q, 2P = perm_2p of that pass).
 cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t batch, uint32_t L,
                                 uint32_t P, uint32_t Q, const float *d_tables, half_bits *d_out,
-                                bool k2_major, cudaStream_t s);
+                                bool k2_major, uint32_t perm_q, uint32_t perm_2p, cudaStream_t s);
 // L/2 float4 (alpha_k, beta_k) in natural k order (P Q = L/2).
 cudaError_t launch_pack_tables(uint32_t L, uint32_t P, uint32_t Q, float *d_tables,
                                cudaStream_t s);
@@ -155,7 +169,10 @@ bool spectral_pack_supported(uint64_t L);
 cudaError_t launch_spectral_pack(const uint8_t *d_payload, uint64_t bmb, const uint32_t *d_chunk,
                                  const uint64_t *d_meta, uint64_t batch, uint32_t L, uint32_t P,
                                  uint32_t Q, const float *d_tables, half_bits *d_out,
-                                 bool k2_major, cudaStream_t s);
+                                 bool k2_major, uint32_t perm_q, uint32_t perm_2p,
+                                 cudaStream_t s, bool transposed = false);
+// transposed: no pack; each line is written as out[slot][k2][r] = c[Q r + k2]
+// (L values per line), the input of stage mode 6 (Q % 8 == 0, 2P <= 128).
 // ---- HoloTensor SV03 fragments (holo.cu) ---------------------------------
 // One residue class r of the raster positions p = r + F i: fragment values
 // vals[src + i - q0] for q0 <= i < q0 + count, no fragment when count == 0.

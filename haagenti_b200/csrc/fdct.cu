@@ -81,6 +81,14 @@ __device__ __forceinline__ void st_global_v8(uint32_t *p, const uint32_t (&v)[8]
                  : "memory");
 }
 
+// Output slot of line b: b itself, or, when the next pass folds the Makhoul
+// pack into its stage 1 (stage mode 6), (b mod pq) p2 + b / pq for that
+// pass's factors pq = Q and p2 = 2P, so that its lines read
+// T'[n][k2][r] = x[Q r + k2] as whole 2P-value columns.
+__device__ __forceinline__ uint64_t line_slot(uint64_t b, uint32_t pq, uint32_t p2) {
+    return pq ? (b % pq) * p2 + b / pq : b;
+}
+
 __device__ __forceinline__ float ld_h(const uint16_t *s, uint32_t i) {
     return __half2float(__ushort_as_half(s[i]));
 }
@@ -246,7 +254,7 @@ template <int THREADS, int QC, int J>
 __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 7 : 3) makhoul_pack_kernel(
     const uint16_t *__restrict__ in, uint64_t ld_in, uint64_t B, uint32_t L, uint32_t P,
     uint32_t Q, const float4 *__restrict__ coef, float4 rot, uint32_t *__restrict__ out,
-    uint64_t bs, uint64_t ks) {
+    uint64_t bs, uint64_t ks, uint32_t pq, uint32_t p2) {
     extern __shared__ uint4 smem_v[];
     uint16_t *srow = reinterpret_cast<uint16_t *>(smem_v);
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -265,9 +273,8 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 7 : 3) makhoul_pack_
             for (uint32_t k = threadIdx.x; k < L; k += THREADS) srow[spad<QC>(k)] = row[k];
         }
         __syncthreads();
-        pack_row<QC, J, true>(srow, coef, rot, L, P, Q, out + b * bs, ks, warp,
-                                 THREADS / 32,
-                        lane);
+        pack_row<QC, J, true>(srow, coef, rot, L, P, Q, out + line_slot(b, pq, p2) * bs, ks,
+                              warp, THREADS / 32, lane);
     }
 }
 
@@ -283,12 +290,12 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 7 : 3) makhoul_pack_
 __global__ void __launch_bounds__(256) makhoul_pack_generic_kernel(
     const uint16_t *__restrict__ in, uint64_t ld_in, uint64_t B, uint32_t L, uint32_t P,
     uint32_t Pp, uint32_t Q, const float4 *__restrict__ coef, uint32_t *__restrict__ out,
-    uint64_t bs, uint64_t ks) {
+    uint64_t bs, uint64_t ks, uint32_t pq, uint32_t p2) {
     const uint32_t H = L / 2, runs = Pp / 4;
     const uint64_t items = (uint64_t)runs * Q;
     for (uint64_t b = blockIdx.y; b < B; b += gridDim.y) {
         const uint16_t *row = in + b * ld_in;
-        uint32_t *orow = out + b * bs;
+        uint32_t *orow = out + line_slot(b, pq, p2) * bs;
         for (uint64_t it = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; it < items;
              it += (uint64_t)gridDim.x * blockDim.x) {
             const uint32_t g = (uint32_t)(it / Q), k2 = (uint32_t)(it - (uint64_t)g * Q);
@@ -349,6 +356,17 @@ __host__ __device__ __forceinline__ size_t spack_smem_bytes(uint32_t L, int qc) 
            spack_stage_bytes(L);
 }
 
+// Transposed staging of the TR variant (output for stage mode 6): Q rows
+// (k2) of tr_pitch(P) fp16 (r), 16-byte chunk c of row k2 at chunk
+// c ^ ((k2 >> 3) & 7), so that the expand's 2-byte stores (8 lanes at k2
+// 8 apart) and the copy-out's 16-byte loads are free of bank conflicts.
+__host__ __device__ __forceinline__ uint32_t tr_pitch(uint32_t P) {
+    return (2 * P + 63) / 64 * 64 + 8;
+}
+__host__ __device__ __forceinline__ size_t spack_tr_smem_bytes(uint32_t L, uint32_t P, uint32_t Q) {
+    return (size_t)Q * tr_pitch(P) * 2 + (size_t)spack_words_pad(L) * 12 + spack_stage_bytes(L);
+}
+
 // 16 bits of the nibble section at byte nb (even); bytes at or past nib_len
 // read as zero
 __device__ __forceinline__ uint32_t ld_nib16(const uint8_t *nibbles, uint32_t nb,
@@ -362,19 +380,27 @@ __device__ __forceinline__ uint16_t deq_nibble_h(uint32_t byte, uint32_t r, floa
     return __half_as_ushort(__float2half_rn(__fmul_rn((float)((int)nib - 8), scale)));
 }
 
-template <int THREADS, int QC, int J>
+// TR: instead of the pack, each line is written transposed, out[slot][k2][r]
+// = c[Q r + k2] (Q % 8 == 0, 2P <= 128), the input of stage mode 6 (which
+// folds the Makhoul pack into its matrices); steps C and D become
+//   C'. the expanded 8 elements of a byte (one r, k2 .. k2 + 7) are stored
+//       into the transposed staging;
+//   D'. the staging is copied out as 16-byte chunks of the contiguous
+//       2 P Q-value output line.
+template <int THREADS, int QC, int J, bool TR>
 __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack_kernel(
     const uint8_t *__restrict__ payload, uint64_t bmb, const uint32_t *__restrict__ chunk_base,
     uint64_t group_off, const uint64_t *__restrict__ meta, uint64_t B, uint32_t L, uint32_t P,
     uint32_t Q, const float4 *__restrict__ coef, float4 rot, uint32_t *__restrict__ out,
-    uint64_t bs, uint64_t ks) {
+    uint64_t bs, uint64_t ks, uint32_t pq, uint32_t p2) {
     constexpr uint32_t NW = THREADS / 32;
     extern __shared__ uint4 smem_v[];
     __shared__ uint32_t warp_tot[NW];
     __shared__ uint32_t s_rank0;
     const uint32_t W = L / 64;
     uint16_t *srow = reinterpret_cast<uint16_t *>(smem_v);
-    uint64_t *sw = reinterpret_cast<uint64_t *>(srow + srow_halves(L, QC));
+    const uint32_t pitch = tr_pitch(P);
+    uint64_t *sw = reinterpret_cast<uint64_t *>(srow + (TR ? Q * pitch : srow_halves(L, QC)));
     uint32_t *swr = reinterpret_cast<uint32_t *>(sw + spack_words_pad(L));
     uint8_t *stage = reinterpret_cast<uint8_t *>(swr + spack_words_pad(L));
     uint16_t *vals_s = reinterpret_cast<uint16_t *>(stage);
@@ -392,7 +418,7 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack
     // expand geometry of this lane: byte (lane & 7) of word (lane >> 3) of a span
     const uint32_t sub = lane >> 3, bsh = 8 * (lane & 7);
     const uint64_t below8 = (1ull << bsh) - 1ull;
-    if (tid == 0) srow[spad<QC>(L)] = 0;  // c[L] = 0 (never overwritten)
+    if (!TR && tid == 0) srow[spad<QC>(L)] = 0;  // c[L] = 0 (never overwritten)
 
     for (uint64_t b = blockIdx.x; b < B; b += gridDim.x) {
         __syncthreads();  // previous row fully consumed
@@ -507,13 +533,34 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack
                         gr += bit;
                     }
                 }
-                *reinterpret_cast<uint4 *>(srow + spad<QC>(64 * w + 8 * (lane & 7))) =
-                    make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16),
-                               h[6] | (h[7] << 16));
+                if (TR) {
+                    // elements n0 .. n0 + 7: one r, k2 = k20 .. k20 + 7
+                    const uint32_t n0 = 64 * w + 8 * (lane & 7);
+                    const uint32_t r = n0 / Q, k20 = n0 - r * Q;
+                    uint16_t *d = srow + k20 * pitch + 8 * ((r >> 3) ^ ((k20 >> 3) & 7)) + (r & 7);
+#pragma unroll
+                    for (int t = 0; t < 8; t++) d[t * pitch] = (uint16_t)h[t];
+                } else {
+                    *reinterpret_cast<uint4 *>(srow + spad<QC>(64 * w + 8 * (lane & 7))) =
+                        make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16),
+                                   h[6] | (h[7] << 16));
+                }
             }
         }
         __syncthreads();
-        pack_row<QC, J, false>(srow, coef, rot, L, P, Q, out + b * bs, ks, warp, NW, lane);
+        if (TR) {
+            // D'. line slot: Q rows of 2P values, contiguous
+            const uint32_t cpr = 2 * P / 8;  // 16-byte chunks per k2 row
+            uint4 *dst = reinterpret_cast<uint4 *>(out + line_slot(b, pq, p2) * bs);
+            for (uint32_t j = tid; j < L / 8; j += THREADS) {
+                const uint32_t k2 = j / cpr, c = j - k2 * cpr;
+                dst[j] = *reinterpret_cast<const uint4 *>(srow + k2 * pitch +
+                                                          8 * (c ^ ((k2 >> 3) & 7)));
+            }
+        } else {
+            pack_row<QC, J, false>(srow, coef, rot, L, P, Q, out + line_slot(b, pq, p2) * bs, ks,
+                                   warp, NW, lane);
+        }
     }
 }
 
@@ -583,6 +630,86 @@ __global__ void twiddled_dft_kernel(uint32_t P, uint32_t Q, uint32_t w_rows, uin
     }
 }
 
+// Per-pair stage-1 matrices of stage mode 6: the Makhoul pack and the
+// twiddle folded into stage 1.  That stage reads, for 128 lines n and a pair
+// u in [0, Q/2], columns u and (Q - u) mod Q of T'[n][k2][r] = x[Q r + k2]
+// (x the line of length L = 2H, H = P Q), each as kbc k-blocks of 64 values
+// (K = 128 kbc; the values past r = 2P read as zero).  Rows 0..127 (half
+// h = 0) give G[m1][k2] for k2 = u, rows 128..255 (h = 1) for k2 = Q - u
+// (zero for u = 0 and u = Q/2, whose pair has one k2):
+//   G[m1][k2] = sum_k1 e^{2 pi i m1 k / H} Z[k],  k = Q k1 + k2,
+//   Z[k] = alpha_k (a - i b) + beta_k (c - i d),
+//   a = x[k], b = x[L - k], c = x[H + k], d = x[H - k]   (x[L] = 0),
+// alpha_k and beta_k as in pack_tables_kernel.  The four inputs sit at
+//   a: column k2, r = k1            c: column k2, r = P + k1
+//   b: column C,  r = 2P - 1 - k1   d: column C,  r = P - 1 - k1   (C = Q - k2, k2 >= 1)
+//   b: column 0,  r = 2P - k1 (k1 >= 1)   d: column 0, r = P - k1  (k2 = 0)
+// where the k2 of the half is in block h of K and C in the other block.
+// Entry (u, 128 h + 2 m1 + ri, 64 kbc blk + r) is the real (ri = 0) or
+// imaginary (ri = 1) part of the complex coefficient of that real input,
+// evaluated in f64 and rounded once to fp16.
+__global__ void makhoul_fold_kernel(uint32_t P, uint32_t Q, uint32_t kbc, uint16_t *out) {
+    const uint64_t H = (uint64_t)P * Q, L = 2 * H;
+    const uint32_t K = 128 * kbc, KC = 64 * kbc;
+    const uint64_t per_u = 256ull * K, total = per_u * (Q / 2 + 1);
+    for (uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+         idx += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t u = (uint32_t)(idx / per_u);
+        const uint32_t rem = (uint32_t)(idx - (uint64_t)u * per_u);
+        const uint32_t row = rem / K, kk = rem - row * K;
+        const uint32_t h = row >> 7, m1 = (row & 127) >> 1, ri = row & 1;
+        const uint32_t blk = kk / KC, r = kk - blk * KC;
+        double v = 0.0;
+        if (m1 < P && r < 2 * P && (h == 0 || (u != 0 && 2 * u != Q))) {
+            const uint32_t k2 = h ? Q - u : u;
+            int role = -1;  // 0 a, 1 b, 2 c, 3 d
+            uint32_t k1 = 0;
+            if (blk == h) {
+                role = r < P ? 0 : 2;
+                k1 = r < P ? r : r - P;
+            } else if (k2 != 0) {
+                role = r < P ? 3 : 1;
+                k1 = r < P ? P - 1 - r : 2 * P - 1 - r;
+            } else if (r != 0) {
+                role = r <= P ? 3 : 1;
+                k1 = r <= P ? P - r : 2 * P - r;
+            }
+            if (role >= 0) {
+                const uint64_t k = (uint64_t)Q * k1 + k2;
+                double cr, ci;
+                if (role <= 1) {
+                    // alpha = w e^{i pi k / 2L} (1 + i t), t = e^{2 pi i k / L}
+                    double sa, ca, st, ct;
+                    sincospi((double)k / (2.0 * (double)L), &sa, &ca);
+                    sincospi(2.0 * (double)k / (double)L, &st, &ct);
+                    const double w = k == 0 ? 0.70710678118654752440 : 0.5;
+                    const double pr = 1.0 - st, pi_ = ct;
+                    cr = w * (ca * pr - sa * pi_);
+                    ci = w * (ca * pi_ + sa * pr);
+                } else {
+                    // beta = 1/2 e^{i pi (k + H) / 2L} (1 - i t)
+                    double sb, cb, st, ct;
+                    sincospi((double)(k + H) / (2.0 * (double)L), &sb, &cb);
+                    sincospi(2.0 * (double)k / (double)L, &st, &ct);
+                    const double qr = 1.0 + st, qi = -ct;
+                    cr = 0.5 * (cb * qr - sb * qi);
+                    ci = 0.5 * (cb * qi + sb * qr);
+                }
+                if (role == 1 || role == 3) {  // times -i
+                    const double t = cr;
+                    cr = ci;
+                    ci = -t;
+                }
+                const uint64_t j = ((uint64_t)m1 * k) % H;
+                double sn, cs;
+                sincospi(2.0 * (double)j / (double)H, &sn, &cs);
+                v = ri ? cs * ci + sn * cr : cs * cr - sn * ci;
+            }
+        }
+        out[idx] = __half_as_ushort(__double2half(v));
+    }
+}
+
 // e^{2 pi i j / H} for j < H, complex fp32 (re, im).
 __global__ void twiddle_table_kernel(uint32_t H, float2 *out) {
     for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j < H; j += gridDim.x * blockDim.x) {
@@ -644,10 +771,12 @@ int pack_qc(uint32_t P, uint32_t Q) {
 }
 
 using MakhoulFn = void (*)(const uint16_t *, uint64_t, uint64_t, uint32_t, uint32_t, uint32_t,
-                           const float4 *, float4, uint32_t *, uint64_t, uint64_t);
+                           const float4 *, float4, uint32_t *, uint64_t, uint64_t, uint32_t,
+                           uint32_t);
 using SpectralFn = void (*)(const uint8_t *, uint64_t, const uint32_t *, uint64_t,
                             const uint64_t *, uint64_t, uint32_t, uint32_t, uint32_t,
-                            const float4 *, float4, uint32_t *, uint64_t, uint64_t);
+                            const float4 *, float4, uint32_t *, uint64_t, uint64_t, uint32_t,
+                            uint32_t);
 
 // (e^{i pi Q / 2L}, e^{i 5 pi Q / 2L}): the steps of u and v along k1 (pack_run)
 float4 pack_rot(uint32_t L, uint32_t Q) {
@@ -668,9 +797,9 @@ MakhoulFn makhoul_fn(int qc) {
 template <int T>
 SpectralFn spectral_fn(int qc) {
     switch (qc) {
-        case 64: return spectral_pack_kernel<T, 64, 8>;
-        case 128: return spectral_pack_kernel<T, 128, 8>;
-        default: return spectral_pack_kernel<T, 0, 4>;
+        case 64: return spectral_pack_kernel<T, 64, 8, false>;
+        case 128: return spectral_pack_kernel<T, 128, 8, false>;
+        default: return spectral_pack_kernel<T, 0, 4, false>;
     }
 }
 
@@ -695,8 +824,9 @@ cudaError_t row_grid(F kern, int threads, size_t smem, uint64_t B, unsigned *gri
 
 cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t B, uint32_t L,
                                 uint32_t P, uint32_t Q, const float *d_tables, half_bits *d_out,
-                                bool k2_major, cudaStream_t s) {
+                                bool k2_major, uint32_t perm_q, uint32_t perm_2p, cudaStream_t s) {
     if ((uint64_t)P * Q != L / 2 || Q % 4 || L % 8) return cudaErrorInvalidValue;
+    if (perm_q && (uint64_t)perm_q * perm_2p != B) return cudaErrorInvalidValue;
     const uint64_t Pp = fdct_padded_p(P);
     // Z[b][k2][k1] (b stride Q Pp, k2 stride Pp) or Z[k2][b][k1] (Pp, B Pp)
     const uint64_t bs = k2_major ? Pp : (uint64_t)Q * Pp, ks = k2_major ? B * Pp : Pp;
@@ -707,7 +837,7 @@ cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t 
         const unsigned gy = (unsigned)std::min<uint64_t>(B, 65535);
         makhoul_pack_generic_kernel<<<dim3(gx, gy), 256, 0, s>>>(
             d_in, ld_in, B, L, P, fdct_padded_p(P), Q, reinterpret_cast<const float4 *>(d_tables),
-            reinterpret_cast<uint32_t *>(d_out), bs, ks);
+            reinterpret_cast<uint32_t *>(d_out), bs, ks, perm_q, perm_2p);
         return cudaGetLastError();
     }
     if (L % 32) return cudaErrorInvalidValue;
@@ -723,7 +853,7 @@ cudaError_t launch_makhoul_pack(const half_bits *d_in, uint64_t ld_in, uint64_t 
     if (e != cudaSuccess) return e;
     kern<<<g, threads, smem, s>>>(d_in, ld_in, B, L, P, Q,
                                   reinterpret_cast<const float4 *>(d_tables), pack_rot(L, Q),
-                                  reinterpret_cast<uint32_t *>(d_out), bs, ks);
+                                  reinterpret_cast<uint32_t *>(d_out), bs, ks, perm_q, perm_2p);
     return cudaGetLastError();
 }
 
@@ -736,9 +866,29 @@ bool spectral_pack_supported(uint64_t L) {
 cudaError_t launch_spectral_pack(const uint8_t *d_payload, uint64_t bmb, const uint32_t *d_chunk,
                                  const uint64_t *d_meta, uint64_t B, uint32_t L, uint32_t P,
                                  uint32_t Q, const float *d_tables, half_bits *d_out,
-                                 bool k2_major, cudaStream_t s) {
+                                 bool k2_major, uint32_t perm_q, uint32_t perm_2p,
+                                 cudaStream_t s, bool transposed) {
     if (!spectral_pack_supported(L) || (uint64_t)P * Q != L / 2 || P % 4 || Q % 4)
         return cudaErrorInvalidValue;
+    if (perm_q && (uint64_t)perm_q * perm_2p != B) return cudaErrorInvalidValue;
+    if (transposed) {
+        // lines of L values (16-byte aligned), Q a multiple of 8, 2P <= 128
+        if (Q % 8 || 2 * P > 128 || ((uintptr_t)d_out & 15)) return cudaErrorInvalidValue;
+        const size_t smem = spack_tr_smem_bytes(L, P, Q);
+        if (smem > 200 * 1024) return cudaErrorInvalidValue;
+        const bool small = L <= 16384;
+        const int threads = small ? 128 : 256;
+        SpectralFn kern = small ? spectral_pack_kernel<128, 0, 4, true>
+                                : spectral_pack_kernel<256, 0, 4, true>;
+        unsigned g = 0;
+        cudaError_t e = row_grid(kern, threads, smem, B, &g);
+        if (e != cudaSuccess) return e;
+        kern<<<g, threads, smem, s>>>(d_payload, bmb, d_chunk, rank_group_offset(B * (uint64_t)L),
+                                      d_meta, B, L, P, Q, reinterpret_cast<const float4 *>(d_tables),
+                                      pack_rot(L, Q), reinterpret_cast<uint32_t *>(d_out), L / 2, 0,
+                                      perm_q, perm_2p);
+        return cudaGetLastError();
+    }
     const uint64_t bs = k2_major ? P : (uint64_t)Q * P, ks = k2_major ? B * P : P;
     const int qc = ((uintptr_t)d_out & 31) ? 0 : pack_qc(P, Q);
     const size_t smem = spack_smem_bytes(L, qc);
@@ -750,7 +900,8 @@ cudaError_t launch_spectral_pack(const uint8_t *d_payload, uint64_t bmb, const u
     if (e != cudaSuccess) return e;
     kern<<<g, threads, smem, s>>>(d_payload, bmb, d_chunk, rank_group_offset(B * (uint64_t)L),
                                   d_meta, B, L, P, Q, reinterpret_cast<const float4 *>(d_tables),
-                                  pack_rot(L, Q), reinterpret_cast<uint32_t *>(d_out), bs, ks);
+                                  pack_rot(L, Q), reinterpret_cast<uint32_t *>(d_out), bs, ks,
+                                  perm_q, perm_2p);
     return cudaGetLastError();
 }
 
@@ -773,6 +924,15 @@ cudaError_t launch_twiddled_dft_table(uint32_t P, uint32_t Q, uint32_t w_rows, u
     const uint64_t total = (uint64_t)Q * w_rows * ld;
     const uint64_t g = std::min<uint64_t>((total + 255) / 256, 148ull * 64);
     twiddled_dft_kernel<<<(unsigned)g, 256, 0, s>>>(P, Q, w_rows, ld, d_out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_makhoul_fold_table(uint32_t P, uint32_t Q, uint32_t kbc, half_bits *d_out,
+                                      cudaStream_t s) {
+    if (kbc < 1 || kbc > 2 || 2 * P > 64 * kbc || Q % 2) return cudaErrorInvalidValue;
+    const uint64_t total = 256ull * 128 * kbc * (Q / 2 + 1);
+    const uint64_t g = std::min<uint64_t>((total + 255) / 256, 148ull * 32);
+    makhoul_fold_kernel<<<(unsigned)g, 256, 0, s>>>(P, Q, kbc, d_out);
     return cudaGetLastError();
 }
 

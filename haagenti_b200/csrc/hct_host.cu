@@ -179,6 +179,7 @@ struct hct_b200_ctx {
     std::map<uint32_t, std::unique_ptr<DevBuf>> twiddles;  // e^{2 pi i j / H}, complex f32
     std::map<uint32_t, std::unique_ptr<DevBuf>> pack_tabs;  // Makhoul-pack twiddles per length
     std::map<uint64_t, std::unique_ptr<DevBuf>> fold_tabs;  // per-k2 stage-1 matrices (P, Q, rows)
+    std::map<uint64_t, std::unique_ptr<DevBuf>> mfold_tabs;  // mode-6 per-pair matrices (P, Q)
     DevBuf cos_tbl;
     int idct_mode = HCT_B200_IDCT_AUTO;
     bool profiling = false;
@@ -307,6 +308,15 @@ namespace {
 #ifndef FDCT_FOLD_TWIDDLE
 #define FDCT_FOLD_TWIDDLE 1
 #endif
+// The second pass's Makhoul pack folded into its stage 1 (stage mode 6) where
+// the shapes allow.
+#ifndef FDCT_FOLD_MAKHOUL
+#define FDCT_FOLD_MAKHOUL 1
+#endif
+// ... and the first pass's, from a spectral payload
+#ifndef FDCT_FOLD_ROW
+#define FDCT_FOLD_ROW 1
+#endif
 
 int ensure_device(hct_b200_ctx *ctx) {
     cudaError_t e = cudaSetDevice(ctx->device);
@@ -417,15 +427,33 @@ bool spectral_fused(const hct_b200_ctx *ctx, uint64_t rows, uint64_t cols) {
            spectral_pack_supported(cols);
 }
 
+// Whether a pass over `batch` lines of length 2 P Q can take the Makhoul
+// pack folded into stage 1 (stage mode 6 reading the previous pass's
+// transposed output in the permuted line order, then stage 2 as mode 5).
+bool makhoul_fold_ok(uint64_t batch, uint32_t P, uint32_t Q) {
+    return FDCT_FOLD_MAKHOUL && FDCT_FOLD_TWIDDLE && batch % 128 == 0 && P % 4 == 0 &&
+           2 * P >= 64 && 2 * P <= 128 && Q % 32 == 0 && 2 * Q <= 256;
+}
+
+// Options of one pass: the slot order its pack writes the lines in (for a
+// next pass with the Makhoul fold; perm_q = 0 keeps line b at slot b), and
+// whether this pass is such a next pass (its input `in` then holds the lines
+// as T'[n][k2][r] and no pack runs).
+struct AxisOpts {
+    uint32_t perm_q = 0, perm_2p = 0;
+    bool makhoul_fold = false;
+};
+
 // One axis of the factored IDCT: rows of length L (fp16, stride ld_in) in
-// `in`, batch rows; the result is written transposed, out[n * ldo + b], in
+// `in`, batch rows; the result is written transposed, out[n * ldo + slot(b)], in
 // out_dtype (pack -> DFT stage 1 -> DFT stage 2, see fdct.cu).
 // The pack reads dense fp16 rows (`in`, stride ld_in) or, when `payload` is
 // set, decodes the rows straight from a spectral payload whose rank directory
 // launch_spectral_rank has put in dir.chunk / dir.meta.
 int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint8_t *payload,
               const RankDir &dir, uint64_t batch, uint64_t L, uint32_t P, uint32_t Q, void *out,
-              uint64_t ldo, int out_dtype, cudaStream_t s, hct_b200_error *err) {
+              uint64_t ldo, int out_dtype, cudaStream_t s, hct_b200_error *err,
+              const AxisOpts &opt = AxisOpts()) {
     const uint32_t H = (uint32_t)(L / 2);
     const uint32_t Pp = fdct_padded_p(P);  // Z rows: Pp complex, zeros past P
     const half_bits *wp = nullptr, *wq = nullptr;
@@ -443,6 +471,63 @@ int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint
     }
     int *flag = dir.flag;
     const double elems = (double)batch * (double)L;
+    CK(ctx->sched.reserve(64));
+    GemmArgs g2{ctx->zb.as<half_bits>(), wq, (uint64_t)P * batch, 2ull * Q, 2ull * Q, batch,
+                2ull * Q, out, ldo, 5, out_dtype, flag};
+    g2.tile_counter = ctx->sched.as<uint32_t>() + 1;
+    g2.P = P;
+    g2.Q = Q;
+    g2.H = H;
+    g2.batch = batch;
+    g2.scale = (float)std::sqrt(2.0 / (double)L);
+    if (opt.makhoul_fold) {
+        // no pack: stage 1 reads two columns of 128 lines of T' per tile and
+        // multiplies them by the pair's matrix (Makhoul coefficients and
+        // twiddle folded in), stage 2 as mode 5.  T' is the previous pass's
+        // output (`in`), or, for a spectral payload, the decoded lines written
+        // transposed by the spectral pack's TR variant.
+        if (!makhoul_fold_ok(batch, P, Q)) {
+            set_err(err, HCT_B200_ERR_INVALID_ARGUMENT, -1, 0, 0, 0,
+                    "Makhoul fold: unsupported pass (P %u, Q %u, %llu lines)", P, Q,
+                    (unsigned long long)batch);
+            return HCT_B200_ERR_INVALID_ARGUMENT;
+        }
+        const uint32_t kbc = (2 * P + 63) / 64;
+        const uint64_t key = ((uint64_t)P << 32) | Q;
+        auto it = ctx->mfold_tabs.find(key);
+        if (it == ctx->mfold_tabs.end()) {
+            auto b = std::make_unique<DevBuf>();
+            CK(b->reserve((size_t)(Q / 2 + 1) * 256 * 128 * kbc * 2));
+            CK(launch_makhoul_fold_table(P, Q, kbc, b->as<half_bits>(), s));
+            it = ctx->mfold_tabs.emplace(key, std::move(b)).first;
+        }
+        const half_bits *tin = in;
+        uint64_t tld = ld_in;
+        int slot = -1;
+        if (payload) {
+            const uint64_t bmb = (batch * L + 7) / 8;
+            slot = ctx->prof_begin(s);
+            CK(launch_spectral_pack(payload, bmb, dir.chunk, dir.meta, batch, (uint32_t)L, P, Q,
+                                    pt->second->as<float>(), ctx->za.as<half_bits>(), false,
+                                    opt.perm_q, opt.perm_2p, s, true));
+            ctx->prof_end(slot, PK_SPACK, (double)bmb + 0.17 * elems + 2.0 * elems, s);
+            tin = ctx->za.as<half_bits>();
+            tld = L;
+        }
+        GemmArgs g1{tin, it->second->as<half_bits>(), (uint64_t)(Q / 2 + 1) * batch, 256,
+                    128ull * kbc, tld, 128ull * kbc, ctx->zb.p, 0, 6, HCT_B200_F16, flag};
+        g1.P = P;
+        g1.Q = Q;
+        g1.H = H;
+        g1.batch = batch;
+        slot = ctx->prof_begin(s);
+        CK(launch_umma_gemm(g1, s));
+        ctx->prof_end(slot, PK_DFT1, 4.0 * elems, s);
+        slot = ctx->prof_begin(s);
+        CK(launch_umma_gemm(g2, s));
+        ctx->prof_end(slot, PK_DFT2, (2.0 + (out_dtype == HCT_B200_F32 ? 4.0 : 2.0)) * elems, s);
+        return HCT_B200_OK;
+    }
     // Twiddle folded into per-k2 stage-1 matrices (stage modes 4 and 5): Z is
     // written k2-major, stage 1 multiplies 128 lines of one k2 by that k2's
     // matrix and stores G[m1][k2][ri][b] without any epilogue arithmetic, and
@@ -468,15 +553,14 @@ int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint
         const uint64_t bmb = (batch * L + 7) / 8;
         CK(launch_spectral_pack(payload, bmb, dir.chunk, dir.meta,
                                 batch, (uint32_t)L, P, Q, pt->second->as<float>(),
-                                ctx->za.as<half_bits>(), fold, s));
+                                ctx->za.as<half_bits>(), fold, opt.perm_q, opt.perm_2p, s));
         // bitmap + ~0.3 of the INT4 section read, fp16 pairs written
         ctx->prof_end(slot, PK_SPACK, (double)bmb + 0.17 * elems + 2.0 * elems, s);
     } else {
         CK(launch_makhoul_pack(in, ld_in, batch, (uint32_t)L, P, Q, pt->second->as<float>(),
-                               ctx->za.as<half_bits>(), fold, s));
+                               ctx->za.as<half_bits>(), fold, opt.perm_q, opt.perm_2p, s));
         ctx->prof_end(slot, PK_PACK, 4.0 * elems, s);
     }
-    CK(ctx->sched.reserve(64));
     GemmArgs g1{ctx->za.as<half_bits>(), fold ? w4 : wp, batch * Q, 2ull * P, 2ull * Pp, 2ull * Pp,
                 2ull * Pp, ctx->zb.p, 0, fold ? 4 : 2, HCT_B200_F16, flag};
     g1.tile_counter = ctx->sched.as<uint32_t>();
@@ -488,14 +572,10 @@ int fdct_axis(hct_b200_ctx *ctx, const half_bits *in, uint64_t ld_in, const uint
     slot = ctx->prof_begin(s);
     CK(launch_umma_gemm(g1, s));
     ctx->prof_end(slot, PK_DFT1, 4.0 * elems, s);
-    GemmArgs g2{ctx->zb.as<half_bits>(), wq, (uint64_t)P * batch, 2ull * Q, 2ull * Q,
-                fold ? batch : 2ull * Q, 2ull * Q, out, ldo, fold ? 5 : 3, out_dtype, flag};
-    g2.tile_counter = ctx->sched.as<uint32_t>() + 1;
-    g2.P = P;
-    g2.Q = Q;
-    g2.H = H;
-    g2.batch = batch;
-    g2.scale = (float)std::sqrt(2.0 / (double)L);
+    if (!fold) {
+        g2.lda = 2ull * Q;
+        g2.mode = 3;
+    }
     slot = ctx->prof_begin(s);
     CK(launch_umma_gemm(g2, s));
     ctx->prof_end(slot, PK_DFT2, (2.0 + (out_dtype == HCT_B200_F32 ? 4.0 : 2.0)) * elems, s);
@@ -536,11 +616,23 @@ int run_idct(hct_b200_ctx *ctx, uint64_t rows, uint64_t cols, void *d_out, int o
         if (rows == 1)
             return fdct_axis(ctx, ctx->dense.as<half_bits>(), ldw, src, dir, 1, cols, pn, qn, d_out,
                              1, out_dtype, s, err);
+        // the column pass takes the Makhoul fold where it can: the row pass
+        // then writes its lines in that pass's column order
+        AxisOpts row_opt, col_opt;
+        if (makhoul_fold_ok(cols, pm, qm)) {
+            row_opt.perm_q = qm;
+            row_opt.perm_2p = 2 * pm;
+            col_opt.makhoul_fold = true;
+        }
+        // a spectral payload's row pass takes it too (its pack then only
+        // decodes and transposes)
+        row_opt.makhoul_fold = src != nullptr && FDCT_FOLD_ROW && makhoul_fold_ok(rows, pn, qn) &&
+                               qn % 8 == 0;
         int rc = fdct_axis(ctx, ctx->dense.as<half_bits>(), ldw, src, dir, rows, cols, pn, qn,
-                           ctx->tt.p, ldh, HCT_B200_F16, s, err);
+                           ctx->tt.p, ldh, HCT_B200_F16, s, err, row_opt);
         if (rc) return rc;
         return fdct_axis(ctx, ctx->tt.as<half_bits>(), ldh, nullptr, dir, cols, rows, pm, qm,
-                         d_out, cols, out_dtype, s, err);
+                         d_out, cols, out_dtype, s, err, col_opt);
     }
     const Basis *bw = nullptr, *bh = nullptr;
     int rc = get_basis(ctx, cols, &bw, s, err);

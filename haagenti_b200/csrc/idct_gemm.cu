@@ -67,8 +67,11 @@ struct StageParams {
     uint64_t batch;
     const float2 *twiddle;
     float scale;
-    // modes 4 and 5: data tiles per k2 (mode 4) or per m1 (mode 5), batch / 128
+    // modes 4, 5 and 6: data tiles per k2 (mode 4), per m1 (mode 5) or per
+    // column pair (mode 6), batch / 128
     uint32_t tiles_per_group;
+    // mode 6: 64-wide k-blocks per column (2P <= 64 kbc)
+    uint32_t kbc;
 };
 
 constexpr uint64_t WAIT_TIMEOUT_NS = 2000000000ull;  // 2 s per wait
@@ -122,6 +125,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
         " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar,
+                                            int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
         : "memory");
 }
 
@@ -567,17 +579,15 @@ __device__ __forceinline__ void stage1_chunk_t(const uint32_t (&r)[32], uint32_t
     __syncwarp();
 }
 
-// Stage 1 chunk of mode 4 (twiddle folded into the per-k2 W): lane o = 2 m1 + ri
-// holds columns c..c+31 of the tile, the 32 consecutive b at (tile % tpg) * 128
-// + c of one k2 = tile / tpg; each output row is 64 contiguous bytes of
-// G[m1][k2][ri][b], the MN-major layout stage 2 (mode 5) reads.  The warp's 32
-// rows are staged as 64-byte rows (16-byte pieces XOR-swizzled as in stage 2)
-// and stored 4 lanes per row, so every store instruction writes 8 whole rows.
-__device__ __forceinline__ void stage1_chunk_g4(const uint32_t (&r)[32], uint32_t o, uint32_t tile,
-                                                uint32_t c, void *out, const StageParams &sp,
-                                                uint8_t *xs, int lane) {
-    const uint32_t k2 = tile / sp.tiles_per_group;
-    const uint64_t b0 = (uint64_t)(tile - k2 * sp.tiles_per_group) * 128 + c;
+// Stage 1 chunk of modes 4 and 6 (twiddle folded into the per-k2 W): lane
+// o = 2 m1 + ri holds 32 consecutive lines b0..b0+31 of one k2; each output
+// row is 64 contiguous bytes of G[m1][k2][ri][b], the MN-major layout stage 2
+// (mode 5) reads.  The warp's 32 rows are staged as 64-byte rows (16-byte
+// pieces XOR-swizzled as in stage 2) and stored 4 lanes per row, so every
+// store instruction writes 8 whole rows.
+__device__ __forceinline__ void stage1_chunk_g(const uint32_t (&r)[32], uint32_t o, uint32_t k2,
+                                               uint64_t b0, void *out, const StageParams &sp,
+                                               uint8_t *xs, int lane) {
     const uint32_t wsw = ((uint32_t)lane >> 1) & 3;
 #pragma unroll
     for (int t = 0; t < 4; t++)
@@ -746,8 +756,10 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmD))
                          : "memory");
             const uint32_t wb = smem_u32(&ctl->wfull);
-            // mode 4: the per-k2 W is loaded when the k2 of the tiles changes
-            if (mode != 4) {
+            // modes 4 and 6: the per-group W is loaded when the group of the
+            // tiles changes
+            const bool wgroup = mode == 4 || mode == 6;
+            if (!wgroup) {
                 mbar_expect_tx(wb, (uint32_t)(kbs * SC::W_KB_BYTES));
                 for (int kb = 0; kb < kbs; kb++)
                     tma_load_2d(smem_u32(w_smem + (size_t)kb * SC::W_KB_BYTES), &tmW, wb, kb * BK,
@@ -760,8 +772,8 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
                 // the next tile: the CTA's range (mode 4), the counter, or every
                 // gridDim.x-th
                 const uint32_t t =
-                    mode == 4 ? (i < per_cta ? blockIdx.x * per_cta + i : m_tiles)
-                              : (tile_counter ? atomicAdd(tile_counter, 1u) : blockIdx.x + i * gridDim.x);
+                    wgroup ? (i < per_cta ? blockIdx.x * per_cta + i : m_tiles)
+                           : (tile_counter ? atomicAdd(tile_counter, 1u) : blockIdx.x + i * gridDim.x);
                 const int slot = (int)(i % TILE_SLOTS);
                 if (*(volatile int *)&ctl->abort) break;
                 if (!mbar_wait(smem_u32(&ctl->tid_empty[slot]), ((i / TILE_SLOTS) & 1u) ^ 1u)) {
@@ -773,7 +785,7 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
                 mbar_arrive(smem_u32(&ctl->tid_full[slot]));
                 if (t >= m_tiles) break;
                 const int r0 = (int)(t * NT);
-                if (mode == 4 && t / tpg != cur_g) {
+                if (wgroup && t / tpg != cur_g) {
                     // the previous W must no longer be read by any MMA
                     if (w_issued > 0 &&
                         !mbar_wait(smem_u32(&ctl->wempty), (uint32_t)(w_issued - 1) & 1u)) {
@@ -809,6 +821,14 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
                         tma_load_2d(smem_u32(slot_p), &tmD, fb, (int)b0, y);
                         tma_load_2d(smem_u32(slot_p + SC::B_TILE_BYTES / 2), &tmD, fb, (int)b0 + 64,
                                     y);
+                    } else if (mode == 6) {
+                        // k-block kb: 64 values of column u (first kbc blocks) or of
+                        // column (Q - u) mod Q, for 128 lines
+                        const uint32_t u = t / tpg, n0 = (t - u * tpg) * NT;
+                        const uint32_t blk = (uint32_t)kb / sp.kbc;
+                        const uint32_t col = blk == 0 ? u : (sp.Q - u) % sp.Q;
+                        tma_load_3d(smem_u32(slot_p), &tmD, fb, (int)(((uint32_t)kb - blk * sp.kbc) * BK),
+                                    (int)col, (int)n0);
                     } else {
                         tma_load_2d(smem_u32(slot_p), &tmD, fb, kb * BK, r0);
                     }
@@ -822,7 +842,8 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
             bool ok = true;
             int w_waited = 0;
             uint32_t cur_g = 0xffffffffu;
-            if (mode != 4) {
+            const bool wgroup = mode == 4 || mode == 6;
+            if (!wgroup) {
                 ok = mbar_wait(smem_u32(&ctl->wfull), 0);
                 if (ok) *(volatile int *)&ctl->w_waited = w_waited = 1;
             }
@@ -840,7 +861,7 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
                 const int tile = *(volatile int *)&ctl->tiles[slot];
                 mbar_arrive(smem_u32(&ctl->tid_empty[slot]));
                 if (tile < 0) break;
-                if (mode == 4 && (uint32_t)tile / tpg != cur_g) {
+                if (wgroup && (uint32_t)tile / tpg != cur_g) {
                     if (!mbar_wait(smem_u32(&ctl->wfull), (uint32_t)w_waited & 1u)) {
                         ok = false;
                         break;
@@ -876,7 +897,7 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
                 }
                 if (!ok) break;
                 umma_commit(smem_u32(&ctl->tfull[buf]));
-                if (mode == 4) {
+                if (wgroup) {
                     // the last tile of this W: release it to the producer once read
                     const uint32_t nx = (uint32_t)tile + 1;
                     const bool last = i + 1 >= per_cta || nx >= m_tiles || nx / tpg != cur_g;
@@ -936,13 +957,26 @@ __global__ void __launch_bounds__(STAGE_THREADS, MT == 1 ? 2 : 1)
             const uint32_t r0 = (uint32_t)tile * NT;
             const uint32_t taddr =
                 tmem + (uint32_t)(buf * MT * NT + hh * NT) + ((uint32_t)(q * 32) << 16);
+            // modes 4 and 6: the k2 of my outputs and the tile's first line
+            const uint32_t grp = (uint32_t)tile / tpg;
+            const uint64_t line0 = (uint64_t)((uint32_t)tile - grp * tpg) * NT;
+            uint32_t k2 = grp;
+            bool live = true;
+            if (mode == 6) {
+                // W half hh computes k2 = u (hh = 0) or Q - u (hh = 1); the
+                // pairs u = 0 and u = Q/2 have no second k2
+                k2 = hh ? sp.Q - grp : grp;
+                live = hh == 0 || (grp != 0 && 2 * grp != sp.Q);
+            }
 #pragma unroll
             for (int ci = 0; ci < NCH; ci++) {
                 const int c = c_begin + 32 * ci;
                 uint32_t r[32];
+                if (!live) break;  // warp-uniform
                 tmem_ld32(taddr + (uint32_t)c, r);
-                if (mode == 4) {
-                    stage1_chunk_g4(r, o, (uint32_t)tile, (uint32_t)c, out, sp, xs, lane);
+                if (mode == 4 || mode == 6) {
+                    stage1_chunk_g(r, mode == 6 ? o - 128u * (uint32_t)hh : o, k2, line0 + c, out,
+                                   sp, xs, lane);
                 } else if (mode == 2) {
                     stage1_chunk_t(r, o, r0 + c, M, out, sp, xs, lane, tw_first[ci], tw_step,
                                    tw_fixed);
@@ -1041,6 +1075,24 @@ bool make_operand_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_
     return r == CUDA_SUCCESS;
 }
 
+// 3-D fp16 operand of mode 6: lines of `cols` columns of `len` values each
+// (line stride ld elements), read as boxes of 64 values of one column for
+// box_lines lines (128-byte rows: the K-major, 128B-swizzled layout).
+bool make_column_map(CUtensorMap *map, const void *base, uint64_t len, uint64_t cols,
+                     uint64_t lines, uint64_t ld, uint32_t box_lines) {
+    EncodeTiledFn enc = get_encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[3] = {len, cols, lines};
+    cuuint64_t strides[2] = {len * 2, ld * 2};
+    cuuint32_t box[3] = {BK, 1, box_lines};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims,
+                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 cudaError_t launch_basis(const double *d_cos_table, uint64_t n, half_bits *d_basis, uint64_t ld,
@@ -1092,18 +1144,35 @@ template <int MT>
 cudaError_t launch_stage_t(const GemmArgs &a, cudaStream_t s) {
     using SC = StageTCfg<MT>;
     if (a.K > (uint64_t)SC::KB_MAX * BK || a.N > (uint64_t)SC::WROWS) return cudaErrorInvalidValue;
-    if ((a.mode == 4 || a.mode == 5) && a.batch % SC::NT) return cudaErrorInvalidValue;
+    if ((a.mode == 4 || a.mode == 5 || a.mode == 6) && a.batch % SC::NT)
+        return cudaErrorInvalidValue;
     if (a.mode == 5 && a.K % BK) return cudaErrorInvalidValue;  // K-row boxes stay in one m1
+    uint32_t kbc = 0;
+    if (a.mode == 6) {
+        // two columns of 2P values per line, each in kbc 64-wide k-blocks; the
+        // first box of a column lies inside it, 16-byte strides
+        kbc = (2 * a.P + BK - 1) / BK;
+        if (MT != 2 || 2 * a.P < (uint32_t)BK || 2 * a.P > 2u * BK || a.P % 4 || a.Q % 2 ||
+            a.K != 2ull * kbc * BK || a.M != (uint64_t)(a.Q / 2 + 1) * a.batch || a.lda % 8 ||
+            a.lda < 2ull * a.P * a.Q)
+            return cudaErrorInvalidValue;
+    }
     alignas(64) CUtensorMap td, tw;
     if (a.mode == 5) {
         // G[m1][k2][ri][b]: P * 2Q rows of batch b, read as 64 x 64 MN-major boxes
         if (!make_operand_map(&td, a.A, (uint64_t)a.P * a.K, a.batch, a.lda, BK))
             return cudaErrorInvalidValue;
+    } else if (a.mode == 6) {
+        // T'[n][k2][r]: batch lines of lda values, a line's Q columns of 2P
+        if (!make_column_map(&td, a.A, 2ull * a.P, a.Q, a.batch, a.lda, SC::NT))
+            return cudaErrorInvalidValue;
     } else if (!make_operand_map(&td, a.A, a.M, a.K, a.lda, SC::NT)) {
         return cudaErrorInvalidValue;
     }
-    // mode 4: the table of per-k2 matrices, WROWS rows each
-    const uint64_t w_rows = a.mode == 4 ? (uint64_t)a.Q * SC::WROWS : a.N;
+    // modes 4 and 6: the table of per-group matrices, WROWS rows each
+    const uint64_t w_rows = a.mode == 4   ? (uint64_t)a.Q * SC::WROWS
+                            : a.mode == 6 ? (uint64_t)(a.Q / 2 + 1) * SC::WROWS
+                                          : a.N;
     if (!make_operand_map(&tw, a.B, w_rows, a.K, a.ldb, SC::WROWS)) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(dft_stage_t_kernel<MT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1116,7 +1185,7 @@ cudaError_t launch_stage_t(const GemmArgs &a, cudaStream_t s) {
     // 16-byte output runs need an aligned base and row stride (stage 2)
     const uint32_t vec = ((uintptr_t)a.out % 16 == 0) && (a.ldo % 8 == 0);
     StageParams sp{a.P, a.Q, a.H, vec, a.batch, reinterpret_cast<const float2 *>(a.twiddle),
-                   a.scale, (uint32_t)(a.batch / SC::NT)};
+                   a.scale, (uint32_t)(a.batch / SC::NT), kbc};
     if (a.tile_counter) {
         e = cudaMemsetAsync(a.tile_counter, 0, sizeof(uint32_t), s);
         if (e != cudaSuccess) return e;
@@ -1149,6 +1218,10 @@ cudaError_t launch_umma_gemm(const GemmArgs &a, cudaStream_t s) {
     if (a.mode == 4 || a.mode == 5) {
         if (!a.P || !a.Q || !a.batch || a.N > 256 || a.K > 256) return cudaErrorInvalidValue;
         if (stage_w_rows(a.N, a.K) == 128) return launch_stage_t<1>(a, s);
+        return launch_stage_t<2>(a, s);
+    }
+    if (a.mode == 6) {
+        if (!a.P || !a.Q || !a.batch || a.N != 256 || a.K > 256) return cudaErrorInvalidValue;
         return launch_stage_t<2>(a, s);
     }
     if (a.N <= 128) return launch_bn<128>(a, s);

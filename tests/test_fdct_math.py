@@ -85,3 +85,87 @@ def test_two_axes_give_idct_2d():
     tt = axis(F, 8, 8)          # (128, 64) = T^T
     X = axis(tt, 4, 8)          # (64, 128)
     np.testing.assert_allclose(X, scipy.fft.idctn(F, type=2, norm="ortho"), atol=1e-10)
+
+
+def makhoul_fold_table(P, Q, kbc):
+    """The per-pair matrices of stage mode 6 (fdct.cu makhoul_fold_kernel), f64:
+    (Q/2 + 1, 256, 128 kbc), rows 128 h + 2 m1 + ri, columns 64 kbc blk + r."""
+    H = P * Q
+    L = 2 * H
+    KC = 64 * kbc
+    T = np.zeros((Q // 2 + 1, 256, 2 * KC))
+    m1 = np.arange(P)
+    for u in range(Q // 2 + 1):
+        for h in (0, 1):
+            if h == 1 and (u == 0 or 2 * u == Q):
+                continue
+            k2 = Q - u if h else u
+            for blk in (0, 1):
+                for r in range(2 * P):
+                    if blk == h:
+                        role, k1 = (0, r) if r < P else (2, r - P)
+                    elif k2 != 0:
+                        role, k1 = (3, P - 1 - r) if r < P else (1, 2 * P - 1 - r)
+                    elif r != 0:
+                        role, k1 = (3, P - r) if r <= P else (1, 2 * P - r)
+                    else:
+                        continue
+                    k = Q * k1 + k2
+                    if role <= 1:
+                        w = 1 / np.sqrt(2.0) if k == 0 else 0.5
+                        coef = w * np.exp(1j * np.pi * k / (2 * L)) * (1 + 1j * np.exp(2j * np.pi * k / L))
+                    else:
+                        coef = 0.5 * np.exp(1j * np.pi * (k + H) / (2 * L)) * (1 - 1j * np.exp(2j * np.pi * k / L))
+                    if role in (1, 3):
+                        coef = -1j * coef
+                    C = np.exp(2j * np.pi * ((m1 * k) % H) / H) * coef
+                    T[u, 128 * h + 2 * m1, KC * blk + r] = C.real
+                    T[u, 128 * h + 2 * m1 + 1, KC * blk + r] = C.imag
+    return T
+
+
+def stage1_fold(c, P, Q):
+    """Lines c (B, L) -> G[m1][b][k2] the way stage mode 6 computes it: the
+    lines read as T'[b][k2][r] = c[b][Q r + k2], pair u's tile multiplies
+    columns u and (Q - u) mod Q by the pair's matrix (no pack)."""
+    B, L = c.shape
+    kbc = (2 * P + 63) // 64
+    KC = 64 * kbc
+    tab = makhoul_fold_table(P, Q, kbc)
+    Tp = np.zeros((B, Q, KC))
+    Tp[:, :, : 2 * P] = c.reshape(B, 2 * P, Q).transpose(0, 2, 1)
+    G = np.zeros((P, B, Q), dtype=complex)
+    for u in range(Q // 2 + 1):
+        X = np.concatenate([Tp[:, u, :], Tp[:, (Q - u) % Q, :]], axis=1)  # (B, K)
+        D = tab[u] @ X.T  # (256, B)
+        G[:, :, u] = D[0 : 2 * P : 2] + 1j * D[1 : 2 * P : 2]
+        if u != 0 and 2 * u != Q:
+            G[:, :, Q - u] = D[128 : 128 + 2 * P : 2] + 1j * D[129 : 129 + 2 * P : 2]
+    return G
+
+
+@pytest.mark.parametrize("L,P,Q", [(8192, 64, 64), (4096, 32, 64), (14336, 56, 128),
+                                   (256, 32, 4), (512, 32, 8)])
+def test_makhoul_fold_matches_dct_iii(L, P, Q):
+    """Stage mode 6 (Makhoul pack and twiddle folded into per-pair matrices)
+    followed by stage 2 is the orthonormal DCT-III of the lines."""
+    c = np.random.default_rng(L + 7).standard_normal((3, L))
+    y = stage2(stage1_fold(c, P, Q), P, Q, L)
+    ref = scipy.fft.idct(c, type=2, norm="ortho", axis=1)
+    assert np.abs(y.T - ref).max() < 1e-9 * np.sqrt(L)
+
+
+def test_line_slot_permutation_feeds_the_fold():
+    """The row pass writes line b at slot (b % Q) 2P + b // Q (fdct.cu line_slot);
+    its transposed output row n is then T'[n][k2][r] = x_n[Q r + k2]."""
+    P, Q = 4, 8
+    M = 2 * P * Q
+    x = np.arange(M * 3).reshape(M, 3)  # x[b][n]: column n is the line of the next pass
+    slot = (np.arange(M) % Q) * 2 * P + np.arange(M) // Q
+    Tt = np.empty((3, M), dtype=x.dtype)
+    Tt[:, slot] = x.T
+    Tp = Tt.reshape(3, Q, 2 * P)
+    for n in range(3):
+        for k2 in range(Q):
+            for r in range(2 * P):
+                assert Tp[n, k2, r] == x[Q * r + k2, n]

@@ -71,7 +71,10 @@ def test_factored_full_gate_shape(hb, dev, ctxs):
 
 
 @pytest.mark.parametrize("shape", [(1024, 8192), (8192, 1024), (4096, 14336), (256, 512),
-                                   (320, 4608), (64, 28672)])
+                                   (320, 4608), (64, 28672),
+                                   # column passes with the Makhoul pack folded into
+                                   # stage 1 (2P = 128, 64 and 112 with Q = 128)
+                                   (8192, 256), (4096, 384), (14336, 256)])
 def test_factored_hct_decode(hb, orc, shape):
     from oracle import hct as OH
 
