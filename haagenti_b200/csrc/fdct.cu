@@ -400,6 +400,7 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack
     const uint32_t W = L / 64;
     uint16_t *srow = reinterpret_cast<uint16_t *>(smem_v);
     const uint32_t pitch = tr_pitch(P);
+    const int qsh = (Q & (Q - 1)) == 0 ? __ffs(Q) - 1 : -1;  // log2 Q, or -1
     uint64_t *sw = reinterpret_cast<uint64_t *>(srow + (TR ? Q * pitch : srow_halves(L, QC)));
     uint32_t *swr = reinterpret_cast<uint32_t *>(sw + spack_words_pad(L));
     uint8_t *stage = reinterpret_cast<uint8_t *>(swr + spack_words_pad(L));
@@ -536,7 +537,8 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack
                 if (TR) {
                     // elements n0 .. n0 + 7: one r, k2 = k20 .. k20 + 7
                     const uint32_t n0 = 64 * w + 8 * (lane & 7);
-                    const uint32_t r = n0 / Q, k20 = n0 - r * Q;
+                    const uint32_t r = qsh >= 0 ? n0 >> qsh : n0 / Q;
+                    const uint32_t k20 = n0 - r * Q;
                     uint16_t *d = srow + k20 * pitch + 8 * ((r >> 3) ^ ((k20 >> 3) & 7)) + (r & 7);
 #pragma unroll
                     for (int t = 0; t < 8; t++) d[t * pitch] = (uint16_t)h[t];
@@ -549,13 +551,16 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack
         }
         __syncthreads();
         if (TR) {
-            // D'. line slot: Q rows of 2P values, contiguous
-            const uint32_t cpr = 2 * P / 8;  // 16-byte chunks per k2 row
+            // D'. line slot: Q rows of 2P values, contiguous.  A warp step
+            // copies 32 / cp2 rows, lane (sub-row, chunk c) with cp2 the power
+            // of two >= the row's cpr 16-byte chunks (8 or 16)
+            const uint32_t cpr = 2 * P / 8;
+            const uint32_t csh = cpr > 8 ? 4 : 3, sr = lane >> csh, c = lane & ((1u << csh) - 1);
             uint4 *dst = reinterpret_cast<uint4 *>(out + line_slot(b, pq, p2) * bs);
-            for (uint32_t j = tid; j < L / 8; j += THREADS) {
-                const uint32_t k2 = j / cpr, c = j - k2 * cpr;
-                dst[j] = *reinterpret_cast<const uint4 *>(srow + k2 * pitch +
-                                                          8 * (c ^ ((k2 >> 3) & 7)));
+            if (c < cpr) {
+                for (uint32_t k2 = warp * (32u >> csh) + sr; k2 < Q; k2 += NW * (32u >> csh))
+                    dst[k2 * cpr + c] = *reinterpret_cast<const uint4 *>(
+                        srow + k2 * pitch + 8 * (c ^ ((k2 >> 3) & 7)));
             }
         } else {
             pack_row<QC, J, false>(srow, coef, rot, L, P, Q, out + line_slot(b, pq, p2) * bs, ks,

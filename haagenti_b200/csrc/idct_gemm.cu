@@ -446,6 +446,11 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 }
 
 constexpr int STAGE_THREADS = 320;  // producer, MMA, 8 epilogue warps
+constexpr int CTL_BYTES = 512;      // the StageCtl block at the end of shared memory
+static_assert(sizeof(StageCtl) <= CTL_BYTES, "StageCtl outgrew its reserve");
+#ifndef STAGE_RING2
+#define STAGE_RING2 5  // ring slots of the one-CTA-per-SM configuration (MT = 2)
+#endif
 
 // ---------------------------------------------------------------- output-major stages
 
@@ -479,13 +484,13 @@ struct StageTCfg {
     static constexpr int W_KB_BYTES = WROWS * BK * 2;  // one 64-column k-block of W
     static constexpr int NT = 128;                     // data rows per tile (MMA N)
     static constexpr int B_TILE_BYTES = NT * BK * 2;
-    static constexpr int RING = MT == 1 ? 3 : 4;
+    static constexpr int RING = MT == 1 ? 3 : STAGE_RING2;
     static constexpr int TMEM_COLS = 2 * MT * NT;      // double-buffered
     static constexpr int X_BYTES = 8 * XWARP_BYTES;    // epilogue staging, 8 warps
     // MT = 1: 32 KB of W + 48 KB ring + 16 KB staging -> two CTAs per SM;
-    // MT = 2: 128 KB of W + 64 KB ring + 16 KB staging -> one
+    // MT = 2: 128 KB of W + 80 KB ring + 16 KB staging -> one
     static constexpr size_t SMEM_BYTES = 1024 + (size_t)KB_MAX * W_KB_BYTES +
-                                         (size_t)RING * B_TILE_BYTES + X_BYTES + 256;
+                                         (size_t)RING * B_TILE_BYTES + X_BYTES + CTL_BYTES;
     static constexpr uint32_t IDESC =
         (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 };
