@@ -383,25 +383,26 @@ __device__ __forceinline__ uint16_t deq_nibble_h(uint32_t byte, uint32_t r, floa
 // TR: instead of the pack, each line is written transposed, out[slot][k2][r]
 // = c[Q r + k2] (Q % 8 == 0, 2P <= 128), the input of stage mode 6 (which
 // folds the Makhoul pack into its matrices); steps C and D become
-//   C'. the expanded 8 elements of a byte (one r, k2 .. k2 + 7) are stored
-//       into the transposed staging;
+//   C'. the staging (pitch TRP = tr_pitch(P), a compile-time 72 or 136) is
+//       cleared with 16-byte stores; then the set bits of a byte (one r,
+//       k2 .. k2 + 7) store their values into it, clear bits store nothing;
 //   D'. the staging is copied out as 16-byte chunks of the contiguous
 //       2 P Q-value output line.
-template <int THREADS, int QC, int J, bool TR>
+template <int THREADS, int QC, int J, int TRP>
 __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack_kernel(
     const uint8_t *__restrict__ payload, uint64_t bmb, const uint32_t *__restrict__ chunk_base,
     uint64_t group_off, const uint64_t *__restrict__ meta, uint64_t B, uint32_t L, uint32_t P,
     uint32_t Q, const float4 *__restrict__ coef, float4 rot, uint32_t *__restrict__ out,
     uint64_t bs, uint64_t ks, uint32_t pq, uint32_t p2) {
     constexpr uint32_t NW = THREADS / 32;
+    constexpr bool TR = TRP != 0;
     extern __shared__ uint4 smem_v[];
     __shared__ uint32_t warp_tot[NW];
     __shared__ uint32_t s_rank0;
     const uint32_t W = L / 64;
     uint16_t *srow = reinterpret_cast<uint16_t *>(smem_v);
-    const uint32_t pitch = tr_pitch(P);
     const int qsh = (Q & (Q - 1)) == 0 ? __ffs(Q) - 1 : -1;  // log2 Q, or -1
-    uint64_t *sw = reinterpret_cast<uint64_t *>(srow + (TR ? Q * pitch : srow_halves(L, QC)));
+    uint64_t *sw = reinterpret_cast<uint64_t *>(srow + (TR ? Q * (uint32_t)TRP : srow_halves(L, QC)));
     uint32_t *swr = reinterpret_cast<uint32_t *>(sw + spack_words_pad(L));
     uint8_t *stage = reinterpret_cast<uint8_t *>(swr + spack_words_pad(L));
     uint16_t *vals_s = reinterpret_cast<uint16_t *>(stage);
@@ -423,6 +424,11 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack
 
     for (uint64_t b = blockIdx.x; b < B; b += gridDim.x) {
         __syncthreads();  // previous row fully consumed
+        if (TR) {
+            // C'. (first half) the staging reads zero where no bit is set
+            for (uint32_t i = tid; i < Q * (uint32_t)TRP / 8; i += THREADS)
+                reinterpret_cast<uint4 *>(srow)[i] = make_uint4(0u, 0u, 0u, 0u);
+        }
         // A. bitmap words and their ranks
         uint32_t cnt = 0;
         for (uint32_t i = 0; i < wpt; i++) {
@@ -514,6 +520,32 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack
                 const uint64_t x = sw[w];
                 const uint32_t byte = bad ? 0u : (uint32_t)(x >> bsh) & 0xffu;
                 const uint32_t q = swr[w] + __popcll(x & below8);  // rank within the row
+                if (TR) {
+                    // elements n0 .. n0 + 7: one r, k2 = k20 .. k20 + 7
+                    const uint32_t n0 = 64 * w + 8 * (lane & 7);
+                    const uint32_t rr = qsh >= 0 ? n0 >> qsh : n0 / Q;
+                    const uint32_t k20 = n0 - rr * Q;
+                    uint16_t *d = srow + k20 * (uint32_t)TRP + 8 * ((rr >> 3) ^ ((k20 >> 3) & 7)) +
+                                  (rr & 7);
+                    if (packed) {
+                        uint32_t r = q + roff;
+#pragma unroll
+                        for (int t = 0; t < 8; t++) {
+                            if ((byte >> t) & 1u) d[t * TRP] = vals_s[r++];
+                        }
+                    } else {
+                        uint32_t gr = rank0 + q;
+#pragma unroll
+                        for (int t = 0; t < 8; t++) {
+                            if ((byte >> t) & 1u) {
+                                d[t * TRP] = deq_nibble_h(nib_s[(gr >> 1) - nb0], gr,
+                                                          sc_s[(gr >> 5) - sb0]);
+                                gr++;
+                            }
+                        }
+                    }
+                    continue;
+                }
                 uint32_t h[8];
                 if (packed) {
                     uint32_t r = q + roff;
@@ -534,19 +566,9 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack
                         gr += bit;
                     }
                 }
-                if (TR) {
-                    // elements n0 .. n0 + 7: one r, k2 = k20 .. k20 + 7
-                    const uint32_t n0 = 64 * w + 8 * (lane & 7);
-                    const uint32_t r = qsh >= 0 ? n0 >> qsh : n0 / Q;
-                    const uint32_t k20 = n0 - r * Q;
-                    uint16_t *d = srow + k20 * pitch + 8 * ((r >> 3) ^ ((k20 >> 3) & 7)) + (r & 7);
-#pragma unroll
-                    for (int t = 0; t < 8; t++) d[t * pitch] = (uint16_t)h[t];
-                } else {
-                    *reinterpret_cast<uint4 *>(srow + spad<QC>(64 * w + 8 * (lane & 7))) =
-                        make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16),
-                                   h[6] | (h[7] << 16));
-                }
+                *reinterpret_cast<uint4 *>(srow + spad<QC>(64 * w + 8 * (lane & 7))) =
+                    make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16),
+                               h[6] | (h[7] << 16));
             }
         }
         __syncthreads();
@@ -560,7 +582,7 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack
             if (c < cpr) {
                 for (uint32_t k2 = warp * (32u >> csh) + sr; k2 < Q; k2 += NW * (32u >> csh))
                     dst[k2 * cpr + c] = *reinterpret_cast<const uint4 *>(
-                        srow + k2 * pitch + 8 * (c ^ ((k2 >> 3) & 7)));
+                        srow + k2 * (uint32_t)TRP + 8 * (c ^ ((k2 >> 3) & 7)));
             }
         } else {
             pack_row<QC, J, false>(srow, coef, rot, L, P, Q, out + line_slot(b, pq, p2) * bs, ks,
@@ -802,9 +824,9 @@ MakhoulFn makhoul_fn(int qc) {
 template <int T>
 SpectralFn spectral_fn(int qc) {
     switch (qc) {
-        case 64: return spectral_pack_kernel<T, 64, 8, false>;
-        case 128: return spectral_pack_kernel<T, 128, 8, false>;
-        default: return spectral_pack_kernel<T, 0, 4, false>;
+        case 64: return spectral_pack_kernel<T, 64, 8, 0>;
+        case 128: return spectral_pack_kernel<T, 128, 8, 0>;
+        default: return spectral_pack_kernel<T, 0, 4, 0>;
     }
 }
 
@@ -883,8 +905,11 @@ cudaError_t launch_spectral_pack(const uint8_t *d_payload, uint64_t bmb, const u
         if (smem > 200 * 1024) return cudaErrorInvalidValue;
         const bool small = L <= 16384;
         const int threads = small ? 128 : 256;
-        SpectralFn kern = small ? spectral_pack_kernel<128, 0, 4, true>
-                                : spectral_pack_kernel<256, 0, 4, true>;
+        const bool narrow = tr_pitch(P) == 72;  // 2P <= 64; else 136
+        SpectralFn kern = small ? (narrow ? spectral_pack_kernel<128, 0, 4, 72>
+                                          : spectral_pack_kernel<128, 0, 4, 136>)
+                                : (narrow ? spectral_pack_kernel<256, 0, 4, 72>
+                                          : spectral_pack_kernel<256, 0, 4, 136>);
         unsigned g = 0;
         cudaError_t e = row_grid(kern, threads, smem, B, &g);
         if (e != cudaSuccess) return e;
