@@ -444,7 +444,7 @@ def model_leg(H, torch, dev, args, arch: str, seed: int, world: int, rank: int, 
                 pools[key] = torch.empty(s, dtype=torch.bfloat16, device=dev)
             outs[n] = pools[key]
     names = [n for n, _, _ in units]
-    window = max(1, min(MODEL_WINDOW, len(names) - 1))
+    window = max(1, min(getattr(args, "window", MODEL_WINDOW), len(names) - 1))
     pinned = None
 
     def run(steps, upload=False, serial=False):
@@ -560,7 +560,8 @@ def model_leg(H, torch, dev, args, arch: str, seed: int, world: int, rank: int, 
                                     "stream, no decode), the slowest rank",
                 "path": "HctReader.upload (pinned host -> HBM, copy stream) + "
                         "HctReader.decode_async per tensor, statuses read back "
-                        f"{window} tensors behind"},
+                        f"{window} tensors behind",
+                "host_binding": getattr(args, "host_binding", None)},
         "kernels": ks, "ms_prof": ms_prof, "clocks": clk.summary() if clk else None,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -636,6 +637,35 @@ def roofline_of(ks: dict, ms_prof, ms_per_step: float, steps: int,
     return roof, kern
 
 
+def bind_host_cpus(torch, local: int, enabled: bool = True) -> dict:
+    """Pin this rank's process to the CPUs NVML reports as local to its GPU, so
+    that the pinned host buffers it first-touches (the end-to-end uploads) sit
+    on the GPU's own NUMA node.  Reads the topology only; changes no GPU
+    setting.  Returns what was done (for the JSON line)."""
+    if not enabled:
+        return {"bound": False, "why": "--no-bind"}
+    try:
+        import pynvml
+
+        p = torch.cuda.get_device_properties(local)
+        bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            ncpu = os.cpu_count() or 1
+            masks = pynvml.nvmlDeviceGetCpuAffinity(h, (ncpu + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {64 * i + b for i, m in enumerate(masks) for b in range(64) if (int(m) >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return {"bound": False, "why": "no local CPUs reported"}
+        os.sched_setaffinity(0, cpus)
+        return {"bound": True, "pci": bus, "cpus": len(cpus)}
+    except Exception as e:  # no NVML, or no topology: run unbound
+        return {"bound": False, "why": f"{type(e).__name__}: {e}"[:120]}
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -645,6 +675,7 @@ def run_b200(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    args.host_binding = bind_host_cpus(torch, local, not args.no_bind)
     if world > 1:
         from datetime import timedelta
 
@@ -708,7 +739,7 @@ def run_b200(args):
                                "(partition.rs create_for_layers), embed/lm_head/norm by size; "
                                "no collective on the decode path",
                 "pipelining": "every tensor's decode enqueued on one of two decode contexts "
-                              f"(own stream each); statuses read back {MODEL_WINDOW} tensors "
+                              f"(own stream each); statuses read back {args.window} tensors "
                               "behind; steps follow each other without a drain",
                 "instrumentation": "value and e2e timed without the per-kernel profiling "
                                    "hook; kernel times from one more step with it, one tensor "
@@ -1310,6 +1341,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-bind", action="store_true",
+                    help="leave the process unbound (default: the GPU's local CPUs)")
+    ap.add_argument("--window", type=int, default=MODEL_WINDOW,
+                    help="whole-model legs: decodes in flight before a status is read back")
     ap.add_argument("--no-secondary", action="store_true", help="skip the LZ4 / INT4 lines")
     ap.add_argument("--tensors", default="", help="comma list of layer tensors (default: all)")
     ap.add_argument("--idct", choices=["auto", "scatter", "dense"], default="auto",
@@ -1335,6 +1370,7 @@ def run_leg(args):
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    args.host_binding = bind_host_cpus(torch, 0, not args.no_bind)
     stream = torch.cuda.current_stream(dev)
     if args.leg in ("model", "model8b", "layer"):
         # the decode legs alone on one GPU (profiling runs of their kernels)
