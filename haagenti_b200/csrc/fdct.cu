@@ -360,6 +360,9 @@ __host__ __device__ __forceinline__ size_t spack_smem_bytes(uint32_t L, int qc) 
 // (k2) of tr_pitch(P) fp16 (r), 16-byte chunk c of row k2 at chunk
 // c ^ ((k2 >> 3) & 7), so that the expand's 2-byte stores (8 lanes at k2
 // 8 apart) and the copy-out's 16-byte loads are free of bank conflicts.
+#ifndef SPACK_TR_CTAS
+#define SPACK_TR_CTAS 8  // resident CTAs per SM of the 128-thread TR variant (<= 64 registers)
+#endif
 __host__ __device__ __forceinline__ uint32_t tr_pitch(uint32_t P) {
     return (2 * P + 63) / 64 * 64 + 8;
 }
@@ -389,7 +392,8 @@ __device__ __forceinline__ uint16_t deq_nibble_h(uint32_t byte, uint32_t r, floa
 //   D'. the staging is copied out as 16-byte chunks of the contiguous
 //       2 P Q-value output line.
 template <int THREADS, int QC, int J, int TRP>
-__global__ void __launch_bounds__(THREADS, THREADS == 128 ? 6 : 2) spectral_pack_kernel(
+__global__ void __launch_bounds__(THREADS, THREADS == 128 ? (TRP ? SPACK_TR_CTAS : 6) : 2)
+    spectral_pack_kernel(
     const uint8_t *__restrict__ payload, uint64_t bmb, const uint32_t *__restrict__ chunk_base,
     uint64_t group_off, const uint64_t *__restrict__ meta, uint64_t B, uint32_t L, uint32_t P,
     uint32_t Q, const float4 *__restrict__ coef, float4 rot, uint32_t *__restrict__ out,

@@ -234,13 +234,15 @@ def test_overlapping_matches_all_periods(hb, orc, dev, staged):
 @pytest.mark.parametrize("staged", [False, True])
 def test_long_literal_runs_every_alignment_phase(hb, orc, dev, staged):
     """Literal runs of 1 KiB and more (copied 16 bytes at a time from two
-    aligned loads in the device-memory variant) at every source-minus-
+    aligned loads in the device-memory variant; from 2 KiB on through the
+    bulk-copied shared-memory chunks of 4080 new bytes each, so lengths
+    around one, two and three chunks are included) at every source-minus-
     destination offset mod 16 and several block starts: same bytes as the oracle."""
     import torch
 
     rng = np.random.default_rng(14)
     comps, sizes = [], []
-    for run in (1024, 1031, 2063, 8200, 9001):
+    for run in (1024, 1031, 2063, 4079, 4097, 8161, 8200, 9001, 12241):
         for shift in range(16):
             for lead in (5, 6, 7, 8):
                 head = rng.integers(0, 256, lead, dtype=np.uint8).tobytes()
