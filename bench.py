@@ -422,8 +422,13 @@ def model_leg(H, torch, dev, args, arch: str, seed: int, world: int, rank: int, 
     barrier()
     ctxs = (H.Context(local), H.Context(local))
     stream = torch.cuda.current_stream(dev)
-    stream2 = torch.cuda.Stream(dev)
-    streams = (stream, stream2)
+    if args.priority:
+        # the two decode streams above the library's side streams (default,
+        # lowest priority): stage-kernel CTAs are scheduled before front-end ones
+        streams = (torch.cuda.Stream(dev, priority=-args.priority),
+                   torch.cuda.Stream(dev, priority=-args.priority))
+    else:
+        streams = (stream, torch.cuda.Stream(dev))
     copy_stream = torch.cuda.Stream(dev)
     lane = {n: i % 2 for i, (n, _, _) in enumerate(units)}
     readers = {n: H.HctReader(files[n], ctxs[lane[n]]) for n, _, _ in units}
@@ -468,12 +473,15 @@ def model_leg(H, torch, dev, args, arch: str, seed: int, world: int, rank: int, 
         barrier()
         torch.cuda.synchronize(dev)
         e0.record(stream)
-        stream2.wait_event(e0)
-        copy_stream.wait_event(e0)
+        for s_ in streams + (copy_stream,):
+            if s_ != stream:
+                s_.wait_event(e0)
         run(steps, upload)
-        done2 = torch.cuda.Event()
-        done2.record(stream2)
-        stream.wait_event(done2)
+        for s_ in streams:
+            if s_ != stream:
+                done = torch.cuda.Event()
+                done.record(s_)
+                stream.wait_event(done)
         e1.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
@@ -1343,6 +1351,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-bind", action="store_true",
                     help="leave the process unbound (default: the GPU's local CPUs)")
+    ap.add_argument("--priority", type=int, default=0,
+                    help="whole-model legs: decode streams at this priority above the default")
     ap.add_argument("--window", type=int, default=MODEL_WINDOW,
                     help="whole-model legs: decodes in flight before a status is read back")
     ap.add_argument("--no-secondary", action="store_true", help="skip the LZ4 / INT4 lines")

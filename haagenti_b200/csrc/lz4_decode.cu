@@ -184,6 +184,9 @@ constexpr uint32_t LZ4_OUT_MAX = 16384;                  // staged decompressed 
 constexpr uint32_t LZ4_OUT_BYTES = LZ4_OUT_MAX + 32;
 constexpr uint32_t LZ4_SLOT_BYTES = LZ4_STAGE_BYTES + LZ4_OUT_BYTES;
 constexpr int LZ4_STAGED_WARPS = 2;  // warps per CTA: 64 KiB of shared memory, 3 CTAs per SM
+#ifndef LZ4_STAGED_MAX_CTAS
+#define LZ4_STAGED_MAX_CTAS (148ull * 3)  // grid cap: one resident wave, CTAs loop over blocks
+#endif
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     const uint32_t sa = (uint32_t)__cvta_generic_to_shared(smem);
@@ -382,7 +385,7 @@ cudaError_t launch_lz4_blocks(const uint8_t *d_src, const hct_b200_lz4_block *d_
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         uint64_t ctas = (n + LZ4_STAGED_WARPS - 1) / LZ4_STAGED_WARPS;
-        if (ctas > 148ull * 3) ctas = 148ull * 3;
+        if (ctas > LZ4_STAGED_MAX_CTAS) ctas = LZ4_STAGED_MAX_CTAS;
         lz4_decode_blocks_kernel<true><<<(unsigned)ctas, 32 * LZ4_STAGED_WARPS, smem, s>>>(
             d_src, d_blocks, n, d_dst, d_status);
         return cudaGetLastError();
