@@ -23,6 +23,15 @@
 //   stage 2 G  rows (m1, b), K=2Q   -> Y  [n][b]              (transposed)
 // so two applications (rows, then the rows of the transposed result) give
 // the 2-D transform X = A_M F A_N^T with the output in row-major order.
+// The folded forms (stage modes 4-6, idct_gemm.cu) change the layouts:
+//   mode 4: Z [k2][b][k1] (the pack's k2_major output), stage 1 with the
+//           twiddle in per-k2 matrices -> G [m1][k2][re,im][b];
+//   mode 6: no Z at all where 64 <= 2P <= 128: the lines stored as
+//           T'[b][k2][r] = x[Q r + k2] (the spectral pack's TR output, or the
+//           previous pass's transposed output with its lines in the slot
+//           order of line_slot) and stage 1 with the Makhoul coefficients
+//           and the twiddle in per-(k2, Q - k2) matrices -> the same G;
+//   mode 5: stage 2 reading G as an MN-major operand -> Y [n][b].
 //
 // The pack is written with the combined coefficients
 //   alpha_k = w_k' e^{i pi k / 2L} (1 + i e^{2 pi i k / L}),  w_0' = 1/sqrt(2), w_k' = 1/2
