@@ -413,13 +413,15 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // ---------------------------------------------------------------- DFT stages
 //
-// Persistent kernel for the factored-DCT stages (modes 2 and 3): the stage's
-// realified DFT matrix (the B operand, at most 256 x 256 fp16) is loaded into
-// shared memory once per CTA; 128-row tiles of the data (the A operand) then
-// stream through a ring of 64-column k-block stages, and two TMEM
-// accumulators alternate so that the epilogue of one tile overlaps the TMA
-// loads and MMAs of the next.  One CTA per SM; same warp roles and bounded
-// waits as umma_gemm_kernel.
+// Persistent kernel for the factored-DCT stages (modes 2-6): the stage's
+// realified DFT matrix (at most 256 x 256 fp16; per k2 in mode 4 and per
+// k2 pair in mode 6, reloaded when the tiles' group changes) is loaded into
+// shared memory as the A operand; 128-line tiles of the data (the B
+// operand) then stream through a ring of 64-column k-block stages, and two
+// TMEM accumulators alternate so that the epilogue of one tile overlaps the
+// TMA loads and MMAs of the next.  Two CTAs per SM for matrices of at most
+// 128 rows and columns, one for up to 256; same warp roles and bounded waits
+// as umma_gemm_kernel.
 constexpr int TILE_SLOTS = 4;  // tiles announced ahead by the producer
 
 struct StageCtl {
