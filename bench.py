@@ -455,9 +455,15 @@ def model_leg(H, torch, dev, args, arch: str, seed: int, world: int, rank: int, 
     def run(steps, upload=False, serial=False):
         pend = deque()
         for _ in range(steps):
+            if upload and args.upload_first:
+                # the step's files go to the copy stream first (each waits only
+                # for the previous decode of its own reader), so that the copy
+                # engine never waits for the host's decode loop
+                for n in names:
+                    readers[n].upload(pinned[n], stream=copy_stream)
             for n in names:
                 r = readers[n]
-                if upload:
+                if upload and not args.upload_first:
                     r.upload(pinned[n], stream=copy_stream)
                 r.decode_async(outs[n], H.BF16, stream=streams[lane[n]])
                 pend.append(r)
@@ -566,8 +572,10 @@ def model_leg(H, torch, dev, args, arch: str, seed: int, world: int, rank: int, 
                 "h2d_ceiling_GBps_per_rank": round(h2d / (copy_ms / 1e3) / 1e9, 2),
                 "h2d_ceiling_note": "the same uploads alone on every rank at once (copy "
                                     "stream, no decode), the slowest rank",
-                "path": "HctReader.upload (pinned host -> HBM, copy stream) + "
-                        "HctReader.decode_async per tensor, statuses read back "
+                "path": "HctReader.upload (pinned host -> HBM, copy stream"
+                        + (", a step's uploads enqueued before its decodes"
+                           if getattr(args, "upload_first", True) else "")
+                        + ") + HctReader.decode_async per tensor, statuses read back "
                         f"{window} tensors behind",
                 "host_binding": getattr(args, "host_binding", None)},
         "kernels": ks, "ms_prof": ms_prof, "clocks": clk.summary() if clk else None,
@@ -1351,6 +1359,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-bind", action="store_true",
                     help="leave the process unbound (default: the GPU's local CPUs)")
+    ap.add_argument("--interleave-uploads", dest="upload_first", action="store_false",
+                    help="end to end: upload each file just before its decode "
+                         "(default: a step's uploads are enqueued before its decodes)")
     ap.add_argument("--priority", type=int, default=0,
                     help="whole-model legs: decode streams at this priority above the default")
     ap.add_argument("--window", type=int, default=MODEL_WINDOW,
